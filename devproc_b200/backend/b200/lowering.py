@@ -1,0 +1,821 @@
+"""Lower an IR Function to launch records over a statically planned arena.
+
+Replaces the reference's compile step (src/devproc/backend/triton/
+compiler.py:476-536), which recorded ``tensor_allocations`` and placeholder
+kernel specs and left all real work to a per-call, per-op JIT loop
+(compiler.py:206-358).  Here every decision is made once, on the host, at
+compile time:
+
+* fusion — one launch per dataflow region:
+    - ``resize`` → [to(f32)] → [normalize] → [transpose to planar] → [to(float)]
+      becomes one preprocessing record (``dp_preproc``);
+    - ``linear``/``matmul`` absorb a following bias add, one activation
+      (relu / gelu / silu), a residual add and a float cast into the GEMM
+      epilogue (``dp_gemm``);
+    - softmax / argmax / sum / max / min / mean / layer_norm / rms_norm over the
+      last dim become one row-reduction record, argmax absorbing its int cast;
+    - remaining chains of elementwise ops (casts, normalise, activations,
+      broadcast arithmetic, transposes) become one region record each;
+* views — ``reshape`` aliases storage, ``transpose`` only permutes strides;
+  a consumer that needs contiguous data gets a region copy;
+* memory — every intermediate lives in one arena at an offset chosen by
+  liveness (first fit, 256-byte aligned), so running allocates nothing.
+"""
+
+import ctypes
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Tuple
+
+from ... import _native as N
+from ...ir.base import Op, Value
+from ...ir.function import Function
+from ...ir.types import DTYPE_BYTES, FLOAT_DTYPES, ScalarType, TensorType
+from ..base import CompilationError, UnsupportedOpError
+
+ALIGN = 256
+
+ELEMENTWISE_UNARY = {"relu": "relu", "sigmoid": "sigmoid", "tanh": "tanh", "exp": "exp", "neg": "neg",
+                     "abs": "abs", "silu": "silu"}
+ELEMENTWISE_BINARY = {"add": "add", "sub": "sub", "mul": "mul", "div": "div"}
+SCALAR_OPS = {"add_scalar": "add", "sub_scalar": "sub", "mul_scalar": "mul", "div_scalar": "div",
+              "pow_scalar": None}
+ELEMENTWISE = (set(ELEMENTWISE_UNARY) | set(ELEMENTWISE_BINARY) | {k for k, v in SCALAR_OPS.items() if v}
+               | {"gelu", "to", "normalize", "transpose", "reshape"})
+ROW_OPS = {"softmax", "argmax", "sum", "max", "min", "mean", "layer_norm", "rms_norm"}
+HOST_OPS = {"load_tokenizer", "tokenize_encode", "tokenize_decode", "string_length", "string_concat",
+            "string_slice", "string_format", "dict_create", "dict_get", "dict_set", "dict_size"}
+
+
+def contiguous_strides(shape: Tuple[int, ...]) -> Tuple[int, ...]:
+    st, acc = [], 1
+    for s in reversed(shape):
+        st.append(acc)
+        acc *= s
+    return tuple(reversed(st))
+
+
+def _prod(xs) -> int:
+    p = 1
+    for x in xs:
+        p *= x
+    return p
+
+
+@dataclass(eq=False)
+class Buffer:
+    """One storage slot of the program."""
+    kind: str            # "input" | "const" | "output" | "arena"
+    dtype: str
+    shape: Tuple[int, ...]
+    name: str
+    offset: int = 0      # arena byte offset
+    first: int = -1      # first record touching it
+    last: int = -1       # last record touching it
+    slot: int = -1
+
+    @property
+    def nbytes(self) -> int:
+        return max(1, _prod(self.shape)) * DTYPE_BYTES[self.dtype]
+
+
+@dataclass
+class View:
+    """An IR value seen as (buffer, shape, element strides, element offset)."""
+    buf: Buffer
+    shape: Tuple[int, ...]
+    strides: Tuple[int, ...]
+    offset: int = 0
+
+    @property
+    def contiguous(self) -> bool:
+        return self.offset == 0 and all(
+            st == cs for st, cs, s in zip(self.strides, contiguous_strides(self.shape), self.shape) if s != 1)
+
+
+@dataclass
+class Record:
+    kernel: int
+    operands: List[Optional[Buffer]]
+    params: ctypes.Structure
+    label: str
+    flops: int = 0
+    bytes: int = 0
+
+
+@dataclass
+class Lowered:
+    """Everything the runtime needs: buffers, records, I/O order."""
+    name: str
+    buffers: List[Buffer]
+    records: List[Record]
+    inputs: List[Tuple[str, Buffer]]          # runtime inputs in IR order
+    consts: List[Tuple[str, Buffer]]          # inputs bound once from constants
+    outputs: List[Tuple[str, Buffer]]         # function outputs in order
+    arena_bytes: int = 0
+    labels: List[str] = field(default_factory=list)
+
+    def plan_bytes(self) -> bytes:
+        """Serialise to the dp_plan blob (header, slots, records)."""
+        hdr = N.PlanHeader(N.DP_PLAN_MAGIC, N.DP_PLAN_VERSION, len(self.buffers), len(self.records),
+                           self.arena_bytes, 0)
+        out = [bytes(hdr)]
+        for b in self.buffers:
+            kind = N.DP_SLOT_ARENA if b.kind == "arena" else N.DP_SLOT_BOUND
+            out.append(bytes(N.PlanSlot(kind, N.DTYPE_CODE[b.dtype], b.offset if b.kind == "arena" else 0,
+                                        b.nbytes)))
+        for r in self.records:
+            rec = N.PlanRecord()
+            rec.kernel = r.kernel
+            rec.n_operands = len(r.operands)
+            for i in range(N.DP_RECORD_MAX_OPERANDS):
+                rec.operand[i] = -1
+            for i, b in enumerate(r.operands):
+                rec.operand[i] = b.slot if b is not None else -1
+            raw = bytes(r.params)
+            ctypes.memmove(rec.params, raw, len(raw))
+            out.append(bytes(rec))
+        return b"".join(out)
+
+
+class Lowerer:
+    def __init__(self, fn: Function, const_names=()):
+        self.fn = fn
+        self.const_names = set(const_names)
+        self.views: Dict[str, View] = {}
+        self.buffers: List[Buffer] = []
+        self.records: List[Record] = []
+        self.done = set()   # ids of ops already lowered (fused)
+        self.uses: Dict[str, List[Op]] = {}
+        self.out_names = {v.name for v in fn.outputs}
+        for op in fn.block.ops:
+            for v in op.inputs:
+                self.uses.setdefault(v.name, []).append(op)
+
+    # ------------------------------------------------------------ helpers
+    def new_buffer(self, kind, dtype, shape, name) -> Buffer:
+        b = Buffer(kind, dtype, tuple(shape), name)
+        self.buffers.append(b)
+        return b
+
+    def new_value_view(self, value: Value, dtype=None, shape=None) -> View:
+        t = value.type
+        shape = tuple(shape if shape is not None else materialized_shape(value))
+        dtype = dtype or t.dtype
+        buf = self.new_buffer("arena", dtype, shape, value.name)
+        v = View(buf, shape, contiguous_strides(shape))
+        self.views[value.name] = v
+        return v
+
+    def single_use(self, v: Value) -> Optional[Op]:
+        """The only consumer of ``v`` if it has exactly one and is not a function output."""
+        us = self.uses.get(v.name, [])
+        if len(us) == 1 and v.name not in self.out_names:
+            return us[0]
+        return None
+
+    def emit(self, kernel, operands, params, label, flops=0, nbytes=0) -> Record:
+        r = Record(kernel, operands, params, label, flops, nbytes)
+        idx = len(self.records)
+        for b in operands:
+            if b is not None:
+                if b.first < 0:
+                    b.first = idx
+                b.last = idx
+        self.records.append(r)
+        return r
+
+    def contiguous(self, value: Value) -> View:
+        """View of ``value``; a strided view is first copied to a new buffer."""
+        v = self.views[value.name]
+        if v.contiguous:
+            return v
+        return self.copy_view(v, value.name + "_c")
+
+    def copy_view(self, v: View, name: str) -> View:
+        out = View(self.new_buffer("arena", v.buf.dtype, v.shape, name), v.shape, contiguous_strides(v.shape))
+        rb = RegionBuilder(out.shape)
+        r = rb.load(v)
+        rb.store(out, r)
+        self.emit_region(rb, f"copy {name}")
+        return out
+
+    def emit_region(self, rb: "RegionBuilder", label: str) -> None:
+        desc, operands = rb.finish()
+        nbytes = sum(b.nbytes for b in set(operands))
+        self.emit(N.DP_K_REGION, operands, desc, label, 0, nbytes)
+
+    # ------------------------------------------------------------- driver
+    def run(self) -> Lowered:
+        ins, consts = [], []
+        for v in self.fn.inputs:
+            if not isinstance(v.type, TensorType):
+                raise CompilationError(f"input {v.name}: {v.type!r} is a host value; the GPU backend runs "
+                                       "tensor programs only")
+            kind = "const" if v.name in self.const_names else "input"
+            b = self.new_buffer(kind, v.type.dtype, v.type.shape, v.name)
+            self.views[v.name] = View(b, v.type.shape, contiguous_strides(v.type.shape))
+            (consts if kind == "const" else ins).append((v.name, b))
+        for op in self.fn.block.ops:
+            if id(op) in self.done:
+                continue
+            self.lower_op(op)
+            self.done.add(id(op))
+        outs = self.bind_outputs()
+        arena = plan_arena(self.buffers)
+        for i, b in enumerate(self.buffers):
+            b.slot = i
+        low = Lowered(self.fn.name, self.buffers, self.records, ins, consts, outs, arena)
+        low.labels = [r.label for r in self.records]
+        return low
+
+    def bind_outputs(self):
+        outs, taken = [], set()
+        if not self.fn.outputs:
+            raise CompilationError("function has no output")
+        for v in self.fn.outputs:
+            view = self.views.get(v.name)
+            if view is None:
+                raise CompilationError(f"output {v.name} was never produced")
+            shape = materialized_shape(v)
+            if view.buf.kind == "arena" and view.contiguous and id(view.buf) not in taken \
+                    and _prod(view.shape) == _prod(view.buf.shape):
+                view.buf.kind = "output"
+                view.buf.shape = tuple(shape)
+                view.buf.name = v.name
+                buf = view.buf
+            else:
+                buf = self.new_buffer("output", view.buf.dtype, shape, v.name)
+                dst = View(buf, view.shape, contiguous_strides(view.shape))
+                rb = RegionBuilder(view.shape)
+                rb.store(dst, rb.load(view))
+                self.emit_region(rb, f"output copy {v.name}")
+            taken.add(id(buf))
+            outs.append((v.name, buf))
+        return outs
+
+    def lower_op(self, op: Op) -> None:
+        name = op.name
+        if name in HOST_OPS:
+            raise CompilationError(f"op '{name}' is a host string/tokenizer/dict op; the GPU backend does not "
+                                   "execute it")
+        if name == "resize":
+            return self.lower_preproc(op)
+        if name in ("linear", "matmul"):
+            return self.lower_gemm(op)
+        if name in ROW_OPS:
+            return self.lower_rowreduce(op)
+        if name == "embedding":
+            return self.lower_embedding(op)
+        if name == "reshape":
+            src = self.contiguous(op.inputs[0])
+            out = op.outputs[0]
+            shape = out.type.shape
+            self.views[out.name] = View(src.buf, shape, contiguous_strides(shape), src.offset)
+            return
+        if name == "transpose":
+            v = self.views[op.inputs[0].name]
+            dims = op.attr("dims")
+            self.views[op.outputs[0].name] = View(v.buf, tuple(v.shape[d] for d in dims),
+                                                  tuple(v.strides[d] for d in dims), v.offset)
+            return
+        if name in ELEMENTWISE:
+            return self.lower_region(op)
+        if name == "sdpa":
+            raise UnsupportedOpError("sdpa")
+        raise UnsupportedOpError(name)
+
+    # --------------------------------------------------------- preprocess
+    def lower_preproc(self, op: Op) -> None:
+        x = self.contiguous(op.inputs[0])
+        layout = op.attr("layout")
+        if "C" not in layout:
+            raise CompilationError(f"resize: layout {layout} has no channel dim")
+        t_in = op.inputs[0].type
+        in_shape = t_in.shape
+        H, W = in_shape[layout.index("H")], in_shape[layout.index("W")]
+        C = in_shape[layout.index("C")]
+        B = in_shape[0] if layout.startswith("N") else 1
+        oh, ow = op.attr("size")
+        if C > 4:
+            raise CompilationError("resize: at most 4 channels")
+        if t_in.dtype not in ("uint8", "float32", "bfloat16", "float16"):
+            raise CompilationError(f"resize: input dtype {t_in.dtype} unsupported")
+        channels_last = layout in ("HWC", "NHWC")
+        out_channels_last = channels_last
+        out_dtype = op.outputs[0].type.dtype
+        mean, std = None, None
+        cur = op.outputs[0]
+        chain_end = cur
+        while True:
+            nxt = self.single_use(cur)
+            if nxt is None or id(nxt) in self.done:
+                break
+            if nxt.name == "to" and nxt.attr("dtype") in ("float32", "bfloat16", "float16"):
+                if nxt.attr("dtype") != "float32" and mean is None and self._later_normalize(nxt):
+                    break  # narrowing before a normalise would round early
+                out_dtype = nxt.attr("dtype")
+            elif nxt.name == "normalize" and mean is None and out_dtype == "float32":
+                cd = nxt.attr("channel_dim")
+                if nxt.attr("mean") is not None:
+                    rank = len(nxt.inputs[0].type.shape)
+                    want = (rank - 1) if out_channels_last else (rank - 3)
+                    if cd != want:
+                        break
+                    mean, std = nxt.attr("mean"), nxt.attr("std")
+                out_dtype = "float32"
+            elif nxt.name == "transpose":
+                dims = tuple(nxt.attr("dims"))
+                rank = len(dims)
+                to_planar = {3: (2, 0, 1), 4: (0, 3, 1, 2)}.get(rank)
+                to_last = {3: (1, 2, 0), 4: (0, 2, 3, 1)}.get(rank)
+                if out_channels_last and dims == to_planar:
+                    out_channels_last = False
+                elif not out_channels_last and dims == to_last:
+                    out_channels_last = True
+                else:
+                    break
+            else:
+                break
+            self.done.add(id(nxt))
+            cur = nxt.outputs[0]
+            chain_end = cur
+        p = N.PreprocParams()
+        p.batch, p.in_h, p.in_w, p.channels, p.out_h, p.out_w = B, H, W, C, oh, ow
+        p.in_dtype = N.DTYPE_CODE[t_in.dtype]
+        p.in_layout = N.DP_LAYOUT_NHWC if channels_last else N.DP_LAYOUT_NCHW
+        p.out_dtype = N.DTYPE_CODE[out_dtype]
+        p.out_layout = N.DP_LAYOUT_NHWC if out_channels_last else N.DP_LAYOUT_NCHW
+        p.normalize = 1 if mean is not None else 0
+        for c in range(4):
+            p.mean[c] = mean[c] if mean is not None and c < C else 0.0
+            p.stdv[c] = std[c] if std is not None and c < C else 1.0
+        out = self.new_value_view(chain_end, dtype=out_dtype)
+        in_bytes = B * C * H * W * DTYPE_BYTES[t_in.dtype]
+        out_bytes = out.buf.nbytes
+        self.emit(N.DP_K_PREPROC, [x.buf, out.buf], p,
+                  f"preproc {layout}{'+norm' if mean is not None else ''} {H}x{W}->{oh}x{ow} {out_dtype}",
+                  0, in_bytes + out_bytes)
+
+    def _later_normalize(self, op: Op) -> bool:
+        cur = op.outputs[0]
+        for _ in range(4):
+            nxt = self.single_use(cur)
+            if nxt is None:
+                return False
+            if nxt.name == "normalize":
+                return True
+            cur = nxt.outputs[0]
+        return False
+
+    # --------------------------------------------------------------- GEMM
+    def lower_gemm(self, op: Op) -> None:
+        p = N.GemmParams()
+        if op.name == "linear":
+            x = self.contiguous(op.inputs[0])
+            w = self.contiguous(op.inputs[1])
+            K = x.shape[-1]
+            M = _prod(x.shape[:-1])
+            Nn = w.shape[0]
+            p.M, p.N, p.K = M, Nn, K
+            p.lda, p.ldb = K, K
+            p.b_layout = N.DP_B_NK
+            p.batch, p.stride_a, p.stride_b = 1, 0, 0
+            a_dtype, b_dtype = x.buf.dtype, w.buf.dtype
+            a_buf, b_buf = x, w
+            bias = None
+            if len(op.inputs) > 2:
+                bias = self.contiguous(op.inputs[2])
+        else:
+            a = self.contiguous(op.inputs[0])
+            bview = self.views[op.inputs[1].name]
+            ta, tb = op.inputs[0].type, op.inputs[1].type
+            M, K = ta.shape[-2], ta.shape[-1]
+            Nn = tb.shape[-1]
+            batch_a, batch_b = ta.shape[:-2], tb.shape[:-2]
+            # B as [N, K] when it is a transposed view of a row-major [N, K] tensor.
+            bs = bview.strides
+            if bs[-2] == 1 and bs[-1] == K and bview.offset == 0 and _prod(batch_b) == 1:
+                b_buf, p.b_layout, p.ldb = bview, N.DP_B_NK, K
+            else:
+                b_buf = self.contiguous(op.inputs[1])
+                p.b_layout, p.ldb = N.DP_B_KN, Nn
+            bb = _prod(batch_b)
+            ba = _prod(batch_a)
+            if bb == 1:
+                # fold A's batch dims into M
+                M = M * ba
+                p.batch, p.stride_a, p.stride_b = 1, 0, 0
+            elif ba == bb and batch_a == batch_b:
+                p.batch, p.stride_a, p.stride_b = ba, M * K, K * Nn
+            else:
+                raise CompilationError(f"matmul: batch broadcast {batch_a} x {batch_b} unsupported")
+            p.M, p.N, p.K = M, Nn, K
+            p.lda = K
+            a_dtype, b_dtype = a.buf.dtype, b_buf.buf.dtype
+            a_buf = a
+            bias = None
+        if a_dtype != b_dtype or a_dtype not in ("float32", "bfloat16"):
+            raise CompilationError(f"{op.name}: operand dtypes {a_dtype} x {b_dtype}; supported: "
+                                   "float32 x float32, bfloat16 x bfloat16")
+        p.a_dtype = p.b_dtype = N.DTYPE_CODE[a_dtype]
+        epi = 0
+        residual = None
+        c_dtype = op.outputs[0].type.dtype
+        if bias is not None:
+            epi |= N.DP_EPI_BIAS
+        act_done = False
+        cur = op.outputs[0]
+        out_shape = op.outputs[0].type.shape
+        while True:
+            nxt = self.single_use(cur)
+            if nxt is None or id(nxt) in self.done:
+                break
+            if nxt.name == "add":
+                other = nxt.inputs[1] if nxt.inputs[0] is cur else nxt.inputs[0]
+                ot = other.type
+                if nxt.outputs[0].type.shape != out_shape:
+                    break
+                if (bias is None and not act_done and residual is None and ot.shape[-1:] == (p.N,)
+                        and _prod(ot.shape) == p.N):
+                    bias = self.contiguous(other)
+                    epi |= N.DP_EPI_BIAS
+                elif residual is None and ot.shape == out_shape and ot.dtype in FLOAT_DTYPES:
+                    residual = self.contiguous(other)
+                    epi |= N.DP_EPI_RESIDUAL
+                else:
+                    break
+                c_dtype = nxt.outputs[0].type.dtype
+            elif nxt.name in ("relu", "gelu", "silu") and not act_done and residual is None:
+                if nxt.name == "relu":
+                    epi |= N.DP_EPI_RELU
+                elif nxt.name == "silu":
+                    epi |= N.DP_EPI_SILU
+                else:
+                    epi |= N.DP_EPI_GELU_TANH if nxt.attr("approximate") == "tanh" else N.DP_EPI_GELU_ERF
+                act_done = True
+            elif nxt.name == "to" and nxt.attr("dtype") in ("float32", "bfloat16", "float16"):
+                c_dtype = nxt.attr("dtype")
+                self.done.add(id(nxt))
+                cur = nxt.outputs[0]
+                break
+            else:
+                break
+            self.done.add(id(nxt))
+            cur = nxt.outputs[0]
+        p.epilogue = epi
+        p.c_dtype = N.DTYPE_CODE[c_dtype]
+        p.ldc = p.N
+        p.stride_c = p.M * p.N if p.batch > 1 else 0
+        if bias is not None:
+            p.bias_dtype = N.DTYPE_CODE[bias.buf.dtype]
+        if residual is not None:
+            p.r_dtype = N.DTYPE_CODE[residual.buf.dtype]
+            p.ldr = p.N
+            p.stride_r = p.M * p.N if p.batch > 1 else 0
+        out = self.new_value_view(cur, dtype=c_dtype)
+        flops = 2 * p.M * p.N * p.K * p.batch
+        ops_ = [a_buf.buf, b_buf.buf, out.buf, bias.buf if bias is not None else None,
+                residual.buf if residual is not None else None]
+        nb = sum(b.nbytes for b in ops_ if b is not None)
+        self.emit(N.DP_K_GEMM, ops_, p, f"gemm {op.name} M{p.M} N{p.N} K{p.K} b{p.batch} {a_dtype} epi{epi}",
+                  flops, nb)
+
+    # ------------------------------------------------------ row reductions
+    def lower_rowreduce(self, op: Op) -> None:
+        x_val = op.inputs[0]
+        t = x_val.type
+        rank = len(t.shape)
+        dim = op.attr("dim", -1)
+        if op.name in ("layer_norm", "rms_norm"):
+            dim = -1
+        d = dim % rank
+        xv = self.views[x_val.name]
+        if d != rank - 1:
+            # move the reduced dim last with a strided copy
+            perm = [i for i in range(rank) if i != d] + [d]
+            xv = self.copy_view(View(xv.buf, tuple(xv.shape[i] for i in perm),
+                                     tuple(xv.strides[i] for i in perm), xv.offset), x_val.name + "_t")
+        elif not xv.contiguous:
+            xv = self.copy_view(xv, x_val.name + "_c")
+        cols = t.shape[d]
+        rows = t.numel // cols
+        if t.dtype not in ("float32", "bfloat16", "float16"):
+            raise CompilationError(f"{op.name}: input dtype {t.dtype} unsupported (float types only)")
+        p = N.RowReduceParams()
+        p.rows, p.cols, p.in_row_stride = rows, cols, cols
+        p.in_dtype = N.DTYPE_CODE[t.dtype]
+        kind = {"sum": N.DP_RED_SUM, "max": N.DP_RED_MAX, "min": N.DP_RED_MIN, "mean": N.DP_RED_MEAN,
+                "argmax": N.DP_RED_ARGMAX, "softmax": N.DP_RED_SOFTMAX, "rms_norm": N.DP_RED_RMSNORM,
+                "layer_norm": N.DP_RED_LAYERNORM}[op.name]
+        p.kind = kind
+        w = b = None
+        out_val = op.outputs[0]
+        if op.name == "argmax":
+            out_dtype = out_val.type.dtype
+            nxt = self.single_use(out_val)
+            if nxt is not None and nxt.name == "to" and nxt.attr("dtype") in ("int32", "int64"):
+                out_dtype = nxt.attr("dtype")
+                self.done.add(id(nxt))
+                out_val = nxt.outputs[0]
+            p.out_row_stride = 1
+        elif op.name in ("sum", "max", "min", "mean"):
+            out_dtype = out_val.type.dtype
+            p.out_row_stride = 1
+        else:
+            out_dtype = out_val.type.dtype
+            p.out_row_stride = cols
+            if op.name == "layer_norm":
+                p.eps = op.attr("eps")
+                idx = 1
+                if op.attr("has_weight"):
+                    w = self._param_like(op.inputs[idx], t.dtype)
+                    idx += 1
+                if op.attr("has_bias"):
+                    b = self._param_like(op.inputs[idx], t.dtype)
+            elif op.name == "rms_norm":
+                p.eps = op.attr("eps")
+                p.weight_offset = op.attr("weight_offset", 0.0)
+                if op.attr("has_weight"):
+                    w = self._param_like(op.inputs[1], t.dtype)
+            p.has_weight = 1 if w is not None else 0
+            p.has_bias = 1 if b is not None else 0
+        p.out_dtype = N.DTYPE_CODE[out_dtype]
+        out = self.new_value_view(out_val, dtype=out_dtype)
+        nbytes = xv.buf.nbytes + out.buf.nbytes
+        self.emit(N.DP_K_ROWREDUCE, [xv.buf, w.buf if w else None, b.buf if b else None, out.buf], p,
+                  f"rowreduce {op.name} {rows}x{cols} {t.dtype}->{out_dtype}", 0, nbytes)
+
+    def _param_like(self, value: Value, dtype: str) -> View:
+        v = self.contiguous(value)
+        if v.buf.dtype == dtype:
+            return v
+        out = View(self.new_buffer("arena", dtype, v.shape, value.name + "_cast"), v.shape,
+                   contiguous_strides(v.shape))
+        rb = RegionBuilder(v.shape)
+        rb.store(out, rb.load(v))
+        self.emit_region(rb, f"cast {value.name} to {dtype}")
+        return out
+
+    # ------------------------------------------------------------ embedding
+    def lower_embedding(self, op: Op) -> None:
+        ids = self.contiguous(op.inputs[0])
+        w = self.contiguous(op.inputs[1])
+        out = self.new_value_view(op.outputs[0])
+        p = N.EmbeddingParams()
+        p.n_ids = _prod(ids.shape)
+        p.vocab, p.dim = w.shape
+        p.id_dtype = N.DTYPE_CODE[ids.buf.dtype]
+        p.w_dtype = N.DTYPE_CODE[w.buf.dtype]
+        self.emit(N.DP_K_EMBEDDING, [ids.buf, w.buf, out.buf], p, f"embedding {p.n_ids}x{p.dim}", 0,
+                  ids.buf.nbytes + 2 * out.buf.nbytes)
+
+    # -------------------------------------------------------------- regions
+    def lower_region(self, op: Op) -> None:
+        shape = materialized_shape(op.outputs[0])
+        rb = RegionBuilder(shape)
+        regs: Dict[str, int] = {}
+        cur = op
+        while True:
+            r = self._emit_elementwise(rb, cur, regs)
+            out_v = cur.outputs[0]
+            regs[out_v.name] = r
+            nxt = self.single_use(out_v)
+            narrowing = cur.name == "to" and cur.attr("dtype") not in ("float32", "float64")
+            if (nxt is None or id(nxt) in self.done or nxt.name not in ELEMENTWISE or nxt.name == "reshape"
+                    or nxt.name == "transpose" or materialized_shape(nxt.outputs[0]) != shape or narrowing
+                    or not rb.room()):
+                break
+            self.done.add(id(nxt))
+            cur = nxt
+        out_v = cur.outputs[0]
+        out = self.new_value_view(out_v)
+        rb.store(out, regs[out_v.name])
+        self.emit_region(rb, f"region {'+'.join(rb.names)} {shape}")
+
+    def _emit_elementwise(self, rb: "RegionBuilder", op: Op, regs: Dict[str, int]) -> int:
+        def operand(v: Value) -> int:
+            if v.name in regs:
+                return regs[v.name]
+            return rb.load(self.views[v.name])
+
+        rb.names.append(op.name)
+        n = op.name
+        if n in ELEMENTWISE_UNARY:
+            return rb.unary(ELEMENTWISE_UNARY[n], operand(op.inputs[0]))
+        if n == "gelu":
+            return rb.unary("gelu_tanh" if op.attr("approximate") == "tanh" else "gelu_erf", operand(op.inputs[0]))
+        if n in ELEMENTWISE_BINARY:
+            return rb.binary(ELEMENTWISE_BINARY[n], operand(op.inputs[0]), operand(op.inputs[1]))
+        if n in SCALAR_OPS:
+            x = operand(op.inputs[0])
+            c = rb.const(op.attr("scalar"))
+            a, b = (c, x) if op.attr("reverse") else (x, c)
+            return rb.binary(SCALAR_OPS[n], a, b)
+        if n == "to":
+            return rb.unary("mov", operand(op.inputs[0]))
+        if n == "normalize":
+            x = operand(op.inputs[0])
+            if op.attr("mean") is None:
+                return rb.unary("mov", x)
+            cd = op.attr("channel_dim")
+            m = rb.chansel(op.attr("mean"), cd)
+            s = rb.chansel(op.attr("std"), cd)
+            return rb.binary("div", rb.binary("sub", x, m), s)
+        raise UnsupportedOpError(n)
+
+
+class RegionBuilder:
+    """Assembles one dp_region_desc: operands, registers, instructions."""
+
+    def __init__(self, shape: Tuple[int, ...]):
+        self.shape = tuple(shape) if shape else (1,)
+        self.operands: List[Tuple[View, bool]] = []   # (view, is_output)
+        self.instr: List[Tuple[str, int, int, int]] = []
+        self.consts: List[float] = []
+        self.nregs = 0
+        self.chan_dims = set()
+        self.names: List[str] = []
+        self._loaded: Dict[Tuple, int] = {}
+
+    def room(self) -> bool:
+        return (len(self.instr) < N.DP_REGION_MAX_INSTR - 8 and self.nregs < N.DP_REGION_MAX_REGS - 2
+                and len(self.operands) < N.DP_REGION_MAX_OPERANDS - 2)
+
+    def _reg(self) -> int:
+        r = self.nregs
+        self.nregs += 1
+        if self.nregs > N.DP_REGION_MAX_REGS:
+            raise CompilationError("region: out of registers")
+        return r
+
+    def _bstrides(self, v: View) -> Tuple[int, ...]:
+        """Strides of ``v`` broadcast to this region's shape."""
+        rank = len(self.shape)
+        vs = (1,) * (rank - len(v.shape)) + tuple(v.shape)
+        st = (0,) * (rank - len(v.strides)) + tuple(v.strides)
+        out = []
+        for s_out, s_in, stv in zip(self.shape, vs, st):
+            if s_in == s_out:
+                out.append(stv if s_in != 1 else 0)
+            elif s_in == 1:
+                out.append(0)
+            else:
+                raise CompilationError(f"region: {v.shape} does not broadcast to {self.shape}")
+        return tuple(out)
+
+    def load(self, v: View) -> int:
+        key = (id(v.buf), v.offset, tuple(v.shape), tuple(v.strides))
+        if key in self._loaded:
+            return self._loaded[key]
+        if v.offset != 0:
+            raise CompilationError("region: offset views are not supported")
+        self.operands.append((View(v.buf, v.shape, self._bstrides(v)), False))
+        r = self._reg()
+        self.instr.append(("load", r, len(self.operands) - 1, 0))
+        self._loaded[key] = r
+        return r
+
+    def store(self, v: View, r: int) -> None:
+        self.operands.append((View(v.buf, v.shape, self._bstrides(v)), True))
+        self.instr.append(("store", 0, len(self.operands) - 1, r))
+
+    def const(self, c: float) -> int:
+        self.consts.append(float(c))
+        r = self._reg()
+        self.instr.append(("const", r, len(self.consts) - 1, 0))
+        return r
+
+    def chansel(self, values, dim: int) -> int:
+        base = len(self.consts)
+        self.consts.extend(float(x) for x in values)
+        if len(self.consts) > N.DP_REGION_MAX_CONST:
+            raise CompilationError("region: too many per-channel constants")
+        d = dim % len(self.shape)
+        self.chan_dims.add(d)
+        r = self._reg()
+        self.instr.append(("chansel", r, base, d))
+        return r
+
+    def unary(self, name: str, a: int) -> int:
+        r = self._reg()
+        self.instr.append((name, r, a, 0))
+        return r
+
+    def binary(self, name: str, a: int, b: int) -> int:
+        r = self._reg()
+        self.instr.append((name, r, a, b))
+        return r
+
+    def finish(self):
+        # Inputs first, then outputs (the kernel's operand order).
+        order = [i for i, (_, o) in enumerate(self.operands) if not o] + \
+                [i for i, (_, o) in enumerate(self.operands) if o]
+        remap = {old: new for new, old in enumerate(order)}
+        n_in = sum(1 for _, o in self.operands if not o)
+        shape, strides, dim_map = collapse_dims(self.shape, [self.operands[i][0].strides for i in order],
+                                                self.chan_dims)
+        d = N.RegionDesc()
+        d.rank = len(shape)
+        d.n_in = n_in
+        d.n_out = len(self.operands) - n_in
+        d.n_instr = len(self.instr)
+        if d.n_instr > N.DP_REGION_MAX_INSTR:
+            raise CompilationError("region: too many instructions")
+        for k, s in enumerate(shape):
+            d.shape[k] = s
+        for new, old in enumerate(order):
+            v = self.operands[old][0]
+            d.dtype[new] = N.DTYPE_CODE[v.buf.dtype]
+            for k in range(len(shape)):
+                d.stride[new][k] = strides[new][k]
+        for pc, (name, dst, a, b) in enumerate(self.instr):
+            code = N.OP[name]
+            if name in ("load", "store"):
+                a = remap[a]
+            if name == "chansel":
+                b = dim_map[b]
+            d.instr[pc] = code | (dst << 8) | (a << 16) | (b << 24)
+        for i, c in enumerate(self.consts):
+            d.consts[i] = c
+        return d, [self.operands[i][0].buf for i in order]
+
+
+def collapse_dims(shape, strides_list, keep):
+    """Merge adjacent dims that every operand walks contiguously.
+
+    Dims in ``keep`` (per-channel constant selectors) are never merged.
+    Returns (shape, strides per operand, old-dim → new-dim map).
+    """
+    shape = list(shape)
+    groups = [[0]]
+    cur_shape = [shape[0]]
+    cur_strides = [[s[0]] for s in strides_list]
+    for i in range(1, len(shape)):
+        mergeable = (i not in keep) and (groups[-1][-1] not in keep) and all(
+            cs[-1] == s[i] * shape[i] for cs, s in zip(cur_strides, strides_list))
+        if mergeable:
+            groups[-1] = groups[-1] + [i]
+            cur_shape[-1] *= shape[i]
+            for cs, s in zip(cur_strides, strides_list):
+                cs[-1] = s[i]
+        else:
+            groups.append([i])
+            cur_shape.append(shape[i])
+            for cs, s in zip(cur_strides, strides_list):
+                cs.append(s[i])
+    if len(cur_shape) > N.DP_REGION_MAX_RANK:
+        raise CompilationError(f"region: rank {len(cur_shape)} after collapsing exceeds {N.DP_REGION_MAX_RANK}")
+    dim_map = {}
+    for new, g in enumerate(groups):
+        for old in g:
+            dim_map[old] = new
+    return tuple(cur_shape), cur_strides, dim_map
+
+
+def materialized_shape(v: Value) -> Tuple[int, ...]:
+    """Shape stored for ``v``; a legacy scalar argmax stores one index per reduced row."""
+    t = v.type
+    if isinstance(t, TensorType):
+        return t.shape if t.shape else (1,)
+    if isinstance(t, ScalarType) and v.op is not None and v.op.name == "argmax":
+        xt = v.op.inputs[0].type
+        d = v.op.attr("dim") % len(xt.shape)
+        shape = tuple(s for i, s in enumerate(xt.shape) if i != d)
+        return shape if shape else (1,)
+    raise CompilationError(f"value {v.name} of type {t!r} has no tensor storage")
+
+
+def value_dtype(v: Value) -> str:
+    return v.type.dtype
+
+
+def plan_arena(buffers: List[Buffer]) -> int:
+    """First-fit offsets for arena buffers whose live ranges overlap in time."""
+    arena = [b for b in buffers if b.kind == "arena"]
+    for b in arena:
+        if b.first < 0:  # produced but never used: keep it alive at its producer only
+            b.first = b.last = 0
+    placed: List[Buffer] = []
+    top = 0
+    for b in sorted(arena, key=lambda x: (-x.nbytes, x.first)):
+        size = _round(b.nbytes)
+        busy = sorted((p.offset, p.offset + _round(p.nbytes)) for p in placed
+                      if not (p.last < b.first or b.last < p.first))
+        off = 0
+        for lo, hi in busy:
+            if off + size <= lo:
+                break
+            off = max(off, hi)
+        b.offset = off
+        placed.append(b)
+        top = max(top, off + size)
+    return top
+
+
+def _round(n: int) -> int:
+    return (n + ALIGN - 1) // ALIGN * ALIGN
+
+
+def lower(fn: Function, const_names=()) -> Lowered:
+    return Lowerer(fn, const_names).run()

@@ -1,0 +1,58 @@
+// GEMM epilogue shared by the FFMA and tcgen05 GEMMs:
+//   v = acc (+ bias[n]) → activation → (+ residual[m, n]) → cast → C[m, n].
+#pragma once
+
+#include "dp_common.cuh"
+
+namespace dp {
+
+__device__ __forceinline__ float act_gelu_erf(float x) { return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f)); }
+__device__ __forceinline__ float act_gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f, k1 = 0.044715f;
+  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+}
+
+struct Epilogue {
+  const dp_gemm_params &p;
+  void *C;
+  const void *bias;
+  const void *res;
+  int64_t c_off, r_off;
+
+  __device__ __forceinline__ Epilogue(const dp_gemm_params &p_, void *C_, const void *bias_, const void *res_,
+                                      int64_t batch)
+      : p(p_), C(C_), bias(bias_), res(res_), c_off(batch * p_.stride_c), r_off(batch * p_.stride_r) {}
+
+  __device__ __forceinline__ float apply(int64_t m, int64_t n, float v) const {
+    if (p.epilogue & DP_EPI_BIAS) v += load_as_f32(bias, n, p.bias_dtype);
+    if (p.epilogue & DP_EPI_RELU) v = v > 0.0f ? v : (isnan(v) ? v : 0.0f);
+    if (p.epilogue & DP_EPI_GELU_ERF) v = act_gelu_erf(v);
+    if (p.epilogue & DP_EPI_GELU_TANH) v = act_gelu_tanh(v);
+    if (p.epilogue & DP_EPI_SILU) v = v / (1.0f + expf(-v));
+    if (p.epilogue & DP_EPI_RESIDUAL) v += load_as_f32(res, r_off + m * p.ldr + n, p.r_dtype);
+    return v;
+  }
+
+  // Four consecutive columns n .. n+3 of row m (each bounds-checked).
+  __device__ __forceinline__ void store4(int64_t m, int64_t n, float v0, float v1, float v2, float v3) const {
+    float v[4] = {v0, v1, v2, v3};
+    const int64_t base = c_off + m * p.ldc + n;
+    if (n + 3 < p.N && p.c_dtype == DP_F32 && (base & 3) == 0 &&
+        (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[j] = apply(m, n + j, v[j]);
+      *reinterpret_cast<float4 *>(static_cast<float *>(C) + base) = make_float4(v[0], v[1], v[2], v[3]);
+      return;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (n + j < p.N) store_from_f32(C, base + j, p.c_dtype, apply(m, n + j, v[j]));
+  }
+};
+
+int launch_gemm_simt(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias,
+                     const void *res, cudaStream_t s);
+int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias,
+                   const void *res, cudaStream_t s);
+
+}  // namespace dp

@@ -1,0 +1,43 @@
+// GEMM entry point: validates the request and picks the kernel.
+// bf16 × bf16 goes to the tcgen05 tensor-core kernel when its TMA alignment
+// rules hold (row strides and K multiples of 8 elements, 16-byte aligned
+// bases); everything else (fp32, or bf16 with odd strides) runs the FFMA
+// kernel.  Both share one epilogue.
+#include "dp_gemm_epilogue.cuh"
+
+namespace dp {
+
+int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias, const void *res,
+                cudaStream_t s) {
+  DP_REQUIRE(A && B && C, DP_ERR_ARG, "gemm: null A/B/C");
+  DP_REQUIRE(p.M > 0 && p.N > 0 && p.K > 0 && p.batch > 0, DP_ERR_SHAPE, "gemm: sizes must be positive");
+  DP_REQUIRE(p.lda >= p.K, DP_ERR_SHAPE, "gemm: lda < K");
+  DP_REQUIRE(p.b_layout == DP_B_NK ? p.ldb >= p.K : p.ldb >= p.N, DP_ERR_SHAPE, "gemm: ldb too small");
+  DP_REQUIRE(p.ldc >= p.N, DP_ERR_SHAPE, "gemm: ldc < N");
+  DP_REQUIRE(p.M < (1ll << 31) / 1 && p.batch < 65536, DP_ERR_UNSUPPORTED, "gemm: M or batch too large");
+  DP_REQUIRE(p.c_dtype == DP_F32 || p.c_dtype == DP_BF16 || p.c_dtype == DP_F16, DP_ERR_ARG,
+             "gemm: C must be f32/bf16/f16");
+  if (p.epilogue & DP_EPI_BIAS) DP_REQUIRE(bias != nullptr && dtype_bytes(p.bias_dtype) > 0, DP_ERR_ARG, "gemm: bias");
+  if (p.epilogue & DP_EPI_RESIDUAL) {
+    DP_REQUIRE(res != nullptr && dtype_bytes(p.r_dtype) > 0, DP_ERR_ARG, "gemm: residual");
+    DP_REQUIRE(p.ldr >= p.N, DP_ERR_SHAPE, "gemm: ldr < N");
+  }
+  const int acts = !!(p.epilogue & DP_EPI_RELU) + !!(p.epilogue & DP_EPI_GELU_ERF) +
+                   !!(p.epilogue & DP_EPI_GELU_TANH) + !!(p.epilogue & DP_EPI_SILU);
+  DP_REQUIRE(acts <= 1, DP_ERR_ARG, "gemm: at most one activation");
+  if (p.a_dtype == DP_BF16 && p.b_dtype == DP_BF16) {
+    auto al = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+    const bool tc_ok = p.b_layout == DP_B_NK && p.K % 8 == 0 && p.lda % 8 == 0 && p.ldb % 8 == 0 &&
+                       p.stride_a % 8 == 0 && p.stride_b % 8 == 0 && al(A) && al(B);
+    if (tc_ok) return launch_gemm_tc(p, A, B, C, bias, res, s);
+  }
+  return launch_gemm_simt(p, A, B, C, bias, res, s);
+}
+
+}  // namespace dp
+
+extern "C" int dp_gemm(const dp_gemm_params *p, const void *A, const void *B, void *C, const void *bias,
+                       const void *residual, void *stream) {
+  if (!p) return dp::set_error(DP_ERR_ARG, "dp_gemm: null params");
+  return dp::launch_gemm(*p, A, B, C, bias, residual, dp::as_stream(stream));
+}

@@ -1,0 +1,310 @@
+// Fused preprocessing region: image load → bilinear resize → fp32 cast →
+// (x - mean[c]) / std[c] → layout change → store, in one HBM pass.
+//
+// Replaces the reference's per-op chain handle_resize (F.interpolate) →
+// normalize_kernel → to_dtype_kernel → handle_transpose
+// (src/devproc/backend/triton/ops.py:21-53, 320-432; templates/elementwise.py).
+//
+// Work unit = one output row (image b, output row y).  It needs input rows
+// y0 and y0+1 of every channel plane; they are adjacent in memory, so one
+// bulk copy (TMA engine, cp.async.bulk) per plane stages them in shared
+// memory.  A persistent block keeps STAGES units in flight (mbarrier per
+// stage) while its threads compute the current row: thread x produces output
+// column x of every channel, so stores are coalesced per channel plane.
+//
+// Arithmetic follows torch's CPU upsample_bilinear2d (torch 2.11,
+// align_corners=False) operation for operation, which makes the result
+// bit-identical to F.interpolate on float input:
+//   scale = in / out (fp32); src = fma(scale, o + 0.5, -0.5), clamped at 0;
+//   i0 = min(floor(src), in-1); l1 = clamp(src - i0, 0, 1); l0 = 1 - l1;
+//   i1 = i0 + (i0 < in-1); equal sizes copy (l0 = 1, l1 = 0);
+//   row = fma(x[i0], l0, x[i1] * l1); out = fma(row0, h0, row1 * h1).
+#include "dp_common.cuh"
+
+namespace {
+
+constexpr int kStages = 4;
+constexpr int kMaxThreads = 256;
+
+struct Coef {
+  int i0, i1;
+  float l0, l1;
+};
+
+__device__ __forceinline__ Coef src_coef(int o, int in_size, int out_size, float scale) {
+  Coef c;
+  if (in_size == out_size) {
+    c.i0 = c.i1 = o;
+    c.l0 = 1.0f;
+    c.l1 = 0.0f;
+    return c;
+  }
+  float src = __fmaf_rn(scale, (float)o + 0.5f, -0.5f);
+  if (src < 0.0f) src = 0.0f;
+  int i0 = (int)floorf(src);
+  if (i0 > in_size - 1) i0 = in_size - 1;
+  float l1 = fminf(fmaxf(__fsub_rn(src, (float)i0), 0.0f), 1.0f);
+  c.i0 = i0;
+  c.i1 = i0 + (i0 < in_size - 1 ? 1 : 0);
+  c.l1 = l1;
+  c.l0 = __fsub_rn(1.0f, l1);
+  return c;
+}
+
+struct Geo {
+  int B, H, W, C, OH, OW;
+  int planes;          // 1 for NHWC input, C for NCHW
+  int row_elems;       // elements of one input row of one plane
+  int rows_staged;     // 2, or 1 when H == 1
+  int plane_stride_s;  // elements between planes in a smem stage (16-B padded)
+  float sy, sx;
+  int normalize;
+  float mean[4], inv_unused[4], stdv[4];
+};
+
+template <typename TIn, bool IN_NCHW>
+__device__ __forceinline__ const TIn *plane_src(const TIn *in, const Geo &g, int b, int plane, int y_start) {
+  if (IN_NCHW) return in + ((int64_t)(b * g.C + plane) * g.H + y_start) * g.W;
+  return in + ((int64_t)b * g.H + y_start) * (int64_t)g.W * g.C;
+}
+
+// Computes output row (b, oy) from the staged rows in ``st``.
+template <typename TIn, typename TOut, bool IN_NCHW, bool OUT_NCHW>
+__device__ __forceinline__ void compute_row(const TIn *st, const Geo &g, int b, int oy, int y_start,
+                                            TOut *out, const Coef &cx_first) {
+  Coef cy = src_coef(oy, g.H, g.OH, g.sy);
+  const int r0 = cy.i0 - y_start, r1 = cy.i1 - y_start;
+  for (int ox = threadIdx.x; ox < g.OW; ox += blockDim.x) {
+    const Coef cx = (ox == (int)threadIdx.x) ? cx_first : src_coef(ox, g.W, g.OW, g.sx);
+#pragma unroll 4
+    for (int c = 0; c < g.C; ++c) {
+      const TIn *p0, *p1;
+      int e0, e1;
+      if (IN_NCHW) {
+        p0 = st + c * g.plane_stride_s + r0 * g.row_elems;
+        p1 = st + c * g.plane_stride_s + r1 * g.row_elems;
+        e0 = cx.i0;
+        e1 = cx.i1;
+      } else {
+        p0 = st + r0 * g.row_elems;
+        p1 = st + r1 * g.row_elems;
+        e0 = cx.i0 * g.C + c;
+        e1 = cx.i1 * g.C + c;
+      }
+      float a = to_f32(p0[e0]), bb = to_f32(p0[e1]);
+      float cc = to_f32(p1[e0]), d = to_f32(p1[e1]);
+      float row0 = __fmaf_rn(a, cx.l0, __fmul_rn(bb, cx.l1));
+      float row1 = __fmaf_rn(cc, cx.l0, __fmul_rn(d, cx.l1));
+      float v = __fmaf_rn(row0, cy.l0, __fmul_rn(row1, cy.l1));
+      if (g.normalize) v = __fdiv_rn(__fsub_rn(v, g.mean[c]), g.stdv[c]);
+      int64_t o;
+      if (OUT_NCHW)
+        o = (((int64_t)b * g.C + c) * g.OH + oy) * g.OW + ox;
+      else
+        o = (((int64_t)b * g.OH + oy) * g.OW + ox) * g.C + c;
+      out[o] = from_f32<TOut>(v);
+    }
+  }
+}
+
+__device__ __forceinline__ int staged_start(int oy, const Geo &g) {
+  if (g.rows_staged == 1) return 0;
+  Coef cy = src_coef(oy, g.H, g.OH, g.sy);
+  return cy.i0 < g.H - 1 ? cy.i0 : g.H - 2;
+}
+
+// TMA path: every plane's staged rows are 16-byte aligned, multiple-of-16
+// sized, and rows_staged * row bytes fits one bulk copy.
+template <typename TIn, typename TOut, bool IN_NCHW, bool OUT_NCHW>
+__global__ void __launch_bounds__(kMaxThreads) preproc_bulk_kernel(Geo g, const TIn *__restrict__ in,
+                                                                   TOut *__restrict__ out, int n_units) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kStages];
+  const int stage_elems = g.planes * g.plane_stride_s;
+  TIn *stage0 = reinterpret_cast<TIn *>(smem_raw);
+  const uint32_t plane_bytes = (uint32_t)(g.rows_staged * g.row_elems * sizeof(TIn));
+  const uint32_t stage_bytes = plane_bytes * g.planes;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int k) {  // thread 0 only: stage unit #k of this block
+    const int u = blockIdx.x + k * gridDim.x;
+    if (u >= n_units) return;
+    const int b = u / g.OH, oy = u % g.OH;
+    const int ys = staged_start(oy, g);
+    const int s = k % kStages;
+    mbar_arrive_expect_tx(&bars[s], stage_bytes);
+    for (int p = 0; p < g.planes; ++p)
+      bulk_g2s(stage0 + s * stage_elems + p * g.plane_stride_s, plane_src<TIn, IN_NCHW>(in, g, b, p, ys),
+               plane_bytes, &bars[s]);
+  };
+
+  const int my_units = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  if (threadIdx.x == 0)
+    for (int k = 0; k < kStages && k < my_units; ++k) issue(k);
+
+  const Coef cx_first = src_coef((int)threadIdx.x < g.OW ? (int)threadIdx.x : 0, g.W, g.OW, g.sx);
+  int k = 0;
+  for (; k < my_units; ++k) {
+    const int s = k % kStages;
+    const uint32_t phase = (uint32_t)(k / kStages) & 1u;
+    // A thread whose wait gave up still computes (on possibly stale data,
+    // with the error word set) so that the block stays in lock-step; the
+    // vote below then stops the whole block together.
+    const bool ok = mbar_wait_bounded(&bars[s], phase, 100 + s);
+    const int u = blockIdx.x + k * gridDim.x;
+    const int b = u / g.OH, oy = u % g.OH;
+    compute_row<TIn, TOut, IN_NCHW, OUT_NCHW>(stage0 + s * stage_elems, g, b, oy, staged_start(oy, g), out,
+                                              cx_first);
+    if (!__syncthreads_and(ok)) break;  // also: everyone is done reading stage s
+    if (threadIdx.x == 0 && k + kStages < my_units) issue(k + kStages);
+  }
+  if (k < my_units && threadIdx.x == 0) {
+    // Drain: wait (bounded) for every copy this block still has in flight
+    // (units k .. k+kStages-1) before its shared memory goes away.
+    for (int j = k; j < my_units && j < k + kStages; ++j)
+      mbar_wait_bounded(&bars[j % kStages], (uint32_t)(j / kStages) & 1u, 199, 100000000ull);
+  }
+  __syncthreads();
+}
+
+// Plain-load path for sizes or alignments the bulk copy cannot take.
+template <typename TIn, typename TOut, bool IN_NCHW, bool OUT_NCHW>
+__global__ void __launch_bounds__(kMaxThreads) preproc_plain_kernel(Geo g, const TIn *__restrict__ in,
+                                                                    TOut *__restrict__ out, int n_units) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  TIn *st = reinterpret_cast<TIn *>(smem_raw);
+  const int plane_elems = g.rows_staged * g.row_elems;
+  const Coef cx_first = src_coef((int)threadIdx.x < g.OW ? (int)threadIdx.x : 0, g.W, g.OW, g.sx);
+  for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    const int b = u / g.OH, oy = u % g.OH;
+    const int ys = staged_start(oy, g);
+    for (int p = 0; p < g.planes; ++p) {
+      const TIn *src = plane_src<TIn, IN_NCHW>(in, g, b, p, ys);
+      for (int i = threadIdx.x; i < plane_elems; i += blockDim.x) st[p * g.plane_stride_s + i] = src[i];
+    }
+    __syncthreads();
+    compute_row<TIn, TOut, IN_NCHW, OUT_NCHW>(st, g, b, oy, ys, out, cx_first);
+    __syncthreads();
+  }
+}
+
+template <typename TIn, typename TOut, bool IN_NCHW, bool OUT_NCHW>
+int launch_typed(const Geo &g, const void *in, void *out, cudaStream_t s) {
+  const int n_units = g.B * g.OH;
+  const int threads = g.OW >= kMaxThreads ? kMaxThreads : ((g.OW + 31) / 32) * 32;
+  const size_t stage_bytes = (size_t)g.planes * g.plane_stride_s * sizeof(TIn);
+  const uintptr_t base = reinterpret_cast<uintptr_t>(in);
+  const size_t plane_bytes = (size_t)g.rows_staged * g.row_elems * sizeof(TIn);
+  const size_t row_bytes = (size_t)g.row_elems * sizeof(TIn);
+  // Every copy source is base + k * row_bytes (k integer), so 16-B alignment
+  // of base and of row_bytes makes every copy aligned.
+  const bool bulk = (base % 16 == 0) && (row_bytes % 16 == 0) && (plane_bytes % 16 == 0) &&
+                    (plane_bytes < (1u << 20)) && (stage_bytes * kStages <= 200 * 1024);
+  const int sms = dp::num_sms();
+  if (bulk) {
+    auto kern = preproc_bulk_kernel<TIn, TOut, IN_NCHW, OUT_NCHW>;
+    const size_t smem = stage_bytes * kStages;
+    DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    DP_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem));
+    if (per_sm < 1) per_sm = 1;
+    int grid = sms * per_sm;
+    if (grid > n_units) grid = n_units;
+    kern<<<grid, threads, smem, s>>>(g, static_cast<const TIn *>(in), static_cast<TOut *>(out), n_units);
+  } else {
+    auto kern = preproc_plain_kernel<TIn, TOut, IN_NCHW, OUT_NCHW>;
+    const size_t smem = stage_bytes;
+    DP_REQUIRE(smem <= 200 * 1024, DP_ERR_UNSUPPORTED, "preproc: input rows too wide for shared memory");
+    DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int per_sm = 0;
+    DP_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem));
+    if (per_sm < 1) per_sm = 1;
+    int grid = sms * per_sm;
+    if (grid > n_units) grid = n_units;
+    kern<<<grid, threads, smem, s>>>(g, static_cast<const TIn *>(in), static_cast<TOut *>(out), n_units);
+  }
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
+template <typename TIn, typename TOut>
+int launch_layouts(const Geo &g, bool in_nchw, bool out_nchw, const void *in, void *out, cudaStream_t s) {
+  if (in_nchw) {
+    return out_nchw ? launch_typed<TIn, TOut, true, true>(g, in, out, s)
+                    : launch_typed<TIn, TOut, true, false>(g, in, out, s);
+  }
+  return out_nchw ? launch_typed<TIn, TOut, false, true>(g, in, out, s)
+                  : launch_typed<TIn, TOut, false, false>(g, in, out, s);
+}
+
+template <typename TIn>
+int launch_out(const Geo &g, int out_dtype, bool in_nchw, bool out_nchw, const void *in, void *out,
+               cudaStream_t s) {
+  switch (out_dtype) {
+    case DP_F32: return launch_layouts<TIn, float>(g, in_nchw, out_nchw, in, out, s);
+    case DP_BF16: return launch_layouts<TIn, __nv_bfloat16>(g, in_nchw, out_nchw, in, out, s);
+    case DP_F16: return launch_layouts<TIn, __half>(g, in_nchw, out_nchw, in, out, s);
+    default: return dp::set_error(DP_ERR_UNSUPPORTED, "preproc: output dtype must be f32, bf16 or f16");
+  }
+}
+
+}  // namespace
+
+namespace dp {
+
+int launch_preproc(const dp_preproc_params &p, const void *in, void *out, cudaStream_t s) {
+  DP_REQUIRE(in && out, DP_ERR_ARG, "preproc: null pointer");
+  DP_REQUIRE(p.batch > 0 && p.in_h > 0 && p.in_w > 0 && p.out_h > 0 && p.out_w > 0, DP_ERR_SHAPE,
+             "preproc: sizes must be positive");
+  DP_REQUIRE(p.channels >= 1 && p.channels <= 4, DP_ERR_UNSUPPORTED, "preproc: 1 to 4 channels");
+  DP_REQUIRE((int64_t)p.batch * p.out_h < (1ll << 31), DP_ERR_UNSUPPORTED, "preproc: too many output rows");
+  DP_REQUIRE(p.in_layout == DP_LAYOUT_NHWC || p.in_layout == DP_LAYOUT_NCHW, DP_ERR_ARG, "preproc: in_layout");
+  DP_REQUIRE(p.out_layout == DP_LAYOUT_NHWC || p.out_layout == DP_LAYOUT_NCHW, DP_ERR_ARG, "preproc: out_layout");
+  Geo g;
+  g.B = p.batch;
+  g.H = p.in_h;
+  g.W = p.in_w;
+  g.C = p.channels;
+  g.OH = p.out_h;
+  g.OW = p.out_w;
+  const bool in_nchw = p.in_layout == DP_LAYOUT_NCHW;
+  g.planes = in_nchw ? p.channels : 1;
+  g.row_elems = in_nchw ? p.in_w : p.in_w * p.channels;
+  g.rows_staged = p.in_h >= 2 ? 2 : 1;
+  const int eb = dtype_bytes(p.in_dtype);
+  DP_REQUIRE(eb > 0, DP_ERR_ARG, "preproc: bad input dtype");
+  // Pad each staged plane to 16 bytes so every bulk destination is aligned.
+  const int plane_elems = g.rows_staged * g.row_elems;
+  const int pad = 16 / eb;
+  g.plane_stride_s = ((plane_elems + pad - 1) / pad) * pad;
+  g.sy = (float)p.in_h / (float)p.out_h;
+  g.sx = (float)p.in_w / (float)p.out_w;
+  g.normalize = p.normalize;
+  for (int c = 0; c < 4; ++c) {
+    g.mean[c] = p.normalize ? p.mean[c] : 0.0f;
+    g.stdv[c] = p.normalize ? p.stdv[c] : 1.0f;
+    g.inv_unused[c] = 0.0f;
+    if (p.normalize && c < p.channels)
+      DP_REQUIRE(p.stdv[c] != 0.0f, DP_ERR_ARG, "preproc: std must be non-zero");
+  }
+  const bool out_nchw = p.out_layout == DP_LAYOUT_NCHW;
+  switch (p.in_dtype) {
+    case DP_U8: return launch_out<uint8_t>(g, p.out_dtype, in_nchw, out_nchw, in, out, s);
+    case DP_F32: return launch_out<float>(g, p.out_dtype, in_nchw, out_nchw, in, out, s);
+    case DP_BF16: return launch_out<__nv_bfloat16>(g, p.out_dtype, in_nchw, out_nchw, in, out, s);
+    case DP_F16: return launch_out<__half>(g, p.out_dtype, in_nchw, out_nchw, in, out, s);
+    default: return set_error(DP_ERR_UNSUPPORTED, "preproc: input dtype must be u8, f32, bf16 or f16");
+  }
+}
+
+}  // namespace dp
+
+extern "C" int dp_preproc(const dp_preproc_params *p, const void *in, void *out, void *stream) {
+  if (!p) return dp::set_error(DP_ERR_ARG, "dp_preproc: null params");
+  return dp::launch_preproc(*p, in, out, dp::as_stream(stream));
+}

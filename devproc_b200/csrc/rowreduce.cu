@@ -1,0 +1,437 @@
+// Row reductions over the contiguous last dim: sum, max, min, mean, argmax,
+// softmax, RMSNorm, LayerNorm.
+//
+// Replaces the reference's reduce templates (src/devproc/backend/triton/
+// templates/reduce.py:11-214): argmax_kernel (grid=(M,) with BLOCK_M=16, so
+// each row was computed up to 16 times), softmax_kernel (one 1024-wide block,
+// wrong for N > 1024) and reduce_sum_kernel (never wired to a handler).
+//
+// One CTA per row (grid-stride over rows), 128-bit vector loads when the row
+// start and length allow it, warp-shuffle then shared-memory combine.  The
+// value reductions stream the row once.  Softmax and the norms keep the row in
+// registers between their passes when it fits (≤ 8 vectors per thread), so
+// HBM sees one read and one write per element; longer rows re-read from L2.
+//
+// Semantics (checked against torch on the CPU): max/min/softmax propagate
+// NaN; argmax returns the first index of the maximum with NaN counted as the
+// maximum; mean = sum / cols; RMSNorm = x · rsqrt(mean(x²) + eps) · (w + off);
+// LayerNorm = (x - mean) · rsqrt(var + eps) · w + b with biased variance.
+#include <cfloat>
+
+#include "dp_common.cuh"
+
+namespace dpk_rowreduce {
+
+constexpr int kMaxThreads = 256;
+
+struct ArgVal {
+  float v;
+  long long i;
+};
+
+// True when (v2, i2) should replace (v1, i1) as the running argmax.
+__device__ __forceinline__ bool arg_better(float v2, long long i2, float v1, long long i1) {
+  const bool n1 = isnan(v1), n2 = isnan(v2);
+  if (n1 || n2) return n2 && (!n1 || i2 < i1);
+  return v2 > v1 || (v2 == v1 && i2 < i1);
+}
+
+__device__ __forceinline__ float nan_max(float a, float b) { return (a > b || isnan(a)) ? a : b; }
+__device__ __forceinline__ float nan_min(float a, float b) { return (a < b || isnan(a)) ? a : b; }
+
+template <typename Op>
+__device__ __forceinline__ float block_reduce(float v, Op op, float *red) {
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();  // red[] may still be read from a previous reduction
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  v = red[0];
+  for (int w = 1; w < nw; ++w) v = op(v, red[w]);
+  return v;
+}
+
+__device__ __forceinline__ ArgVal block_argmax(ArgVal a, float *redv, long long *redi) {
+  for (int o = 16; o > 0; o >>= 1) {
+    float v2 = __shfl_xor_sync(0xffffffffu, a.v, o);
+    long long i2 = __shfl_xor_sync(0xffffffffu, a.i, o);
+    if (arg_better(v2, i2, a.v, a.i)) {
+      a.v = v2;
+      a.i = i2;
+    }
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (lane == 0) {
+    redv[warp] = a.v;
+    redi[warp] = a.i;
+  }
+  __syncthreads();
+  a.v = redv[0];
+  a.i = redi[0];
+  for (int w = 1; w < nw; ++w)
+    if (arg_better(redv[w], redi[w], a.v, a.i)) {
+      a.v = redv[w];
+      a.i = redi[w];
+    }
+  return a;
+}
+
+// VEC consecutive elements of one row as floats.
+template <typename T, int VEC>
+__device__ __forceinline__ void load_vec(const T *p, float (&v)[VEC]) {
+  if constexpr (VEC == 1) {
+    v[0] = to_f32(p[0]);
+  } else {
+    static_assert(sizeof(T) * VEC == 16, "vector loads are 16 bytes");
+    uint4 raw = __ldg(reinterpret_cast<const uint4 *>(p));
+    const T *e = reinterpret_cast<const T *>(&raw);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) v[j] = to_f32(e[j]);
+  }
+}
+
+template <typename T, int VEC>
+__device__ __forceinline__ void store_vec(T *p, const float (&v)[VEC]) {
+  if constexpr (sizeof(T) * VEC == 16) {
+    uint4 raw;
+    T *e = reinterpret_cast<T *>(&raw);
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) e[j] = from_f32<T>(v[j]);
+    *reinterpret_cast<uint4 *>(p) = raw;
+  } else {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) p[j] = from_f32<T>(v[j]);
+  }
+}
+
+__device__ __forceinline__ void write_scalar(void *out, int64_t i, int dt, float v, long long idx) {
+  switch (dt) {
+    case DP_I32: reinterpret_cast<int32_t *>(out)[i] = (int32_t)idx; break;
+    case DP_I64: reinterpret_cast<long long *>(out)[i] = idx; break;
+    default: store_from_f32(out, i, dt, v); break;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// sum / max / min / mean / argmax: one streaming pass.
+template <typename TIn, int VEC>
+__global__ void __launch_bounds__(kMaxThreads) reduce_stream_kernel(dp_rowreduce_params p,
+                                                                    const TIn *__restrict__ in, void *out) {
+  __shared__ float redv[32];
+  __shared__ long long redi[32];
+  const int64_t step = (int64_t)blockDim.x * VEC;
+  for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const TIn *x = in + row * p.in_row_stride;
+    float acc = (p.kind == DP_RED_MAX) ? -INFINITY : (p.kind == DP_RED_MIN ? INFINITY : 0.0f);
+    ArgVal best{-INFINITY, (long long)p.cols};  // index cols = "none yet"
+    int64_t c = (int64_t)threadIdx.x * VEC;
+#pragma unroll 4
+    for (; c < p.cols; c += step) {
+      float v[VEC];
+      load_vec<TIn, VEC>(x + c, v);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        switch (p.kind) {
+          case DP_RED_MAX: acc = nan_max(acc, v[j]); break;
+          case DP_RED_MIN: acc = nan_min(acc, v[j]); break;
+          case DP_RED_ARGMAX:
+            if (arg_better(v[j], c + j, best.v, best.i)) {
+              best.v = v[j];
+              best.i = c + j;
+            }
+            break;
+          default: acc += v[j]; break;
+        }
+      }
+    }
+    if (p.kind == DP_RED_ARGMAX) {
+      best = block_argmax(best, redv, redi);
+      if (threadIdx.x == 0) write_scalar(out, row * p.out_row_stride, p.out_dtype, 0.0f, best.i);
+    } else {
+      if (p.kind == DP_RED_MAX)
+        acc = block_reduce(acc, nan_max, redv);
+      else if (p.kind == DP_RED_MIN)
+        acc = block_reduce(acc, nan_min, redv);
+      else
+        acc = block_reduce(acc, [](float a, float b) { return a + b; }, redv);
+      if (p.kind == DP_RED_MEAN) acc = acc / (float)p.cols;
+      if (threadIdx.x == 0) write_scalar(out, row * p.out_row_stride, p.out_dtype, acc, 0);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// softmax / rmsnorm / layernorm.  NV > 0: the row lives in registers (NV
+// vectors of VEC per thread).  NV == 0: streaming, three passes over the row.
+template <typename TIn, typename TOut, int VEC, int NV>
+__global__ void __launch_bounds__(kMaxThreads) norm_kernel(dp_rowreduce_params p, const TIn *__restrict__ in,
+                                                           const TIn *__restrict__ w, const TIn *__restrict__ bias,
+                                                           TOut *__restrict__ out) {
+  __shared__ float red[32];
+  const int64_t step = (int64_t)blockDim.x * VEC;
+  const float n = (float)p.cols;
+  for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+    const TIn *x = in + row * p.in_row_stride;
+    TOut *y = out + row * p.out_row_stride;
+    if constexpr (NV > 0) {
+      float v[NV][VEC];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t c = (int64_t)threadIdx.x * VEC + i * step;
+        if (c < p.cols) {
+          load_vec<TIn, VEC>(x + c, v[i]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) v[i][j] = 0.0f;
+        }
+      }
+      float scale = 1.0f, shift = 0.0f;
+      if (p.kind == DP_RED_SOFTMAX) {
+        float m = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+          if ((int64_t)threadIdx.x * VEC + i * step < p.cols)
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) m = nan_max(m, v[i][j]);
+        m = block_reduce(m, nan_max, red);
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const bool live = (int64_t)threadIdx.x * VEC + i * step < p.cols;
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            v[i][j] = live ? expf(v[i][j] - m) : 0.0f;
+            s += v[i][j];
+          }
+        }
+        s = block_reduce(s, [](float a, float b) { return a + b; }, red);
+        scale = s;  // divide below
+      } else if (p.kind == DP_RED_RMSNORM) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+        ss = block_reduce(ss, [](float a, float b) { return a + b; }, red);
+        scale = rsqrtf(ss / n + p.eps);
+      } else {  // layernorm
+        float s = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i)
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) s += v[i][j];
+        const float mean = block_reduce(s, [](float a, float b) { return a + b; }, red) / n;
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < NV; ++i) {
+          const bool live = (int64_t)threadIdx.x * VEC + i * step < p.cols;
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            const float d = live ? v[i][j] - mean : 0.0f;
+            q = fmaf(d, d, q);
+          }
+        }
+        const float var = block_reduce(q, [](float a, float b) { return a + b; }, red) / n;
+        scale = rsqrtf(var + p.eps);
+        shift = mean;
+      }
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const int64_t c = (int64_t)threadIdx.x * VEC + i * step;
+        if (c >= p.cols) continue;
+        float o[VEC];
+        float wv[VEC], bv[VEC];
+        if (p.kind != DP_RED_SOFTMAX && p.has_weight) load_vec<TIn, VEC>(w + c, wv);
+        if (p.kind == DP_RED_LAYERNORM && p.has_bias) load_vec<TIn, VEC>(bias + c, bv);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          if (p.kind == DP_RED_SOFTMAX) {
+            o[j] = v[i][j] / scale;
+          } else {
+            float t = (v[i][j] - shift) * scale;
+            if (p.has_weight) t = t * (wv[j] + p.weight_offset);
+            if (p.kind == DP_RED_LAYERNORM && p.has_bias) t = t + bv[j];
+            o[j] = t;
+          }
+        }
+        store_vec<TOut, VEC>(y + c, o);
+      }
+    } else {
+      // Streaming: pass 1 statistics, pass 2 (softmax sum / layernorm var), pass 3 write.
+      float a = (p.kind == DP_RED_SOFTMAX) ? -INFINITY : 0.0f;
+      for (int64_t c = (int64_t)threadIdx.x * VEC; c < p.cols; c += step) {
+        float v[VEC];
+        load_vec<TIn, VEC>(x + c, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          if (p.kind == DP_RED_SOFTMAX) a = nan_max(a, v[j]);
+          else if (p.kind == DP_RED_RMSNORM) a = fmaf(v[j], v[j], a);
+          else a += v[j];
+        }
+      }
+      float scale, shift = 0.0f;
+      if (p.kind == DP_RED_SOFTMAX) {
+        const float m = block_reduce(a, nan_max, red);
+        float s = 0.0f;
+        for (int64_t c = (int64_t)threadIdx.x * VEC; c < p.cols; c += step) {
+          float v[VEC];
+          load_vec<TIn, VEC>(x + c, v);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) s += expf(v[j] - m);
+        }
+        scale = block_reduce(s, [](float u, float t) { return u + t; }, red);
+        shift = m;
+      } else if (p.kind == DP_RED_RMSNORM) {
+        scale = rsqrtf(block_reduce(a, [](float u, float t) { return u + t; }, red) / n + p.eps);
+      } else {
+        const float mean = block_reduce(a, [](float u, float t) { return u + t; }, red) / n;
+        float q = 0.0f;
+        for (int64_t c = (int64_t)threadIdx.x * VEC; c < p.cols; c += step) {
+          float v[VEC];
+          load_vec<TIn, VEC>(x + c, v);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) q = fmaf(v[j] - mean, v[j] - mean, q);
+        }
+        scale = rsqrtf(block_reduce(q, [](float u, float t) { return u + t; }, red) / n + p.eps);
+        shift = mean;
+      }
+      for (int64_t c = (int64_t)threadIdx.x * VEC; c < p.cols; c += step) {
+        float v[VEC], o[VEC], wv[VEC], bv[VEC];
+        load_vec<TIn, VEC>(x + c, v);
+        if (p.kind != DP_RED_SOFTMAX && p.has_weight) load_vec<TIn, VEC>(w + c, wv);
+        if (p.kind == DP_RED_LAYERNORM && p.has_bias) load_vec<TIn, VEC>(bias + c, bv);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          if (p.kind == DP_RED_SOFTMAX) {
+            o[j] = expf(v[j] - shift) / scale;
+          } else {
+            float t = (v[j] - shift) * scale;
+            if (p.has_weight) t = t * (wv[j] + p.weight_offset);
+            if (p.kind == DP_RED_LAYERNORM && p.has_bias) t = t + bv[j];
+            o[j] = t;
+          }
+        }
+        store_vec<TOut, VEC>(y + c, o);
+      }
+    }
+  }
+}
+
+int grid_for(int64_t rows, int threads) {
+  const int per_sm = 2048 / threads;
+  int64_t g = (int64_t)dp::num_sms() * per_sm * 4;
+  return (int)(rows < g ? rows : g);
+}
+
+template <typename TIn, int VEC>
+int launch_stream(const dp_rowreduce_params &p, const void *in, void *out, cudaStream_t s) {
+  int64_t per_thread_vecs = (p.cols + VEC - 1) / VEC;
+  int threads = per_thread_vecs >= kMaxThreads ? kMaxThreads : (int)(((per_thread_vecs + 31) / 32) * 32);
+  if (threads < 32) threads = 32;
+  reduce_stream_kernel<TIn, VEC><<<grid_for(p.rows, threads), threads, 0, s>>>(p, static_cast<const TIn *>(in), out);
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
+template <typename TIn, typename TOut, int VEC>
+int launch_norm(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
+                cudaStream_t s) {
+  const int64_t vecs = (p.cols + VEC - 1) / VEC;
+  int threads = vecs >= kMaxThreads ? kMaxThreads : (int)(((vecs + 31) / 32) * 32);
+  if (threads < 32) threads = 32;
+  const int64_t nv = (vecs + threads - 1) / threads;
+  const int grid = grid_for(p.rows, threads);
+  auto *x = static_cast<const TIn *>(in);
+  auto *wp = static_cast<const TIn *>(w);
+  auto *bp = static_cast<const TIn *>(b);
+  auto *y = static_cast<TOut *>(out);
+  if (nv <= 1)
+    norm_kernel<TIn, TOut, VEC, 1><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+  else if (nv <= 2)
+    norm_kernel<TIn, TOut, VEC, 2><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+  else if (nv <= 4)
+    norm_kernel<TIn, TOut, VEC, 4><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+  else if (nv <= 8)
+    norm_kernel<TIn, TOut, VEC, 8><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+  else
+    norm_kernel<TIn, TOut, VEC, 0><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
+template <typename TIn, typename TOut>
+int launch_norm_vec(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
+                    cudaStream_t s) {
+  constexpr int V = 16 / (int)sizeof(TIn);
+  constexpr int VO = 16 / (int)sizeof(TOut);
+  const bool vec_ok = V == VO || sizeof(TOut) * V <= 16;
+  auto al = [](const void *q, size_t a) { return q == nullptr || reinterpret_cast<uintptr_t>(q) % a == 0; };
+  const bool ok = vec_ok && p.cols % V == 0 && p.in_row_stride % V == 0 && p.out_row_stride % V == 0 &&
+                  al(in, 16) && al(w, 16) && al(b, 16) && al(out, sizeof(TOut) * V);
+  if (ok) return launch_norm<TIn, TOut, V>(p, in, w, b, out, s);
+  return launch_norm<TIn, TOut, 1>(p, in, w, b, out, s);
+}
+
+template <typename TIn>
+int launch_norm_out(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
+                    cudaStream_t s) {
+  switch (p.out_dtype) {
+    case DP_F32: return launch_norm_vec<TIn, float>(p, in, w, b, out, s);
+    case DP_BF16: return launch_norm_vec<TIn, __nv_bfloat16>(p, in, w, b, out, s);
+    case DP_F16: return launch_norm_vec<TIn, __half>(p, in, w, b, out, s);
+    default: return dp::set_error(DP_ERR_UNSUPPORTED, "rowreduce: norm output dtype must be f32/bf16/f16");
+  }
+}
+
+template <typename TIn>
+int launch_stream_vec(const dp_rowreduce_params &p, const void *in, void *out, cudaStream_t s) {
+  constexpr int V = 16 / (int)sizeof(TIn);
+  const bool ok = p.cols % V == 0 && p.in_row_stride % V == 0 && reinterpret_cast<uintptr_t>(in) % 16 == 0;
+  if (ok) return launch_stream<TIn, V>(p, in, out, s);
+  return launch_stream<TIn, 1>(p, in, out, s);
+}
+
+}  // namespace dpk_rowreduce
+
+namespace dp {
+
+int launch_rowreduce(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
+                     cudaStream_t s) {
+  using namespace dpk_rowreduce;
+  DP_REQUIRE(in && out, DP_ERR_ARG, "rowreduce: null pointer");
+  DP_REQUIRE(p.rows > 0 && p.cols > 0, DP_ERR_SHAPE, "rowreduce: rows and cols must be positive");
+  DP_REQUIRE(p.in_row_stride >= p.cols, DP_ERR_SHAPE, "rowreduce: in_row_stride < cols");
+  DP_REQUIRE(p.kind >= DP_RED_SUM && p.kind <= DP_RED_LAYERNORM, DP_ERR_ARG, "rowreduce: bad kind");
+  const bool value_kind = p.kind <= DP_RED_ARGMAX;
+  if (value_kind) {
+    if (p.kind == DP_RED_ARGMAX)
+      DP_REQUIRE(p.out_dtype == DP_I32 || p.out_dtype == DP_I64, DP_ERR_SHAPE, "rowreduce: argmax writes i32/i64");
+    else
+      DP_REQUIRE(p.out_dtype == DP_F32 || p.out_dtype == DP_BF16 || p.out_dtype == DP_F16, DP_ERR_SHAPE,
+                 "rowreduce: value output dtype must be f32/bf16/f16");
+    switch (p.in_dtype) {
+      case DP_F32: return launch_stream_vec<float>(p, in, out, s);
+      case DP_BF16: return launch_stream_vec<__nv_bfloat16>(p, in, out, s);
+      case DP_F16: return launch_stream_vec<__half>(p, in, out, s);
+      default: return set_error(DP_ERR_UNSUPPORTED, "rowreduce: input dtype must be f32/bf16/f16");
+    }
+  }
+  DP_REQUIRE(p.out_row_stride >= p.cols, DP_ERR_SHAPE, "rowreduce: out_row_stride < cols");
+  DP_REQUIRE(!(p.has_weight && !w), DP_ERR_ARG, "rowreduce: has_weight without weight pointer");
+  DP_REQUIRE(!(p.has_bias && !b), DP_ERR_ARG, "rowreduce: has_bias without bias pointer");
+  switch (p.in_dtype) {
+    case DP_F32: return launch_norm_out<float>(p, in, w, b, out, s);
+    case DP_BF16: return launch_norm_out<__nv_bfloat16>(p, in, w, b, out, s);
+    case DP_F16: return launch_norm_out<__half>(p, in, w, b, out, s);
+    default: return set_error(DP_ERR_UNSUPPORTED, "rowreduce: input dtype must be f32/bf16/f16");
+  }
+}
+
+}  // namespace dp
+
+extern "C" int dp_rowreduce(const dp_rowreduce_params *p, const void *in, const void *weight, const void *bias,
+                            void *out, void *stream) {
+  if (!p) return dp::set_error(DP_ERR_ARG, "dp_rowreduce: null params");
+  return dp::launch_rowreduce(*p, in, weight, bias, out, dp::as_stream(stream));
+}

@@ -1,0 +1,221 @@
+/*
+ * devproc_b200.h — C ABI of the DevProc B200 execution backend.
+ *
+ * Plain pointers, sizes and POD parameter blocks; no torch or C++ types.
+ * Every function returns an int status (DP_OK == 0); on failure the calling
+ * thread's last error text is available through dp_last_error().  No call
+ * falls back to another implementation: an unsupported case is an error.
+ *
+ * Stream arguments are cudaStream_t passed as void* (NULL = legacy default
+ * stream).  Kernels are enqueued asynchronously; nothing here synchronises
+ * except dp_device_error() and dp_program_create().
+ *
+ * Reference interfaces replaced (paths inside the DevProc project):
+ *   dp_program_*     ← TritonCompiledProgram.run/_run_jit_with_ir,
+ *                      src/devproc/backend/triton/compiler.py:54-68, 206-250,
+ *                      and the ctypes launcher that never ran,
+ *                      src/devproc/backend/triton/runtime/kernel_launcher.py:59-273
+ *   dp_preproc       ← handle_resize / handle_normalize / handle_to /
+ *                      handle_transpose, src/devproc/backend/triton/ops.py:21-53,
+ *                      320-432, templates/elementwise.py:11-31, 80-101
+ *   dp_rowreduce     ← launch_argmax / launch_softmax / launch_reduce_sum,
+ *                      src/devproc/backend/triton/templates/reduce.py:151-214
+ *   dp_gemm          ← launch_matmul / launch_linear,
+ *                      src/devproc/backend/triton/templates/matmul.py:230-296
+ *   dp_region        ← launch_relu / launch_sigmoid / launch_add / launch_to_dtype,
+ *                      src/devproc/backend/triton/templates/elementwise.py:132-184
+ *   dp_embedding     ← (no reference kernel; FX "embedding" was unsupported,
+ *                      src/devproc/ir/fx_converter.py:197-199)
+ */
+#ifndef DEVPROC_B200_H
+#define DEVPROC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DP_ABI_VERSION 1
+
+/* ---- status codes ---------------------------------------------------- */
+enum {
+  DP_OK = 0,
+  DP_ERR_ARG = 1,         /* null pointer, bad enum, bad size            */
+  DP_ERR_SHAPE = 2,       /* shape / dtype / byte-size mismatch          */
+  DP_ERR_CUDA = 3,        /* a CUDA runtime or driver call failed        */
+  DP_ERR_UNSUPPORTED = 4, /* valid request this backend does not handle  */
+  DP_ERR_PLAN = 5,        /* malformed program plan                      */
+  DP_ERR_STATE = 6,       /* e.g. running a program with unbound slots   */
+  DP_ERR_DEVICE = 7       /* a kernel reported an error through the device error word */
+};
+
+/* ---- element types ---------------------------------------------------- */
+enum {
+  DP_U8 = 0, DP_I8 = 1, DP_I16 = 2, DP_I32 = 3, DP_I64 = 4,
+  DP_F16 = 5, DP_BF16 = 6, DP_F32 = 7, DP_F64 = 8, DP_BOOL = 9
+};
+
+/* ---- device error word codes (read with dp_device_error) -------------- */
+enum {
+  DP_DEVERR_NONE = 0,
+  DP_DEVERR_INDEX = 1,    /* embedding id out of range (row written as zeros) */
+  DP_DEVERR_TIMEOUT = 2   /* a bounded wait inside a kernel gave up            */
+};
+
+/* ---- library ----------------------------------------------------------- */
+int dp_version(void);                         /* returns DP_ABI_VERSION*10000 + minor */
+int dp_last_error(char *buf, size_t buf_len); /* copies this thread's last error text */
+int dp_device_init(int device);               /* sets the device, checks it is sm_100 */
+/* Reads and clears the device error word of the current device (synchronises
+ * the device).  *code receives a DP_DEVERR_* value, *info the first bad index
+ * or wait site recorded. */
+int dp_device_error(int *code, int64_t *info);
+
+/* ---- fused preprocessing region ------------------------------------------
+ * out[b, c, y, x] (or out[b, y, x, c]) =
+ *     cast((bilinear(in)[b, y, x, c] - mean[c]) / std[c])
+ * bilinear = align_corners=False, computed in fp32 with no intermediate
+ * rounding; identical sizes copy exactly.  Input uint8 / fp32 / bf16 / fp16,
+ * layout NHWC or NCHW; output fp32 / bf16 / fp16, layout NCHW or NHWC. */
+enum { DP_LAYOUT_NHWC = 0, DP_LAYOUT_NCHW = 1 };
+typedef struct dp_preproc_params {
+  int32_t batch, in_h, in_w, channels;
+  int32_t out_h, out_w;
+  int32_t in_dtype, in_layout;
+  int32_t out_dtype, out_layout;
+  int32_t normalize, reserved;
+  float mean[4];
+  float stdv[4];
+} dp_preproc_params;
+int dp_preproc(const dp_preproc_params *p, const void *in, void *out, void *stream);
+
+/* ---- row reductions ------------------------------------------------------
+ * rows × cols, reduction over the contiguous last dim (row stride given in
+ * elements).  Value kinds write out[rows] (or out[rows, cols] for softmax and
+ * the norms).  ARGMAX: first index of the maximum, NaN counts as maximum,
+ * output int32 or int64.  RMSNORM: x / sqrt(mean(x²) + eps) · (w + w_offset).
+ * LAYERNORM: (x - mean) / sqrt(var + eps) · w + b (biased variance). */
+enum {
+  DP_RED_SUM = 0, DP_RED_MAX = 1, DP_RED_MIN = 2, DP_RED_MEAN = 3,
+  DP_RED_ARGMAX = 4, DP_RED_SOFTMAX = 5, DP_RED_RMSNORM = 6, DP_RED_LAYERNORM = 7
+};
+typedef struct dp_rowreduce_params {
+  int32_t kind, in_dtype, out_dtype, has_weight;
+  int32_t has_bias, reserved;
+  int64_t rows, cols;
+  int64_t in_row_stride, out_row_stride;
+  float eps, weight_offset;
+} dp_rowreduce_params;
+int dp_rowreduce(const dp_rowreduce_params *p, const void *in, const void *weight,
+                 const void *bias, void *out, void *stream);
+
+/* ---- GEMM -----------------------------------------------------------------
+ * C[b] = epilogue(A[b] · op(B[b]))  with fp32 accumulation.
+ * A: [M, K] row-major (lda).  B: [N, K] row-major when b_layout == DP_B_NK
+ * (nn.Linear weight, K contiguous) or [K, N] row-major when DP_B_KN.
+ * bf16 × bf16 runs on tcgen05 tensor cores (TMEM accumulator, TMA loads);
+ * fp32 × fp32 runs an exact-fp32 FFMA kernel.
+ * Epilogue order: + bias[n] → activation → + residual[m, n] → cast to C. */
+enum { DP_B_NK = 0, DP_B_KN = 1 };
+enum {
+  DP_EPI_BIAS = 1, DP_EPI_RELU = 2, DP_EPI_GELU_ERF = 4, DP_EPI_GELU_TANH = 8,
+  DP_EPI_RESIDUAL = 16, DP_EPI_SILU = 32
+};
+typedef struct dp_gemm_params {
+  int64_t M, N, K;
+  int64_t lda, ldb, ldc, ldr;
+  int64_t batch, stride_a, stride_b, stride_c, stride_r;
+  int32_t a_dtype, b_dtype, c_dtype, r_dtype;
+  int32_t b_layout, epilogue;
+  int32_t bias_dtype, reserved;
+} dp_gemm_params;
+int dp_gemm(const dp_gemm_params *p, const void *A, const void *B, void *C,
+            const void *bias, const void *residual, void *stream);
+
+/* ---- elementwise region (one kernel per fused IR dataflow region) --------
+ * A small register program run per element of an iteration space of up to
+ * DP_REGION_MAX_RANK dims.  Operands 0..n_in-1 are inputs, n_in.. are
+ * outputs; each has a dtype and per-dim element strides (0 = broadcast).
+ * Instruction word: opcode | dst << 8 | a << 16 | b << 24. */
+#define DP_REGION_MAX_OPERANDS 8
+#define DP_REGION_MAX_RANK 6
+#define DP_REGION_MAX_INSTR 64
+#define DP_REGION_MAX_CONST 32
+#define DP_REGION_MAX_REGS 8
+enum {
+  DP_OP_LOAD = 1,    /* r[dst] = float(operand a)                          */
+  DP_OP_STORE = 2,   /* operand a = cast(r[b])                              */
+  DP_OP_CONST = 3,   /* r[dst] = consts[a]                                  */
+  DP_OP_CHANSEL = 4, /* r[dst] = consts[a + coord[b]]  (per-channel consts) */
+  DP_OP_ADD = 10, DP_OP_SUB = 11, DP_OP_MUL = 12, DP_OP_DIV = 13,
+  DP_OP_MAX = 14, DP_OP_MIN = 15,
+  DP_OP_NEG = 20, DP_OP_ABS = 21, DP_OP_RELU = 22, DP_OP_SIGMOID = 23,
+  DP_OP_TANH = 24, DP_OP_EXP = 25, DP_OP_GELU_ERF = 26, DP_OP_GELU_TANH = 27,
+  DP_OP_SILU = 28, DP_OP_MOV = 29
+};
+typedef struct dp_region_desc {
+  int32_t rank, n_in, n_out, n_instr;
+  int64_t shape[DP_REGION_MAX_RANK];
+  int32_t dtype[DP_REGION_MAX_OPERANDS];
+  int64_t stride[DP_REGION_MAX_OPERANDS][DP_REGION_MAX_RANK];
+  uint32_t instr[DP_REGION_MAX_INSTR];
+  float consts[DP_REGION_MAX_CONST];
+} dp_region_desc;
+int dp_region(const dp_region_desc *d, const void *const *operands, void *stream);
+
+/* ---- embedding gather -------------------------------------------------------
+ * out[i, :] = weight[ids[i], :] for i < n_ids; ids int32 or int64.  An id
+ * outside [0, vocab) writes a zero row and sets DP_DEVERR_INDEX. */
+typedef struct dp_embedding_params {
+  int64_t n_ids, vocab, dim;
+  int32_t id_dtype, w_dtype;
+} dp_embedding_params;
+int dp_embedding(const dp_embedding_params *p, const void *ids, const void *weight,
+                 void *out, void *stream);
+
+/* ---- compiled program ------------------------------------------------------
+ * A plan is a little-endian blob: dp_plan_header, n_slots × dp_plan_slot,
+ * n_records × dp_plan_record.  Slots of kind DP_SLOT_BOUND are caller-owned
+ * buffers (inputs, weights, outputs) attached with dp_program_bind; kind
+ * DP_SLOT_ARENA slots live at a fixed offset of the program's arena, which
+ * dp_program_create allocates once.  dp_program_run enqueues every record in
+ * order on the given stream and allocates nothing. */
+#define DP_PLAN_MAGIC 0x32425044u /* "DPB2" */
+#define DP_PLAN_VERSION 1
+#define DP_RECORD_MAX_OPERANDS 8
+#define DP_RECORD_PARAM_BYTES 1280
+enum { DP_SLOT_BOUND = 0, DP_SLOT_ARENA = 1 };
+enum {
+  DP_K_PREPROC = 1, DP_K_ROWREDUCE = 2, DP_K_GEMM = 3, DP_K_REGION = 4,
+  DP_K_EMBEDDING = 5, DP_K_COPY = 6
+};
+typedef struct dp_plan_header {
+  uint32_t magic, version, n_slots, n_records;
+  uint64_t arena_bytes, reserved;
+} dp_plan_header;
+typedef struct dp_plan_slot {
+  uint32_t kind, dtype;
+  uint64_t offset, bytes;
+} dp_plan_slot;
+typedef struct dp_plan_record {
+  uint32_t kernel, n_operands;
+  int32_t operand[DP_RECORD_MAX_OPERANDS];
+  uint8_t params[DP_RECORD_PARAM_BYTES];
+} dp_plan_record;
+
+typedef struct dp_program dp_program;
+int dp_program_create(const void *plan, size_t plan_bytes, int device, dp_program **out);
+int dp_program_bind(dp_program *prog, int slot, void *dev_ptr, size_t bytes);
+int dp_program_run(dp_program *prog, void *stream);
+/* Capture the record sequence into a CUDA graph on first run after binding,
+ * then replay it; rebinding any slot drops the graph. */
+int dp_program_set_graph(dp_program *prog, int enable);
+int dp_program_arena_bytes(const dp_program *prog, uint64_t *bytes);
+int dp_program_destroy(dp_program *prog);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* DEVPROC_B200_H */

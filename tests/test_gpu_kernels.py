@@ -1,0 +1,339 @@
+"""Parity of each sm_100a kernel with the CPU oracle, through the C ABI.
+
+Tolerances (stated per test, following the pipeline's bar: bit-exact for
+integer/index results, rtol 1e-4 for fp32, 2e-2 for bf16):
+* preprocessing — bit-exact against the oracle's resize arithmetic;
+* argmax / max / min / casts / gathers / transposes — exact;
+* sum / mean — |Δ| ≤ 1e-6 · Σ|x| (a float32 summation-order bound);
+* softmax — rtol 1e-5, atol 1e-8;  RMSNorm / LayerNorm — rtol 1e-4, atol 1e-5;
+* fp32 GEMM — |Δ| ≤ 1e-4 · (|ref| + Σ_k |a_k b_k| / sqrt(K));
+* bf16 results — rtol 2e-2, atol 2e-2.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from devproc_b200 import _native as N
+from devproc_b200.ir.function import Function
+from devproc_b200.ir.ops import OpBuilder
+from devproc_b200.ir.types import TensorType
+from devproc_b200 import workloads
+from oracle import interp, preproc_np
+
+pytestmark = pytest.mark.gpu
+
+MEAN, STD = workloads.IMAGENET_MEAN, workloads.IMAGENET_STD
+
+
+def _dt(t):
+    return N.DTYPE_CODE[str(t.dtype).replace("torch.", "")]
+
+
+def _sync():
+    torch.cuda.synchronize()
+    code, info = N.device_error()
+    assert code == N.DP_DEVERR_NONE, (code, info)
+
+
+# ---------------------------------------------------------------- preprocess
+def _preproc_ref(x_nhwc_u8, oh, ow, normalize=True):
+    y = preproc_np.resize_nhwc(x_nhwc_u8.numpy(), oh, ow)
+    if normalize:
+        y = ((y - np.asarray(MEAN, np.float32)).astype(np.float32) / np.asarray(STD, np.float32)).astype(np.float32)
+    return torch.from_numpy(np.ascontiguousarray(y))
+
+
+@pytest.mark.parametrize("B,H,W,OH,OW", [(4, 480, 640, 224, 224), (3, 96, 128, 56, 64), (2, 37, 53, 224, 99),
+                                         (2, 1, 40, 3, 5), (2, 224, 224, 224, 224), (2, 17, 37, 8, 300)])
+def test_preproc_nhwc_u8_to_nchw_bf16_bit_exact(cuda, B, H, W, OH, OW):
+    x = workloads.preprocess_images(B, H, W, seed=B * H + W)
+    out = torch.empty(B, 3, OH, OW, dtype=torch.bfloat16, device=cuda)
+    p = N.PreprocParams(B, H, W, 3, OH, OW, N.DP_U8, N.DP_LAYOUT_NHWC, N.DP_BF16, N.DP_LAYOUT_NCHW, 1, 0)
+    for c in range(3):
+        p.mean[c], p.stdv[c] = MEAN[c], STD[c]
+    N.preproc(p, x.to(cuda), out)
+    _sync()
+    ref = _preproc_ref(x, OH, OW).permute(0, 3, 1, 2).to(torch.bfloat16)
+    assert torch.equal(out.cpu().view(torch.int16), ref.contiguous().view(torch.int16))
+
+
+def test_preproc_float_nchw_and_nhwc_out_bit_exact(cuda):
+    g = torch.Generator().manual_seed(3)
+    x = torch.rand(2, 3, 40, 72, generator=g) * 255  # NCHW fp32
+    out = torch.empty(2, 31, 45, 3, dtype=torch.float32, device=cuda)  # NHWC fp32 out
+    p = N.PreprocParams(2, 40, 72, 3, 31, 45, N.DP_F32, N.DP_LAYOUT_NCHW, N.DP_F32, N.DP_LAYOUT_NHWC, 0, 0)
+    N.preproc(p, x.to(cuda), out)
+    _sync()
+    ref = preproc_np.resize_nhwc(x.permute(0, 2, 3, 1).numpy(), 31, 45)
+    assert np.array_equal(out.cpu().numpy(), ref)
+
+
+def test_preproc_full_batch_sampled_parity(cuda):
+    """Full 256-image batch; 6 images across the batch checked bit-exactly."""
+    x = workloads.preprocess_images()
+    out = torch.empty(256, 3, 224, 224, dtype=torch.bfloat16, device=cuda)
+    p = N.PreprocParams(256, 480, 640, 3, 224, 224, N.DP_U8, N.DP_LAYOUT_NHWC, N.DP_BF16, N.DP_LAYOUT_NCHW, 1, 0)
+    for c in range(3):
+        p.mean[c], p.stdv[c] = MEAN[c], STD[c]
+    N.preproc(p, x.to(cuda), out)
+    _sync()
+    idx = [0, 1, 77, 128, 200, 255]
+    ref = _preproc_ref(x[idx], 224, 224).permute(0, 3, 1, 2).to(torch.bfloat16)
+    assert torch.equal(out[idx].cpu().view(torch.int16), ref.contiguous().view(torch.int16))
+    assert torch.isfinite(out.float()).all()
+
+
+def test_preproc_rejects_bad_arguments(cuda):
+    p = N.PreprocParams(1, 8, 8, 5, 4, 4, N.DP_U8, 0, N.DP_BF16, 1, 0, 0)
+    with pytest.raises(N.DevProcError, match="4 channels"):
+        N.preproc(p, torch.zeros(1, 8, 8, 5, dtype=torch.uint8, device=cuda),
+                  torch.empty(1, 5, 4, 4, dtype=torch.bfloat16, device=cuda))
+
+
+# ---------------------------------------------------------------- rowreduce
+def _rr(kind, x, out_dtype, w=None, b=None, eps=0.0):
+    rows, cols = x.shape
+    if kind in (N.DP_RED_SOFTMAX, N.DP_RED_RMSNORM, N.DP_RED_LAYERNORM):
+        out = torch.empty(rows, cols, dtype=out_dtype, device=x.device)
+        ors = cols
+    else:
+        out = torch.empty(rows, dtype=out_dtype, device=x.device)
+        ors = 1
+    p = N.RowReduceParams(kind, _dt(x), _dt(out), int(w is not None), int(b is not None), 0, rows, cols, cols, ors,
+                          eps, 0.0)
+    N.rowreduce(p, x, out, w, b)
+    _sync()
+    return out.cpu()
+
+
+@pytest.mark.parametrize("rows,cols", [(1024, 4096), (37, 1000), (8, 32000), (5, 3), (300, 8192 * 3 + 5)])
+def test_value_reductions(cuda, rows, cols):
+    g = torch.Generator().manual_seed(rows + cols)
+    x = torch.randn(rows, cols, generator=g)
+    xd = x.to(cuda)
+    bound = 1e-6 * x.abs().sum(-1)
+    s = _rr(N.DP_RED_SUM, xd, torch.float32)
+    assert ((s - x.double().sum(-1).float()).abs() <= bound + 1e-7).all()
+    m = _rr(N.DP_RED_MEAN, xd, torch.float32)
+    assert ((m - x.double().mean(-1).float()).abs() <= bound / cols + 1e-7).all()
+    assert torch.equal(_rr(N.DP_RED_MAX, xd, torch.float32), x.amax(-1))
+    assert torch.equal(_rr(N.DP_RED_MIN, xd, torch.float32), x.amin(-1))
+    assert torch.equal(_rr(N.DP_RED_ARGMAX, xd, torch.int64), x.argmax(-1))
+    assert torch.equal(_rr(N.DP_RED_ARGMAX, xd, torch.int32), x.argmax(-1).int())
+
+
+def test_argmax_ties_and_nan_first_index(cuda):
+    x = torch.tensor([[1.0, 3.0, 3.0, 2.0] * 300, [float("nan")] * 1200, [-1.0] * 1200])
+    x[1, :5] = 0.0
+    x[1, 7] = float("nan")
+    out = _rr(N.DP_RED_ARGMAX, x.to(cuda), torch.int64)
+    assert out.tolist() == torch.argmax(x, -1).tolist() == [1, 5, 0]
+    mx = _rr(N.DP_RED_MAX, x.to(cuda), torch.float32)
+    assert torch.isnan(mx[1]) and mx[0] == 3.0
+
+
+def test_argmax_golden_vectors(cuda, golden):
+    for case in ("argmax_small", "argmax_wide", "argmax_ties"):
+        x = torch.from_numpy(golden[f"{case}/x"])
+        out = _rr(N.DP_RED_ARGMAX, x.to(cuda), torch.int64)
+        assert torch.equal(out, torch.from_numpy(golden[f"{case}/y"])), case
+
+
+@pytest.mark.parametrize("rows,cols", [(1024, 4096), (37, 1000), (64, 512), (16, 20000), (3, 7)])
+def test_softmax_and_norms_fp32(cuda, rows, cols):
+    g = torch.Generator().manual_seed(7 * rows + cols)
+    x = torch.randn(rows, cols, generator=g) * 3
+    w = torch.randn(cols, generator=g)
+    b = torch.randn(cols, generator=g)
+    xd = x.to(cuda)
+    sm = _rr(N.DP_RED_SOFTMAX, xd, torch.float32)
+    assert torch.allclose(sm, torch.softmax(x, -1), rtol=1e-5, atol=1e-8)
+    rn = _rr(N.DP_RED_RMSNORM, xd, torch.float32, w=w.to(cuda), eps=1e-6)
+    ref = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + 1e-6) * w
+    assert torch.allclose(rn, ref, rtol=1e-4, atol=1e-5)
+    ln = _rr(N.DP_RED_LAYERNORM, xd, torch.float32, w=w.to(cuda), b=b.to(cuda), eps=1e-5)
+    assert torch.allclose(ln, torch.nn.functional.layer_norm(x, (cols,), w, b, 1e-5), rtol=1e-4, atol=1e-5)
+
+
+def test_softmax_golden_vector(cuda, golden):
+    x = torch.from_numpy(golden["softmax/x"])
+    assert torch.allclose(_rr(N.DP_RED_SOFTMAX, x.to(cuda), torch.float32), torch.from_numpy(golden["softmax/y"]),
+                          rtol=1e-5, atol=1e-8)
+
+
+def test_norms_bf16(cuda):
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn(256, 1152, generator=g).bfloat16()
+    w = (1 + 0.1 * torch.randn(1152, generator=g)).bfloat16()
+    b = (0.1 * torch.randn(1152, generator=g)).bfloat16()
+    ln = _rr(N.DP_RED_LAYERNORM, x.to(cuda), torch.bfloat16, w=w.to(cuda), b=b.to(cuda), eps=1e-6)
+    ref = torch.nn.functional.layer_norm(x.float(), (1152,), w.float(), b.float(), 1e-6)
+    assert torch.allclose(ln.float(), ref, rtol=2e-2, atol=2e-2)
+
+
+# ------------------------------------------------------------------- region
+def _fn_of(build, *examples):
+    fn = Function("t")
+    vals = []
+    for i, t in enumerate(examples):
+        v = OpBuilder.input(f"x{i}", TensorType(tuple(t.shape), str(t.dtype).replace("torch.", ""))).outputs[0]
+        fn.add_input(v)
+        vals.append(v)
+    ops = build(*vals)
+    for op in ops:
+        fn.add_op(op)
+    fn.output = ops[-1].outputs[0]
+    return fn
+
+
+def _compile_run(fn, inputs):
+    from devproc_b200.backend.b200 import B200Compiler
+    prog = B200Compiler().compile(fn)
+    out = prog.run(**inputs)
+    return prog, out
+
+
+def test_region_chain_with_broadcast(cuda):
+    g = torch.Generator().manual_seed(5)
+    x, y = torch.randn(333, 65, generator=g), torch.randn(65, generator=g)
+
+    def build(a, b):
+        o1 = OpBuilder.relu(a)
+        o2 = OpBuilder.add(o1.outputs[0], b)
+        o3 = OpBuilder.sigmoid(o2.outputs[0])
+        return [o1, o2, o3]
+
+    fn = _fn_of(build, x, y)
+    prog, out = _compile_run(fn, {"x0": x, "x1": y})
+    assert [r["kernel"] for r in prog.spec.records] == ["region"]
+    ref = interp.run_function(fn, {"x0": x, "x1": y})[0]
+    assert torch.allclose(out[0], ref, rtol=1e-6, atol=1e-7)
+
+
+def test_region_golden_vectors(cuda, golden):
+    for case, build in (("relu", OpBuilder.relu), ("normalize_f32", OpBuilder.normalize),
+                        ("normalize_u8", OpBuilder.normalize)):
+        x = torch.from_numpy(golden[f"{case}/x"])
+        fn = _fn_of(lambda a: [build(a)], x)
+        _, out = _compile_run(fn, {"x0": x})
+        assert torch.equal(out[0], torch.from_numpy(golden[f"{case}/y"])), case
+    x, x2 = torch.from_numpy(golden["add/x"]), torch.from_numpy(golden["add/x2"])
+    fn = _fn_of(lambda a, b: [OpBuilder.add(a, b)], x, x2)
+    _, out = _compile_run(fn, {"x0": x, "x1": x2})
+    assert torch.equal(out[0], torch.from_numpy(golden["add/y"]))
+    x = torch.from_numpy(golden["to_i32/x"])
+    fn = _fn_of(lambda a: [OpBuilder.to(a, "int32")], x)
+    _, out = _compile_run(fn, {"x0": x})
+    assert torch.equal(out[0], torch.from_numpy(golden["to_i32/y"]))
+    x = torch.from_numpy(golden["sigmoid/x"])
+    fn = _fn_of(lambda a: [OpBuilder.sigmoid(a)], x)
+    _, out = _compile_run(fn, {"x0": x})
+    assert torch.allclose(out[0], torch.from_numpy(golden["sigmoid/y"]), rtol=1e-6, atol=1e-7)
+
+
+def test_region_transpose_and_channel_normalize(cuda):
+    x = workloads.preprocess_images(2, 12, 20, seed=9)
+
+    def build(a):
+        o1 = OpBuilder.normalize(a, MEAN, STD)
+        o2 = OpBuilder.transpose(o1.outputs[0], (0, 3, 1, 2))
+        o3 = OpBuilder.to(o2.outputs[0], "float16")
+        return [o1, o2, o3]
+
+    fn = _fn_of(build, x)
+    _, out = _compile_run(fn, {"x0": x})
+    ref = interp.run_function(fn, {"x0": x})[0]
+    assert torch.equal(out[0].view(torch.int16), ref.view(torch.int16))
+
+
+# --------------------------------------------------------------------- GEMM
+def _gemm_bound(a, b_nk, ref):
+    k = a.shape[-1]
+    mag = (a.abs().double() @ b_nk.abs().double().T) / k ** 0.5
+    return 1e-4 * (ref.abs().double() + mag)
+
+
+@pytest.mark.parametrize("M,N,K", [(1024, 2048, 512), (37, 53, 29), (128, 32000, 512), (1, 10, 256)])
+def test_gemm_fp32_linear_bias_gelu(cuda, M, N, K):
+    g = torch.Generator().manual_seed(M + N + K)
+    a = torch.randn(M, K, generator=g)
+    w = torch.randn(N, K, generator=g) * 0.02
+    bias = torch.randn(N, generator=g)
+    c = torch.empty(M, N, device=cuda)
+    p = N.GemmParams()
+    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, N, K, K, K, N, 1
+    p.a_dtype = p.b_dtype = p.c_dtype = p.bias_dtype = N.DP_F32
+    p.b_layout = N.DP_B_NK
+    p.epilogue = N.DP_EPI_BIAS | N.DP_EPI_GELU_ERF
+    N.gemm(p, a.to(cuda), w.to(cuda), c, bias=bias.to(cuda))
+    _sync()
+    pre = (a.double() @ w.double().T + bias.double())
+    ref = torch.nn.functional.gelu(pre)
+    assert ((c.cpu().double() - ref).abs() <= _gemm_bound(a, w, ref) + 1e-6).all()
+
+
+def test_gemm_fp32_matmul_kn_and_residual(cuda):
+    g = torch.Generator().manual_seed(2)
+    M, N_, K = 200, 72, 130
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(K, N_, generator=g)
+    r = torch.randn(M, N_, generator=g)
+    c = torch.empty(M, N_, device=cuda)
+    p = N.GemmParams()
+    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.ldr, p.batch = M, N_, K, K, N_, N_, N_, 1
+    p.a_dtype = p.b_dtype = p.c_dtype = p.r_dtype = N.DP_F32
+    p.b_layout = N.DP_B_KN
+    p.epilogue = N.DP_EPI_RESIDUAL
+    N.gemm(p, a.to(cuda), b.to(cuda), c, residual=r.to(cuda))
+    _sync()
+    ref = a.double() @ b.double() + r.double()
+    assert ((c.cpu().double() - ref).abs() <= _gemm_bound(a, b.T, ref) + 1e-6).all()
+
+
+def test_gemm_golden_vectors(cuda, golden):
+    x, w = torch.from_numpy(golden["matmul/x"]), torch.from_numpy(golden["matmul/x2"])
+    fn = _fn_of(lambda a, b: [OpBuilder.matmul(a, b)], x, w)
+    _, out = _compile_run(fn, {"x0": x, "x1": w})
+    assert torch.allclose(out[0], torch.from_numpy(golden["matmul/y"]), rtol=1e-5, atol=1e-5)
+    x, w, b = (torch.from_numpy(golden[f"linear/{k}"]) for k in ("x", "x2", "b"))
+    fn = _fn_of(lambda a, ww, bb: [OpBuilder.linear(a, ww, bb)], x, w, b)
+    _, out = _compile_run(fn, {"x0": x, "x1": w, "x2": b})
+    assert torch.allclose(out[0], torch.from_numpy(golden["linear/y"]), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (4096, 4096, 4096)])
+def test_gemm_bf16(cuda, M, N, K):
+    g = torch.Generator().manual_seed(M ^ N ^ K)
+    a = torch.randn(M, K, generator=g).bfloat16()
+    w = torch.randn(N, K, generator=g).bfloat16()
+    c = torch.empty(M, N, device=cuda)
+    p = N.GemmParams()
+    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, N, K, K, K, N, 1
+    p.a_dtype = p.b_dtype = N.DP_BF16
+    p.c_dtype = N.DP_F32
+    p.b_layout = N.DP_B_NK
+    N.gemm(p, a.to(cuda), w.to(cuda), c)
+    _sync()
+    rows = slice(0, M) if M <= 512 else torch.arange(0, M, 61)
+    ref = a[rows].float() @ w.float().T
+    got = c.cpu()[rows]
+    assert torch.allclose(got, ref, rtol=2e-2, atol=2e-2 * K ** 0.5 / 8)
+
+
+# ---------------------------------------------------------------- embedding
+def test_embedding_exact_and_index_error(cuda):
+    g = torch.Generator().manual_seed(4)
+    w = torch.randn(1000, 96, generator=g)
+    ids = torch.randint(0, 1000, (7, 13), generator=g, dtype=torch.int32)
+    out = torch.empty(7 * 13, 96, device=cuda)
+    p = N.EmbeddingParams(ids.numel(), 1000, 96, N.DP_I32, N.DP_F32)
+    N.embedding(p, ids.to(cuda), w.to(cuda), out)
+    _sync()
+    assert torch.equal(out.cpu().view(7, 13, 96), w[ids.long()])
+    ids[3, 4] = 1000  # out of range
+    N.embedding(p, ids.to(cuda), w.to(cuda), out)
+    torch.cuda.synchronize()
+    code, info = N.device_error()
+    assert code == N.DP_DEVERR_INDEX and info == 3 * 13 + 4
+    assert (out.cpu()[3 * 13 + 4] == 0).all()
