@@ -43,7 +43,7 @@ FALLBACK_HBM_GBS = 6650.0
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=10000)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--batch", type=int, default=256)
@@ -91,11 +91,18 @@ class ClockSampler:
         fd, self.path = tempfile.mkstemp(suffix=".csv")
         os.close(fd)
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
                                           "--format=csv,noheader,nounits", "-lms", "200"],
                                          stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
+            return self
+        # Start timing only once the sampler is producing lines.
+        t0 = time.time()
+        while time.time() - t0 < 5 and os.path.getsize(self.path) == 0:
+            time.sleep(0.05)
+        with open(self.path) as f:
+            self.skip = len(f.readlines())
         return self
 
     def __exit__(self, *exc):
@@ -111,7 +118,7 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in open(self.path):
+        for line in open(self.path).readlines()[getattr(self, "skip", 0):]:
             f = [x.strip() for x in line.split(",")]
             if len(f) < 9:
                 continue

@@ -193,6 +193,230 @@ __global__ void __launch_bounds__(kMaxThreads) preproc_plain_kernel(Geo g, const
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fast path: uint8 NHWC, 3 channels, even output width, input width a
+// multiple of 16 (so every staged row is 16-byte aligned), planar output.
+// Each thread produces two adjacent output columns of one output row for all
+// three channels; a block covers R output rows per unit.  Per output element
+// the kernel spends ~24 full-rate instructions:
+//   * the 6 bytes of an (x0, x0+1) pixel pair come from two 8-byte shared
+//     loads plus funnel shifts; byte → float is exact via the 2^23 magic
+//     number (byte | 0x4B000000 reinterpreted, minus 2^23) instead of I2F;
+//   * the three interpolation FMAs are the generic path's, unchanged;
+//   * (v - mean) / std is computed as the correctly rounded quotient with
+//     Markstein's FMA correction (P. Markstein, "Computation of elementary
+//     functions on the IBM RISC System/6000 processor", IBM J. R&D 34(1),
+//     1990): y = RN(1/std) precomputed on the host, q = RN(t·y),
+//     r = fma(-q, std, t) (exact), result = RN(q + r·y) — equal to IEEE
+//     t / std for these finite, normal operands;
+//   * two output columns are packed into one 32-bit (bf16/f16) or 64-bit
+//     (f32) store per channel.
+constexpr int kFastStages = 4;
+
+struct FastGeo {
+  int B, H, W, OH, OW;
+  int R, tpr, upi;     // rows per unit, threads per row, units per image
+  int row_bytes;       // W * 3
+  int slot_bytes;      // shared bytes per output row: 2 input rows + 16 B slack, 16-B rounded
+  float sy, sx;
+  int normalize;
+  float mean[3], stdv[3], rcp[3];
+};
+
+__device__ __forceinline__ float byte_to_f32(uint32_t word, int k) {
+  // k in 0..3: byte k of ``word`` as an exact float.
+  const uint32_t b = (word >> (8 * k)) & 0xffu;
+  return __int_as_float((int)(b | 0x4B000000u)) - 8388608.0f;
+}
+
+__device__ __forceinline__ float div_rn(float t, float d, float y) {
+  const float q = __fmul_rn(t, y);
+  const float r = __fmaf_rn(-q, d, t);
+  return __fmaf_rn(r, y, q);
+}
+
+struct ColWin {
+  int ws;   // 8-byte aligned start of the 16-byte window in the row
+  int sh;   // bit shift after dropping whole words
+  bool hi;  // window starts in the second word
+  int d;    // byte distance from pixel x0 to pixel x1 (3, or 0 at the right edge)
+  float l0, l1;
+};
+
+__device__ __forceinline__ ColWin make_win(const Coef &c) {
+  ColWin w;
+  const int b0 = 3 * c.i0;
+  w.ws = b0 & ~7;
+  const int o = b0 - w.ws;  // 0..7
+  w.hi = o >= 4;
+  w.sh = 8 * (o & 3);
+  w.d = c.i1 != c.i0 ? 3 : 0;
+  w.l0 = c.l0;
+  w.l1 = c.l1;
+  return w;
+}
+
+// Six bytes of pixels x0, x1 (channels 0..2 each) as 8 aligned bytes a0:a1
+// starting at pixel x0.
+__device__ __forceinline__ void fetch_pair(const uint8_t *row, const ColWin &w, uint32_t &a0, uint32_t &a1) {
+  const uint2 lo = *reinterpret_cast<const uint2 *>(row + w.ws);
+  const uint2 hi = *reinterpret_cast<const uint2 *>(row + w.ws + 8);
+  const uint32_t w0 = w.hi ? lo.y : lo.x, w1 = w.hi ? hi.x : lo.y, w2 = w.hi ? hi.y : hi.x;
+  a0 = __funnelshift_r(w0, w1, w.sh);
+  a1 = __funnelshift_r(w1, w2, w.sh);
+}
+
+__device__ __forceinline__ float pix(uint32_t a0, uint32_t a1, int idx) {
+  // byte idx (0..7) of the pair a0:a1
+  return idx < 4 ? byte_to_f32(a0, idx) : byte_to_f32(a1, idx - 4);
+}
+
+template <typename TOut>
+__device__ __forceinline__ void store_pair(TOut *p, float v0, float v1);
+template <>
+__device__ __forceinline__ void store_pair<__nv_bfloat16>(__nv_bfloat16 *p, float v0, float v1) {
+  *reinterpret_cast<__nv_bfloat162 *>(p) = __floats2bfloat162_rn(v0, v1);
+}
+template <>
+__device__ __forceinline__ void store_pair<__half>(__half *p, float v0, float v1) {
+  *reinterpret_cast<__half2 *>(p) = __floats2half2_rn(v0, v1);
+}
+template <>
+__device__ __forceinline__ void store_pair<float>(float *p, float v0, float v1) {
+  *reinterpret_cast<float2 *>(p) = make_float2(v0, v1);
+}
+
+template <typename TOut>
+__global__ void __launch_bounds__(kMaxThreads) preproc_u8c3_kernel(FastGeo g, const uint8_t *__restrict__ in,
+                                                                   TOut *__restrict__ out, int n_units) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[kFastStages];
+  const int stage_bytes = g.R * g.slot_bytes;
+  const uint32_t copy_bytes = (uint32_t)(2 * g.row_bytes);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kFastStages; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+
+  const int r = threadIdx.x / g.tpr;
+  const int j = threadIdx.x - r * g.tpr;
+  const bool active = r < g.R;
+  const int ox = 2 * j;
+  const ColWin c0 = make_win(src_coef(active ? ox : 0, g.W, g.OW, g.sx));
+  const ColWin c1 = make_win(src_coef(active ? ox + 1 : 0, g.W, g.OW, g.sx));
+
+  auto unit_rows = [&](int u, int &b, int &oy0) {
+    b = u / g.upi;
+    oy0 = (u - b * g.upi) * g.R;
+  };
+  auto row_start = [&](int oy) {  // first staged input row of output row oy
+    Coef cy = src_coef(oy, g.H, g.OH, g.sy);
+    return cy.i0 < g.H - 1 ? cy.i0 : g.H - 2;
+  };
+  auto issue = [&](int k) {  // thread 0: stage unit #k of this block
+    const int u = blockIdx.x + k * gridDim.x;
+    int b, oy0;
+    unit_rows(u, b, oy0);
+    const int nrows = min(g.R, g.OH - oy0);
+    const int s = k % kFastStages;
+    mbar_arrive_expect_tx(&bars[s], copy_bytes * nrows);
+    for (int rr = 0; rr < nrows; ++rr) {
+      const uint8_t *src = in + ((int64_t)b * g.H + row_start(oy0 + rr)) * g.row_bytes;
+      bulk_g2s(smem_raw + s * stage_bytes + rr * g.slot_bytes, src, copy_bytes, &bars[s]);
+    }
+  };
+
+  const int my_units = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  if (threadIdx.x == 0)
+    for (int k = 0; k < kFastStages && k < my_units; ++k) issue(k);
+
+  int k = 0;
+  for (; k < my_units; ++k) {
+    const int s = k % kFastStages;
+    const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)(k / kFastStages) & 1u, 120 + s);
+    const int u = blockIdx.x + k * gridDim.x;
+    int b, oy0;
+    unit_rows(u, b, oy0);
+    const int oy = oy0 + r;
+    if (active && oy < g.OH) {
+      const Coef cy = src_coef(oy, g.H, g.OH, g.sy);
+      const int ys = cy.i0 < g.H - 1 ? cy.i0 : g.H - 2;
+      const uint8_t *base = smem_raw + s * stage_bytes + r * g.slot_bytes;
+      const uint8_t *row0 = base + (cy.i0 - ys) * g.row_bytes;
+      const uint8_t *row1 = base + (cy.i1 - ys) * g.row_bytes;
+      uint32_t p00, p01, p10, p11, q00, q01, q10, q11;  // [col][row] pairs
+      fetch_pair(row0, c0, p00, p01);
+      fetch_pair(row1, c0, p10, p11);
+      fetch_pair(row0, c1, q00, q01);
+      fetch_pair(row1, c1, q10, q11);
+#pragma unroll
+      for (int c = 0; c < 3; ++c) {
+        float v[2];
+#pragma unroll
+        for (int col = 0; col < 2; ++col) {
+          const ColWin &w = col ? c1 : c0;
+          const uint32_t r0a = col ? q00 : p00, r0b = col ? q01 : p01;
+          const uint32_t r1a = col ? q10 : p10, r1b = col ? q11 : p11;
+          const float a = byte_to_f32(r0a, c), bb = pix(r0a, r0b, w.d + c);
+          const float cc = byte_to_f32(r1a, c), d = pix(r1a, r1b, w.d + c);
+          const float row0v = __fmaf_rn(a, w.l0, __fmul_rn(bb, w.l1));
+          const float row1v = __fmaf_rn(cc, w.l0, __fmul_rn(d, w.l1));
+          float t = __fmaf_rn(row0v, cy.l0, __fmul_rn(row1v, cy.l1));
+          if (g.normalize) t = div_rn(__fsub_rn(t, g.mean[c]), g.stdv[c], g.rcp[c]);
+          v[col] = t;
+        }
+        store_pair<TOut>(out + (((int64_t)b * 3 + c) * g.OH + oy) * g.OW + ox, v[0], v[1]);
+      }
+    }
+    if (!__syncthreads_and(ok)) break;
+    if (threadIdx.x == 0 && k + kFastStages < my_units) issue(k + kFastStages);
+  }
+  if (k < my_units && threadIdx.x == 0) {
+    for (int jj = k; jj < my_units && jj < k + kFastStages; ++jj)
+      mbar_wait_bounded(&bars[jj % kFastStages], (uint32_t)(jj / kFastStages) & 1u, 199, 100000000ull);
+  }
+  __syncthreads();
+}
+
+template <typename TOut>
+int launch_fast(const dp_preproc_params &p, const void *in, void *out, cudaStream_t s) {
+  FastGeo g;
+  g.B = p.batch;
+  g.H = p.in_h;
+  g.W = p.in_w;
+  g.OH = p.out_h;
+  g.OW = p.out_w;
+  g.tpr = p.out_w / 2;
+  g.R = g.tpr >= kMaxThreads ? 1 : kMaxThreads / g.tpr;
+  if (g.R > g.OH) g.R = g.OH;
+  g.upi = (g.OH + g.R - 1) / g.R;
+  g.row_bytes = 3 * p.in_w;
+  g.slot_bytes = ((2 * g.row_bytes + 16) + 15) / 16 * 16;
+  g.sy = (float)p.in_h / (float)p.out_h;
+  g.sx = (float)p.in_w / (float)p.out_w;
+  g.normalize = p.normalize;
+  for (int c = 0; c < 3; ++c) {
+    g.mean[c] = p.normalize ? p.mean[c] : 0.0f;
+    g.stdv[c] = p.normalize ? p.stdv[c] : 1.0f;
+    g.rcp[c] = 1.0f / g.stdv[c];
+  }
+  const int threads = ((g.R * g.tpr + 31) / 32) * 32;
+  const size_t smem = (size_t)kFastStages * g.R * g.slot_bytes;
+  const int n_units = g.B * g.upi;
+  auto kern = preproc_u8c3_kernel<TOut>;
+  DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  DP_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem));
+  if (per_sm < 1) per_sm = 1;
+  int grid = dp::num_sms() * per_sm;
+  if (grid > n_units) grid = n_units;
+  kern<<<grid, threads, smem, s>>>(g, static_cast<const uint8_t *>(in), static_cast<TOut *>(out), n_units);
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
 template <typename TIn, typename TOut, bool IN_NCHW, bool OUT_NCHW>
 int launch_typed(const Geo &g, const void *in, void *out, cudaStream_t s) {
   const int n_units = g.B * g.OH;
@@ -293,6 +517,18 @@ int launch_preproc(const dp_preproc_params &p, const void *in, void *out, cudaSt
       DP_REQUIRE(p.stdv[c] != 0.0f, DP_ERR_ARG, "preproc: std must be non-zero");
   }
   const bool out_nchw = p.out_layout == DP_LAYOUT_NCHW;
+  const bool fast = p.in_dtype == DP_U8 && !in_nchw && out_nchw && p.channels == 3 && p.in_w % 16 == 0 &&
+                    p.out_w % 2 == 0 && p.in_h >= 2 && reinterpret_cast<uintptr_t>(in) % 16 == 0 &&
+                    reinterpret_cast<uintptr_t>(out) % 8 == 0 && 2 * 3 * p.in_w + 16 <= 96 * 1024 &&
+                    p.out_w / 2 <= 1024;
+  if (fast) {
+    switch (p.out_dtype) {
+      case DP_BF16: return launch_fast<__nv_bfloat16>(p, in, out, s);
+      case DP_F16: return launch_fast<__half>(p, in, out, s);
+      case DP_F32: return launch_fast<float>(p, in, out, s);
+      default: break;
+    }
+  }
   switch (p.in_dtype) {
     case DP_U8: return launch_out<uint8_t>(g, p.out_dtype, in_nchw, out_nchw, in, out, s);
     case DP_F32: return launch_out<float>(g, p.out_dtype, in_nchw, out_nchw, in, out, s);

@@ -45,7 +45,9 @@ def _preproc_ref(x_nhwc_u8, oh, ow, normalize=True):
 
 
 @pytest.mark.parametrize("B,H,W,OH,OW", [(4, 480, 640, 224, 224), (3, 96, 128, 56, 64), (2, 37, 53, 224, 99),
-                                         (2, 1, 40, 3, 5), (2, 224, 224, 224, 224), (2, 17, 37, 8, 300)])
+                                         (2, 1, 40, 3, 5), (2, 224, 224, 224, 224), (2, 17, 37, 8, 300),
+                                         (2, 50, 32, 7, 2), (1, 64, 2048, 5, 1000), (2, 480, 640, 480, 640),
+                                         (3, 100, 48, 300, 96)])
 def test_preproc_nhwc_u8_to_nchw_bf16_bit_exact(cuda, B, H, W, OH, OW):
     x = workloads.preprocess_images(B, H, W, seed=B * H + W)
     out = torch.empty(B, 3, OH, OW, dtype=torch.bfloat16, device=cuda)
@@ -56,6 +58,19 @@ def test_preproc_nhwc_u8_to_nchw_bf16_bit_exact(cuda, B, H, W, OH, OW):
     _sync()
     ref = _preproc_ref(x, OH, OW).permute(0, 3, 1, 2).to(torch.bfloat16)
     assert torch.equal(out.cpu().view(torch.int16), ref.contiguous().view(torch.int16))
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.float16])
+def test_preproc_fast_path_other_output_types(cuda, out_dtype):
+    x = workloads.preprocess_images(3, 240, 320, seed=5)
+    out = torch.empty(3, 3, 112, 160, dtype=out_dtype, device=cuda)
+    p = N.PreprocParams(3, 240, 320, 3, 112, 160, N.DP_U8, N.DP_LAYOUT_NHWC, _dt(out), N.DP_LAYOUT_NCHW, 1, 0)
+    for c in range(3):
+        p.mean[c], p.stdv[c] = MEAN[c], STD[c]
+    N.preproc(p, x.to(cuda), out)
+    _sync()
+    ref = _preproc_ref(x, 112, 160).permute(0, 3, 1, 2).to(out_dtype).contiguous()
+    assert torch.equal(out.cpu(), ref)
 
 
 def test_preproc_float_nchw_and_nhwc_out_bit_exact(cuda):
@@ -69,8 +84,8 @@ def test_preproc_float_nchw_and_nhwc_out_bit_exact(cuda):
     assert np.array_equal(out.cpu().numpy(), ref)
 
 
-def test_preproc_full_batch_sampled_parity(cuda):
-    """Full 256-image batch; 6 images across the batch checked bit-exactly."""
+def test_preproc_full_batch_parity(cuda):
+    """Full 256-image batch, every output element checked bit-exactly."""
     x = workloads.preprocess_images()
     out = torch.empty(256, 3, 224, 224, dtype=torch.bfloat16, device=cuda)
     p = N.PreprocParams(256, 480, 640, 3, 224, 224, N.DP_U8, N.DP_LAYOUT_NHWC, N.DP_BF16, N.DP_LAYOUT_NCHW, 1, 0)
@@ -78,9 +93,10 @@ def test_preproc_full_batch_sampled_parity(cuda):
         p.mean[c], p.stdv[c] = MEAN[c], STD[c]
     N.preproc(p, x.to(cuda), out)
     _sync()
-    idx = [0, 1, 77, 128, 200, 255]
-    ref = _preproc_ref(x[idx], 224, 224).permute(0, 3, 1, 2).to(torch.bfloat16)
-    assert torch.equal(out[idx].cpu().view(torch.int16), ref.contiguous().view(torch.int16))
+    got = out.cpu().view(torch.int16)
+    for lo in range(0, 256, 32):
+        ref = _preproc_ref(x[lo:lo + 32], 224, 224).permute(0, 3, 1, 2).to(torch.bfloat16)
+        assert torch.equal(got[lo:lo + 32], ref.contiguous().view(torch.int16)), lo
     assert torch.isfinite(out.float()).all()
 
 
@@ -254,15 +270,15 @@ def _gemm_bound(a, b_nk, ref):
     return 1e-4 * (ref.abs().double() + mag)
 
 
-@pytest.mark.parametrize("M,N,K", [(1024, 2048, 512), (37, 53, 29), (128, 32000, 512), (1, 10, 256)])
-def test_gemm_fp32_linear_bias_gelu(cuda, M, N, K):
-    g = torch.Generator().manual_seed(M + N + K)
+@pytest.mark.parametrize("M,Nn,K", [(1024, 2048, 512), (37, 53, 29), (128, 32000, 512), (1, 10, 256)])
+def test_gemm_fp32_linear_bias_gelu(cuda, M, Nn, K):
+    g = torch.Generator().manual_seed(M + Nn + K)
     a = torch.randn(M, K, generator=g)
-    w = torch.randn(N, K, generator=g) * 0.02
-    bias = torch.randn(N, generator=g)
-    c = torch.empty(M, N, device=cuda)
+    w = torch.randn(Nn, K, generator=g) * 0.02
+    bias = torch.randn(Nn, generator=g)
+    c = torch.empty(M, Nn, device=cuda)
     p = N.GemmParams()
-    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, N, K, K, K, N, 1
+    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, Nn, K, K, K, Nn, 1
     p.a_dtype = p.b_dtype = p.c_dtype = p.bias_dtype = N.DP_F32
     p.b_layout = N.DP_B_NK
     p.epilogue = N.DP_EPI_BIAS | N.DP_EPI_GELU_ERF
@@ -302,14 +318,14 @@ def test_gemm_golden_vectors(cuda, golden):
     assert torch.allclose(out[0], torch.from_numpy(golden["linear/y"]), rtol=1e-5, atol=1e-5)
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 512, 1024), (4096, 4096, 4096)])
-def test_gemm_bf16(cuda, M, N, K):
-    g = torch.Generator().manual_seed(M ^ N ^ K)
+@pytest.mark.parametrize("M,Nn,K", [(256, 512, 1024), (4096, 4096, 4096)])
+def test_gemm_bf16(cuda, M, Nn, K):
+    g = torch.Generator().manual_seed(M ^ Nn ^ K)
     a = torch.randn(M, K, generator=g).bfloat16()
-    w = torch.randn(N, K, generator=g).bfloat16()
-    c = torch.empty(M, N, device=cuda)
+    w = torch.randn(Nn, K, generator=g).bfloat16()
+    c = torch.empty(M, Nn, device=cuda)
     p = N.GemmParams()
-    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, N, K, K, K, N, 1
+    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, Nn, K, K, K, Nn, 1
     p.a_dtype = p.b_dtype = N.DP_BF16
     p.c_dtype = N.DP_F32
     p.b_layout = N.DP_B_NK
