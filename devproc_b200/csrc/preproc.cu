@@ -520,7 +520,7 @@ int launch_preproc(const dp_preproc_params &p, const void *in, void *out, cudaSt
   const bool fast = p.in_dtype == DP_U8 && !in_nchw && out_nchw && p.channels == 3 && p.in_w % 16 == 0 &&
                     p.out_w % 2 == 0 && p.in_h >= 2 && reinterpret_cast<uintptr_t>(in) % 16 == 0 &&
                     reinterpret_cast<uintptr_t>(out) % 8 == 0 && 2 * 3 * p.in_w + 16 <= 96 * 1024 &&
-                    p.out_w / 2 <= 1024;
+                    p.out_w / 2 <= kMaxThreads;
   if (fast) {
     switch (p.out_dtype) {
       case DP_BF16: return launch_fast<__nv_bfloat16>(p, in, out, s);
