@@ -235,11 +235,14 @@ __device__ __forceinline__ float div_rn(float t, float d, float y) {
   return __fmaf_rn(r, y, q);
 }
 
+// Window of one output column: the 8-byte aligned 16-byte span of the row
+// holding pixels x0 and x1, and how to shift it so that pixel x0 starts at
+// byte 0.  ``edge`` marks the clamped right edge (x1 == x0).
 struct ColWin {
-  int ws;   // 8-byte aligned start of the 16-byte window in the row
-  int sh;   // bit shift after dropping whole words
-  bool hi;  // window starts in the second word
-  int d;    // byte distance from pixel x0 to pixel x1 (3, or 0 at the right edge)
+  int ws;
+  int sh;
+  bool hi;
+  bool edge;
   float l0, l1;
 };
 
@@ -250,14 +253,14 @@ __device__ __forceinline__ ColWin make_win(const Coef &c) {
   const int o = b0 - w.ws;  // 0..7
   w.hi = o >= 4;
   w.sh = 8 * (o & 3);
-  w.d = c.i1 != c.i0 ? 3 : 0;
+  w.edge = c.i1 == c.i0;
   w.l0 = c.l0;
   w.l1 = c.l1;
   return w;
 }
 
-// Six bytes of pixels x0, x1 (channels 0..2 each) as 8 aligned bytes a0:a1
-// starting at pixel x0.
+// Bytes of pixels x0 and x0+1 (3 channels each) as a0 = [x0.c0 x0.c1 x0.c2 x1.c0],
+// a1 = [x1.c1 x1.c2 . .].
 __device__ __forceinline__ void fetch_pair(const uint8_t *row, const ColWin &w, uint32_t &a0, uint32_t &a1) {
   const uint2 lo = *reinterpret_cast<const uint2 *>(row + w.ws);
   const uint2 hi = *reinterpret_cast<const uint2 *>(row + w.ws + 8);
@@ -266,9 +269,34 @@ __device__ __forceinline__ void fetch_pair(const uint8_t *row, const ColWin &w, 
   a1 = __funnelshift_r(w1, w2, w.sh);
 }
 
-__device__ __forceinline__ float pix(uint32_t a0, uint32_t a1, int idx) {
-  // byte idx (0..7) of the pair a0:a1
-  return idx < 4 ? byte_to_f32(a0, idx) : byte_to_f32(a1, idx - 4);
+// Byte SEL (compile-time, 0..3) of ``word`` as an exact float: one byte permute
+// builds the bits of 2^23 + byte, one add removes 2^23.
+template <int SEL>
+__device__ __forceinline__ float bytef(uint32_t word) {
+  return __int_as_float((int)__byte_perm(word, 0x4B000000u, 0x7440u | SEL)) - 8388608.0f;
+}
+
+// Output value of one channel at one column: bilinear then normalise.
+template <int C, bool EDGE>
+__device__ __forceinline__ float pixel_value(uint32_t r0a, uint32_t r0b, uint32_t r1a, uint32_t r1b,
+                                             const ColWin &w, float h0, float h1, const FastGeo &g) {
+  const float a = bytef<C>(r0a), cc = bytef<C>(r1a);
+  float bb, d;
+  if (EDGE) {
+    bb = a;
+    d = cc;
+  } else if (C == 0) {
+    bb = bytef<3>(r0a);
+    d = bytef<3>(r1a);
+  } else {
+    bb = bytef<C - 1>(r0b);
+    d = bytef<C - 1>(r1b);
+  }
+  const float row0v = __fmaf_rn(a, w.l0, __fmul_rn(bb, w.l1));
+  const float row1v = __fmaf_rn(cc, w.l0, __fmul_rn(d, w.l1));
+  float t = __fmaf_rn(row0v, h0, __fmul_rn(row1v, h1));
+  if (g.normalize) t = div_rn(__fsub_rn(t, g.mean[C]), g.stdv[C], g.rcp[C]);
+  return t;
 }
 
 template <typename TOut>
@@ -286,6 +314,33 @@ __device__ __forceinline__ void store_pair<float>(float *p, float v0, float v1) 
   *reinterpret_cast<float2 *>(p) = make_float2(v0, v1);
 }
 
+// Vertical coefficients of every output row, built once per block in shared
+// memory: first staged input row, rows of y0/y1 inside the staged pair, weights.
+struct RowCoef {
+  int ys;
+  int r01;  // (y0 - ys) | (y1 - ys) << 8
+  float h0, h1;
+};
+
+template <typename TOut, bool C1_EDGE>
+__device__ __forceinline__ void compute_two_cols(const uint8_t *row0, const uint8_t *row1, const ColWin &c0,
+                                                 const ColWin &c1, float h0, float h1, const FastGeo &g,
+                                                 TOut *o, int64_t plane) {
+  uint32_t p0a, p0b, p1a, p1b, q0a, q0b, q1a, q1b;
+  fetch_pair(row0, c0, p0a, p0b);
+  fetch_pair(row1, c0, p1a, p1b);
+  fetch_pair(row0, c1, q0a, q0b);
+  fetch_pair(row1, c1, q1a, q1b);
+  store_pair<TOut>(o, pixel_value<0, false>(p0a, p0b, p1a, p1b, c0, h0, h1, g),
+                   pixel_value<0, C1_EDGE>(q0a, q0b, q1a, q1b, c1, h0, h1, g));
+  store_pair<TOut>(o + plane, pixel_value<1, false>(p0a, p0b, p1a, p1b, c0, h0, h1, g),
+                   pixel_value<1, C1_EDGE>(q0a, q0b, q1a, q1b, c1, h0, h1, g));
+  store_pair<TOut>(o + 2 * plane, pixel_value<2, false>(p0a, p0b, p1a, p1b, c0, h0, h1, g),
+                   pixel_value<2, C1_EDGE>(q0a, q0b, q1a, q1b, c1, h0, h1, g));
+}
+
+constexpr int kMaxFastOH = 2048;
+
 template <typename TOut>
 __global__ void __launch_bounds__(kMaxThreads) preproc_u8c3_kernel(FastGeo g, const uint8_t *__restrict__ in,
                                                                    TOut *__restrict__ out, int n_units) {
@@ -293,10 +348,20 @@ __global__ void __launch_bounds__(kMaxThreads) preproc_u8c3_kernel(FastGeo g, co
   __shared__ __align__(8) uint64_t bars[kFastStages];
   const int stage_bytes = g.R * g.slot_bytes;
   const uint32_t copy_bytes = (uint32_t)(2 * g.row_bytes);
+  RowCoef *rows = reinterpret_cast<RowCoef *>(smem_raw + kFastStages * stage_bytes);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFastStages; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
+  }
+  for (int oy = threadIdx.x; oy < g.OH; oy += blockDim.x) {
+    const Coef cy = src_coef(oy, g.H, g.OH, g.sy);
+    RowCoef rc;
+    rc.ys = cy.i0 < g.H - 1 ? cy.i0 : g.H - 2;
+    rc.r01 = (cy.i0 - rc.ys) | ((cy.i1 - rc.ys) << 8);
+    rc.h0 = cy.l0;
+    rc.h1 = cy.l1;
+    rows[oy] = rc;
   }
   __syncthreads();
 
@@ -306,24 +371,17 @@ __global__ void __launch_bounds__(kMaxThreads) preproc_u8c3_kernel(FastGeo g, co
   const int ox = 2 * j;
   const ColWin c0 = make_win(src_coef(active ? ox : 0, g.W, g.OW, g.sx));
   const ColWin c1 = make_win(src_coef(active ? ox + 1 : 0, g.W, g.OW, g.sx));
+  const int64_t plane = (int64_t)g.OH * g.OW;
 
-  auto unit_rows = [&](int u, int &b, int &oy0) {
-    b = u / g.upi;
-    oy0 = (u - b * g.upi) * g.R;
-  };
-  auto row_start = [&](int oy) {  // first staged input row of output row oy
-    Coef cy = src_coef(oy, g.H, g.OH, g.sy);
-    return cy.i0 < g.H - 1 ? cy.i0 : g.H - 2;
-  };
   auto issue = [&](int k) {  // thread 0: stage unit #k of this block
     const int u = blockIdx.x + k * gridDim.x;
-    int b, oy0;
-    unit_rows(u, b, oy0);
+    const int b = u / g.upi;
+    const int oy0 = (u - b * g.upi) * g.R;
     const int nrows = min(g.R, g.OH - oy0);
     const int s = k % kFastStages;
     mbar_arrive_expect_tx(&bars[s], copy_bytes * nrows);
     for (int rr = 0; rr < nrows; ++rr) {
-      const uint8_t *src = in + ((int64_t)b * g.H + row_start(oy0 + rr)) * g.row_bytes;
+      const uint8_t *src = in + ((int64_t)b * g.H + rows[oy0 + rr].ys) * g.row_bytes;
       bulk_g2s(smem_raw + s * stage_bytes + rr * g.slot_bytes, src, copy_bytes, &bars[s]);
     }
   };
@@ -337,38 +395,20 @@ __global__ void __launch_bounds__(kMaxThreads) preproc_u8c3_kernel(FastGeo g, co
     const int s = k % kFastStages;
     const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)(k / kFastStages) & 1u, 120 + s);
     const int u = blockIdx.x + k * gridDim.x;
-    int b, oy0;
-    unit_rows(u, b, oy0);
-    const int oy = oy0 + r;
+    const int b = u / g.upi;
+    const int oy = (u - b * g.upi) * g.R + r;
     if (active && oy < g.OH) {
-      const Coef cy = src_coef(oy, g.H, g.OH, g.sy);
-      const int ys = cy.i0 < g.H - 1 ? cy.i0 : g.H - 2;
+      const RowCoef rc = rows[oy];
       const uint8_t *base = smem_raw + s * stage_bytes + r * g.slot_bytes;
-      const uint8_t *row0 = base + (cy.i0 - ys) * g.row_bytes;
-      const uint8_t *row1 = base + (cy.i1 - ys) * g.row_bytes;
-      uint32_t p00, p01, p10, p11, q00, q01, q10, q11;  // [col][row] pairs
-      fetch_pair(row0, c0, p00, p01);
-      fetch_pair(row1, c0, p10, p11);
-      fetch_pair(row0, c1, q00, q01);
-      fetch_pair(row1, c1, q10, q11);
-#pragma unroll
-      for (int c = 0; c < 3; ++c) {
-        float v[2];
-#pragma unroll
-        for (int col = 0; col < 2; ++col) {
-          const ColWin &w = col ? c1 : c0;
-          const uint32_t r0a = col ? q00 : p00, r0b = col ? q01 : p01;
-          const uint32_t r1a = col ? q10 : p10, r1b = col ? q11 : p11;
-          const float a = byte_to_f32(r0a, c), bb = pix(r0a, r0b, w.d + c);
-          const float cc = byte_to_f32(r1a, c), d = pix(r1a, r1b, w.d + c);
-          const float row0v = __fmaf_rn(a, w.l0, __fmul_rn(bb, w.l1));
-          const float row1v = __fmaf_rn(cc, w.l0, __fmul_rn(d, w.l1));
-          float t = __fmaf_rn(row0v, cy.l0, __fmul_rn(row1v, cy.l1));
-          if (g.normalize) t = div_rn(__fsub_rn(t, g.mean[c]), g.stdv[c], g.rcp[c]);
-          v[col] = t;
-        }
-        store_pair<TOut>(out + (((int64_t)b * 3 + c) * g.OH + oy) * g.OW + ox, v[0], v[1]);
-      }
+      const uint8_t *row0 = base + (rc.r01 & 0xff) * g.row_bytes;
+      const uint8_t *row1 = base + (rc.r01 >> 8) * g.row_bytes;
+      TOut *o = out + ((int64_t)b * 3 * g.OH + oy) * g.OW + ox;
+      // With in_w > out_w only the last output column can sit on the clamped
+      // right edge, so the first column of a pair never does.
+      if (!c1.edge)
+        compute_two_cols<TOut, false>(row0, row1, c0, c1, rc.h0, rc.h1, g, o, plane);
+      else
+        compute_two_cols<TOut, true>(row0, row1, c0, c1, rc.h0, rc.h1, g, o, plane);
     }
     if (!__syncthreads_and(ok)) break;
     if (threadIdx.x == 0 && k + kFastStages < my_units) issue(k + kFastStages);
@@ -403,10 +443,12 @@ int launch_fast(const dp_preproc_params &p, const void *in, void *out, cudaStrea
     g.rcp[c] = 1.0f / g.stdv[c];
   }
   const int threads = ((g.R * g.tpr + 31) / 32) * 32;
-  const size_t smem = (size_t)kFastStages * g.R * g.slot_bytes;
+  const size_t smem = (size_t)kFastStages * g.R * g.slot_bytes + (size_t)g.OH * sizeof(RowCoef);
   const int n_units = g.B * g.upi;
   auto kern = preproc_u8c3_kernel<TOut>;
   DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                     (int)cudaSharedmemCarveoutMaxShared));
   int per_sm = 0;
   DP_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem));
   if (per_sm < 1) per_sm = 1;
@@ -520,7 +562,7 @@ int launch_preproc(const dp_preproc_params &p, const void *in, void *out, cudaSt
   const bool fast = p.in_dtype == DP_U8 && !in_nchw && out_nchw && p.channels == 3 && p.in_w % 16 == 0 &&
                     p.out_w % 2 == 0 && p.in_h >= 2 && reinterpret_cast<uintptr_t>(in) % 16 == 0 &&
                     reinterpret_cast<uintptr_t>(out) % 8 == 0 && 2 * 3 * p.in_w + 16 <= 96 * 1024 &&
-                    p.out_w / 2 <= kMaxThreads;
+                    p.out_w / 2 <= kMaxThreads && p.out_h <= kMaxFastOH && p.in_w > p.out_w;
   if (fast) {
     switch (p.out_dtype) {
       case DP_BF16: return launch_fast<__nv_bfloat16>(p, in, out, s);
