@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(kMaxThreads) preproc_plain_kernel(Geo g, const
 //     t / std for these finite, normal operands;
 //   * two output columns are packed into one 32-bit (bf16/f16) or 64-bit
 //     (f32) store per channel.
-constexpr int kFastStages = 4;
+constexpr int kFastStages = 2;
 
 struct FastGeo {
   int B, H, W, OH, OW;
@@ -222,12 +222,6 @@ struct FastGeo {
   int normalize;
   float mean[3], stdv[3], rcp[3];
 };
-
-__device__ __forceinline__ float byte_to_f32(uint32_t word, int k) {
-  // k in 0..3: byte k of ``word`` as an exact float.
-  const uint32_t b = (word >> (8 * k)) & 0xffu;
-  return __int_as_float((int)(b | 0x4B000000u)) - 8388608.0f;
-}
 
 __device__ __forceinline__ float div_rn(float t, float d, float y) {
   const float q = __fmul_rn(t, y);
@@ -273,7 +267,7 @@ __device__ __forceinline__ void fetch_pair(const uint8_t *row, const ColWin &w, 
 // builds the bits of 2^23 + byte, one add removes 2^23.
 template <int SEL>
 __device__ __forceinline__ float bytef(uint32_t word) {
-  return __int_as_float((int)__byte_perm(word, 0x4B000000u, 0x7440u | SEL)) - 8388608.0f;
+  return __int_as_float((int)__byte_perm(word, 0x4B000000u, 0x7440u | (unsigned)SEL)) - 8388608.0f;
 }
 
 // Output value of one channel at one column: bilinear then normalise.
@@ -282,10 +276,10 @@ __device__ __forceinline__ float pixel_value(uint32_t r0a, uint32_t r0b, uint32_
                                              const ColWin &w, float h0, float h1, const FastGeo &g) {
   const float a = bytef<C>(r0a), cc = bytef<C>(r1a);
   float bb, d;
-  if (EDGE) {
+  if constexpr (EDGE) {
     bb = a;
     d = cc;
-  } else if (C == 0) {
+  } else if constexpr (C == 0) {
     bb = bytef<3>(r0a);
     d = bytef<3>(r1a);
   } else {
@@ -340,18 +334,33 @@ __device__ __forceinline__ void compute_two_cols(const uint8_t *row0, const uint
 }
 
 constexpr int kMaxFastOH = 2048;
+constexpr int kFastRowsPerThread = 4;  // output rows a thread computes per unit
 
+// Warp-specialised pipeline: warp 0 lane 0 is the producer (bulk copies into
+// kFastStages stages, each guarded by a "full" and an "empty" mbarrier);
+// warps 1.. are consumers, one column pair per lane, walking the R output
+// rows of each unit.  Consumers never wait for each other: a warp releases a
+// stage with one arrive on its "empty" barrier.  Every wait is bounded; a
+// timeout sets the device error word and a shared abort flag, after which
+// all warps stop and the producer waits (bounded) for the copies it issued.
 template <typename TOut>
-__global__ void __launch_bounds__(kMaxThreads) preproc_u8c3_kernel(FastGeo g, const uint8_t *__restrict__ in,
-                                                                   TOut *__restrict__ out, int n_units) {
+__global__ void __launch_bounds__(kMaxThreads + 32) preproc_u8c3_kernel(FastGeo g, const uint8_t *__restrict__ in,
+                                                                        TOut *__restrict__ out, int n_units) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[kFastStages];
+  __shared__ __align__(8) uint64_t full[kFastStages];
+  __shared__ __align__(8) uint64_t empty[kFastStages];
+  __shared__ int abort_flag;
   const int stage_bytes = g.R * g.slot_bytes;
   const uint32_t copy_bytes = (uint32_t)(2 * g.row_bytes);
   RowCoef *rows = reinterpret_cast<RowCoef *>(smem_raw + kFastStages * stage_bytes);
+  const int n_consumer_warps = (g.tpr + 31) / 32;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kFastStages; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < kFastStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], n_consumer_warps);
+    }
+    abort_flag = 0;
     fence_barrier_init();
   }
   for (int oy = threadIdx.x; oy < g.OH; oy += blockDim.x) {
@@ -365,59 +374,83 @@ __global__ void __launch_bounds__(kMaxThreads) preproc_u8c3_kernel(FastGeo g, co
   }
   __syncthreads();
 
-  const int r = threadIdx.x / g.tpr;
-  const int j = threadIdx.x - r * g.tpr;
-  const bool active = r < g.R;
+  const int my_units = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int issued = 0;
+      for (int k = 0; k < my_units; ++k) {
+        const int s = k % kFastStages;
+        if (k >= kFastStages &&
+            !mbar_wait_bounded(&empty[s], (uint32_t)((k / kFastStages) - 1) & 1u, 130 + s)) {
+          atomicExch(&abort_flag, 1);
+          break;
+        }
+        if (*(volatile int *)&abort_flag) break;
+        const int u = blockIdx.x + k * gridDim.x;
+        const int b = u / g.upi;
+        const int oy0 = (u - b * g.upi) * g.R;
+        const int nrows = min(g.R, g.OH - oy0);
+        mbar_arrive_expect_tx(&full[s], copy_bytes * nrows);
+        for (int rr = 0; rr < nrows; ++rr) {
+          const uint8_t *src = in + ((int64_t)b * g.H + rows[oy0 + rr].ys) * g.row_bytes;
+          bulk_g2s(smem_raw + s * stage_bytes + rr * g.slot_bytes, src, copy_bytes, &full[s]);
+        }
+        issued = k + 1;
+      }
+      if (*(volatile int *)&abort_flag) {
+        // Wait (bounded) for the copies of the last kFastStages issued units.
+        for (int k = issued - kFastStages < 0 ? 0 : issued - kFastStages; k < issued; ++k)
+          mbar_wait_bounded(&full[k % kFastStages], (uint32_t)(k / kFastStages) & 1u, 199, 100000000ull);
+      }
+    }
+    return;
+  }
+
+  // Consumers: one column pair per lane.
+  const int j = threadIdx.x - 32;
+  const bool active = j < g.tpr;
   const int ox = 2 * j;
   const ColWin c0 = make_win(src_coef(active ? ox : 0, g.W, g.OW, g.sx));
   const ColWin c1 = make_win(src_coef(active ? ox + 1 : 0, g.W, g.OW, g.sx));
   const int64_t plane = (int64_t)g.OH * g.OW;
-
-  auto issue = [&](int k) {  // thread 0: stage unit #k of this block
-    const int u = blockIdx.x + k * gridDim.x;
-    const int b = u / g.upi;
-    const int oy0 = (u - b * g.upi) * g.R;
-    const int nrows = min(g.R, g.OH - oy0);
+  // Running (image, unit-in-image) of unit blockIdx.x + k * gridDim.x.
+  const int step_b = (int)gridDim.x / g.upi, step_u = (int)gridDim.x - step_b * g.upi;
+  int cur_b = (int)blockIdx.x / g.upi, cur_u = (int)blockIdx.x - cur_b * g.upi;
+  for (int k = 0; k < my_units; ++k) {
     const int s = k % kFastStages;
-    mbar_arrive_expect_tx(&bars[s], copy_bytes * nrows);
-    for (int rr = 0; rr < nrows; ++rr) {
-      const uint8_t *src = in + ((int64_t)b * g.H + rows[oy0 + rr].ys) * g.row_bytes;
-      bulk_g2s(smem_raw + s * stage_bytes + rr * g.slot_bytes, src, copy_bytes, &bars[s]);
+    if (!mbar_wait_bounded(&full[s], (uint32_t)(k / kFastStages) & 1u, 120 + s)) atomicExch(&abort_flag, 1);
+    if (__any_sync(0xffffffffu, *(volatile int *)&abort_flag)) break;
+    const int oy0 = cur_u * g.R;
+    if (active) {
+      const int nrows = min(g.R, g.OH - oy0);
+      const uint8_t *stage = smem_raw + s * stage_bytes;
+      TOut *o = out + ((int64_t)cur_b * 3 * g.OH + oy0) * g.OW + ox;
+#pragma unroll 2
+      for (int rr = 0; rr < nrows; ++rr) {
+        const RowCoef rc = rows[oy0 + rr];
+        const uint8_t *base = stage + rr * g.slot_bytes;
+        const uint8_t *row0 = base + (rc.r01 & 0xff) * g.row_bytes;
+        const uint8_t *row1 = base + (rc.r01 >> 8) * g.row_bytes;
+        // With in_w > out_w only the last output column can sit on the
+        // clamped right edge, so the first column of a pair never does.
+        if (!c1.edge)
+          compute_two_cols<TOut, false>(row0, row1, c0, c1, rc.h0, rc.h1, g, o, plane);
+        else
+          compute_two_cols<TOut, true>(row0, row1, c0, c1, rc.h0, rc.h1, g, o, plane);
+        o += g.OW;
+      }
     }
-  };
-
-  const int my_units = (n_units - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
-  if (threadIdx.x == 0)
-    for (int k = 0; k < kFastStages && k < my_units; ++k) issue(k);
-
-  int k = 0;
-  for (; k < my_units; ++k) {
-    const int s = k % kFastStages;
-    const bool ok = mbar_wait_bounded(&bars[s], (uint32_t)(k / kFastStages) & 1u, 120 + s);
-    const int u = blockIdx.x + k * gridDim.x;
-    const int b = u / g.upi;
-    const int oy = (u - b * g.upi) * g.R + r;
-    if (active && oy < g.OH) {
-      const RowCoef rc = rows[oy];
-      const uint8_t *base = smem_raw + s * stage_bytes + r * g.slot_bytes;
-      const uint8_t *row0 = base + (rc.r01 & 0xff) * g.row_bytes;
-      const uint8_t *row1 = base + (rc.r01 >> 8) * g.row_bytes;
-      TOut *o = out + ((int64_t)b * 3 * g.OH + oy) * g.OW + ox;
-      // With in_w > out_w only the last output column can sit on the clamped
-      // right edge, so the first column of a pair never does.
-      if (!c1.edge)
-        compute_two_cols<TOut, false>(row0, row1, c0, c1, rc.h0, rc.h1, g, o, plane);
-      else
-        compute_two_cols<TOut, true>(row0, row1, c0, c1, rc.h0, rc.h1, g, o, plane);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+    cur_u += step_u;
+    cur_b += step_b;
+    if (cur_u >= g.upi) {
+      cur_u -= g.upi;
+      ++cur_b;
     }
-    if (!__syncthreads_and(ok)) break;
-    if (threadIdx.x == 0 && k + kFastStages < my_units) issue(k + kFastStages);
   }
-  if (k < my_units && threadIdx.x == 0) {
-    for (int jj = k; jj < my_units && jj < k + kFastStages; ++jj)
-      mbar_wait_bounded(&bars[jj % kFastStages], (uint32_t)(jj / kFastStages) & 1u, 199, 100000000ull);
-  }
-  __syncthreads();
 }
 
 template <typename TOut>
@@ -429,8 +462,7 @@ int launch_fast(const dp_preproc_params &p, const void *in, void *out, cudaStrea
   g.OH = p.out_h;
   g.OW = p.out_w;
   g.tpr = p.out_w / 2;
-  g.R = g.tpr >= kMaxThreads ? 1 : kMaxThreads / g.tpr;
-  if (g.R > g.OH) g.R = g.OH;
+  g.R = kFastRowsPerThread < g.OH ? kFastRowsPerThread : g.OH;
   g.upi = (g.OH + g.R - 1) / g.R;
   g.row_bytes = 3 * p.in_w;
   g.slot_bytes = ((2 * g.row_bytes + 16) + 15) / 16 * 16;
@@ -442,7 +474,7 @@ int launch_fast(const dp_preproc_params &p, const void *in, void *out, cudaStrea
     g.stdv[c] = p.normalize ? p.stdv[c] : 1.0f;
     g.rcp[c] = 1.0f / g.stdv[c];
   }
-  const int threads = ((g.R * g.tpr + 31) / 32) * 32;
+  const int threads = 32 + ((g.tpr + 31) / 32) * 32;
   const size_t smem = (size_t)kFastStages * g.R * g.slot_bytes + (size_t)g.OH * sizeof(RowCoef);
   const int n_units = g.B * g.upi;
   auto kern = preproc_u8c3_kernel<TOut>;
@@ -561,7 +593,7 @@ int launch_preproc(const dp_preproc_params &p, const void *in, void *out, cudaSt
   const bool out_nchw = p.out_layout == DP_LAYOUT_NCHW;
   const bool fast = p.in_dtype == DP_U8 && !in_nchw && out_nchw && p.channels == 3 && p.in_w % 16 == 0 &&
                     p.out_w % 2 == 0 && p.in_h >= 2 && reinterpret_cast<uintptr_t>(in) % 16 == 0 &&
-                    reinterpret_cast<uintptr_t>(out) % 8 == 0 && 2 * 3 * p.in_w + 16 <= 96 * 1024 &&
+                    reinterpret_cast<uintptr_t>(out) % 8 == 0 && 2 * 3 * p.in_w + 16 <= 12 * 1024 &&
                     p.out_w / 2 <= kMaxThreads && p.out_h <= kMaxFastOH && p.in_w > p.out_w;
   if (fast) {
     switch (p.out_dtype) {
