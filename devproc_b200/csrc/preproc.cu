@@ -223,11 +223,6 @@ struct FastGeo {
   float mean[3], stdv[3], rcp[3];
 };
 
-__device__ __forceinline__ float div_rn(float t, float d, float y) {
-  const float q = __fmul_rn(t, y);
-  const float r = __fmaf_rn(-q, d, t);
-  return __fmaf_rn(r, y, q);
-}
 
 // Window of one output column: the 8-byte aligned 16-byte span of the row
 // holding pixels x0 and x1, and how to shift it so that pixel x0 starts at
@@ -263,33 +258,57 @@ __device__ __forceinline__ void fetch_pair(const uint8_t *row, const ColWin &w, 
   a1 = __funnelshift_r(w1, w2, w.sh);
 }
 
-// Byte SEL (compile-time, 0..3) of ``word`` as an exact float: one byte permute
-// builds the bits of 2^23 + byte, one add removes 2^23.
+
+// Output values of one channel at the thread's two columns, computed as f32x2
+// pairs (sm_100 packed FMA/ADD/MUL; each lane rounds exactly like the scalar
+// instruction, so the arithmetic is the generic path's, two columns at once).
+// Bytes are turned into floats by building the bits of 2^23 + byte with one
+// byte permute and subtracting 2^23.
 template <int SEL>
-__device__ __forceinline__ float bytef(uint32_t word) {
-  return __int_as_float((int)__byte_perm(word, 0x4B000000u, 0x7440u | (unsigned)SEL)) - 8388608.0f;
+__device__ __forceinline__ float magic_bits(uint32_t word) {
+  return __int_as_float((int)__byte_perm(word, 0x4B000000u, 0x7440u | (unsigned)SEL));
 }
 
-// Output value of one channel at one column: bilinear then normalise.
 template <int C, bool EDGE>
-__device__ __forceinline__ float pixel_value(uint32_t r0a, uint32_t r0b, uint32_t r1a, uint32_t r1b,
-                                             const ColWin &w, float h0, float h1, const FastGeo &g) {
-  const float a = bytef<C>(r0a), cc = bytef<C>(r1a);
-  float bb, d;
-  if constexpr (EDGE) {
-    bb = a;
-    d = cc;
-  } else if constexpr (C == 0) {
-    bb = bytef<3>(r0a);
-    d = bytef<3>(r1a);
+__device__ __forceinline__ float2 pair_value(uint32_t p0a, uint32_t p0b, uint32_t p1a, uint32_t p1b,  // col 0
+                                             uint32_t q0a, uint32_t q0b, uint32_t q1a, uint32_t q1b,  // col 1
+                                             float2 L0, float2 L1, float2 H0, float2 H1, const FastGeo &g) {
+  const float2 m23 = make_float2(-8388608.0f, -8388608.0f);
+  // pixel x0 of both columns, rows 0 and 1
+  const float2 A = __fadd2_rn(make_float2(magic_bits<C>(p0a), magic_bits<C>(q0a)), m23);
+  const float2 Cc = __fadd2_rn(make_float2(magic_bits<C>(p1a), magic_bits<C>(q1a)), m23);
+  // pixel x1: byte C+3 of the pair window (column 1 repeats x0 at the right edge)
+  float b0, b1, d0, d1;
+  if constexpr (C == 0) {
+    b0 = magic_bits<3>(p0a);
+    d0 = magic_bits<3>(p1a);
   } else {
-    bb = bytef<C - 1>(r0b);
-    d = bytef<C - 1>(r1b);
+    b0 = magic_bits<C - 1>(p0b);
+    d0 = magic_bits<C - 1>(p1b);
   }
-  const float row0v = __fmaf_rn(a, w.l0, __fmul_rn(bb, w.l1));
-  const float row1v = __fmaf_rn(cc, w.l0, __fmul_rn(d, w.l1));
-  float t = __fmaf_rn(row0v, h0, __fmul_rn(row1v, h1));
-  if (g.normalize) t = div_rn(__fsub_rn(t, g.mean[C]), g.stdv[C], g.rcp[C]);
+  if constexpr (EDGE) {
+    b1 = magic_bits<C>(q0a);
+    d1 = magic_bits<C>(q1a);
+  } else if constexpr (C == 0) {
+    b1 = magic_bits<3>(q0a);
+    d1 = magic_bits<3>(q1a);
+  } else {
+    b1 = magic_bits<C - 1>(q0b);
+    d1 = magic_bits<C - 1>(q1b);
+  }
+  const float2 B = __fadd2_rn(make_float2(b0, b1), m23);
+  const float2 D = __fadd2_rn(make_float2(d0, d1), m23);
+  const float2 row0 = __ffma2_rn(A, L0, __fmul2_rn(B, L1));
+  const float2 row1 = __ffma2_rn(Cc, L0, __fmul2_rn(D, L1));
+  float2 t = __ffma2_rn(row0, H0, __fmul2_rn(row1, H1));
+  if (g.normalize) {
+    // (t - mean) / std, correctly rounded (Markstein): q = t·y, r = t - q·std, q + r·y.
+    t = __fadd2_rn(t, make_float2(-g.mean[C], -g.mean[C]));
+    const float2 y = make_float2(g.rcp[C], g.rcp[C]);
+    const float2 q = __fmul2_rn(t, y);
+    const float2 r = __ffma2_rn(q, make_float2(-g.stdv[C], -g.stdv[C]), t);
+    t = __ffma2_rn(r, y, q);
+  }
   return t;
 }
 
@@ -325,12 +344,14 @@ __device__ __forceinline__ void compute_two_cols(const uint8_t *row0, const uint
   fetch_pair(row1, c0, p1a, p1b);
   fetch_pair(row0, c1, q0a, q0b);
   fetch_pair(row1, c1, q1a, q1b);
-  store_pair<TOut>(o, pixel_value<0, false>(p0a, p0b, p1a, p1b, c0, h0, h1, g),
-                   pixel_value<0, C1_EDGE>(q0a, q0b, q1a, q1b, c1, h0, h1, g));
-  store_pair<TOut>(o + plane, pixel_value<1, false>(p0a, p0b, p1a, p1b, c0, h0, h1, g),
-                   pixel_value<1, C1_EDGE>(q0a, q0b, q1a, q1b, c1, h0, h1, g));
-  store_pair<TOut>(o + 2 * plane, pixel_value<2, false>(p0a, p0b, p1a, p1b, c0, h0, h1, g),
-                   pixel_value<2, C1_EDGE>(q0a, q0b, q1a, q1b, c1, h0, h1, g));
+  const float2 L0 = make_float2(c0.l0, c1.l0), L1 = make_float2(c0.l1, c1.l1);
+  const float2 H0 = make_float2(h0, h0), H1 = make_float2(h1, h1);
+  float2 v = pair_value<0, C1_EDGE>(p0a, p0b, p1a, p1b, q0a, q0b, q1a, q1b, L0, L1, H0, H1, g);
+  store_pair<TOut>(o, v.x, v.y);
+  v = pair_value<1, C1_EDGE>(p0a, p0b, p1a, p1b, q0a, q0b, q1a, q1b, L0, L1, H0, H1, g);
+  store_pair<TOut>(o + plane, v.x, v.y);
+  v = pair_value<2, C1_EDGE>(p0a, p0b, p1a, p1b, q0a, q0b, q1a, q1b, L0, L1, H0, H1, g);
+  store_pair<TOut>(o + 2 * plane, v.x, v.y);
 }
 
 constexpr int kMaxFastOH = 2048;
