@@ -147,20 +147,23 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
   return t;
 }
 
-// Bounded wait: gives up once ``timeout_ns`` of wall time has passed
-// (%globaltimer), records DP_DEVERR_TIMEOUT with ``site`` and returns false.
-// No wait in this library can spin forever.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, int site,
-                                                  uint64_t timeout_ns = 2000000000ull) {
+// Waits at most ``timeout_ns`` of wall time (%globaltimer); false on timeout.
+__device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t phase, uint64_t timeout_ns) {
   if (mbar_try_wait(bar, phase)) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, phase)) {
-    if (globaltimer_ns() - t0 > timeout_ns) {
-      dp_report(DP_DEVERR_TIMEOUT, site);
-      return false;
-    }
-  }
+  while (!mbar_try_wait(bar, phase))
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
   return true;
+}
+
+// Bounded wait: gives up once ``timeout_ns`` of wall time has passed,
+// records DP_DEVERR_TIMEOUT with ``site`` and returns false.  No wait in
+// this library can spin forever.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, int site,
+                                                  uint64_t timeout_ns = 2000000000ull) {
+  if (mbar_wait_for(bar, phase, timeout_ns)) return true;
+  dp_report(DP_DEVERR_TIMEOUT, site);
+  return false;
 }
 
 // 1-D bulk copy global → shared (TMA engine), completion on ``bar``.

@@ -1,10 +1,335 @@
-// tcgen05 GEMM (placeholder until the tensor-core kernel lands): routes to
-// the FFMA kernel so bf16 graphs run end to end.
+// bf16 GEMM on the 5th-generation tensor cores: tcgen05.mma with the fp32
+// accumulator in tensor memory (TMEM), operands staged by TMA.
+//
+// Replaces the reference's Triton matmul_kernel / linear_kernel
+// (src/devproc/backend/triton/templates/matmul.py:24-224) for bf16 operands.
+//
+// C[b] = epilogue(A[b] · B[b]ᵀ); A [M, K] row-major, B [N, K] row-major (both
+// K-major, the nn.Linear layout), fp32 accumulation.
+//
+// Persistent kernel, one CTA per SM, 256 threads in four roles:
+//   warp 0  TMA producer: 128×64 A tile + 256×64 B tile per stage (128-byte
+//           swizzle), kStages stages guarded by full/empty mbarriers;
+//   warp 1  MMA issuer (one thread): 4 × tcgen05.mma (M=128, N=256, K=16) per
+//           stage into one of two TMEM accumulators, tcgen05.commit frees the
+//           stage and, after the last K block, hands the accumulator over;
+//   warp 2  allocates / frees the 512 TMEM columns (2 × 256 fp32 accumulators);
+//   warps 4-7 epilogue: tcgen05.ld 32 columns at a time (each thread owns one
+//           accumulator row), bias → activation → residual → cast, store, then
+//           release the accumulator so the next tile's MMAs overlap this one.
+// Tiles are visited in GROUP_M-row bands for L2 reuse of B.
+//
+// Every mbarrier wait is bounded (%globaltimer); on a timeout the kernel
+// records DP_DEVERR_TIMEOUT, all roles stop, the CTA lets in-flight copies and
+// MMAs drain for a bounded time, frees its TMEM and returns.
+#include <cuda.h>
+
 #include "dp_gemm_epilogue.cuh"
 
-namespace dp {
-int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias,
-                   const void *res, cudaStream_t s) {
-  return launch_gemm_simt(p, A, B, C, bias, res, s);
+namespace dpk_tcgemm {
+
+constexpr int BM = 128, BN = 256, BK = 64;
+constexpr int kStages = 4;
+constexpr int kThreads = 256;
+constexpr int kGroupM = 8;
+constexpr uint32_t kTileABytes = BM * BK * 2;  // 16 KB
+constexpr uint32_t kTileBBytes = BN * BK * 2;  // 32 KB
+constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
+constexpr int kTmemCols = 512;                 // two 256-column fp32 accumulators
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024;  // + alignment slack
+
+struct Shape {
+  int M, N, K, batch;
+  int tiles_m, tiles_n, tiles_per_batch, num_tiles, k_blocks;
+};
+
+// ------------------------------------------------------------------ PTX
+__device__ __forceinline__ void tma_load_3d(void *smem, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(smem)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
 }
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes, 8-row groups 1024 bytes apart (SBO), version 1 (sm_100).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;                    // LBO (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;          // SBO
+  d |= (uint64_t)1 << 46;                    // version
+  d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, both K-major.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tile_coords(const Shape &s, int t, int &b, int &tm, int &tn) {
+  b = t / s.tiles_per_batch;
+  const int r = t - b * s.tiles_per_batch;
+  const int band = kGroupM * s.tiles_n;
+  const int g = r / band;
+  const int first_m = g * kGroupM;
+  const int gsize = min(kGroupM, s.tiles_m - first_m);
+  const int in_band = r - g * band;
+  tm = first_m + in_band % gsize;
+  tn = in_band / gsize;
+}
+
+__device__ __forceinline__ bool aborted(volatile int *flag) { return *flag != 0; }
+
+// Waits in 0.2 s slices, re-reading the CTA's abort flag between slices, for
+// at most 2 s in total; on giving up records DP_DEVERR_TIMEOUT and raises the
+// abort flag so that the other roles stop too.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, int site, volatile int *flag) {
+  for (int slice = 0; slice < 10; ++slice) {
+    if (aborted(flag)) return false;
+    if (mbar_wait_for(bar, parity, 200000000ull)) return true;
+  }
+  dp_report(DP_DEVERR_TIMEOUT, site);
+  *flag = 1;
+  return false;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   dp_gemm_params p, Shape s, void *C, const void *bias, const void *res) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ int abort_flag;
+
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_map(&map_a);
+    prefetch_map(&map_b);
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_slot;
+  volatile int *flag = &abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int it = 0;
+      for (int t = blockIdx.x; t < s.num_tiles && !aborted(flag); t += gridDim.x) {
+        int b, tm, tn;
+        tile_coords(s, t, b, tm, tn);
+        for (int kb = 0; kb < s.k_blocks; ++kb, ++it) {
+          const int st = it % kStages;
+          if (!wait_or_abort(&empty[st], ((it / kStages) & 1) ^ 1, 300 + st, flag)) break;
+          uint8_t *sa = smem + st * kStageBytes;
+          uint8_t *sb = sa + kTileABytes;
+          mbar_arrive_expect_tx(&full[st], kStageBytes);
+          tma_load_3d(sa, &map_a, kb * BK, tm * BM, b, &full[st]);
+          tma_load_3d(sb, &map_b, kb * BK, tn * BN, b, &full[st]);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      const uint32_t idesc = instr_desc(BM, BN);
+      int it = 0, local = 0;
+      for (int t = blockIdx.x; t < s.num_tiles && !aborted(flag); t += gridDim.x, ++local) {
+        const int a = local & 1;
+        if (!wait_or_abort(&acc_empty[a], ((local >> 1) & 1) ^ 1, 310 + a, flag)) break;
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + (uint32_t)(a * BN);
+        bool ok = true;
+        for (int kb = 0; kb < s.k_blocks; ++kb, ++it) {
+          const int st = it % kStages;
+          if (!wait_or_abort(&full[st], (it / kStages) & 1, 320 + st, flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + st * kStageBytes);
+          const uint32_t sb = sa + kTileABytes;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16(tmem_d, smem_desc(sa + k * 32), smem_desc(sb + k * 32), idesc, (kb | k) != 0);
+          mma_commit(&empty[st]);  // stage is free once these MMAs have read it
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[a]);  // accumulator complete
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- epilogue: thread owns accumulator row (warp-4)*32 + lane
+    const int q = warp - 4;
+    const int row = q * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
+      const int a = local & 1;
+      // tcgen05.ld is warp-collective: the whole warp continues or stops together.
+      const bool got = wait_or_abort(&acc_full[a], (local >> 1) & 1, 330 + a, flag);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      int b, tm, tn;
+      tile_coords(s, t, b, tm, tn);
+      const int64_t m = (int64_t)tm * BM + row;
+      dp::Epilogue ep(p, C, bias, res, b);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tbase + c * 32, r);
+        const int64_t n0 = (int64_t)tn * BN + c * 32;
+        if (m < s.M && n0 < s.N) {
+#pragma unroll
+          for (int j = 0; j < 32; j += 4)
+            ep.store4(m, n0 + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                      __uint_as_float(r[j + 3]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[a]);
+    }
+  }
+
+  __syncthreads();
+  if (aborted(flag) && threadIdx.x == 0) {
+    // Let in-flight TMA copies and MMAs finish (bounded) before TMEM and
+    // shared memory go away.
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 2000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ host
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// rows × K bf16 operand (row stride ld elements), batch planes ``bstride`` apart.
+int make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t K, int64_t ld, int64_t batch,
+             int64_t bstride, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  DP_REQUIRE(fn != nullptr, DP_ERR_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)((batch > 1 ? bstride : rows * ld) * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  DP_REQUIRE(r == CUDA_SUCCESS, DP_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return DP_OK;
+}
+
+}  // namespace dpk_tcgemm
+
+namespace dp {
+
+int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias,
+                   const void *res, cudaStream_t stream) {
+  using namespace dpk_tcgemm;
+  CUtensorMap ma, mb;
+  int st = make_map(&ma, A, p.M, p.K, p.lda, p.batch, p.stride_a, BM);
+  if (st != DP_OK) return st;
+  st = make_map(&mb, B, p.N, p.K, p.ldb, p.batch, p.stride_b, BN);
+  if (st != DP_OK) return st;
+  Shape s;
+  s.M = (int)p.M;
+  s.N = (int)p.N;
+  s.K = (int)p.K;
+  s.batch = (int)p.batch;
+  s.tiles_m = (int)((p.M + BM - 1) / BM);
+  s.tiles_n = (int)((p.N + BN - 1) / BN);
+  s.tiles_per_batch = s.tiles_m * s.tiles_n;
+  s.num_tiles = s.tiles_per_batch * s.batch;
+  s.k_blocks = (int)((p.K + BK - 1) / BK);
+  DP_REQUIRE(p.N < (1ll << 31) && p.K < (1ll << 31), DP_ERR_UNSUPPORTED, "gemm: N or K too large");
+  static bool attr_set = false;
+  if (!attr_set) {
+    DP_CHECK_CUDA(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    attr_set = true;
+  }
+  int grid = num_sms();
+  if (grid > s.num_tiles) grid = s.num_tiles;
+  tc_gemm_kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, p, s, C, bias, res);
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
 }  // namespace dp

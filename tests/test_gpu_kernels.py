@@ -337,6 +337,47 @@ def test_gemm_bf16(cuda, M, Nn, K):
     assert torch.allclose(got, ref, rtol=2e-2, atol=2e-2 * K ** 0.5 / 8)
 
 
+def _bf16_gemm(cuda, M, Nn, K, epi=0, c_dtype=torch.float32, batch=1, bias=None, res=None, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    a = torch.randn(batch, M, K, generator=g).bfloat16()
+    w = torch.randn(batch, Nn, K, generator=g).bfloat16()
+    c = torch.empty(batch, M, Nn, dtype=c_dtype, device=cuda)
+    p = N.GemmParams()
+    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, Nn, K, K, K, Nn, batch
+    p.stride_a, p.stride_b, p.stride_c = M * K, Nn * K, M * Nn
+    p.a_dtype = p.b_dtype = N.DP_BF16
+    p.c_dtype = _dt(c)
+    p.b_layout = N.DP_B_NK
+    p.epilogue = epi
+    if bias is not None:
+        p.bias_dtype = _dt(bias)
+    if res is not None:
+        p.r_dtype, p.ldr, p.stride_r = _dt(res), Nn, M * Nn
+    N.gemm(p, a.to(cuda), w.to(cuda), c, bias=None if bias is None else bias.to(cuda),
+           residual=None if res is None else res.to(cuda))
+    _sync()
+    return a, w, c.cpu()
+
+
+@pytest.mark.parametrize("M,Nn,K", [(128, 256, 64), (256, 512, 1024), (37, 300, 72), (1, 10, 256), (300, 1000, 1152)])
+def test_gemm_bf16_tensor_core_shapes(cuda, M, Nn, K):
+    a, w, c = _bf16_gemm(cuda, M, Nn, K, seed=M + Nn)
+    ref = a.float() @ w.float().transpose(-1, -2)
+    assert torch.allclose(c, ref, rtol=1e-3, atol=1e-3 * K ** 0.5)
+
+
+def test_gemm_bf16_epilogues_and_batch(cuda):
+    g = torch.Generator().manual_seed(9)
+    M, Nn, K = 200, 384, 256
+    bias = torch.randn(Nn, generator=g).bfloat16()
+    res = torch.randn(2, M, Nn, generator=g).bfloat16()
+    a, w, c = _bf16_gemm(cuda, M, Nn, K, epi=N.DP_EPI_BIAS | N.DP_EPI_GELU_TANH | N.DP_EPI_RESIDUAL,
+                         c_dtype=torch.bfloat16, batch=2, bias=bias, res=res, seed=3)
+    acc = a.float() @ w.float().transpose(-1, -2) + bias.float()
+    ref = torch.nn.functional.gelu(acc, approximate="tanh") + res.float()
+    assert torch.allclose(c.float(), ref, rtol=2e-2, atol=2e-2)
+
+
 # ---------------------------------------------------------------- embedding
 def test_embedding_exact_and_index_error(cuda):
     g = torch.Generator().manual_seed(4)
