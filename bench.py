@@ -49,11 +49,17 @@ def parse():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--cpu-sample", type=int, default=64, help="images in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=["preprocess", "gemm", "reduce", "token"], default="preprocess",
+                    help="preprocess = the headline pipeline; gemm / reduce / token = template microbenches "
+                         "and the fp32 token pipeline")
     return ap.parse_args()
 
 
 def dist_env():
     return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+FALLBACK_BF16_TFLOPS = 1590.0
 
 
 def peaks():
@@ -62,6 +68,106 @@ def peaks():
         d = json.loads(p.read_text())
         return float(d["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def tensor_peak():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), "measured (burst)"
+    return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def time_region(fn, steps, warmup, stream):
+    """Average ms per call of ``fn`` over ``steps`` calls, CUDA events on ``stream``."""
+    for _ in range(max(warmup, 3)):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def micro_gemm(args, dev):
+    """bf16 × bf16 → bf16 GEMM, fp32 accumulate, B as [N, K] (tcgen05 kernel)."""
+    from devproc_b200 import _native as N
+    peak, kind = tensor_peak()
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    for (M, Nn, K) in [(4096, 4096, 4096), (8192, 2048, 16384)]:
+        g = torch.Generator(device=dev).manual_seed(0)
+        a = torch.randn(M, K, device=dev, generator=g).bfloat16()
+        b = torch.randn(Nn, K, device=dev, generator=g).bfloat16()
+        c = torch.empty(M, Nn, device=dev, dtype=torch.bfloat16)
+        p = N.GemmParams()
+        p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, Nn, K, K, K, Nn, 1
+        p.a_dtype = p.b_dtype = p.c_dtype = N.DP_BF16
+        p.b_layout = N.DP_B_NK
+        sp = stream.cuda_stream
+        ms = time_region(lambda: N.gemm(p, a, b, c, stream=sp), min(args.steps, 200), args.warmup, stream)
+        tf = 2.0 * M * Nn * K / (ms / 1e3) / 1e12
+        out[f"{M}x{Nn}x{K}"] = {"ms": ms, "tflops": tf, "frac": tf / peak}
+    best = max(out.values(), key=lambda v: v["tflops"])
+    return {"metric": "bf16 GEMM TFLOP/s (fp32 accumulate)", "value": out["4096x4096x4096"]["tflops"],
+            "unit": "TFLOP/s", "higher_is_better": True, "dtype": "bf16", "shapes": out,
+            "roofline": {"bound": "tensor", "achieved": best["tflops"], "peak": peak, "unit": "TFLOP/s",
+                         "frac": best["tflops"] / peak, "peak_kind": kind, "kernel": "tc_gemm_kernel"},
+            "config": {"workload": "GEMM 4096^3 and 8192x2048x16384, inputs N(0,1)"}}
+
+
+def micro_reduce(args, dev):
+    """Row reductions over fp32 [65536, 4096]."""
+    from devproc_b200 import _native as N
+    peak, kind = peaks()
+    rows, cols = 65536, 4096
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = torch.randn(rows, cols, device=dev, generator=g)
+    ones = torch.ones(cols, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    sp = stream.cuda_stream
+    res = {}
+    for name, kind_c, odt, nbytes in [("sum", N.DP_RED_SUM, torch.float32, rows * cols * 4 + rows * 4),
+                                      ("max", N.DP_RED_MAX, torch.float32, rows * cols * 4 + rows * 4),
+                                      ("argmax", N.DP_RED_ARGMAX, torch.int64, rows * cols * 4 + rows * 8),
+                                      ("softmax", N.DP_RED_SOFTMAX, torch.float32, 2 * rows * cols * 4),
+                                      ("rmsnorm", N.DP_RED_RMSNORM, torch.float32, 2 * rows * cols * 4)]:
+        full = kind_c in (N.DP_RED_SOFTMAX, N.DP_RED_RMSNORM)
+        out = torch.empty((rows, cols) if full else (rows,), device=dev, dtype=odt)
+        p = N.RowReduceParams(kind_c, N.DP_F32, N.DTYPE_CODE[str(odt).replace("torch.", "")],
+                              1 if kind_c == N.DP_RED_RMSNORM else 0, 0, 0, rows, cols, cols, cols if full else 1,
+                              1e-6, 0.0)
+        w = ones if kind_c == N.DP_RED_RMSNORM else None
+        ms = time_region(lambda: N.rowreduce(p, x, out, weight=w, stream=sp), min(args.steps, 200), args.warmup,
+                         stream)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        res[name] = {"ms": ms, "gbs": gbs, "frac": gbs / peak}
+    worst = min(v["frac"] for v in res.values())
+    return {"metric": "row reduction HBM GB/s, fp32 [65536, 4096]", "value": res["sum"]["gbs"], "unit": "GB/s",
+            "higher_is_better": True, "dtype": "f32", "kinds": res,
+            "roofline": {"bound": "hbm", "achieved": res["softmax"]["gbs"], "peak": peak, "unit": "GB/s",
+                         "frac": res["softmax"]["gbs"] / peak, "peak_kind": kind, "worst_frac": worst},
+            "config": {"workload": "rowreduce fp32 65536x4096 (inputs 1 GiB > L2)"}}
+
+
+def micro_token(args, dev):
+    """The fp32 token pipeline, compiled from the torch module through the FX frontend."""
+    import devproc
+    from devproc_b200 import workloads
+    m = workloads.TokenPipeline().eval()
+    ids = workloads.token_ids()
+    prog = devproc.compile(m, ids)
+    d_ids = ids.to(dev)
+    stream = torch.cuda.current_stream(dev)
+    ms = time_region(lambda: prog.run(d_ids, to_cpu=False), min(args.steps, 500), args.warmup, stream)
+    flops = 2 * 8 * 128 * (512 * 2048 * 2 + 512 * 32000)
+    return {"metric": "pipeline samples/sec (fp32 token pipeline)", "value": 8 / (ms / 1e3), "unit": "samples/s",
+            "higher_is_better": True, "dtype": "f32", "ms_per_step": ms, "tflops": flops / (ms / 1e3) / 1e12,
+            "launches_per_step": len(prog.spec.records), "kernels": [r["label"] for r in prog.spec.records],
+            "config": {"workload": "token pipeline B=8 L=128 fp32 (Embedding 32000x512 .. argmax int32)"}}
 
 
 def ncu_traffic():
@@ -189,6 +295,17 @@ def main():
 
     import devproc
     from devproc_b200 import workloads
+
+    if args.workload != "preprocess":
+        fn = {"gemm": micro_gemm, "reduce": micro_reduce, "token": micro_token}[args.workload]
+        line = fn(args, dev)
+        line.update({"n_gpus": world, "data": "synthetic"})
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
 
     B = args.batch
     images_host = workloads.preprocess_images(B, seed=rank)

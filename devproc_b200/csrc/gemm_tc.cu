@@ -23,6 +23,7 @@
 // records DP_DEVERR_TIMEOUT, all roles stop, the CTA lets in-flight copies and
 // MMAs drain for a bounded time, frees its TMEM and returns.
 #include <cuda.h>
+#include <cstring>
 
 #include "dp_gemm_epilogue.cuh"
 
@@ -36,11 +37,16 @@ constexpr uint32_t kTileABytes = BM * BK * 2;  // 16 KB
 constexpr uint32_t kTileBBytes = BN * BK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kTmemCols = 512;                 // two 256-column fp32 accumulators
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + 1024;  // + alignment slack
+constexpr uint32_t kEpiBufBytes = 32 * 128;     // one 32-row x 128-byte output chunk
+constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBufBytes;  // 4 epilogue warps, double-buffered
+constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kEpiBytes + 1024;  // + alignment slack
 
 struct Shape {
   int M, N, K, batch;
   int tiles_m, tiles_n, tiles_per_batch, num_tiles, k_blocks;
+  int tma_store;     // output written by TMA tensor stores from swizzled chunks
+  int tma_residual;  // residual read by TMA into the same chunks (same dtype as C)
+  int c_bytes;       // element size of C
 };
 
 // ------------------------------------------------------------------ PTX
@@ -51,6 +57,19 @@ __device__ __forceinline__ void tma_load_3d(void *smem, const CUtensorMap *map, 
       "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
       : "memory");
 }
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *smem, int x, int y, int z) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(map),
+               "r"(x), "r"(y), "r"(z), "r"(smem_u32(smem))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled box (rows of 128 B).
+__device__ __forceinline__ uint32_t swz(int r, int j) { return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)); }
 
 __device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -103,6 +122,66 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Epilogue math on 16 consecutive columns n..n+15 of one row (columns past N
+// get bias 0; they are never stored).  One activation switch per call keeps
+// the code small enough for the instruction cache.
+__device__ __forceinline__ void epi16(float (&x)[16], int64_t n, int N, int epi, const void *bias, int bias_dt) {
+  if (epi & DP_EPI_BIAS) {
+    if (bias_dt == DP_BF16 && n + 16 <= N && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 && (n & 7) == 0) {
+      const uint4 *bp = reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(bias) + n);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint4 raw = __ldg(bp + h);
+        const __nv_bfloat162 *b2 = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(b2[e]);
+          x[8 * h + 2 * e] += f.x;
+          x[8 * h + 2 * e + 1] += f.y;
+        }
+      }
+    } else if (bias_dt == DP_F32 && n + 16 <= N && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 && (n & 3) == 0) {
+      const float4 *bp = reinterpret_cast<const float4 *>(static_cast<const float *>(bias) + n);
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float4 f = __ldg(bp + h);
+        x[4 * h] += f.x;
+        x[4 * h + 1] += f.y;
+        x[4 * h + 2] += f.z;
+        x[4 * h + 3] += f.w;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (n + e < N) x[e] += load_as_f32(bias, n + e, bias_dt);
+    }
+  }
+  const int act = epi & (DP_EPI_RELU | DP_EPI_GELU_ERF | DP_EPI_GELU_TANH | DP_EPI_SILU);
+  if (act == DP_EPI_RELU) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) x[e] = x[e] > 0.0f ? x[e] : (isnan(x[e]) ? x[e] : 0.0f);
+  } else if (act == DP_EPI_GELU_ERF) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) x[e] = dp::act_gelu_erf(x[e]);
+  } else if (act == DP_EPI_GELU_TANH) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) x[e] = dp::act_gelu_tanh(x[e]);
+  } else if (act == DP_EPI_SILU) {
+#pragma unroll
+    for (int e = 0; e < 16; ++e) x[e] = x[e] / (1.0f + expf(-x[e]));
+  }
+}
+
 __device__ __forceinline__ void tile_coords(const Shape &s, int t, int &b, int &tm, int &tn) {
   b = t / s.tiles_per_batch;
   const int r = t - b * s.tiles_per_batch;
@@ -130,11 +209,13 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, in
   return false;
 }
 
+template <int CB>  // bytes per element of C (4: fp32, 2: bf16 / f16)
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                   const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_r,
                    dp_gemm_params p, Shape s, void *C, const void *bias, const void *res) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2];
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], res_bar[4];
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
 
@@ -150,6 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 128);
     }
+    for (int i = 0; i < 4; ++i) mbar_init(&res_bar[i], 1);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -220,6 +302,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue: thread owns accumulator row (warp-4)*32 + lane
     const int q = warp - 4;
     const int row = q * 32 + lane;
+    uint8_t *ebuf = smem + kStages * kStageBytes + q * 2 * kEpiBufBytes;
+    constexpr int chunk_cols = 128 / CB;  // 32 fp32 or 64 bf16/f16 columns
+    uint32_t res_phase = 0;
     int local = 0;
     for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
       const int a = local & 1;
@@ -232,21 +317,123 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t m = (int64_t)tm * BM + row;
       dp::Epilogue ep(p, C, bias, res, b);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+      if (s.tma_store) {
+        bool stop = false;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tbase + c * 32, r);
-        const int64_t n0 = (int64_t)tn * BN + c * 32;
-        if (m < s.M && n0 < s.N) {
+        for (int c = 0; c < BN / chunk_cols; ++c) {
+          const int64_t n0 = (int64_t)tn * BN + c * chunk_cols;
+          if (n0 >= s.N) break;
+          uint8_t *buf = ebuf + (c & 1) * kEpiBufBytes;
+          if (lane == 0) bulk_wait_read1();  // the store that last read ``buf`` is done with it
+          __syncwarp();
+          if (s.tma_residual) {
+            if (lane == 0) {
+              mbar_arrive_expect_tx(&res_bar[q], kEpiBufBytes);
+              tma_load_3d(buf, &map_r, (int)n0, tm * BM + q * 32, b, &res_bar[q]);
+            }
+            const bool ok = wait_or_abort(&res_bar[q], res_phase, 340 + q, flag);
+            res_phase ^= 1u;
+            if (!__all_sync(0xffffffffu, ok)) {
+              stop = true;
+              break;
+            }
+          }
+#pragma unroll 1
+          for (int step = 0; step < chunk_cols / 16; ++step) {
+            uint32_t r[16];
+            tmem_ld16(tbase + c * chunk_cols + step * 16, r);
+            float x[16];
 #pragma unroll
-          for (int j = 0; j < 32; j += 4)
-            ep.store4(m, n0 + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                      __uint_as_float(r[j + 3]));
+            for (int e = 0; e < 16; ++e) x[e] = __uint_as_float(r[e]);
+            const int64_t nb = n0 + step * 16;
+            if (p.epilogue) epi16(x, nb, s.N, p.epilogue, bias, p.bias_dtype);
+            if ((p.epilogue & DP_EPI_RESIDUAL) && !s.tma_residual) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                if (m < s.M && nb + e < s.N) x[e] += load_as_f32(res, ep.r_off + m * p.ldr + nb + e, p.r_dtype);
+            }
+            // This step's 16 columns are 16-byte chunks step*2.. (16-bit C) or step*4.. (fp32 C).
+            if constexpr (CB == 4) {
+#pragma unroll
+              for (int h = 0; h < 4; ++h) {
+                float4 *slot = reinterpret_cast<float4 *>(buf + swz(lane, step * 4 + h));
+                float4 f = make_float4(x[4 * h], x[4 * h + 1], x[4 * h + 2], x[4 * h + 3]);
+                if (s.tma_residual) {
+                  const float4 rr = *slot;
+                  f.x += rr.x;
+                  f.y += rr.y;
+                  f.z += rr.z;
+                  f.w += rr.w;
+                }
+                *slot = f;
+              }
+            } else {
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                uint4 *slot = reinterpret_cast<uint4 *>(buf + swz(lane, step * 2 + h));
+                float w[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) w[e] = x[8 * h + e];
+                uint4 packed;
+                if (p.c_dtype == DP_BF16) {
+                  if (s.tma_residual) {
+                    const uint4 rr = *slot;
+                    const __nv_bfloat162 *rb = reinterpret_cast<const __nv_bfloat162 *>(&rr);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                      const float2 f = __bfloat1622float2(rb[e]);
+                      w[2 * e] += f.x;
+                      w[2 * e + 1] += f.y;
+                    }
+                  }
+                  __nv_bfloat162 *pb = reinterpret_cast<__nv_bfloat162 *>(&packed);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) pb[e] = __floats2bfloat162_rn(w[2 * e], w[2 * e + 1]);
+                } else {
+                  if (s.tma_residual) {
+                    const uint4 rr = *slot;
+                    const __half2 *rh = reinterpret_cast<const __half2 *>(&rr);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                      const float2 f = __half22float2(rh[e]);
+                      w[2 * e] += f.x;
+                      w[2 * e + 1] += f.y;
+                    }
+                  }
+                  __half2 *ph = reinterpret_cast<__half2 *>(&packed);
+#pragma unroll
+                  for (int e = 0; e < 4; ++e) ph[e] = __floats2half2_rn(w[2 * e], w[2 * e + 1]);
+                }
+                *slot = packed;
+              }
+            }
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_3d(&map_c, buf, (int)n0, tm * BM + q * 32, b);
+            bulk_commit();
+          }
+        }
+        if (stop) break;
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          const int64_t n0 = (int64_t)tn * BN + c * 32;
+          if (m < s.M && n0 < s.N) {
+#pragma unroll 1
+            for (int j = 0; j < 32; j += 4)
+              ep.store4(m, n0 + j, __uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                        __uint_as_float(r[j + 3]));
+          }
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[a]);
     }
+    if (lane == 0) bulk_wait_all();  // every TMA store of this warp has landed
   }
 
   __syncthreads();
@@ -281,18 +468,22 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// rows × K bf16 operand (row stride ld elements), batch planes ``bstride`` apart.
-int make_map(CUtensorMap *map, const void *base, int64_t rows, int64_t K, int64_t ld, int64_t batch,
-             int64_t bstride, int box_rows) {
+// rows × cols matrix of ``dt`` (row stride ld elements), batch planes
+// ``bstride`` apart, boxes of box_cols × box_rows with 128-byte swizzle.
+int make_map(CUtensorMap *map, const void *base, int dt, int64_t rows, int64_t cols, int64_t ld, int64_t batch,
+             int64_t bstride, int box_cols, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   DP_REQUIRE(fn != nullptr, DP_ERR_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
-  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)((batch > 1 ? bstride : rows * ld) * 2)};
-  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)box_rows, 1};
+  const int eb = dp::dtype_bytes(dt);
+  CUtensorMapDataType t = dt == DP_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                          : dt == DP_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * eb), (cuuint64_t)((batch > 1 ? bstride : rows * ld) * eb)};
+  cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void *>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, t, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   DP_REQUIRE(r == CUDA_SUCCESS, DP_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return DP_OK;
 }
@@ -304,11 +495,28 @@ namespace dp {
 int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias,
                    const void *res, cudaStream_t stream) {
   using namespace dpk_tcgemm;
-  CUtensorMap ma, mb;
-  int st = make_map(&ma, A, p.M, p.K, p.lda, p.batch, p.stride_a, BM);
+  CUtensorMap ma, mb, mc, mr;
+  memset(&mc, 0, sizeof(mc));
+  memset(&mr, 0, sizeof(mr));
+  int st = make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, p.batch, p.stride_a, BK, BM);
   if (st != DP_OK) return st;
-  st = make_map(&mb, B, p.N, p.K, p.ldb, p.batch, p.stride_b, BN);
+  st = make_map(&mb, B, DP_BF16, p.N, p.K, p.ldb, p.batch, p.stride_b, BK, BN);
   if (st != DP_OK) return st;
+  const int cb = dtype_bytes(p.c_dtype);
+  auto al16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  const bool tma_store = (p.ldc * cb) % 16 == 0 && (p.batch == 1 || (p.stride_c * cb) % 16 == 0) && al16(C) &&
+                         (cb == 4 || cb == 2);
+  bool tma_res = false;
+  if (tma_store) {
+    st = make_map(&mc, C, p.c_dtype, p.M, p.N, p.ldc, p.batch, p.stride_c, 128 / cb, 32);
+    if (st != DP_OK) return st;
+    if ((p.epilogue & DP_EPI_RESIDUAL) && p.r_dtype == p.c_dtype && (p.ldr * cb) % 16 == 0 &&
+        (p.batch == 1 || (p.stride_r * cb) % 16 == 0) && al16(res)) {
+      st = make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, p.batch, p.stride_r, 128 / cb, 32);
+      if (st != DP_OK) return st;
+      tma_res = true;
+    }
+  }
   Shape s;
   s.M = (int)p.M;
   s.N = (int)p.N;
@@ -319,15 +527,24 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   s.tiles_per_batch = s.tiles_m * s.tiles_n;
   s.num_tiles = s.tiles_per_batch * s.batch;
   s.k_blocks = (int)((p.K + BK - 1) / BK);
+  s.tma_store = tma_store ? 1 : 0;
+  s.tma_residual = tma_res ? 1 : 0;
+  s.c_bytes = cb;
   DP_REQUIRE(p.N < (1ll << 31) && p.K < (1ll << 31), DP_ERR_UNSUPPORTED, "gemm: N or K too large");
   static bool attr_set = false;
   if (!attr_set) {
-    DP_CHECK_CUDA(cudaFuncSetAttribute(tc_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    DP_CHECK_CUDA(
+        cudaFuncSetAttribute(tc_gemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
+    DP_CHECK_CUDA(
+        cudaFuncSetAttribute(tc_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
     attr_set = true;
   }
   int grid = num_sms();
   if (grid > s.num_tiles) grid = s.num_tiles;
-  tc_gemm_kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, p, s, C, bias, res);
+  if (cb == 4)
+    tc_gemm_kernel<4><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, mr, p, s, C, bias, res);
+  else
+    tc_gemm_kernel<2><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, mr, p, s, C, bias, res);
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }
