@@ -6,15 +6,17 @@
 // each row was computed up to 16 times), softmax_kernel (one 1024-wide block,
 // wrong for N > 1024) and reduce_sum_kernel (never wired to a handler).
 //
-// One CTA per row (grid-stride over rows), 128-bit vector loads when the row
-// start and length allow it, warp-shuffle then shared-memory combine.  The
+// Value reductions: one warp per row (grid-stride over rows), 128-bit vector
+// loads with eight in flight per lane, warp-shuffle combine.  Softmax and the
+// norms: one CTA per row, warp-shuffle then shared-memory combine.  The
 // value reductions stream the row once.  Softmax and the norms keep the row in
 // registers between their passes when it fits (≤ 8 vectors per thread), so
 // HBM sees one read and one write per element; longer rows re-read from L2.
 //
 // Semantics (checked against torch on the CPU): max/min/softmax propagate
 // NaN; argmax returns the first index of the maximum with NaN counted as the
-// maximum; mean = sum / cols; RMSNorm = x · rsqrt(mean(x²) + eps) · (w + off);
+// maximum; mean = sum / cols; softmax = exp(x - max) (the __expf intrinsic)
+// times 1 / sum; RMSNorm = x · rsqrt(mean(x²) + eps) · (w + off);
 // LayerNorm = (x - mean) · rsqrt(var + eps) · w + b with biased variance.
 #include <cfloat>
 
@@ -114,49 +116,72 @@ __device__ __forceinline__ void write_scalar(void *out, int64_t i, int dt, float
 }
 
 // ---------------------------------------------------------------------------
-// sum / max / min / mean / argmax: one streaming pass.
-template <typename TIn, int VEC>
-__global__ void __launch_bounds__(kMaxThreads) reduce_stream_kernel(dp_rowreduce_params p,
-                                                                    const TIn *__restrict__ in, void *out) {
-  __shared__ float redv[32];
-  __shared__ long long redi[32];
-  const int64_t step = (int64_t)blockDim.x * VEC;
-  for (int64_t row = blockIdx.x; row < p.rows; row += gridDim.x) {
+// sum / max / min / mean / argmax: one streaming pass, one warp per row.
+// Each lane walks the row in VEC-element vectors, UNROLL vectors in flight,
+// so a resident warp always has UNROLL × 512 bytes of loads outstanding; the
+// row is combined with warp shuffles only (no block barrier).
+constexpr int kUnroll = 8;
+
+template <int KIND>
+__device__ __forceinline__ void acc_step(float &acc, ArgVal &best, float v, long long idx) {
+  if constexpr (KIND == DP_RED_MAX) acc = nan_max(acc, v);
+  else if constexpr (KIND == DP_RED_MIN) acc = nan_min(acc, v);
+  else if constexpr (KIND == DP_RED_ARGMAX) {
+    if (arg_better(v, idx, best.v, best.i)) {
+      best.v = v;
+      best.i = idx;
+    }
+  } else acc += v;
+}
+
+template <typename TIn, int VEC, int KIND>
+__global__ void __launch_bounds__(256) reduce_warp_kernel(dp_rowreduce_params p, const TIn *__restrict__ in,
+                                                          void *out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t step = 32 * VEC;
+  for (int64_t row = warp0; row < p.rows; row += nwarps) {
     const TIn *x = in + row * p.in_row_stride;
-    float acc = (p.kind == DP_RED_MAX) ? -INFINITY : (p.kind == DP_RED_MIN ? INFINITY : 0.0f);
-    ArgVal best{-INFINITY, (long long)p.cols};  // index cols = "none yet"
-    int64_t c = (int64_t)threadIdx.x * VEC;
-#pragma unroll 4
+    float acc = (KIND == DP_RED_MAX) ? -INFINITY : (KIND == DP_RED_MIN ? INFINITY : 0.0f);
+    ArgVal best{-INFINITY, (long long)p.cols};
+    int64_t c = (int64_t)lane * VEC;
+    for (; c + (kUnroll - 1) * step < p.cols; c += kUnroll * step) {
+      float v[kUnroll][VEC];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) load_vec<TIn, VEC>(x + c + u * step, v[u]);
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc_step<KIND>(acc, best, v[u][j], c + u * step + j);
+    }
     for (; c < p.cols; c += step) {
       float v[VEC];
       load_vec<TIn, VEC>(x + c, v);
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        switch (p.kind) {
-          case DP_RED_MAX: acc = nan_max(acc, v[j]); break;
-          case DP_RED_MIN: acc = nan_min(acc, v[j]); break;
-          case DP_RED_ARGMAX:
-            if (arg_better(v[j], c + j, best.v, best.i)) {
-              best.v = v[j];
-              best.i = c + j;
-            }
-            break;
-          default: acc += v[j]; break;
+      for (int j = 0; j < VEC; ++j) acc_step<KIND>(acc, best, v[j], c + j);
+    }
+    if constexpr (KIND == DP_RED_ARGMAX) {
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float v2 = __shfl_xor_sync(0xffffffffu, best.v, o);
+        const long long i2 = __shfl_xor_sync(0xffffffffu, best.i, o);
+        if (arg_better(v2, i2, best.v, best.i)) {
+          best.v = v2;
+          best.i = i2;
         }
       }
-    }
-    if (p.kind == DP_RED_ARGMAX) {
-      best = block_argmax(best, redv, redi);
-      if (threadIdx.x == 0) write_scalar(out, row * p.out_row_stride, p.out_dtype, 0.0f, best.i);
+      if (lane == 0) write_scalar(out, row * p.out_row_stride, p.out_dtype, 0.0f, best.i);
     } else {
-      if (p.kind == DP_RED_MAX)
-        acc = block_reduce(acc, nan_max, redv);
-      else if (p.kind == DP_RED_MIN)
-        acc = block_reduce(acc, nan_min, redv);
-      else
-        acc = block_reduce(acc, [](float a, float b) { return a + b; }, redv);
-      if (p.kind == DP_RED_MEAN) acc = acc / (float)p.cols;
-      if (threadIdx.x == 0) write_scalar(out, row * p.out_row_stride, p.out_dtype, acc, 0);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float o2 = __shfl_xor_sync(0xffffffffu, acc, o);
+        if constexpr (KIND == DP_RED_MAX) acc = nan_max(acc, o2);
+        else if constexpr (KIND == DP_RED_MIN) acc = nan_min(acc, o2);
+        else acc += o2;
+      }
+      if constexpr (KIND == DP_RED_MEAN) acc = acc / (float)p.cols;
+      if (lane == 0) write_scalar(out, row * p.out_row_stride, p.out_dtype, acc, 0);
     }
   }
 }
@@ -201,12 +226,12 @@ __global__ void __launch_bounds__(kMaxThreads) norm_kernel(dp_rowreduce_params p
           const bool live = (int64_t)threadIdx.x * VEC + i * step < p.cols;
 #pragma unroll
           for (int j = 0; j < VEC; ++j) {
-            v[i][j] = live ? expf(v[i][j] - m) : 0.0f;
+            v[i][j] = live ? __expf(v[i][j] - m) : 0.0f;
             s += v[i][j];
           }
         }
         s = block_reduce(s, [](float a, float b) { return a + b; }, red);
-        scale = s;  // divide below
+        scale = 1.0f / s;  // one divide per row; elements are scaled below
       } else if (p.kind == DP_RED_RMSNORM) {
         float ss = 0.0f;
 #pragma unroll
@@ -247,7 +272,7 @@ __global__ void __launch_bounds__(kMaxThreads) norm_kernel(dp_rowreduce_params p
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
           if (p.kind == DP_RED_SOFTMAX) {
-            o[j] = v[i][j] / scale;
+            o[j] = v[i][j] * scale;
           } else {
             float t = (v[i][j] - shift) * scale;
             if (p.has_weight) t = t * (wv[j] + p.weight_offset);
@@ -278,9 +303,9 @@ __global__ void __launch_bounds__(kMaxThreads) norm_kernel(dp_rowreduce_params p
           float v[VEC];
           load_vec<TIn, VEC>(x + c, v);
 #pragma unroll
-          for (int j = 0; j < VEC; ++j) s += expf(v[j] - m);
+          for (int j = 0; j < VEC; ++j) s += __expf(v[j] - m);
         }
-        scale = block_reduce(s, [](float u, float t) { return u + t; }, red);
+        scale = 1.0f / block_reduce(s, [](float u, float t) { return u + t; }, red);
         shift = m;
       } else if (p.kind == DP_RED_RMSNORM) {
         scale = rsqrtf(block_reduce(a, [](float u, float t) { return u + t; }, red) / n + p.eps);
@@ -304,7 +329,7 @@ __global__ void __launch_bounds__(kMaxThreads) norm_kernel(dp_rowreduce_params p
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
           if (p.kind == DP_RED_SOFTMAX) {
-            o[j] = expf(v[j] - shift) / scale;
+            o[j] = __expf(v[j] - shift) * scale;
           } else {
             float t = (v[j] - shift) * scale;
             if (p.has_weight) t = t * (wv[j] + p.weight_offset);
@@ -318,6 +343,140 @@ __global__ void __launch_bounds__(kMaxThreads) norm_kernel(dp_rowreduce_params p
   }
 }
 
+// ---------------------------------------------------------------------------
+// softmax / rmsnorm / layernorm with one warp per row: the whole row sits in
+// the lane registers (NV vectors of VEC per lane), all loads of a row are in
+// flight together, statistics are combined with shuffles only.
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = nan_max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+template <typename TIn, typename TOut, int VEC, int NV, int KIND>
+__global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, const TIn *__restrict__ in,
+                                                        const TIn *__restrict__ w, const TIn *__restrict__ bias,
+                                                        TOut *__restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int step = 32 * VEC;
+  const float n = (float)p.cols;
+  for (int64_t row = warp0; row < p.rows; row += nwarps) {
+    const TIn *x = in + row * p.in_row_stride;
+    TOut *y = out + row * p.out_row_stride;
+    float v[NV][VEC];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane * VEC + i * step;
+      if (c < p.cols) {
+        load_vec<TIn, VEC>(x + c, v[i]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) v[i][j] = 0.0f;
+      }
+    }
+    float scale = 1.0f, shift = 0.0f;
+    if constexpr (KIND == DP_RED_SOFTMAX) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        if (lane * VEC + i * step < p.cols)
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) m = nan_max(m, v[i][j]);
+      m = warp_max(m);
+      float sum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const bool live = lane * VEC + i * step < p.cols;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          v[i][j] = live ? __expf(v[i][j] - m) : 0.0f;
+          sum += v[i][j];
+        }
+      }
+      scale = 1.0f / warp_sum(sum);
+    } else if constexpr (KIND == DP_RED_RMSNORM) {
+      float ss = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+      scale = rsqrtf(warp_sum(ss) / n + p.eps);
+    } else {
+      float sum = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) sum += v[i][j];
+      const float mean = warp_sum(sum) / n;
+      float q = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        const bool live = lane * VEC + i * step < p.cols;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float d = live ? v[i][j] - mean : 0.0f;
+          q = fmaf(d, d, q);
+        }
+      }
+      scale = rsqrtf(warp_sum(q) / n + p.eps);
+      shift = mean;
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = lane * VEC + i * step;
+      if (c >= p.cols) continue;
+      float o[VEC], wv[VEC], bv[VEC];
+      if (KIND != DP_RED_SOFTMAX && p.has_weight) load_vec<TIn, VEC>(w + c, wv);
+      if (KIND == DP_RED_LAYERNORM && p.has_bias) load_vec<TIn, VEC>(bias + c, bv);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        if constexpr (KIND == DP_RED_SOFTMAX) {
+          o[j] = v[i][j] * scale;
+        } else {
+          float t = (v[i][j] - shift) * scale;
+          if (p.has_weight) t = t * (wv[j] + p.weight_offset);
+          if (KIND == DP_RED_LAYERNORM && p.has_bias) t = t + bv[j];
+          o[j] = t;
+        }
+      }
+      store_vec<TOut, VEC>(y + c, o);
+    }
+  }
+}
+
+template <typename TIn, typename TOut, int VEC, int NV>
+int launch_norm_warp(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
+                     cudaStream_t s) {
+  const int threads = 256;
+  int64_t blocks = (p.rows * 32 + threads - 1) / threads;
+  const int64_t cap = (int64_t)dp::num_sms() * 8 * 8;
+  if (blocks > cap) blocks = cap;
+  auto *x = static_cast<const TIn *>(in);
+  auto *wp = static_cast<const TIn *>(w);
+  auto *bp = static_cast<const TIn *>(b);
+  auto *y = static_cast<TOut *>(out);
+  switch (p.kind) {
+    case DP_RED_SOFTMAX:
+      norm_warp_kernel<TIn, TOut, VEC, NV, DP_RED_SOFTMAX><<<(int)blocks, threads, 0, s>>>(p, x, wp, bp, y);
+      break;
+    case DP_RED_RMSNORM:
+      norm_warp_kernel<TIn, TOut, VEC, NV, DP_RED_RMSNORM><<<(int)blocks, threads, 0, s>>>(p, x, wp, bp, y);
+      break;
+    default:
+      norm_warp_kernel<TIn, TOut, VEC, NV, DP_RED_LAYERNORM><<<(int)blocks, threads, 0, s>>>(p, x, wp, bp, y);
+      break;
+  }
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
 int grid_for(int64_t rows, int threads) {
   const int per_sm = 2048 / threads;
   int64_t g = (int64_t)dp::num_sms() * per_sm * 4;
@@ -326,10 +485,18 @@ int grid_for(int64_t rows, int threads) {
 
 template <typename TIn, int VEC>
 int launch_stream(const dp_rowreduce_params &p, const void *in, void *out, cudaStream_t s) {
-  int64_t per_thread_vecs = (p.cols + VEC - 1) / VEC;
-  int threads = per_thread_vecs >= kMaxThreads ? kMaxThreads : (int)(((per_thread_vecs + 31) / 32) * 32);
-  if (threads < 32) threads = 32;
-  reduce_stream_kernel<TIn, VEC><<<grid_for(p.rows, threads), threads, 0, s>>>(p, static_cast<const TIn *>(in), out);
+  const int threads = 256;
+  int64_t blocks = (p.rows * 32 + threads - 1) / threads;
+  const int64_t cap = (int64_t)dp::num_sms() * 8 * 4;  // 8 blocks of 256 per SM, 4 waves
+  if (blocks > cap) blocks = cap;
+  const TIn *x = static_cast<const TIn *>(in);
+  switch (p.kind) {
+    case DP_RED_SUM: reduce_warp_kernel<TIn, VEC, DP_RED_SUM><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
+    case DP_RED_MAX: reduce_warp_kernel<TIn, VEC, DP_RED_MAX><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
+    case DP_RED_MIN: reduce_warp_kernel<TIn, VEC, DP_RED_MIN><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
+    case DP_RED_MEAN: reduce_warp_kernel<TIn, VEC, DP_RED_MEAN><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
+    default: reduce_warp_kernel<TIn, VEC, DP_RED_ARGMAX><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
+  }
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }
@@ -369,7 +536,14 @@ int launch_norm_vec(const dp_rowreduce_params &p, const void *in, const void *w,
   auto al = [](const void *q, size_t a) { return q == nullptr || reinterpret_cast<uintptr_t>(q) % a == 0; };
   const bool ok = vec_ok && p.cols % V == 0 && p.in_row_stride % V == 0 && p.out_row_stride % V == 0 &&
                   al(in, 16) && al(w, 16) && al(b, 16) && al(out, sizeof(TOut) * V);
-  if (ok) return launch_norm<TIn, TOut, V>(p, in, w, b, out, s);
+  if (ok) {
+    const int64_t per_lane = (p.cols + 32 * V - 1) / (32 * V);  // vectors per lane for a warp-per-row pass
+    if (per_lane <= 4) return launch_norm_warp<TIn, TOut, V, 4>(p, in, w, b, out, s);
+    if (per_lane <= 8) return launch_norm_warp<TIn, TOut, V, 8>(p, in, w, b, out, s);
+    if (per_lane <= 16 && sizeof(TIn) == 4) return launch_norm_warp<TIn, TOut, V, 16>(p, in, w, b, out, s);
+    if (per_lane <= 32 && sizeof(TIn) == 4) return launch_norm_warp<TIn, TOut, V, 32>(p, in, w, b, out, s);
+    return launch_norm<TIn, TOut, V>(p, in, w, b, out, s);
+  }
   return launch_norm<TIn, TOut, 1>(p, in, w, b, out, s);
 }
 
