@@ -46,6 +46,7 @@ OP = {"load": 1, "store": 2, "const": 3, "chansel": 4, "add": 10, "sub": 11, "mu
       "gelu_erf": 26, "gelu_tanh": 27, "silu": 28, "mov": 29}
 
 DP_PLAN_MAGIC, DP_PLAN_VERSION = 0x32425044, 1
+DP_NOALLOC_ARENA_BYTES = 64 << 20
 DP_RECORD_MAX_OPERANDS, DP_RECORD_PARAM_BYTES = 8, 1280
 DP_SLOT_BOUND, DP_SLOT_ARENA = 0, 1
 DP_K_PREPROC, DP_K_ROWREDUCE, DP_K_GEMM, DP_K_REGION, DP_K_EMBEDDING, DP_K_COPY = 1, 2, 3, 4, 5, 6
@@ -128,6 +129,8 @@ EXPORTS = {
     "dp_program_set_graph": [_VP, ctypes.c_int],
     "dp_program_arena_bytes": [_VP, ctypes.POINTER(ctypes.c_uint64)],
     "dp_program_destroy": [_VP],
+    "dp_program_run_noalloc": [_VP, ctypes.c_size_t, ctypes.POINTER(_VP), ctypes.POINTER(ctypes.c_uint64),
+                               ctypes.c_int, _VP],
 }
 
 _lib = None

@@ -1,0 +1,149 @@
+// Running a compiled plan without allocating device memory.
+//
+// dp_program_create allocates the plan's arena (its intermediate buffers)
+// with cudaMalloc.  Some callers cannot do that at run time: a host
+// application that owns every byte of device memory and hands plugins only
+// the buffers they read and write, a latency-critical loop whose owners
+// forbid calls into the driver's allocator, or code that must not grow the
+// process's device footprint after start-up.  dp_program_run_noalloc runs a
+// plan once with its intermediates in g_noalloc_arena, a fixed array in the
+// library's own device memory (DP_NOALLOC_ARENA_BYTES on every GPU that loads
+// the library, held until the process exits).  The caller still passes every
+// input, weight and output buffer.
+#include <cstring>
+#include <mutex>
+
+#include "dp_common.cuh"
+
+static __device__ __align__(256) uint8_t g_noalloc_arena[DP_NOALLOC_ARENA_BYTES];
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr int kMaxSlots = 1024;
+
+std::mutex g_noalloc_mu;
+void *g_noalloc_base[kMaxDevices] = {nullptr};
+
+// Device address of g_noalloc_arena on the current device (looked up once per
+// device; in host code the symbol itself is only a host-side stand-in).
+int noalloc_base(void **out) {
+  int dev = 0;
+  DP_CHECK_CUDA(cudaGetDevice(&dev));
+  DP_REQUIRE(dev >= 0 && dev < kMaxDevices, DP_ERR_UNSUPPORTED, "dp_program_run_noalloc: device index too large");
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_base[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_arena);
+    if (e != cudaSuccess) return dp::cuda_status(e, "cudaGetSymbolAddress(g_noalloc_arena)");
+    DP_REQUIRE(p != nullptr, DP_ERR_CUDA, "dp_program_run_noalloc: null arena address");
+    g_noalloc_base[dev] = p;
+  }
+  *out = g_noalloc_base[dev];
+  return DP_OK;
+}
+
+}  // namespace
+
+extern "C" int dp_program_run_noalloc(const void *plan, size_t plan_bytes, void *const *bound_ptrs,
+                                      const uint64_t *bound_bytes, int n_bound, void *stream) {
+  DP_REQUIRE(plan != nullptr, DP_ERR_ARG, "dp_program_run_noalloc: null plan");
+  DP_REQUIRE(plan_bytes >= sizeof(dp_plan_header), DP_ERR_PLAN, "plan: truncated header");
+  dp_plan_header h;
+  memcpy(&h, plan, sizeof(h));
+  DP_REQUIRE(h.magic == DP_PLAN_MAGIC, DP_ERR_PLAN, "plan: bad magic");
+  DP_REQUIRE(h.version == DP_PLAN_VERSION, DP_ERR_PLAN, "plan: unsupported version");
+  DP_REQUIRE(plan_bytes == sizeof(h) + (size_t)h.n_slots * sizeof(dp_plan_slot) +
+                               (size_t)h.n_records * sizeof(dp_plan_record),
+             DP_ERR_PLAN, "plan: size does not match its header");
+  DP_REQUIRE(h.n_slots <= (uint32_t)kMaxSlots, DP_ERR_UNSUPPORTED,
+             "dp_program_run_noalloc: plans of more than 1024 slots are not supported");
+  DP_REQUIRE(h.arena_bytes <= (uint64_t)DP_NOALLOC_ARENA_BYTES, DP_ERR_UNSUPPORTED,
+             "dp_program_run_noalloc: the plan needs " + std::to_string(h.arena_bytes) +
+                 " bytes of intermediates; the static arena holds " + std::to_string(DP_NOALLOC_ARENA_BYTES));
+  const uint8_t *cur = static_cast<const uint8_t *>(plan) + sizeof(h);
+  const uint8_t *slots = cur;
+  const uint8_t *records = cur + (size_t)h.n_slots * sizeof(dp_plan_slot);
+
+  void *base = nullptr;
+  int st = noalloc_base(&base);
+  if (st != DP_OK) return st;
+
+  // Resolve every slot: caller buffers in slot order, intermediates in the arena.
+  void *ptr[kMaxSlots];
+  int next_bound = 0;
+  for (uint32_t i = 0; i < h.n_slots; ++i) {
+    dp_plan_slot sl;
+    memcpy(&sl, slots + i * sizeof(dp_plan_slot), sizeof(sl));
+    if (sl.kind == DP_SLOT_ARENA) {
+      DP_REQUIRE(sl.offset % 256 == 0 && sl.offset + sl.bytes <= h.arena_bytes, DP_ERR_PLAN,
+                 "plan: arena slot out of range");
+      ptr[i] = static_cast<uint8_t *>(base) + sl.offset;
+    } else {
+      DP_REQUIRE(sl.kind == DP_SLOT_BOUND, DP_ERR_PLAN, "plan: bad slot kind");
+      DP_REQUIRE(bound_ptrs != nullptr && next_bound < n_bound, DP_ERR_ARG,
+                 "dp_program_run_noalloc: fewer buffers than the plan's bound slots");
+      DP_REQUIRE(bound_ptrs[next_bound] != nullptr, DP_ERR_ARG, "dp_program_run_noalloc: null buffer");
+      DP_REQUIRE(bound_bytes == nullptr || bound_bytes[next_bound] >= sl.bytes, DP_ERR_SHAPE,
+                 "dp_program_run_noalloc: buffer " + std::to_string(next_bound) + " is smaller than its slot");
+      ptr[i] = bound_ptrs[next_bound++];
+    }
+  }
+  DP_REQUIRE(next_bound == n_bound, DP_ERR_ARG, "dp_program_run_noalloc: more buffers than bound slots");
+
+  cudaStream_t s = dp::as_stream(stream);
+  for (uint32_t r = 0; r < h.n_records; ++r) {
+    dp_plan_record rec;
+    memcpy(&rec, records + (size_t)r * sizeof(dp_plan_record), sizeof(rec));
+    DP_REQUIRE(rec.n_operands <= DP_RECORD_MAX_OPERANDS, DP_ERR_PLAN, "plan: too many operands");
+    const void *ops[DP_RECORD_MAX_OPERANDS] = {nullptr};
+    for (uint32_t i = 0; i < rec.n_operands; ++i) {
+      DP_REQUIRE(rec.operand[i] >= -1 && rec.operand[i] < (int32_t)h.n_slots, DP_ERR_PLAN,
+                 "plan: operand out of range");
+      ops[i] = rec.operand[i] >= 0 ? ptr[rec.operand[i]] : nullptr;
+    }
+    switch (rec.kernel) {
+      case DP_K_PREPROC: {
+        dp_preproc_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_preproc(p, ops[0], const_cast<void *>(ops[1]), s);
+        break;
+      }
+      case DP_K_ROWREDUCE: {
+        dp_rowreduce_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_rowreduce(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
+        break;
+      }
+      case DP_K_GEMM: {
+        dp_gemm_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_gemm(p, ops[0], ops[1], const_cast<void *>(ops[2]), ops[3], ops[4], s);
+        break;
+      }
+      case DP_K_REGION: {
+        dp_region_desc d;
+        memcpy(&d, rec.params, sizeof(d));
+        st = dp::launch_region(d, ops, s);
+        break;
+      }
+      case DP_K_EMBEDDING: {
+        dp_embedding_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_embedding(p, ops[0], ops[1], const_cast<void *>(ops[2]), s);
+        break;
+      }
+      case DP_K_COPY: {
+        uint64_t bytes;
+        memcpy(&bytes, rec.params, sizeof(bytes));
+        cudaError_t e = cudaMemcpyAsync(const_cast<void *>(ops[1]), ops[0], bytes, cudaMemcpyDeviceToDevice, s);
+        st = e == cudaSuccess ? DP_OK : dp::cuda_status(e, "noalloc copy record");
+        break;
+      }
+      default:
+        st = dp::set_error(DP_ERR_PLAN, "plan: unknown record kind " + std::to_string(rec.kernel));
+    }
+    if (st != DP_OK) return st;
+  }
+  return DP_OK;
+}

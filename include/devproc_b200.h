@@ -215,6 +215,27 @@ int dp_program_set_graph(dp_program *prog, int enable);
 int dp_program_arena_bytes(const dp_program *prog, uint64_t *bytes);
 int dp_program_destroy(dp_program *prog);
 
+/* ---- running a plan without allocating device memory -----------------------
+ * No counterpart in the reference.  For callers that cannot allocate device
+ * memory at run time — a host application that owns every byte of device
+ * memory and hands a plugin only the buffers it reads and writes, or a loop
+ * whose owners forbid calls into the driver's allocator: runs ``plan`` once
+ * with its intermediate buffers in a fixed array of DP_NOALLOC_ARENA_BYTES in
+ * the library's own device memory, present on every GPU that loads the
+ * library until the process exits.  ``bound_ptrs`` (and optionally
+ * ``bound_bytes``, checked against the slot sizes) give one caller buffer per
+ * DP_SLOT_BOUND slot, in slot order: inputs, weights and outputs.  A plan that
+ * needs more intermediate bytes than the limit is rejected with
+ * DP_ERR_UNSUPPORTED.  No cudaMalloc or cudaFree is called.  The first call on
+ * a device looks up the array's device address, so make it before any stream
+ * capture.  Every call shares the one array, which keeps the last call's
+ * contents; each intermediate is written before it is read, so nothing needs
+ * clearing, but calls that overlap on the GPU (other streams or threads) race
+ * on it. */
+#define DP_NOALLOC_ARENA_BYTES (64u << 20)
+int dp_program_run_noalloc(const void *plan, size_t plan_bytes, void *const *bound_ptrs,
+                           const uint64_t *bound_bytes, int n_bound, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
