@@ -395,7 +395,7 @@ def main():
                     "path": "Runtime.run(images=pinned host uint8) -> pinned host bf16"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": ncu_traffic(), "peak_kind": peak_kind,
-                         "kernel": "preproc_bulk_kernel<u8,bf16,NHWC->NCHW>",
+                         "kernel": "preproc_u8c3_kernel<bf16> (NHWC u8 -> NCHW bf16)",
                          "algorithmic_bytes_per_launch": bytes_per_launch},
             "cpu_baseline": cpu,
             "clocks": clocks,
