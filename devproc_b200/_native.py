@@ -75,7 +75,7 @@ class GemmParams(ctypes.Structure):
                 ("stride_c", ctypes.c_int64), ("stride_r", ctypes.c_int64),
                 ("a_dtype", ctypes.c_int32), ("b_dtype", ctypes.c_int32), ("c_dtype", ctypes.c_int32),
                 ("r_dtype", ctypes.c_int32), ("b_layout", ctypes.c_int32), ("epilogue", ctypes.c_int32),
-                ("bias_dtype", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+                ("bias_dtype", ctypes.c_int32), ("alpha", ctypes.c_float)]
 
 
 class RegionDesc(ctypes.Structure):

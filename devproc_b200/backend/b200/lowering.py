@@ -55,6 +55,41 @@ def contiguous_strides(shape: Tuple[int, ...]) -> Tuple[int, ...]:
     return tuple(reversed(st))
 
 
+def view_reshape(shape, strides, new_shape):
+    """Strides that present (shape, strides) as ``new_shape`` without copying, or None.
+
+    Dims that are laid out back to back (stride[i] == stride[i+1] * shape[i+1])
+    form runs that behave like one dim; every new dim must fall inside one run.
+    """
+    runs = []  # (size, innermost stride), outermost first
+    for sz, st in zip(shape, strides):
+        if sz == 1:
+            continue
+        if runs and runs[-1][1] == st * sz:
+            runs[-1] = (runs[-1][0] * sz, st)
+        else:
+            runs.append((sz, st))
+    out = [0] * len(new_shape)
+    ri = len(runs) - 1
+    left, unit = (runs[ri][0], runs[ri][1]) if runs else (1, 1)
+    for i in range(len(new_shape) - 1, -1, -1):
+        n = new_shape[i]
+        if n == 1:
+            out[i] = 0
+            continue
+        while left == 1 and ri > 0:
+            ri -= 1
+            left, unit = runs[ri]
+        if left % n != 0:
+            return None
+        out[i] = unit
+        unit *= n
+        left //= n
+    if left != 1 or ri > 0:
+        return None
+    return tuple(out)
+
+
 def _prod(xs) -> int:
     p = 1
     for x in xs:
@@ -268,10 +303,14 @@ class Lowerer:
         if name == "embedding":
             return self.lower_embedding(op)
         if name == "reshape":
-            src = self.contiguous(op.inputs[0])
             out = op.outputs[0]
             shape = out.type.shape
-            self.views[out.name] = View(src.buf, shape, contiguous_strides(shape), src.offset)
+            v = self.views[op.inputs[0].name]
+            st = view_reshape(v.shape, v.strides, shape)
+            if st is None:
+                v = self.contiguous(op.inputs[0])
+                st = contiguous_strides(shape)
+            self.views[out.name] = View(v.buf, shape, st, v.offset)
             return
         if name == "transpose":
             v = self.views[op.inputs[0].name]
@@ -282,7 +321,7 @@ class Lowerer:
         if name in ELEMENTWISE:
             return self.lower_region(op)
         if name == "sdpa":
-            raise UnsupportedOpError("sdpa")
+            return self.lower_sdpa(op)
         raise UnsupportedOpError(name)
 
     # --------------------------------------------------------- preprocess
@@ -556,6 +595,72 @@ class Lowerer:
         rb.store(out, rb.load(v))
         self.emit_region(rb, f"cast {value.name} to {dtype}")
         return out
+
+    # ------------------------------------------------------------ attention
+    def lower_sdpa(self, op: Op) -> None:
+        """softmax(Q·Kᵀ·scale)·V as two batched tensor-core GEMMs around a row softmax.
+
+        Q [.., Hq, L, D], K [.., Hk, S, D], V [.., Hk, S, Dv], Hq a multiple of Hk
+        (grouped-query attention: the Hq/Hk query heads of a group share one K/V
+        head, so each group is one GEMM of (Hq/Hk)·L rows).  Scores are fp32,
+        probabilities are stored in the operand dtype.
+        """
+        if op.attr("is_causal"):
+            raise CompilationError("sdpa: causal masking is not supported yet")
+        q, k, v = op.inputs
+        tq, tk, tv = q.type, k.type, v.type
+        if len(tq.shape) < 3:
+            raise CompilationError("sdpa: inputs need [.., heads, len, dim]")
+        Hq, L, D = tq.shape[-3:]
+        Hk, S, Dk = tk.shape[-3:]
+        Dv = tv.shape[-1]
+        B = _prod(tq.shape[:-3])
+        if Dk != D or tv.shape[-2] != S or tv.shape[-3] != Hk or Hq % Hk:
+            raise CompilationError("sdpa: inconsistent q/k/v shapes")
+        if tq.dtype != tk.dtype or tq.dtype != tv.dtype or tq.dtype not in ("bfloat16", "float32"):
+            raise CompilationError("sdpa: q, k, v must share dtype bf16 or fp32")
+        g = Hq // Hk
+        qv, kv = self.contiguous(q), self.contiguous(k)
+        vv = self.views[v.name]
+        # V as [B·Hk, Dv, S] (the GEMM's B operand is K-major)
+        vshape = (B, Hk, S, Dv)
+        vst = view_reshape(vv.shape, vv.strides, vshape)
+        if vst is None:
+            vv = self.contiguous(v)
+            vst = contiguous_strides(vshape)
+        vt = self.copy_view(View(vv.buf, (B, Hk, Dv, S), (vst[0], vst[1], vst[3], vst[2]), vv.offset),
+                            v.name + "_t")
+        dt = tq.dtype
+        scores = View(self.new_buffer("arena", "float32", (B * Hk, g * L, S), op.outputs[0].name + "_s"),
+                      (B * Hk, g * L, S), contiguous_strides((B * Hk, g * L, S)))
+        p = N.GemmParams()
+        p.M, p.N, p.K = g * L, S, D
+        p.lda, p.ldb, p.ldc = D, D, S
+        p.batch, p.stride_a, p.stride_b, p.stride_c = B * Hk, g * L * D, S * D, g * L * S
+        p.a_dtype = p.b_dtype = N.DTYPE_CODE[dt]
+        p.c_dtype = N.DP_F32
+        p.b_layout = N.DP_B_NK
+        p.alpha = float(op.attr("scale"))
+        self.emit(N.DP_K_GEMM, [qv.buf, kv.buf, scores.buf, None, None], p,
+                  f"gemm attn-scores b{B * Hk} M{g * L} N{S} K{D} {dt}", 2 * B * Hq * L * S * D,
+                  qv.buf.nbytes + kv.buf.nbytes + scores.buf.nbytes)
+        probs = View(self.new_buffer("arena", dt, (B * Hk, g * L, S), op.outputs[0].name + "_p"),
+                     (B * Hk, g * L, S), contiguous_strides((B * Hk, g * L, S)))
+        r = N.RowReduceParams()
+        r.kind, r.in_dtype, r.out_dtype = N.DP_RED_SOFTMAX, N.DP_F32, N.DTYPE_CODE[dt]
+        r.rows, r.cols, r.in_row_stride, r.out_row_stride = B * Hq * L, S, S, S
+        self.emit(N.DP_K_ROWREDUCE, [scores.buf, None, None, probs.buf], r,
+                  f"rowreduce attn-softmax {B * Hq * L}x{S}", 0, scores.buf.nbytes + probs.buf.nbytes)
+        out = self.new_value_view(op.outputs[0])
+        p2 = N.GemmParams()
+        p2.M, p2.N, p2.K = g * L, Dv, S
+        p2.lda, p2.ldb, p2.ldc = S, S, Dv
+        p2.batch, p2.stride_a, p2.stride_b, p2.stride_c = B * Hk, g * L * S, Dv * S, g * L * Dv
+        p2.a_dtype = p2.b_dtype = p2.c_dtype = N.DTYPE_CODE[dt]
+        p2.b_layout = N.DP_B_NK
+        self.emit(N.DP_K_GEMM, [probs.buf, vt.buf, out.buf, None, None], p2,
+                  f"gemm attn-values b{B * Hk} M{g * L} N{Dv} K{S} {dt}", 2 * B * Hq * L * S * Dv,
+                  probs.buf.nbytes + vt.buf.nbytes + out.buf.nbytes)
 
     # ------------------------------------------------------------ embedding
     def lower_embedding(self, op: Op) -> None:

@@ -24,6 +24,7 @@ struct Epilogue {
       : p(p_), C(C_), bias(bias_), res(res_), c_off(batch * p_.stride_c), r_off(batch * p_.stride_r) {}
 
   __device__ __forceinline__ float apply(int64_t m, int64_t n, float v) const {
+    if (p.alpha != 0.0f) v *= p.alpha;
     if (p.epilogue & DP_EPI_BIAS) v += load_as_f32(bias, n, p.bias_dtype);
     if (p.epilogue & DP_EPI_RELU) v = v > 0.0f ? v : (isnan(v) ? v : 0.0f);
     if (p.epilogue & DP_EPI_GELU_ERF) v = act_gelu_erf(v);

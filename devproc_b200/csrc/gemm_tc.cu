@@ -346,6 +346,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 16; ++e) x[e] = __uint_as_float(r[e]);
             const int64_t nb = n0 + step * 16;
+            if (p.alpha != 0.0f) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) x[e] *= p.alpha;
+            }
             if (p.epilogue) epi16(x, nb, s.N, p.epilogue, bias, p.bias_dtype);
             if ((p.epilogue & DP_EPI_RESIDUAL) && !s.tma_residual) {
 #pragma unroll

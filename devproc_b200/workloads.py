@@ -85,3 +85,80 @@ class TokenPipeline(torch.nn.Module):
 def token_ids(batch: int = 8, length: int = 128, seed: int = 0) -> torch.Tensor:
     g = torch.Generator().manual_seed(seed)
     return torch.randint(0, TokenPipeline.VOCAB, (batch, length), generator=g, dtype=torch.int32)
+
+
+class VitAttention(torch.nn.Module):
+    def __init__(self, dim: int, heads: int):
+        super().__init__()
+        self.heads = heads
+        self.q = torch.nn.Linear(dim, dim)
+        self.k = torch.nn.Linear(dim, dim)
+        self.v = torch.nn.Linear(dim, dim)
+        self.o = torch.nn.Linear(dim, dim)
+
+    def forward(self, x):
+        b, n, d = x.shape
+        h = self.heads
+        q = self.q(x).view(b, n, h, d // h).transpose(1, 2)
+        k = self.k(x).view(b, n, h, d // h).transpose(1, 2)
+        v = self.v(x).view(b, n, h, d // h).transpose(1, 2)
+        o = torch.nn.functional.scaled_dot_product_attention(q, k, v)
+        return self.o(o.transpose(1, 2).reshape(b, n, d))
+
+
+class VitBlock(torch.nn.Module):
+    def __init__(self, dim: int, heads: int, mlp: int, eps: float):
+        super().__init__()
+        self.ln1 = torch.nn.LayerNorm(dim, eps=eps)
+        self.attn = VitAttention(dim, heads)
+        self.ln2 = torch.nn.LayerNorm(dim, eps=eps)
+        self.fc1 = torch.nn.Linear(dim, mlp)
+        self.fc2 = torch.nn.Linear(mlp, dim)
+
+    def forward(self, x):
+        x = x + self.attn(self.ln1(x))
+        return x + self.fc2(torch.nn.functional.gelu(self.fc1(self.ln2(x)), approximate="tanh"))
+
+
+class VitClassifier(torch.nn.Module):
+    """SigLIP-So400m/14-shaped encoder + mean-pool + linear head + argmax.
+
+    Defaults are the benchmark's shape: patch 14 on 224×224 (256 tokens),
+    width 1152, 27 layers, 16 heads, MLP 4304, GELU-tanh, LayerNorm (eps 1e-6),
+    1000 classes; weights N(0, 0.02), biases 0, LayerNorm γ=1, β=0.
+    """
+
+    def __init__(self, layers: int = 27, dim: int = 1152, heads: int = 16, mlp: int = 4304, classes: int = 1000,
+                 patch: int = 14, image: int = 224, seed: int = 1, dtype=torch.bfloat16, logits: bool = False):
+        super().__init__()
+        self.logits = logits
+        self.patch = torch.nn.Conv2d(3, dim, kernel_size=patch, stride=patch)
+        tokens = (image // patch) ** 2
+        self.pos = torch.nn.Parameter(torch.zeros(1, tokens, dim))
+        self.blocks = torch.nn.ModuleList([VitBlock(dim, heads, mlp, 1e-6) for _ in range(layers)])
+        self.post_ln = torch.nn.LayerNorm(dim, eps=1e-6)
+        self.head = torch.nn.Linear(dim, classes)
+        g = torch.Generator().manual_seed(seed)
+        with torch.no_grad():
+            for name, prm in self.named_parameters():
+                if name.endswith("bias"):
+                    prm.zero_()
+                elif ".ln" in name or name.startswith("post_ln"):
+                    prm.fill_(1.0)
+                else:
+                    prm.copy_(torch.randn(prm.shape, generator=g) * 0.02)
+        self.to(dtype)
+
+    def forward(self, pixels):
+        x = self.patch(pixels).flatten(2).transpose(1, 2)
+        x = x + self.pos
+        for blk in self.blocks:
+            x = blk(x)
+        x = self.post_ln(x)
+        y = self.head(x.mean(dim=1))
+        return y if self.logits else y.argmax(-1)
+
+
+def vit_flops_per_image(layers=27, dim=1152, mlp=4304, tokens=256, heads=16, classes=1000, patch_k=588):
+    per_layer = 2 * tokens * dim * dim * 4 + 2 * tokens * dim * mlp * 2 + 2 * 2 * tokens * tokens * dim
+    return layers * per_layer + 2 * tokens * patch_k * dim + 2 * dim * classes

@@ -117,7 +117,8 @@ int dp_rowreduce(const dp_rowreduce_params *p, const void *in, const void *weigh
  * (nn.Linear weight, K contiguous) or [K, N] row-major when DP_B_KN.
  * bf16 × bf16 runs on tcgen05 tensor cores (TMEM accumulator, TMA loads);
  * fp32 × fp32 runs an exact-fp32 FFMA kernel.
- * Epilogue order: + bias[n] → activation → + residual[m, n] → cast to C. */
+ * Epilogue order: × alpha (0 means 1) → + bias[n] → activation →
+ * + residual[m, n] → cast to C. */
 enum { DP_B_NK = 0, DP_B_KN = 1 };
 enum {
   DP_EPI_BIAS = 1, DP_EPI_RELU = 2, DP_EPI_GELU_ERF = 4, DP_EPI_GELU_TANH = 8,
@@ -129,7 +130,8 @@ typedef struct dp_gemm_params {
   int64_t batch, stride_a, stride_b, stride_c, stride_r;
   int32_t a_dtype, b_dtype, c_dtype, r_dtype;
   int32_t b_layout, epilogue;
-  int32_t bias_dtype, reserved;
+  int32_t bias_dtype;
+  float alpha;
 } dp_gemm_params;
 int dp_gemm(const dp_gemm_params *p, const void *A, const void *B, void *C,
             const void *bias, const void *residual, void *stream);
