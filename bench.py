@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--cpu-sample", type=int, default=64, help="images in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["preprocess", "gemm", "reduce", "token"], default="preprocess",
+    ap.add_argument("--workload", choices=["preprocess", "gemm", "reduce", "token", "vit"], default="preprocess",
                     help="preprocess = the headline pipeline; gemm / reduce / token = template microbenches "
                          "and the fp32 token pipeline")
     return ap.parse_args()
@@ -151,6 +151,41 @@ def micro_reduce(args, dev):
             "roofline": {"bound": "hbm", "achieved": res["softmax"]["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": res["softmax"]["gbs"] / peak, "peak_kind": kind, "worst_frac": worst},
             "config": {"workload": "rowreduce fp32 65536x4096 (inputs 1 GiB > L2)"}}
+
+
+def micro_vit(args, dev):
+    """Preprocessing (uint8 480x640 images, batch 128) chained into the SigLIP-shaped ViT classifier, bf16."""
+    import devproc
+    from devproc_b200 import workloads
+    B = 128
+    imgs = workloads.preprocess_images(B)
+    pre = devproc.compile(workloads.vision_preprocess, imgs)
+    m = workloads.VitClassifier().eval()
+    pix = torch.zeros(B, 3, 224, 224, dtype=torch.bfloat16)
+    t0 = time.time()
+    vit = devproc.compile(m, pix)
+    compile_s = time.time() - t0
+    d_imgs = imgs.to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        x = pre.run(images=d_imgs, to_cpu=False)[0]
+        return vit.run(x, to_cpu=False)[0]
+
+    steps = min(args.steps, 20)
+    ms = time_region(step, steps, args.warmup, stream)
+    flops = workloads.vit_flops_per_image() * B
+    peak, kind = tensor_peak()
+    tf = flops / (ms / 1e3) / 1e12
+    return {"metric": "pipeline samples/sec (ViT classifier)", "value": B / (ms / 1e3), "unit": "images/s",
+            "higher_is_better": True, "dtype": "bf16", "ms_per_step": ms, "tflops": tf,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                         "peak_kind": kind},
+            "launches_per_step": len(pre.spec.records) + len(vit.spec.records), "compile_s": compile_s,
+            "arena_mib": vit.spec.arena_bytes / 2 ** 20,
+            "config": {"workload": "preprocess 128x480x640x3 u8 -> SigLIP-So400m/14-shaped ViT (27 layers, width "
+                                   "1152, 16 heads, MLP 4304) -> mean-pool -> Linear 1152->1000 -> argmax, bf16, "
+                                   "random-init weights N(0, 0.02)"}}
 
 
 def micro_token(args, dev):
@@ -297,7 +332,7 @@ def main():
     from devproc_b200 import workloads
 
     if args.workload != "preprocess":
-        fn = {"gemm": micro_gemm, "reduce": micro_reduce, "token": micro_token}[args.workload]
+        fn = {"gemm": micro_gemm, "reduce": micro_reduce, "token": micro_token, "vit": micro_vit}[args.workload]
         line = fn(args, dev)
         line.update({"n_gpus": world, "data": "synthetic"})
         if rank == 0:

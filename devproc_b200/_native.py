@@ -38,6 +38,7 @@ DP_LAYOUT_NHWC, DP_LAYOUT_NCHW = 0, 1
  DP_RED_LAYERNORM) = range(8)
 DP_B_NK, DP_B_KN = 0, 1
 DP_EPI_BIAS, DP_EPI_RELU, DP_EPI_GELU_ERF, DP_EPI_GELU_TANH, DP_EPI_RESIDUAL, DP_EPI_SILU = 1, 2, 4, 8, 16, 32
+DP_EPI_SOFTMAX = 64
 
 DP_REGION_MAX_OPERANDS, DP_REGION_MAX_RANK, DP_REGION_MAX_INSTR = 8, 6, 64
 DP_REGION_MAX_CONST, DP_REGION_MAX_REGS = 32, 8
@@ -75,7 +76,9 @@ class GemmParams(ctypes.Structure):
                 ("stride_c", ctypes.c_int64), ("stride_r", ctypes.c_int64),
                 ("a_dtype", ctypes.c_int32), ("b_dtype", ctypes.c_int32), ("c_dtype", ctypes.c_int32),
                 ("r_dtype", ctypes.c_int32), ("b_layout", ctypes.c_int32), ("epilogue", ctypes.c_int32),
-                ("bias_dtype", ctypes.c_int32), ("alpha", ctypes.c_float)]
+                ("bias_dtype", ctypes.c_int32), ("alpha", ctypes.c_float),
+                ("batch2", ctypes.c_int64), ("stride_a2", ctypes.c_int64), ("stride_b2", ctypes.c_int64),
+                ("stride_c2", ctypes.c_int64), ("stride_r2", ctypes.c_int64)]
 
 
 class RegionDesc(ctypes.Structure):

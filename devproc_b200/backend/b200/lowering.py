@@ -227,6 +227,22 @@ class Lowerer:
             return v
         return self.copy_view(v, value.name + "_c")
 
+    def padded_rows(self, value: Value, K: int) -> View:
+        """[rows, K] copy of ``value`` (leading dims flattened) with rows Kp = ⌈K/8⌉·8 apart."""
+        t = value.type
+        rows = _prod(t.shape[:-1])
+        Kp = (K + 7) // 8 * 8
+        src = self.views[value.name]
+        flat = view_reshape(src.shape, src.strides, (rows, K))
+        if flat is None:
+            src = self.contiguous(value)
+            flat = contiguous_strides((rows, K))
+        out = View(self.new_buffer("arena", t.dtype, (rows, Kp), value.name + "_pad"), (rows, K), (Kp, 1))
+        rb = RegionBuilder((rows, K))
+        rb.store(out, rb.load(View(src.buf, (rows, K), flat, src.offset)))
+        self.emit_region(rb, f"pad {value.name} K{K}->{Kp}")
+        return out
+
     def copy_view(self, v: View, name: str) -> View:
         out = View(self.new_buffer("arena", v.buf.dtype, v.shape, name), v.shape, contiguous_strides(v.shape))
         rb = RegionBuilder(out.shape)
@@ -411,13 +427,18 @@ class Lowerer:
     def lower_gemm(self, op: Op) -> None:
         p = N.GemmParams()
         if op.name == "linear":
-            x = self.contiguous(op.inputs[0])
-            w = self.contiguous(op.inputs[1])
-            K = x.shape[-1]
+            K = op.inputs[0].type.shape[-1]
+            if op.inputs[0].type.dtype == "bfloat16" and K % 8:
+                # tensor-core operands need 16-byte row strides: rows padded to Kp
+                x = self.padded_rows(op.inputs[0], K)
+                w = self.padded_rows(op.inputs[1], K)
+            else:
+                x = self.contiguous(op.inputs[0])
+                w = self.contiguous(op.inputs[1])
             M = _prod(x.shape[:-1])
             Nn = w.shape[0]
             p.M, p.N, p.K = M, Nn, K
-            p.lda, p.ldb = K, K
+            p.lda, p.ldb = x.strides[-2] if len(x.shape) > 1 else K, w.strides[0]
             p.b_layout = N.DP_B_NK
             p.batch, p.stride_a, p.stride_b = 1, 0, 0
             a_dtype, b_dtype = x.buf.dtype, w.buf.dtype
@@ -620,47 +641,83 @@ class Lowerer:
         if tq.dtype != tk.dtype or tq.dtype != tv.dtype or tq.dtype not in ("bfloat16", "float32"):
             raise CompilationError("sdpa: q, k, v must share dtype bf16 or fp32")
         g = Hq // Hk
-        qv, kv = self.contiguous(q), self.contiguous(k)
-        vv = self.views[v.name]
-        # V as [B·Hk, Dv, S] (the GEMM's B operand is K-major)
-        vshape = (B, Hk, S, Dv)
-        vst = view_reshape(vv.shape, vv.strides, vshape)
-        if vst is None:
-            vv = self.contiguous(v)
-            vst = contiguous_strides(vshape)
-        vt = self.copy_view(View(vv.buf, (B, Hk, Dv, S), (vst[0], vst[1], vst[3], vst[2]), vv.offset),
-                            v.name + "_t")
         dt = tq.dtype
-        scores = View(self.new_buffer("arena", "float32", (B * Hk, g * L, S), op.outputs[0].name + "_s"),
-                      (B * Hk, g * L, S), contiguous_strides((B * Hk, g * L, S)))
+
+        def operand(value: Value, rows_shape):
+            """(view, row stride, outer batch stride, inner batch stride) of a
+            [B, H, rows, D] operand read in place when its strides allow it."""
+            vw = self.views[value.name]
+            st = view_reshape(vw.shape, vw.strides, rows_shape)
+            if st is None or st[3] != 1 or any(x % 8 for x in st[:3]):
+                vw = self.contiguous(value)
+                st = view_reshape(vw.shape, vw.strides, rows_shape) or contiguous_strides(rows_shape)
+            return vw, st
+
+        if g == 1:
+            qv, qst = operand(q, (B, Hq, L, D))
+            q_b, q_b2, q_ld = qst[0], qst[1], qst[2]
+            rows_q, batch, batch2 = L, B * Hq, Hq
+        else:
+            # query heads of one group stacked as one (g·L)-row operand
+            qv = self.contiguous(q)
+            q_b, q_b2, q_ld = Hq * L * D, g * L * D, D
+            rows_q, batch, batch2 = g * L, B * Hk, Hk
+        kv, kst = operand(k, (B, Hk, S, D))
+        # V is read in place as the GEMM's [K = keys, N = Dv] operand (N contiguous)
+        vv, vst = operand(v, (B, Hk, S, Dv))
+        # bf16 rows of at most 256 keys: the score GEMM's epilogue computes the row
+        # softmax itself (one tensor-core tile holds a whole row) and writes bf16
+        # probabilities; otherwise fp32 scores go through a separate row softmax.
+        fused = dt == "bfloat16" and S <= 256 and S % 8 == 0
+        probs = View(self.new_buffer("arena", dt, (batch, rows_q, S), op.outputs[0].name + "_p"),
+                     (batch, rows_q, S), contiguous_strides((batch, rows_q, S)))
+        if fused:
+            scores = probs
+        else:
+            scores = View(self.new_buffer("arena", "float32", (batch, rows_q, S), op.outputs[0].name + "_s"),
+                          (batch, rows_q, S), contiguous_strides((batch, rows_q, S)))
         p = N.GemmParams()
-        p.M, p.N, p.K = g * L, S, D
-        p.lda, p.ldb, p.ldc = D, D, S
-        p.batch, p.stride_a, p.stride_b, p.stride_c = B * Hk, g * L * D, S * D, g * L * S
+        p.M, p.N, p.K = rows_q, S, D
+        p.lda, p.ldb, p.ldc = q_ld, kst[2], S
+        p.batch, p.batch2 = batch, batch2
+        p.stride_a, p.stride_a2 = q_b, q_b2
+        p.stride_b, p.stride_b2 = kst[0], kst[1]
+        p.stride_c, p.stride_c2 = batch2 * rows_q * S, rows_q * S
         p.a_dtype = p.b_dtype = N.DTYPE_CODE[dt]
-        p.c_dtype = N.DP_F32
+        p.c_dtype = N.DTYPE_CODE[dt] if fused else N.DP_F32
         p.b_layout = N.DP_B_NK
         p.alpha = float(op.attr("scale"))
+        p.epilogue = N.DP_EPI_SOFTMAX if fused else 0
         self.emit(N.DP_K_GEMM, [qv.buf, kv.buf, scores.buf, None, None], p,
-                  f"gemm attn-scores b{B * Hk} M{g * L} N{S} K{D} {dt}", 2 * B * Hq * L * S * D,
-                  qv.buf.nbytes + kv.buf.nbytes + scores.buf.nbytes)
-        probs = View(self.new_buffer("arena", dt, (B * Hk, g * L, S), op.outputs[0].name + "_p"),
-                     (B * Hk, g * L, S), contiguous_strides((B * Hk, g * L, S)))
-        r = N.RowReduceParams()
-        r.kind, r.in_dtype, r.out_dtype = N.DP_RED_SOFTMAX, N.DP_F32, N.DTYPE_CODE[dt]
-        r.rows, r.cols, r.in_row_stride, r.out_row_stride = B * Hq * L, S, S, S
-        self.emit(N.DP_K_ROWREDUCE, [scores.buf, None, None, probs.buf], r,
-                  f"rowreduce attn-softmax {B * Hq * L}x{S}", 0, scores.buf.nbytes + probs.buf.nbytes)
-        out = self.new_value_view(op.outputs[0])
+                  f"gemm attn-scores{'+softmax' if fused else ''} b{batch} M{rows_q} N{S} K{D} {dt}",
+                  2 * B * Hq * L * S * D, qv.buf.nbytes + kv.buf.nbytes + scores.buf.nbytes)
+        if not fused:
+            r = N.RowReduceParams()
+            r.kind, r.in_dtype, r.out_dtype = N.DP_RED_SOFTMAX, N.DP_F32, N.DTYPE_CODE[dt]
+            r.rows, r.cols, r.in_row_stride, r.out_row_stride = B * Hq * L, S, S, S
+            self.emit(N.DP_K_ROWREDUCE, [scores.buf, None, None, probs.buf], r,
+                      f"rowreduce attn-softmax {B * Hq * L}x{S}", 0, scores.buf.nbytes + probs.buf.nbytes)
         p2 = N.GemmParams()
-        p2.M, p2.N, p2.K = g * L, Dv, S
-        p2.lda, p2.ldb, p2.ldc = S, S, Dv
-        p2.batch, p2.stride_a, p2.stride_b, p2.stride_c = B * Hk, g * L * S, Dv * S, g * L * Dv
+        p2.M, p2.N, p2.K = rows_q, Dv, S
+        p2.lda, p2.ldb = S, vst[2]
+        p2.batch, p2.batch2 = batch, batch2
+        p2.stride_a, p2.stride_a2 = batch2 * rows_q * S, rows_q * S
+        p2.stride_b, p2.stride_b2 = vst[0], vst[1]
         p2.a_dtype = p2.b_dtype = p2.c_dtype = N.DTYPE_CODE[dt]
-        p2.b_layout = N.DP_B_NK
-        self.emit(N.DP_K_GEMM, [probs.buf, vt.buf, out.buf, None, None], p2,
-                  f"gemm attn-values b{B * Hk} M{g * L} N{Dv} K{S} {dt}", 2 * B * Hq * L * S * Dv,
-                  probs.buf.nbytes + vt.buf.nbytes + out.buf.nbytes)
+        p2.b_layout = N.DP_B_KN
+        out_v = op.outputs[0]
+        if g == 1 and len(tq.shape) == 4:
+            # Store token-major [B, L, Hq, Dv]; the value is its [B, Hq, L, Dv] view, so the
+            # usual transpose(1, 2).reshape(B, L, Hq·Dv) that follows costs nothing.
+            buf = self.new_buffer("arena", dt, (B, L, Hq, Dv), out_v.name)
+            self.views[out_v.name] = View(buf, (B, Hq, L, Dv), (L * Hq * Dv, Dv, Hq * Dv, 1))
+            p2.ldc, p2.stride_c, p2.stride_c2 = Hq * Dv, L * Hq * Dv, Dv
+        else:
+            buf = self.new_value_view(out_v).buf
+            p2.ldc, p2.stride_c, p2.stride_c2 = Dv, Hk * rows_q * Dv, rows_q * Dv
+        self.emit(N.DP_K_GEMM, [probs.buf, vv.buf, buf, None, None], p2,
+                  f"gemm attn-values b{batch} M{rows_q} N{Dv} K{S} {dt}", 2 * B * Hq * L * S * Dv,
+                  probs.buf.nbytes + vv.buf.nbytes + buf.nbytes)
 
     # ------------------------------------------------------------ embedding
     def lower_embedding(self, op: Op) -> None:

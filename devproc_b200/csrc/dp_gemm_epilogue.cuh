@@ -21,7 +21,12 @@ struct Epilogue {
 
   __device__ __forceinline__ Epilogue(const dp_gemm_params &p_, void *C_, const void *bias_, const void *res_,
                                       int64_t batch)
-      : p(p_), C(C_), bias(bias_), res(res_), c_off(batch * p_.stride_c), r_off(batch * p_.stride_r) {}
+      : p(p_), C(C_), bias(bias_), res(res_) {
+    const int64_t b2 = p_.batch2 > 1 ? p_.batch2 : 1;
+    const int64_t zo = batch / b2, zi = batch - zo * b2;
+    c_off = zo * p_.stride_c + zi * p_.stride_c2;
+    r_off = zo * p_.stride_r + zi * p_.stride_r2;
+  }
 
   __device__ __forceinline__ float apply(int64_t m, int64_t n, float v) const {
     if (p.alpha != 0.0f) v *= p.alpha;

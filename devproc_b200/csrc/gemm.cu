@@ -1,8 +1,8 @@
 // GEMM entry point: validates the request and picks the kernel.
 // bf16 × bf16 goes to the tcgen05 tensor-core kernel when its TMA alignment
-// rules hold (row strides and K multiples of 8 elements, 16-byte aligned
-// bases); everything else (fp32, or bf16 with odd strides) runs the FFMA
-// kernel.  Both share one epilogue.
+// rules hold (row and batch strides multiples of 8 elements, 16-byte aligned
+// bases), with B either [N, K] or [K, N]; everything else (fp32, or bf16 with
+// odd strides) runs the FFMA kernel.  Both share one epilogue.
 #include "dp_gemm_epilogue.cuh"
 
 namespace dp {
@@ -25,12 +25,19 @@ int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C, 
   const int acts = !!(p.epilogue & DP_EPI_RELU) + !!(p.epilogue & DP_EPI_GELU_ERF) +
                    !!(p.epilogue & DP_EPI_GELU_TANH) + !!(p.epilogue & DP_EPI_SILU);
   DP_REQUIRE(acts <= 1, DP_ERR_ARG, "gemm: at most one activation");
+  DP_REQUIRE(p.batch2 <= 1 || p.batch % p.batch2 == 0, DP_ERR_SHAPE, "gemm: batch must be a multiple of batch2");
+  if (p.epilogue & DP_EPI_SOFTMAX) {
+    DP_REQUIRE(p.epilogue == DP_EPI_SOFTMAX, DP_ERR_ARG, "gemm: the softmax epilogue takes no other epilogue flag");
+    DP_REQUIRE(p.N <= 256, DP_ERR_UNSUPPORTED, "gemm: the softmax epilogue needs N <= 256");
+  }
   if (p.a_dtype == DP_BF16 && p.b_dtype == DP_BF16) {
     auto al = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
-    const bool tc_ok = p.b_layout == DP_B_NK && p.K % 8 == 0 && p.lda % 8 == 0 && p.ldb % 8 == 0 &&
-                       p.stride_a % 8 == 0 && p.stride_b % 8 == 0 && al(A) && al(B);
+    const bool tc_ok = p.lda % 8 == 0 && p.ldb % 8 == 0 && p.stride_a % 8 == 0 &&
+                       p.stride_b % 8 == 0 && p.stride_a2 % 8 == 0 && p.stride_b2 % 8 == 0 && al(A) && al(B);
     if (tc_ok) return launch_gemm_tc(p, A, B, C, bias, res, s);
   }
+  DP_REQUIRE(!(p.epilogue & DP_EPI_SOFTMAX), DP_ERR_UNSUPPORTED,
+             "gemm: the softmax epilogue runs only on the tensor-core path (bf16, 16-byte aligned operands)");
   return launch_gemm_simt(p, A, B, C, bias, res, s);
 }
 

@@ -44,8 +44,12 @@ __global__ void __launch_bounds__(kThreads) sgemm_kernel(dp_gemm_params p, const
   __shared__ __align__(16) float As[2][BK][BM + 4];
   __shared__ __align__(16) float Bs[2][BK][BN + 4];
   const int64_t bz = blockIdx.z;
-  A += bz * p.stride_a;
-  B += bz * p.stride_b;
+  {
+    const int64_t b2 = p.batch2 > 1 ? p.batch2 : 1;
+    const int64_t zo = bz / b2, zi = bz - zo * b2;
+    A += zo * p.stride_a + zi * p.stride_a2;
+    B += zo * p.stride_b + zi * p.stride_b2;
+  }
   const int tid = threadIdx.x;
   const int64_t m0 = (int64_t)blockIdx.y * BM, n0 = (int64_t)blockIdx.x * BN;
   const int tx = tid % 16, ty = tid / 16;
@@ -143,8 +147,10 @@ int launch_typed(const dp_gemm_params &p, const void *A, const void *B, void *C,
   const int esz = sizeof(TA);
   auto al = [](const void *q, int a) { return reinterpret_cast<uintptr_t>(q) % a == 0; };
   const int vbytes = 4 * esz;
-  const bool a_vec = al(A, vbytes) && (p.lda * esz) % vbytes == 0 && (p.stride_a * esz) % vbytes == 0;
-  const bool b_vec = al(B, vbytes) && (p.ldb * esz) % vbytes == 0 && (p.stride_b * esz) % vbytes == 0;
+  const bool a_vec = al(A, vbytes) && (p.lda * esz) % vbytes == 0 && (p.stride_a * esz) % vbytes == 0 &&
+                     (p.stride_a2 * esz) % vbytes == 0;
+  const bool b_vec = al(B, vbytes) && (p.ldb * esz) % vbytes == 0 && (p.stride_b * esz) % vbytes == 0 &&
+                     (p.stride_b2 * esz) % vbytes == 0;
   dim3 grid((unsigned)((p.N + BN - 1) / BN), (unsigned)((p.M + BM - 1) / BM), (unsigned)p.batch);
   if (p.b_layout == DP_B_NK)
     sgemm_kernel<TA, TB, true><<<grid, kThreads, 0, s>>>(p, static_cast<const TA *>(A),

@@ -44,23 +44,30 @@ constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kEpiBytes + 1024; 
 struct Shape {
   int M, N, K, batch;
   int tiles_m, tiles_n, tiles_per_batch, num_tiles, k_blocks;
+  int batch2;        // inner batch count (1 = single-level batch)
+  int b_mn;          // B is [K, N] (N contiguous) instead of [N, K]
   int tma_store;     // output written by TMA tensor stores from swizzled chunks
   int tma_residual;  // residual read by TMA into the same chunks (same dtype as C)
   int c_bytes;       // element size of C
 };
 
 // ------------------------------------------------------------------ PTX
-__device__ __forceinline__ void tma_load_3d(void *smem, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+// Operand maps are 4-D: (cols, rows, inner batch, outer batch); ``z`` is the
+// flat batch index, split here by the inner batch count ``b2``.
+__device__ __forceinline__ void tma_load_4d(void *smem, const CUtensorMap *map, int x, int y, int z, int b2,
+                                            uint64_t *bar) {
+  const int zo = z / b2, zi = z - zo * b2;
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(smem_u32(smem)),
-      "l"(map), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(smem_u32(smem)),
+      "l"(map), "r"(x), "r"(y), "r"(zi), "r"(zo), "r"(smem_u32(bar))
       : "memory");
 }
 
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *smem, int x, int y, int z) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(map),
-               "r"(x), "r"(y), "r"(z), "r"(smem_u32(smem))
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *smem, int x, int y, int z, int b2) {
+  const int zo = z / b2, zi = z - zo * b2;
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(map),
+               "r"(x), "r"(y), "r"(zi), "r"(zo), "r"(smem_u32(smem))
                : "memory");
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
@@ -87,9 +94,24 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, both K-major.
-__host__ __device__ constexpr uint32_t instr_desc(int m, int n) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+// Shared-memory descriptor of an MN-major operand (N contiguous), 128-byte
+// swizzle: each K row holds 64 N elements (128 B), 8-row groups 1024 B apart
+// (SBO), 64-element N chunks 8 KB apart (LBO, one TMA box each).
+__device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)(8192 >> 4) << 16;          // LBO: next 64-element N chunk
+  d |= (uint64_t)(1024 >> 4) << 32;          // SBO: next 8 K rows
+  d |= (uint64_t)1 << 46;                    // version
+  d |= (uint64_t)2 << 61;                    // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, A K-major,
+// B K-major (b_mn = 0) or MN-major (b_mn = 1).
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n, int b_mn = 0) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
 }
 
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -264,15 +286,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t *sa = smem + st * kStageBytes;
           uint8_t *sb = sa + kTileABytes;
           mbar_arrive_expect_tx(&full[st], kStageBytes);
-          tma_load_3d(sa, &map_a, kb * BK, tm * BM, b, &full[st]);
-          tma_load_3d(sb, &map_b, kb * BK, tn * BN, b, &full[st]);
+          tma_load_4d(sa, &map_a, kb * BK, tm * BM, b, s.batch2, &full[st]);
+          if (s.b_mn) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_4d(sb + j * 8192, &map_b, tn * BN + j * 64, kb * BK, b, s.batch2, &full[st]);
+          } else {
+            tma_load_4d(sb, &map_b, kb * BK, tn * BN, b, s.batch2, &full[st]);
+          }
         }
       }
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------- MMA issuer
-      const uint32_t idesc = instr_desc(BM, BN);
+      const uint32_t idesc = instr_desc(BM, BN, s.b_mn);
       int it = 0, local = 0;
       for (int t = blockIdx.x; t < s.num_tiles && !aborted(flag); t += gridDim.x, ++local) {
         const int a = local & 1;
@@ -290,8 +318,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = smem_u32(smem + st * kStageBytes);
           const uint32_t sb = sa + kTileABytes;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_bf16(tmem_d, smem_desc(sa + k * 32), smem_desc(sb + k * 32), idesc, (kb | k) != 0);
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t bdesc = s.b_mn ? smem_desc_mn(sb + k * 2048) : smem_desc(sb + k * 32);
+            mma_bf16(tmem_d, smem_desc(sa + k * 32), bdesc, idesc, (kb | k) != 0);
+          }
           mma_commit(&empty[st]);  // stage is free once these MMAs have read it
         }
         if (!ok) break;
@@ -317,6 +347,33 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int64_t m = (int64_t)tm * BM + row;
       dp::Epilogue ep(p, C, bias, res, b);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+      // Row softmax epilogue: this thread's row is all N (≤ BN) columns of
+      // the accumulator, so max and sum need no cross-thread reduction.
+      float sm_max = 0.0f, sm_inv = 1.0f;
+      const bool softmax = (p.epilogue & DP_EPI_SOFTMAX) != 0;
+      if (softmax) {
+        const float alpha = p.alpha != 0.0f ? p.alpha : 1.0f;
+        float mx = -INFINITY;
+#pragma unroll 1
+        for (int c = 0; c < BN / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c * 16, r);
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if ((int64_t)tn * BN + c * 16 + e < s.N) mx = fmaxf(mx, __uint_as_float(r[e]) * alpha);
+        }
+        float sum = 0.0f;
+#pragma unroll 1
+        for (int c = 0; c < BN / 16; ++c) {
+          uint32_t r[16];
+          tmem_ld16(tbase + c * 16, r);
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            if ((int64_t)tn * BN + c * 16 + e < s.N) sum += __expf(__uint_as_float(r[e]) * alpha - mx);
+        }
+        sm_max = mx;
+        sm_inv = 1.0f / sum;
+      }
       if (s.tma_store) {
         bool stop = false;
 #pragma unroll 1
@@ -329,7 +386,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (s.tma_residual) {
             if (lane == 0) {
               mbar_arrive_expect_tx(&res_bar[q], kEpiBufBytes);
-              tma_load_3d(buf, &map_r, (int)n0, tm * BM + q * 32, b, &res_bar[q]);
+              tma_load_4d(buf, &map_r, (int)n0, tm * BM + q * 32, b, s.batch2, &res_bar[q]);
             }
             const bool ok = wait_or_abort(&res_bar[q], res_phase, 340 + q, flag);
             res_phase ^= 1u;
@@ -350,7 +407,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int e = 0; e < 16; ++e) x[e] *= p.alpha;
             }
-            if (p.epilogue) epi16(x, nb, s.N, p.epilogue, bias, p.bias_dtype);
+            if (softmax) {
+#pragma unroll
+              for (int e = 0; e < 16; ++e) x[e] = __expf(x[e] - sm_max) * sm_inv;
+            } else if (p.epilogue) {
+              epi16(x, nb, s.N, p.epilogue, bias, p.bias_dtype);
+            }
             if ((p.epilogue & DP_EPI_RESIDUAL) && !s.tma_residual) {
 #pragma unroll
               for (int e = 0; e < 16; ++e)
@@ -415,7 +477,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_3d(&map_c, buf, (int)n0, tm * BM + q * 32, b);
+            tma_store_4d(&map_c, buf, (int)n0, tm * BM + q * 32, b, s.batch2);
             bulk_commit();
           }
         }
@@ -472,21 +534,27 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// rows × cols matrix of ``dt`` (row stride ld elements), batch planes
-// ``bstride`` apart, boxes of box_cols × box_rows with 128-byte swizzle.
-int make_map(CUtensorMap *map, const void *base, int dt, int64_t rows, int64_t cols, int64_t ld, int64_t batch,
-             int64_t bstride, int box_cols, int box_rows) {
+// rows × cols matrix of ``dt`` (row stride ld elements) in a two-level batch:
+// outer count ``b1`` with stride ``s1``, inner count ``b2`` with stride ``s2``
+// (elements); boxes of box_cols × box_rows with 128-byte swizzle.
+int make_map(CUtensorMap *map, const void *base, int dt, int64_t rows, int64_t cols, int64_t ld, int64_t b1,
+             int64_t s1, int64_t b2, int64_t s2, int box_cols, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   DP_REQUIRE(fn != nullptr, DP_ERR_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
   const int eb = dp::dtype_bytes(dt);
   CUtensorMapDataType t = dt == DP_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                           : dt == DP_F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
-  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)(ld * eb), (cuuint64_t)((batch > 1 ? bstride : rows * ld) * eb)};
-  cuuint32_t box[3] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = fn(map, t, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  // Unused batch levels get a harmless stride (one matrix further on).
+  const int64_t mat = rows * ld;
+  if (b2 <= 1) s2 = mat;
+  if (b1 <= 1) s1 = (b2 > 1 ? b2 * s2 : mat);
+  cuuint64_t dims[4] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)(b2 > 1 ? b2 : 1),
+                        (cuuint64_t)(b1 > 1 ? b1 : 1)};
+  cuuint64_t strides[3] = {(cuuint64_t)(ld * eb), (cuuint64_t)(s2 * eb), (cuuint64_t)(s1 * eb)};
+  cuuint32_t box[4] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, t, 4, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   DP_REQUIRE(r == CUDA_SUCCESS, DP_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return DP_OK;
@@ -502,21 +570,27 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   CUtensorMap ma, mb, mc, mr;
   memset(&mc, 0, sizeof(mc));
   memset(&mr, 0, sizeof(mr));
-  int st = make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, p.batch, p.stride_a, BK, BM);
+  const int64_t b2 = p.batch2 > 1 ? p.batch2 : 1;
+  const int64_t b1 = p.batch / b2;
+  int st = make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, b1, p.stride_a, b2, p.stride_a2, BK, BM);
   if (st != DP_OK) return st;
-  st = make_map(&mb, B, DP_BF16, p.N, p.K, p.ldb, p.batch, p.stride_b, BK, BN);
+  const bool b_mn = p.b_layout == DP_B_KN;
+  if (b_mn)  // [K, N], N contiguous: boxes of 64 N × 64 K
+    st = make_map(&mb, B, DP_BF16, p.K, p.N, p.ldb, b1, p.stride_b, b2, p.stride_b2, 64, BK);
+  else
+    st = make_map(&mb, B, DP_BF16, p.N, p.K, p.ldb, b1, p.stride_b, b2, p.stride_b2, BK, BN);
   if (st != DP_OK) return st;
   const int cb = dtype_bytes(p.c_dtype);
   auto al16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
-  const bool tma_store = (p.ldc * cb) % 16 == 0 && (p.batch == 1 || (p.stride_c * cb) % 16 == 0) && al16(C) &&
-                         (cb == 4 || cb == 2);
+  const bool tma_store = (p.ldc * cb) % 16 == 0 && (p.batch == 1 || (p.stride_c * cb) % 16 == 0) &&
+                         (b2 == 1 || (p.stride_c2 * cb) % 16 == 0) && al16(C) && (cb == 4 || cb == 2);
   bool tma_res = false;
   if (tma_store) {
-    st = make_map(&mc, C, p.c_dtype, p.M, p.N, p.ldc, p.batch, p.stride_c, 128 / cb, 32);
+    st = make_map(&mc, C, p.c_dtype, p.M, p.N, p.ldc, b1, p.stride_c, b2, p.stride_c2, 128 / cb, 32);
     if (st != DP_OK) return st;
     if ((p.epilogue & DP_EPI_RESIDUAL) && p.r_dtype == p.c_dtype && (p.ldr * cb) % 16 == 0 &&
-        (p.batch == 1 || (p.stride_r * cb) % 16 == 0) && al16(res)) {
-      st = make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, p.batch, p.stride_r, 128 / cb, 32);
+        (p.batch == 1 || (p.stride_r * cb) % 16 == 0) && (b2 == 1 || (p.stride_r2 * cb) % 16 == 0) && al16(res)) {
+      st = make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, b1, p.stride_r, b2, p.stride_r2, 128 / cb, 32);
       if (st != DP_OK) return st;
       tma_res = true;
     }
@@ -531,6 +605,10 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   s.tiles_per_batch = s.tiles_m * s.tiles_n;
   s.num_tiles = s.tiles_per_batch * s.batch;
   s.k_blocks = (int)((p.K + BK - 1) / BK);
+  DP_REQUIRE(tma_store || !(p.epilogue & DP_EPI_SOFTMAX), DP_ERR_UNSUPPORTED,
+             "gemm: the softmax epilogue needs a 16-byte aligned C with 16-byte row strides");
+  s.batch2 = (int)b2;
+  s.b_mn = b_mn ? 1 : 0;
   s.tma_store = tma_store ? 1 : 0;
   s.tma_residual = tma_res ? 1 : 0;
   s.c_bytes = cb;

@@ -118,6 +118,48 @@ __global__ void __launch_bounds__(kThreads) region_kernel(const dp_region_desc d
   }
 }
 
+
+// Tiled transpose for pure copies whose output's innermost dim is strided in
+// the input (e.g. a [.., S, D] → [.., D, S] relayout): 32×32 tiles through
+// shared memory, reads coalesced along the input's unit-stride dim, writes
+// coalesced along the output's innermost dim.  Remaining dims are decomposed
+// from blockIdx.z once per block.
+struct TDims {
+  int rank;  // of the collapsed iteration space
+  int jdim;  // dim with unit input stride
+  int64_t shape[DP_REGION_MAX_RANK];
+  int64_t in_stride[DP_REGION_MAX_RANK];
+  int64_t out_stride[DP_REGION_MAX_RANK];
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) transpose_copy_kernel(TDims d, const T *__restrict__ in, T *__restrict__ out) {
+  __shared__ T tile[32][33];
+  const int last = d.rank - 1;
+  const int64_t j0 = (int64_t)blockIdx.y * 32, l0 = (int64_t)blockIdx.x * 32;
+  // offsets of the other dims
+  int64_t z = blockIdx.z, in_off = 0, out_off = 0;
+  for (int k = last; k >= 0; --k) {
+    if (k == last || k == d.jdim) continue;
+    const int64_t c = z % d.shape[k];
+    z /= d.shape[k];
+    in_off += c * d.in_stride[k];
+    out_off += c * d.out_stride[k];
+  }
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 × 8
+  // read: lanes walk j (unit stride in the input)
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t j = j0 + tx, l = l0 + r;
+    if (j < d.shape[d.jdim] && l < d.shape[last]) tile[r][tx] = in[in_off + j + l * d.in_stride[last]];
+  }
+  __syncthreads();
+  // write: lanes walk the output's innermost dim
+  for (int r = ty; r < 32; r += 8) {
+    const int64_t j = j0 + r, l = l0 + tx;
+    if (j < d.shape[d.jdim] && l < d.shape[last]) out[out_off + j * d.out_stride[d.jdim] + l] = tile[tx][r];
+  }
+}
+
 }  // namespace dpk_region
 
 namespace dp {
@@ -167,6 +209,40 @@ int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t 
         } else {
           return set_error(DP_ERR_ARG, where + " unknown opcode " + std::to_string(op));
         }
+    }
+  }
+  // Pure relayout copies (one load, one store, same element size) whose
+  // innermost output dim is strided in the input go to the tiled transpose.
+  if (d.n_in == 1 && d.n_out == 1 && d.n_instr == 2 && d.rank >= 2 &&
+      dtype_bytes(d.dtype[0]) == dtype_bytes(d.dtype[1]) && d.dtype[0] == d.dtype[1] &&
+      (d.instr[0] & 0xff) == DP_OP_LOAD && (d.instr[1] & 0xff) == DP_OP_STORE &&
+      d.stride[1][d.rank - 1] == 1 && d.stride[0][d.rank - 1] != 1) {
+    int jdim = -1;
+    for (int k = 0; k < d.rank - 1; ++k)
+      if (d.stride[0][k] == 1) jdim = k;
+    if (jdim >= 0) {
+      TDims t;
+      t.rank = d.rank;
+      t.jdim = jdim;
+      int64_t zcount = 1;
+      for (int k = 0; k < d.rank; ++k) {
+        t.shape[k] = d.shape[k];
+        t.in_stride[k] = d.stride[0][k];
+        t.out_stride[k] = d.stride[1][k];
+        if (k != jdim && k != d.rank - 1) zcount *= d.shape[k];
+      }
+      const int64_t gx = (d.shape[d.rank - 1] + 31) / 32, gy = (d.shape[jdim] + 31) / 32;
+      if (gx < (1ll << 31) && gy < 65536 && zcount < 65536) {
+        dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)zcount);
+        switch (dtype_bytes(d.dtype[0])) {
+          case 1: transpose_copy_kernel<uint8_t><<<grid, 256, 0, s>>>(t, (const uint8_t *)ops[0], (uint8_t *)ops[1]); break;
+          case 2: transpose_copy_kernel<uint16_t><<<grid, 256, 0, s>>>(t, (const uint16_t *)ops[0], (uint16_t *)ops[1]); break;
+          case 4: transpose_copy_kernel<uint32_t><<<grid, 256, 0, s>>>(t, (const uint32_t *)ops[0], (uint32_t *)ops[1]); break;
+          default: transpose_copy_kernel<uint64_t><<<grid, 256, 0, s>>>(t, (const uint64_t *)ops[0], (uint64_t *)ops[1]); break;
+        }
+        DP_CHECK_CUDA(cudaGetLastError());
+        return DP_OK;
+      }
     }
   }
   bool fast = d.rank == 1;

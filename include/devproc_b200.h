@@ -122,7 +122,11 @@ int dp_rowreduce(const dp_rowreduce_params *p, const void *in, const void *weigh
 enum { DP_B_NK = 0, DP_B_KN = 1 };
 enum {
   DP_EPI_BIAS = 1, DP_EPI_RELU = 2, DP_EPI_GELU_ERF = 4, DP_EPI_GELU_TANH = 8,
-  DP_EPI_RESIDUAL = 16, DP_EPI_SILU = 32
+  DP_EPI_RESIDUAL = 16, DP_EPI_SILU = 32,
+  /* Row softmax of alpha·(A·Bᵀ) over the N columns (exp via __expf); needs
+   * N ≤ 256 (one tensor-core tile holds a whole row), bf16 operands on the
+   * tensor-core path and no other epilogue flag. */
+  DP_EPI_SOFTMAX = 64
 };
 typedef struct dp_gemm_params {
   int64_t M, N, K;
@@ -132,6 +136,9 @@ typedef struct dp_gemm_params {
   int32_t b_layout, epilogue;
   int32_t bias_dtype;
   float alpha;
+  /* Two-level batches (e.g. [batch, heads]): when batch2 > 1, matrix z of
+   * the batch sits at (z / batch2) * stride_x + (z % batch2) * stride_x2. */
+  int64_t batch2, stride_a2, stride_b2, stride_c2, stride_r2;
 } dp_gemm_params;
 int dp_gemm(const dp_gemm_params *p, const void *A, const void *B, void *C,
             const void *bias, const void *residual, void *stream);

@@ -378,6 +378,46 @@ def test_gemm_bf16_epilogues_and_batch(cuda):
     assert torch.allclose(c.float(), ref, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("M,Nn,K", [(256, 72, 256), (300, 500, 200), (128, 256, 64), (64, 1000, 136)])
+def test_gemm_bf16_b_kn_tensor_core(cuda, M, Nn, K):
+    """B as [K, N] (N contiguous, MN-major on the tensor cores), two-level batch."""
+    g = torch.Generator().manual_seed(M * 7 + Nn)
+    a = torch.randn(2, 3, M, K, generator=g).bfloat16()
+    b = torch.randn(2, 3, K, Nn, generator=g).bfloat16()
+    c = torch.empty(2, 3, M, Nn, dtype=torch.float32, device=cuda)
+    p = N.GemmParams()
+    p.M, p.N, p.K, p.lda, p.ldb, p.ldc = M, Nn, K, K, Nn, Nn
+    p.batch, p.batch2 = 6, 3
+    p.stride_a, p.stride_a2 = 3 * M * K, M * K
+    p.stride_b, p.stride_b2 = 3 * K * Nn, K * Nn
+    p.stride_c, p.stride_c2 = 3 * M * Nn, M * Nn
+    p.a_dtype = p.b_dtype = N.DP_BF16
+    p.c_dtype = N.DP_F32
+    p.b_layout = N.DP_B_KN
+    N.gemm(p, a.to(cuda), b.to(cuda), c)
+    _sync()
+    ref = a.float() @ b.float()
+    assert torch.allclose(c.cpu(), ref, rtol=1e-3, atol=1e-3 * K ** 0.5)
+
+
+def test_gemm_softmax_epilogue(cuda):
+    """Row softmax of alpha·A·Bᵀ fused into the tensor-core epilogue, bf16 out, N < 256 masked."""
+    g = torch.Generator().manual_seed(21)
+    for (M, Nn, K) in [(256, 256, 72), (300, 200, 64)]:
+        a = torch.randn(3, M, K, generator=g).bfloat16()
+        b = torch.randn(3, Nn, K, generator=g).bfloat16()
+        c = torch.empty(3, M, Nn, dtype=torch.bfloat16, device=cuda)
+        p = N.GemmParams()
+        p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, Nn, K, K, K, Nn, 3
+        p.stride_a, p.stride_b, p.stride_c = M * K, Nn * K, M * Nn
+        p.a_dtype = p.b_dtype = p.c_dtype = N.DP_BF16
+        p.b_layout, p.epilogue, p.alpha = N.DP_B_NK, N.DP_EPI_SOFTMAX, K ** -0.5
+        N.gemm(p, a.to(cuda), b.to(cuda), c)
+        _sync()
+        ref = torch.softmax((a.float() @ b.float().transpose(-1, -2)) * K ** -0.5, -1)
+        assert torch.allclose(c.cpu().float(), ref, rtol=2e-2, atol=2e-3)
+
+
 # ---------------------------------------------------------------- embedding
 def test_embedding_exact_and_index_error(cuda):
     g = torch.Generator().manual_seed(4)
