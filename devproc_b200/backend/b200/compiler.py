@@ -45,6 +45,7 @@ class B200Compiler(Backend):
                 raise CompilationError("IR verification failed: " + "; ".join(v.get_errors()))
         consts = dict(getattr(ir_function, "constants", {}) or {})
         consts.update(constants or {})
-        low = lower(ir_function, const_names=consts.keys())
+        low = lower(ir_function, const_names=consts.keys(), const_tensors=consts)
+        consts.update(low.extra_consts)
         spec = ProgramSpec.from_lowered(low)
         return B200CompiledProgram(spec, consts, self.device_id, ir_function, self.use_graph)

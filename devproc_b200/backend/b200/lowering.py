@@ -108,10 +108,16 @@ class Buffer:
     first: int = -1      # first record touching it
     last: int = -1       # last record touching it
     slot: int = -1
+    base: Optional["Buffer"] = None  # set for a slot naming a sub-range of another buffer
+    base_off: int = 0                # byte offset of that sub-range
 
     @property
     def nbytes(self) -> int:
         return max(1, _prod(self.shape)) * DTYPE_BYTES[self.dtype]
+
+    @property
+    def root(self) -> "Buffer":
+        return self.base if self.base is not None else self
 
 
 @dataclass
@@ -149,6 +155,13 @@ class Lowered:
     outputs: List[Tuple[str, Buffer]]         # function outputs in order
     arena_bytes: int = 0
     labels: List[str] = field(default_factory=list)
+    extra_consts: Dict[str, "torch.Tensor"] = field(default_factory=dict)  # constants made by the lowering
+
+    @property
+    def aliases(self) -> List[Tuple[int, int, int]]:
+        """(slot, root slot, byte offset) of every caller-bound sub-range slot."""
+        return [(b.slot, b.root.slot, b.base_off) for b in self.buffers
+                if b.base is not None and b.root.kind != "arena"]
 
     def plan_bytes(self) -> bytes:
         """Serialise to the dp_plan blob (header, slots, records)."""
@@ -156,9 +169,9 @@ class Lowered:
                            self.arena_bytes, 0)
         out = [bytes(hdr)]
         for b in self.buffers:
-            kind = N.DP_SLOT_ARENA if b.kind == "arena" else N.DP_SLOT_BOUND
-            out.append(bytes(N.PlanSlot(kind, N.DTYPE_CODE[b.dtype], b.offset if b.kind == "arena" else 0,
-                                        b.nbytes)))
+            arena = b.root.kind == "arena"
+            kind = N.DP_SLOT_ARENA if arena else N.DP_SLOT_BOUND
+            out.append(bytes(N.PlanSlot(kind, N.DTYPE_CODE[b.dtype], b.offset if arena else 0, b.nbytes)))
         for r in self.records:
             rec = N.PlanRecord()
             rec.kernel = r.kernel
@@ -174,18 +187,23 @@ class Lowered:
 
 
 class Lowerer:
-    def __init__(self, fn: Function, const_names=()):
+    def __init__(self, fn: Function, const_names=(), const_tensors=None):
         self.fn = fn
         self.const_names = set(const_names)
+        self.const_tensors = dict(const_tensors or {})
+        self.new_consts: List[Tuple[str, Buffer]] = []
         self.views: Dict[str, View] = {}
         self.buffers: List[Buffer] = []
         self.records: List[Record] = []
         self.done = set()   # ids of ops already lowered (fused)
         self.uses: Dict[str, List[Op]] = {}
+        self.producer: Dict[str, Op] = {}
         self.out_names = {v.name for v in fn.outputs}
         for op in fn.block.ops:
             for v in op.inputs:
                 self.uses.setdefault(v.name, []).append(op)
+            for v in op.outputs:
+                self.producer[v.name] = op
 
     # ------------------------------------------------------------ helpers
     def new_buffer(self, kind, dtype, shape, name) -> Buffer:
@@ -202,6 +220,20 @@ class Lowerer:
         self.views[value.name] = v
         return v
 
+    def ready(self, v: Value) -> bool:
+        """Whether ``v`` has a view now; a pending reshape / transpose producing it
+        (a pure view, free to lower early) is lowered here if its input is ready."""
+        if v.name in self.views:
+            return True
+        op = self.producer.get(v.name)
+        if op is None or id(op) in self.done or op.name not in ("reshape", "transpose"):
+            return False
+        if not self.ready(op.inputs[0]):
+            return False
+        self.lower_op(op)
+        self.done.add(id(op))
+        return v.name in self.views
+
     def single_use(self, v: Value) -> Optional[Op]:
         """The only consumer of ``v`` if it has exactly one and is not a function output."""
         us = self.uses.get(v.name, [])
@@ -209,14 +241,24 @@ class Lowerer:
             return us[0]
         return None
 
+    def alias(self, buf: Buffer, byte_off: int, name: str) -> Buffer:
+        """A slot for the bytes of ``buf`` from ``byte_off`` (16-byte aligned) on."""
+        root = buf.root
+        off = buf.base_off + byte_off
+        es = DTYPE_BYTES[root.dtype]
+        b = Buffer(root.kind, root.dtype, ((root.nbytes - off) // es,), name, base=root, base_off=off)
+        self.buffers.append(b)
+        return b
+
     def emit(self, kernel, operands, params, label, flops=0, nbytes=0) -> Record:
         r = Record(kernel, operands, params, label, flops, nbytes)
         idx = len(self.records)
         for b in operands:
             if b is not None:
-                if b.first < 0:
-                    b.first = idx
-                b.last = idx
+                for x in (b, b.root):
+                    if x.first < 0:
+                        x.first = idx
+                    x.last = idx
         self.records.append(r)
         return r
 
@@ -234,6 +276,18 @@ class Lowerer:
         Kp = (K + 7) // 8 * 8
         src = self.views[value.name]
         flat = view_reshape(src.shape, src.strides, (rows, K))
+        if flat is not None and flat[1] == 1 and flat[0] % 8 == 0 and src.offset == 0:
+            return View(src.buf, (rows, K), flat)  # rows already 16-byte strided
+        if (src.buf.kind == "const" and src.buf.base is None and src.buf.name in self.const_tensors
+                and flat is not None):
+            import torch
+            name = src.buf.name + "|pad%d" % Kp
+            if name not in self.const_tensors:
+                w = self.const_tensors[src.buf.name].reshape(-1).as_strided((rows, K), flat, src.offset)
+                self.const_tensors[name] = torch.nn.functional.pad(w, (0, Kp - K))
+            buf = self.new_buffer("const", t.dtype, (rows, Kp), name)
+            self.new_consts.append((name, buf))
+            return View(buf, (rows, K), (Kp, 1))
         if flat is None:
             src = self.contiguous(value)
             flat = contiguous_strides((rows, K))
@@ -242,6 +296,41 @@ class Lowerer:
         rb.store(out, rb.load(View(src.buf, (rows, K), flat, src.offset)))
         self.emit_region(rb, f"pad {value.name} K{K}->{Kp}")
         return out
+
+    def copy_view_padded(self, v: View, new_shape: Tuple[int, ...], name: str) -> Optional[View]:
+        """Materialise the reshape of ``v`` to ``new_shape`` (whose last dim K
+        is a product of trailing dims of ``v``) with rows ⌈K/8⌉·8 elements
+        apart, in one copy: the tensor-core operand layout of a linear input
+        whose K is not a multiple of 8 (a conv patchify).  The pad columns are
+        never read (the GEMM's operand map ends at K)."""
+        K = new_shape[-1]
+        acc, j = 1, len(v.shape)
+        while j > 0 and acc < K:
+            j -= 1
+            acc *= v.shape[j]
+        if acc != K:
+            return None
+        Kp = (K + 7) // 8 * 8
+        rows = _prod(v.shape[:j])
+        buf = self.new_buffer("arena", v.buf.dtype, (rows, Kp), name)
+        dst = [0] * len(v.shape)
+        step = 1
+        for i in reversed(range(j, len(v.shape))):
+            dst[i] = step
+            step *= v.shape[i]
+        step = Kp
+        for i in reversed(range(j)):
+            dst[i] = step
+            step *= v.shape[i]
+        rb = RegionBuilder(v.shape)
+        rb.store(View(buf, v.shape, tuple(dst)), rb.load(v))
+        self.emit_region(rb, f"copy {name} K{K}->{Kp}")
+        nst = [1] * len(new_shape)
+        step = Kp
+        for i in reversed(range(len(new_shape) - 1)):
+            nst[i] = step
+            step *= new_shape[i]
+        return View(buf, tuple(new_shape), tuple(nst))
 
     def copy_view(self, v: View, name: str) -> View:
         out = View(self.new_buffer("arena", v.buf.dtype, v.shape, name), v.shape, contiguous_strides(v.shape))
@@ -273,11 +362,16 @@ class Lowerer:
             self.lower_op(op)
             self.done.add(id(op))
         outs = self.bind_outputs()
+        # constants no record reads (weights folded into a fused one) are not bound at all
+        self.buffers = [b for b in self.buffers if not (b.kind == "const" and b.first < 0 and b.base is None)]
+        consts = [(n, b) for n, b in consts if b.first >= 0] + \
+                 [(n, b) for n, b in self.new_consts if b.first >= 0]
         arena = plan_arena(self.buffers)
         for i, b in enumerate(self.buffers):
             b.slot = i
         low = Lowered(self.fn.name, self.buffers, self.records, ins, consts, outs, arena)
         low.labels = [r.label for r in self.records]
+        low.extra_consts = {n: self.const_tensors[n] for n, b in self.new_consts if b.first >= 0}
         return low
 
     def bind_outputs(self):
@@ -324,6 +418,13 @@ class Lowerer:
             v = self.views[op.inputs[0].name]
             st = view_reshape(v.shape, v.strides, shape)
             if st is None:
+                user = self.single_use(out)
+                if (user is not None and user.name == "linear" and user.inputs[0] is out
+                        and out.type.dtype == "bfloat16" and shape[-1] % 8):
+                    pv = self.copy_view_padded(v, tuple(shape), out.name + "_pad")
+                    if pv is not None:
+                        self.views[out.name] = pv
+                        return
                 v = self.contiguous(op.inputs[0])
                 st = contiguous_strides(shape)
             self.views[out.name] = View(v.buf, shape, st, v.offset)
@@ -424,9 +525,107 @@ class Lowerer:
         return False
 
     # --------------------------------------------------------------- GEMM
+    def sibling_linears(self, op: Op) -> List[Op]:
+        """Linears that read the same input as ``op`` with constant weights of
+        the same K and dtype (the q/k/v projections of an attention block),
+        in program order; ``[op]`` alone when there is nothing to fuse.  A
+        linear whose output feeds an epilogue the GEMM would absorb (an
+        activation, an add, a cast) is left on its own."""
+        x = op.inputs[0]
+        w0 = op.inputs[1]
+        if not self.const_tensors or len(w0.type.shape) != 2:
+            return [op]
+        K = w0.type.shape[1]
+        es = DTYPE_BYTES[op.outputs[0].type.dtype]
+
+        def ok(u: Op) -> bool:
+            if u.name != "linear" or id(u) in self.done or u.inputs[0].name != x.name:
+                return False
+            w = u.inputs[1]
+            if (w.name not in self.const_tensors or len(w.type.shape) != 2 or w.type.shape[1] != K
+                    or w.type.dtype != w0.type.dtype or (w.type.shape[0] * es) % 16):
+                return False
+            if (len(u.inputs) > 2) != (len(op.inputs) > 2):
+                return False
+            if len(u.inputs) > 2 and (u.inputs[2].name not in self.const_tensors
+                                      or u.inputs[2].type.dtype != op.inputs[2].type.dtype):
+                return False
+            out = u.outputs[0]
+            if out.type.dtype != op.outputs[0].type.dtype or out.name in self.out_names:
+                return False
+            return not any(c.name in ("relu", "gelu", "silu", "add", "to") for c in self.uses.get(out.name, []))
+
+        group, seen = [], set()
+        for u in self.uses.get(x.name, []):
+            if id(u) not in seen and ok(u):
+                seen.add(id(u))
+                group.append(u)
+        if op not in group or len(group) < 2:
+            return [op]
+        if w0.type.dtype == "bfloat16" and K % 8:
+            return [op]
+        return group
+
+    def lower_linear_group(self, group: List[Op]) -> None:
+        """One GEMM for sibling linears: their weights (and biases) are
+        concatenated into one constant, and each output is a column block of
+        the fused output, read in place through a sub-range slot."""
+        import torch
+        x_val = group[0].inputs[0]
+        x = self.contiguous(x_val)
+        K = group[0].inputs[1].type.shape[1]
+        Ns = [u.inputs[1].type.shape[0] for u in group]
+        Ntot = sum(Ns)
+
+        def fused_const(idx: int, shape) -> View:
+            name = "+".join(u.inputs[idx].name for u in group)
+            if name not in self.const_tensors:
+                self.const_tensors[name] = torch.cat([self.const_tensors[u.inputs[idx].name].reshape(-1, *shape[1:])
+                                                      for u in group], 0)
+            buf = self.new_buffer("const", group[0].inputs[idx].type.dtype, shape, name)
+            self.new_consts.append((name, buf))
+            return View(buf, tuple(shape), contiguous_strides(tuple(shape)))
+
+        w = fused_const(1, (Ntot, K))
+        bias = fused_const(2, (Ntot,)) if len(group[0].inputs) > 2 else None
+        lead = x.shape[:-1]
+        out_dt = group[0].outputs[0].type.dtype
+        out_shape = tuple(lead) + (Ntot,)
+        out_buf = self.new_buffer("arena", out_dt, out_shape, "+".join(u.outputs[0].name for u in group))
+        p = N.GemmParams()
+        p.M, p.N, p.K = _prod(lead), Ntot, K
+        p.lda = x.strides[-2] if len(x.shape) > 1 else K
+        p.ldb, p.ldc = K, Ntot
+        p.b_layout = N.DP_B_NK
+        p.batch = 1
+        a_dt = x.buf.dtype
+        if a_dt != w.buf.dtype or a_dt not in ("float32", "bfloat16"):
+            raise CompilationError(f"linear: operand dtypes {a_dt} x {w.buf.dtype}; supported: "
+                                   "float32 x float32, bfloat16 x bfloat16")
+        p.a_dtype = p.b_dtype = N.DTYPE_CODE[a_dt]
+        p.c_dtype = N.DTYPE_CODE[out_dt]
+        if bias is not None:
+            p.epilogue = N.DP_EPI_BIAS
+            p.bias_dtype = N.DTYPE_CODE[bias.buf.dtype]
+        ops_ = [x.buf, w.buf, out_buf, bias.buf if bias is not None else None, None]
+        self.emit(N.DP_K_GEMM, ops_, p, f"gemm linear x{len(group)} M{p.M} N{Ntot} K{K} {a_dt} epi{p.epilogue}",
+                  2 * p.M * Ntot * K, sum(b.nbytes for b in ops_ if b is not None))
+        es = DTYPE_BYTES[out_dt]
+        strides = contiguous_strides(out_shape)
+        col = 0
+        for u, n in zip(group, Ns):
+            v = u.outputs[0]
+            buf = out_buf if col == 0 else self.alias(out_buf, col * es, v.name)
+            self.views[v.name] = View(buf, tuple(lead) + (n,), strides)
+            col += n
+            self.done.add(id(u))
+
     def lower_gemm(self, op: Op) -> None:
         p = N.GemmParams()
         if op.name == "linear":
+            group = self.sibling_linears(op)
+            if len(group) > 1:
+                return self.lower_linear_group(group)
             K = op.inputs[0].type.shape[-1]
             if op.inputs[0].type.dtype == "bfloat16" and K % 8:
                 # tensor-core operands need 16-byte row strides: rows padded to Kp
@@ -481,28 +680,62 @@ class Lowerer:
         p.a_dtype = p.b_dtype = N.DTYPE_CODE[a_dtype]
         epi = 0
         residual = None
+        shared_rows = 0
         c_dtype = op.outputs[0].type.dtype
         if bias is not None:
             epi |= N.DP_EPI_BIAS
         act_done = False
         cur = op.outputs[0]
-        out_shape = op.outputs[0].type.shape
+        out_shape = tuple(op.outputs[0].type.shape)
+        # The GEMM output as seen through the reshape / transpose views between it
+        # and the next elementwise op; that op fuses only while this stays the
+        # plain row-major layout of the GEMM's own output.
+        sym = (out_shape, contiguous_strides(out_shape))
+        pending: List[Op] = []
         while True:
             nxt = self.single_use(cur)
             if nxt is None or id(nxt) in self.done:
                 break
+            if nxt.name in ("reshape", "transpose"):
+                shp, st = sym
+                if nxt.name == "reshape":
+                    new_shape = tuple(nxt.outputs[0].type.shape)
+                    nst = view_reshape(shp, st, new_shape)
+                    if nst is None:
+                        break
+                    sym = (new_shape, tuple(nst))
+                else:
+                    dims = nxt.attr("dims")
+                    sym = (tuple(shp[d] for d in dims), tuple(st[d] for d in dims))
+                pending.append(nxt)
+                cur = nxt.outputs[0]
+                continue
+            shp, st = sym
+            if not View(None, shp, st).contiguous:
+                break
+            last = False
             if nxt.name == "add":
                 other = nxt.inputs[1] if nxt.inputs[0] is cur else nxt.inputs[0]
+                if other is cur:
+                    break
                 ot = other.type
-                if nxt.outputs[0].type.shape != out_shape:
+                if tuple(nxt.outputs[0].type.shape) != shp:
                     break
                 if (bias is None and not act_done and residual is None and ot.shape[-1:] == (p.N,)
-                        and _prod(ot.shape) == p.N):
+                        and shp[-1] == p.N and _prod(ot.shape) == p.N):
                     bias = self.contiguous(other)
                     epi |= N.DP_EPI_BIAS
-                elif residual is None and ot.shape == out_shape and ot.dtype in FLOAT_DTYPES:
+                elif residual is None and tuple(ot.shape) == shp and ot.dtype in FLOAT_DTYPES:
                     residual = self.contiguous(other)
                     epi |= N.DP_EPI_RESIDUAL
+                elif (residual is None and ot.dtype in FLOAT_DTYPES and op.name == "linear" and p.batch == 1
+                      and len(shp) >= 3 and shp[-1] == p.N and tuple(ot.shape[-2:]) == shp[-2:]
+                      and _prod(ot.shape[:-2]) == 1):
+                    # a [1, T, N] addend shared by every sample (a position embedding):
+                    # the GEMM runs as M/T batches of T rows with a batch-shared residual
+                    residual = self.contiguous(other)
+                    epi |= N.DP_EPI_RESIDUAL
+                    shared_rows = shp[-2]
                 else:
                     break
                 c_dtype = nxt.outputs[0].type.dtype
@@ -516,15 +749,25 @@ class Lowerer:
                 act_done = True
             elif nxt.name == "to" and nxt.attr("dtype") in ("float32", "bfloat16", "float16"):
                 c_dtype = nxt.attr("dtype")
-                self.done.add(id(nxt))
-                cur = nxt.outputs[0]
-                break
+                last = True
             else:
                 break
+            for v in pending:
+                self.done.add(id(v))
+            pending = []
             self.done.add(id(nxt))
             cur = nxt.outputs[0]
+            out_shape = tuple(cur.type.shape)
+            sym = (out_shape, contiguous_strides(out_shape))
+            if last:
+                break
+        if pending:  # views after the last fused op stay ordinary views of its output
+            cur = pending[0].inputs[0]
         p.epilogue = epi
         p.c_dtype = N.DTYPE_CODE[c_dtype]
+        if shared_rows:
+            p.batch, p.M = p.M // shared_rows, shared_rows
+            p.stride_a, p.stride_b = shared_rows * p.lda, 0
         p.ldc = p.N
         p.stride_c = p.M * p.N if p.batch > 1 else 0
         if bias is not None:
@@ -532,7 +775,7 @@ class Lowerer:
         if residual is not None:
             p.r_dtype = N.DTYPE_CODE[residual.buf.dtype]
             p.ldr = p.N
-            p.stride_r = p.M * p.N if p.batch > 1 else 0
+            p.stride_r = p.M * p.N if p.batch > 1 and not shared_rows else 0
         out = self.new_value_view(cur, dtype=c_dtype)
         flops = 2 * p.M * p.N * p.K * p.batch
         ops_ = [a_buf.buf, b_buf.buf, out.buf, bias.buf if bias is not None else None,
@@ -746,7 +989,8 @@ class Lowerer:
             narrowing = cur.name == "to" and cur.attr("dtype") not in ("float32", "float64")
             if (nxt is None or id(nxt) in self.done or nxt.name not in ELEMENTWISE or nxt.name == "reshape"
                     or nxt.name == "transpose" or materialized_shape(nxt.outputs[0]) != shape or narrowing
-                    or not rb.room()):
+                    or not rb.room()
+                    or not all(v.name in regs or self.ready(v) for v in nxt.inputs if v is not out_v)):
                 break
             self.done.add(id(nxt))
             cur = nxt
@@ -799,16 +1043,36 @@ class RegionBuilder:
         self.chan_dims = set()
         self.names: List[str] = []
         self._loaded: Dict[Tuple, int] = {}
+        # Registers holding an op's result (not a cached load): the chain
+        # consumes each exactly once, so an instruction may overwrite one.
+        self._temps = set()
+        self._free: List[int] = []
 
     def room(self) -> bool:
         return (len(self.instr) < N.DP_REGION_MAX_INSTR - 8 and self.nregs < N.DP_REGION_MAX_REGS - 2
                 and len(self.operands) < N.DP_REGION_MAX_OPERANDS - 2)
 
     def _reg(self) -> int:
+        if self._free:
+            return self._free.pop()
         r = self.nregs
         self.nregs += 1
         if self.nregs > N.DP_REGION_MAX_REGS:
             raise CompilationError("region: out of registers")
+        return r
+
+    def _result(self, *args: int) -> int:
+        """Destination for an op reading ``args``: the first temporary among
+        them (freed temporaries go back to the pool), else a new register."""
+        temps = [a for a in dict.fromkeys(args) if a in self._temps]
+        if temps:
+            dst = temps[0]
+            for t in temps[1:]:
+                self._temps.discard(t)
+                self._free.append(t)
+            return dst
+        r = self._reg()
+        self._temps.add(r)
         return r
 
     def _bstrides(self, v: View) -> Tuple[int, ...]:
@@ -845,6 +1109,7 @@ class RegionBuilder:
     def const(self, c: float) -> int:
         self.consts.append(float(c))
         r = self._reg()
+        self._temps.add(r)
         self.instr.append(("const", r, len(self.consts) - 1, 0))
         return r
 
@@ -856,16 +1121,19 @@ class RegionBuilder:
         d = dim % len(self.shape)
         self.chan_dims.add(d)
         r = self._reg()
+        self._temps.add(r)
         self.instr.append(("chansel", r, base, d))
         return r
 
     def unary(self, name: str, a: int) -> int:
-        r = self._reg()
+        if name == "mov":  # a widening cast: the value is already a float in the register
+            return a
+        r = self._result(a)
         self.instr.append((name, r, a, 0))
         return r
 
     def binary(self, name: str, a: int, b: int) -> int:
-        r = self._reg()
+        r = self._result(a, b)
         self.instr.append((name, r, a, b))
         return r
 
@@ -953,8 +1221,9 @@ def value_dtype(v: Value) -> str:
 
 
 def plan_arena(buffers: List[Buffer]) -> int:
-    """First-fit offsets for arena buffers whose live ranges overlap in time."""
-    arena = [b for b in buffers if b.kind == "arena"]
+    """First-fit offsets for arena buffers whose live ranges overlap in time;
+    a sub-range slot sits at its root's offset plus its own."""
+    arena = [b for b in buffers if b.kind == "arena" and b.base is None]
     for b in arena:
         if b.first < 0:  # produced but never used: keep it alive at its producer only
             b.first = b.last = 0
@@ -972,6 +1241,9 @@ def plan_arena(buffers: List[Buffer]) -> int:
         b.offset = off
         placed.append(b)
         top = max(top, off + size)
+    for b in buffers:
+        if b.base is not None and b.root.kind == "arena":
+            b.offset = b.root.offset + b.base_off
     return top
 
 
@@ -979,5 +1251,8 @@ def _round(n: int) -> int:
     return (n + ALIGN - 1) // ALIGN * ALIGN
 
 
-def lower(fn: Function, const_names=()) -> Lowered:
-    return Lowerer(fn, const_names).run()
+def lower(fn: Function, const_names=(), const_tensors=None) -> Lowered:
+    """Lower ``fn``.  With ``const_tensors`` (the constants' values) the
+    lowering may also derive new constants, e.g. the concatenated weight of
+    sibling linears; they are returned in ``Lowered.extra_consts``."""
+    return Lowerer(fn, const_names, const_tensors).run()

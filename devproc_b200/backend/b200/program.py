@@ -57,6 +57,9 @@ class ProgramSpec:
     outputs: List[IOSlot]
     arena_bytes: int
     records: List[Dict[str, Any]] = field(default_factory=list)
+    # caller-bound slots that name a byte range of another slot's buffer:
+    # [slot, root slot, byte offset]; bound at the root's pointer + offset
+    aliases: List[List[int]] = field(default_factory=list)
 
     @staticmethod
     def from_lowered(low) -> "ProgramSpec":
@@ -65,7 +68,7 @@ class ProgramSpec:
         recs = [{"kernel": N.KERNEL_NAMES[r.kernel], "label": r.label, "flops": r.flops, "bytes": r.bytes}
                 for r in low.records]
         return ProgramSpec(low.name, low.plan_bytes(), io(low.inputs), io(low.consts), io(low.outputs),
-                           low.arena_bytes, recs)
+                           low.arena_bytes, recs, [list(a) for a in low.aliases])
 
 
 class B200CompiledProgram(CompiledProgram):
@@ -127,14 +130,21 @@ class B200CompiledProgram(CompiledProgram):
                     raise N.DevProcError(N.DP_ERR_SHAPE, f"constant {c.name}: shape {tuple(t.shape)} != "
                                                          f"{tuple(c.shape)}")
                 self._dev_consts[c.name] = t
-                prog.bind(c.slot, t.data_ptr(), t.numel() * t.element_size())
+                self._bind_slot(prog, c.slot, t.data_ptr(), t.numel() * t.element_size())
             for o in self.spec.outputs:
                 t = torch.empty(o.shape, dtype=TORCH_DTYPES[o.dtype], device=dev)
                 self._outputs.append(t)
-                prog.bind(o.slot, t.data_ptr(), max(1, t.numel()) * t.element_size())
+                self._bind_slot(prog, o.slot, t.data_ptr(), max(1, t.numel()) * t.element_size())
             prog.set_graph(self.use_graph)
             self._host_out = [None] * len(self._outputs)
         self._native = prog
+
+    def _bind_slot(self, prog, slot: int, ptr: int, nbytes: int) -> None:
+        """Bind ``slot`` and every slot that names a byte range of it."""
+        prog.bind(slot, ptr, nbytes)
+        for a, root, off in self.spec.aliases:
+            if root == slot:
+                prog.bind(a, ptr + off, nbytes - off)
 
     def _bind_input(self, io: IOSlot, t: torch.Tensor) -> None:
         want = TORCH_DTYPES[io.dtype]
@@ -157,7 +167,7 @@ class B200CompiledProgram(CompiledProgram):
             src = st
         ptr = src.data_ptr()
         if self._bound.get(io.slot) != ptr:
-            self._native.bind(io.slot, ptr, max(1, src.numel()) * src.element_size())
+            self._bind_slot(self._native, io.slot, ptr, max(1, src.numel()) * src.element_size())
             self._bound[io.slot] = ptr
 
     def run(self, *args, to_cpu: bool = True, reuse_host_buffers: bool = False, **kwargs) -> List[torch.Tensor]:
@@ -232,6 +242,7 @@ class B200CompiledProgram(CompiledProgram):
             "consts": [asdict(c) for c in consts],
             "outputs": [asdict(o) for o in self.spec.outputs],
             "kernels": self.spec.records,
+            "aliases": self.spec.aliases,
             "tensor_allocations": {o.name: {"shape": o.shape, "dtype": o.dtype} for o in self.spec.outputs},
         }
         with open(path + ".meta.json", "w") as f:
@@ -258,7 +269,8 @@ class B200CompiledProgram(CompiledProgram):
                 t = torch.frombuffer(raw, dtype=torch.uint8) if nbytes else torch.empty(0, dtype=torch.uint8)
                 constants[c.name] = t.view(TORCH_DTYPES[c.dtype]).reshape(c.shape)
         spec = ProgramSpec(meta["name"], plan, [IOSlot(**i) for i in meta["inputs"]], consts,
-                           [IOSlot(**o) for o in meta["outputs"]], meta["arena_bytes"], meta["kernels"])
+                           [IOSlot(**o) for o in meta["outputs"]], meta["arena_bytes"], meta["kernels"],
+                           meta.get("aliases", []))
         return B200CompiledProgram(spec, constants, device_id)
 
     def close(self) -> None:

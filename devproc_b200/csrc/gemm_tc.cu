@@ -7,15 +7,16 @@
 // C[b] = epilogue(A[b] · B[b]ᵀ); A [M, K] row-major, B [N, K] row-major (both
 // K-major, the nn.Linear layout), fp32 accumulation.
 //
-// Persistent kernel, one CTA per SM, 256 threads in four roles:
+// Persistent kernel, one CTA per SM, 384 threads in four roles:
 //   warp 0  TMA producer: 128×64 A tile + 256×64 B tile per stage (128-byte
 //           swizzle), kStages stages guarded by full/empty mbarriers;
 //   warp 1  MMA issuer (one thread): 4 × tcgen05.mma (M=128, N=256, K=16) per
 //           stage into one of two TMEM accumulators, tcgen05.commit frees the
 //           stage and, after the last K block, hands the accumulator over;
 //   warp 2  allocates / frees the 512 TMEM columns (2 × 256 fp32 accumulators);
-//   warps 4-7 epilogue: tcgen05.ld 32 columns at a time (each thread owns one
-//           accumulator row), bias → activation → residual → cast, store, then
+//   warps 4-11 epilogue: two warps per TMEM lane quadrant, each taking half of
+//           the columns (each thread owns one accumulator row), 16 columns per
+//           tcgen05.ld: bias → activation → residual → cast, TMA store, then
 //           release the accumulator so the next tile's MMAs overlap this one.
 // Tiles are visited in GROUP_M-row bands for L2 reuse of B.
 //
@@ -30,15 +31,23 @@
 namespace dpk_tcgemm {
 
 constexpr int BM = 128, BN = 256, BK = 64;
-constexpr int kStages = 4;
-constexpr int kThreads = 256;
+#ifndef DP_TC_STAGES
+#define DP_TC_STAGES 3
+#endif
+#ifndef DP_TC_EPI_BUFS
+#define DP_TC_EPI_BUFS 2
+#endif
+constexpr int kStages = DP_TC_STAGES;
+constexpr int kEpiBufs = DP_TC_EPI_BUFS;  // output staging chunks per epilogue warp
+constexpr int kEpiWarps = 8;   // two warps per TMEM lane quadrant, each taking half of the columns
+constexpr int kThreads = 128 + 32 * kEpiWarps;
 constexpr int kGroupM = 8;
 constexpr uint32_t kTileABytes = BM * BK * 2;  // 16 KB
 constexpr uint32_t kTileBBytes = BN * BK * 2;  // 32 KB
 constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kTmemCols = 512;                 // two 256-column fp32 accumulators
 constexpr uint32_t kEpiBufBytes = 32 * 128;     // one 32-row x 128-byte output chunk
-constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBufBytes;  // 4 epilogue warps, double-buffered
+constexpr uint32_t kEpiBytes = kEpiWarps * kEpiBufs * kEpiBufBytes;
 constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kEpiBytes + 1024;  // + alignment slack
 
 struct Shape {
@@ -49,6 +58,7 @@ struct Shape {
   int tma_store;     // output written by TMA tensor stores from swizzled chunks
   int tma_residual;  // residual read by TMA into the same chunks (same dtype as C)
   int c_bytes;       // element size of C
+  int bcast;         // operands shared by every batch (zero batch strides): 1 A, 2 B, 4 residual
 };
 
 // ------------------------------------------------------------------ PTX
@@ -72,6 +82,7 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void 
 }
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
@@ -129,6 +140,12 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
                : "memory");
 }
 
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -157,7 +174,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 // Epilogue math on 16 consecutive columns n..n+15 of one row (columns past N
 // get bias 0; they are never stored).  One activation switch per call keeps
 // the code small enough for the instruction cache.
-__device__ __forceinline__ void epi16(float (&x)[16], int64_t n, int N, int epi, const void *bias, int bias_dt) {
+__device__ __forceinline__ void epi16(float (&x)[16], int64_t n, int N, int epi, const void *bias, int bias_dt,
+                                      bool fast_tanh) {
   if (epi & DP_EPI_BIAS) {
     if (bias_dt == DP_BF16 && n + 16 <= N && (reinterpret_cast<uintptr_t>(bias) & 15) == 0 && (n & 7) == 0) {
       const uint4 *bp = reinterpret_cast<const uint4 *>(static_cast<const __nv_bfloat16 *>(bias) + n);
@@ -196,8 +214,20 @@ __device__ __forceinline__ void epi16(float (&x)[16], int64_t n, int N, int epi,
 #pragma unroll
     for (int e = 0; e < 16; ++e) x[e] = dp::act_gelu_erf(x[e]);
   } else if (act == DP_EPI_GELU_TANH) {
+    if (fast_tanh) {
+      // 16-bit output: the hardware tanh approximation (relative error far
+      // below the output's bf16/fp16 resolution).
 #pragma unroll
-    for (int e = 0; e < 16; ++e) x[e] = dp::act_gelu_tanh(x[e]);
+      for (int e = 0; e < 16; ++e) {
+        const float u = 0.7978845608028654f * (x[e] + 0.044715f * x[e] * x[e] * x[e]);
+        float t;
+        asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+        x[e] = 0.5f * x[e] * (1.0f + t);
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) x[e] = dp::act_gelu_tanh(x[e]);
+    }
   } else if (act == DP_EPI_SILU) {
 #pragma unroll
     for (int e = 0; e < 16; ++e) x[e] = x[e] / (1.0f + expf(-x[e]));
@@ -237,7 +267,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_r,
                    dp_gemm_params p, Shape s, void *C, const void *bias, const void *res) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], res_bar[4];
+  __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], res_bar[kEpiWarps],
+      sm_bar[4];
+  __shared__ float2 sm_part[2][4][2][32];  // softmax (max, sum) per accumulator, quadrant, column half, row
   __shared__ uint32_t tmem_base_slot;
   __shared__ int abort_flag;
 
@@ -251,9 +283,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 128);
+      mbar_init(&acc_empty[i], 32 * kEpiWarps);
     }
-    for (int i = 0; i < 4; ++i) mbar_init(&res_bar[i], 1);
+    for (int i = 0; i < kEpiWarps; ++i) mbar_init(&res_bar[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&sm_bar[i], 64);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -286,13 +319,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t *sa = smem + st * kStageBytes;
           uint8_t *sb = sa + kTileABytes;
           mbar_arrive_expect_tx(&full[st], kStageBytes);
-          tma_load_4d(sa, &map_a, kb * BK, tm * BM, b, s.batch2, &full[st]);
+          const int ba = (s.bcast & 1) ? 0 : b, bb = (s.bcast & 2) ? 0 : b;
+          tma_load_4d(sa, &map_a, kb * BK, tm * BM, ba, s.batch2, &full[st]);
           if (s.b_mn) {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_4d(sb + j * 8192, &map_b, tn * BN + j * 64, kb * BK, b, s.batch2, &full[st]);
+              tma_load_4d(sb + j * 8192, &map_b, tn * BN + j * 64, kb * BK, bb, s.batch2, &full[st]);
           } else {
-            tma_load_4d(sb, &map_b, kb * BK, tn * BN, b, s.batch2, &full[st]);
+            tma_load_4d(sb, &map_b, kb * BK, tn * BN, bb, s.batch2, &full[st]);
           }
         }
       }
@@ -329,10 +363,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else if (warp >= 4) {
-    // ---------------- epilogue: thread owns accumulator row (warp-4)*32 + lane
-    const int q = warp - 4;
+    // ---------------- epilogue: warp 4+e owns TMEM lane quadrant q = warp % 4
+    // (accumulator rows 32q..32q+31) and column half h = e / 4 of the tile.
+    const int e = warp - 4;
+    const int q = warp & 3;
+    const int half = e >> 2;
     const int row = q * 32 + lane;
-    uint8_t *ebuf = smem + kStages * kStageBytes + q * 2 * kEpiBufBytes;
+    uint8_t *ebuf = smem + kStages * kStageBytes + e * kEpiBufs * kEpiBufBytes;
     constexpr int chunk_cols = 128 / CB;  // 32 fp32 or 64 bf16/f16 columns
     uint32_t res_phase = 0;
     int local = 0;
@@ -348,47 +385,69 @@ __global__ void __launch_bounds__(kThreads, 1)
       dp::Epilogue ep(p, C, bias, res, b);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
       // Row softmax epilogue: this thread's row is all N (≤ BN) columns of
-      // the accumulator, so max and sum need no cross-thread reduction.
-      float sm_max = 0.0f, sm_inv = 1.0f;
+      // the accumulator, split between the quadrant's two warps.  Each half
+      // keeps an online (max, sum) over its columns in log2 units; the pair
+      // swaps them through shared memory, guarded by a per-quadrant mbarrier.
+      float sm_max = 0.0f, sm_inv = 1.0f, sm_l2 = 0.0f;
       const bool softmax = (p.epilogue & DP_EPI_SOFTMAX) != 0;
+      const int col_lo = half * (BN / 2);
+      const int col_hi = col_lo + BN / 2;
       if (softmax) {
-        const float alpha = p.alpha != 0.0f ? p.alpha : 1.0f;
-        float mx = -INFINITY;
+        sm_l2 = (p.alpha != 0.0f ? p.alpha : 1.0f) * 1.4426950408889634f;
+        float mx = -INFINITY, sum = 0.0f;
 #pragma unroll 1
-        for (int c = 0; c < BN / 16; ++c) {
+        for (int c = col_lo / 16; c < col_hi / 16; ++c) {
           uint32_t r[16];
           tmem_ld16(tbase + c * 16, r);
+          float v[16];
 #pragma unroll
           for (int e = 0; e < 16; ++e)
-            if ((int64_t)tn * BN + c * 16 + e < s.N) mx = fmaxf(mx, __uint_as_float(r[e]) * alpha);
-        }
-        float sum = 0.0f;
-#pragma unroll 1
-        for (int c = 0; c < BN / 16; ++c) {
-          uint32_t r[16];
-          tmem_ld16(tbase + c * 16, r);
+            v[e] = ((int64_t)tn * BN + c * 16 + e < s.N) ? __uint_as_float(r[e]) * sm_l2 : -INFINITY;
+          float t[8];
 #pragma unroll
-          for (int e = 0; e < 16; ++e)
-            if ((int64_t)tn * BN + c * 16 + e < s.N) sum += __expf(__uint_as_float(r[e]) * alpha - mx);
+          for (int e = 0; e < 8; ++e) t[e] = fmaxf(v[e], v[e + 8]);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) t[e] = fmaxf(t[e], t[e + 4]);
+          const float nm = fmaxf(mx, fmaxf(fmaxf(t[0], t[2]), fmaxf(t[1], t[3])));
+          if (nm == -INFINITY) continue;
+          float s0 = 0.0f, s1 = 0.0f;
+#pragma unroll
+          for (int e = 0; e < 16; e += 2) {
+            s0 += ex2_approx(v[e] - nm);
+            s1 += ex2_approx(v[e + 1] - nm);
+          }
+          sum = sum * ex2_approx(mx - nm) + (s0 + s1);
+          mx = nm;
         }
-        sm_max = mx;
-        sm_inv = 1.0f / sum;
+        sm_part[a][q][half][lane] = make_float2(mx, sum);
+        mbar_arrive(&sm_bar[q]);
+        const bool ok = wait_or_abort(&sm_bar[q], local & 1, 350 + q, flag);
+        if (!__all_sync(0xffffffffu, ok)) break;
+        const float2 o = sm_part[a][q][half ^ 1][lane];
+        const float gm = fmaxf(mx, o.x);
+        const float tot = (mx == -INFINITY ? 0.0f : sum * ex2_approx(mx - gm)) +
+                          (o.x == -INFINITY ? 0.0f : o.y * ex2_approx(o.x - gm));
+        sm_max = gm;
+        sm_inv = 1.0f / tot;
       }
       if (s.tma_store) {
         bool stop = false;
 #pragma unroll 1
-        for (int c = 0; c < BN / chunk_cols; ++c) {
+        for (int c = col_lo / chunk_cols; c < col_hi / chunk_cols; ++c) {
           const int64_t n0 = (int64_t)tn * BN + c * chunk_cols;
           if (n0 >= s.N) break;
-          uint8_t *buf = ebuf + (c & 1) * kEpiBufBytes;
-          if (lane == 0) bulk_wait_read1();  // the store that last read ``buf`` is done with it
+          uint8_t *buf = ebuf + (c % kEpiBufs) * kEpiBufBytes;
+          if (lane == 0) {  // the store that last read ``buf`` is done with it
+            if constexpr (kEpiBufs == 2) bulk_wait_read1();
+            else bulk_wait_read0();
+          }
           __syncwarp();
           if (s.tma_residual) {
             if (lane == 0) {
-              mbar_arrive_expect_tx(&res_bar[q], kEpiBufBytes);
-              tma_load_4d(buf, &map_r, (int)n0, tm * BM + q * 32, b, s.batch2, &res_bar[q]);
+              mbar_arrive_expect_tx(&res_bar[e], kEpiBufBytes);
+              tma_load_4d(buf, &map_r, (int)n0, tm * BM + q * 32, (s.bcast & 4) ? 0 : b, s.batch2, &res_bar[e]);
             }
-            const bool ok = wait_or_abort(&res_bar[q], res_phase, 340 + q, flag);
+            const bool ok = wait_or_abort(&res_bar[e], res_phase, 340 + e, flag);
             res_phase ^= 1u;
             if (!__all_sync(0xffffffffu, ok)) {
               stop = true;
@@ -403,15 +462,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 16; ++e) x[e] = __uint_as_float(r[e]);
             const int64_t nb = n0 + step * 16;
-            if (p.alpha != 0.0f) {
-#pragma unroll
-              for (int e = 0; e < 16; ++e) x[e] *= p.alpha;
-            }
             if (softmax) {
 #pragma unroll
-              for (int e = 0; e < 16; ++e) x[e] = __expf(x[e] - sm_max) * sm_inv;
-            } else if (p.epilogue) {
-              epi16(x, nb, s.N, p.epilogue, bias, p.bias_dtype);
+              for (int e = 0; e < 16; ++e) x[e] = ex2_approx(fmaf(x[e], sm_l2, -sm_max)) * sm_inv;
+            } else {
+              if (p.alpha != 0.0f) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) x[e] *= p.alpha;
+              }
+              if (p.epilogue)
+                epi16(x, nb, s.N, p.epilogue, bias, p.bias_dtype, CB == 2);
             }
             if ((p.epilogue & DP_EPI_RESIDUAL) && !s.tma_residual) {
 #pragma unroll
@@ -484,7 +544,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (stop) break;
       } else {
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = col_lo / 32; c < col_hi / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(tbase + c * 32, r);
           const int64_t n0 = (int64_t)tn * BN + c * 32;
@@ -572,13 +632,20 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   memset(&mr, 0, sizeof(mr));
   const int64_t b2 = p.batch2 > 1 ? p.batch2 : 1;
   const int64_t b1 = p.batch / b2;
-  int st = make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, b1, p.stride_a, b2, p.stride_a2, BK, BM);
+  // An operand with zero batch strides is one matrix shared by every batch:
+  // its map has no batch extent and the kernel reads it at batch 0.
+  auto shared = [&](int64_t s1, int64_t s2) { return p.batch > 1 && s1 == 0 && (b2 == 1 || s2 == 0); };
+  const bool a_sh = shared(p.stride_a, p.stride_a2), b_sh = shared(p.stride_b, p.stride_b2);
+  const bool r_sh = (p.epilogue & DP_EPI_RESIDUAL) && shared(p.stride_r, p.stride_r2);
+  int st = a_sh ? make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, 1, 0, 1, 0, BK, BM)
+                : make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, b1, p.stride_a, b2, p.stride_a2, BK, BM);
   if (st != DP_OK) return st;
   const bool b_mn = p.b_layout == DP_B_KN;
+  const int64_t mb1 = b_sh ? 1 : b1, mb2 = b_sh ? 1 : b2;
   if (b_mn)  // [K, N], N contiguous: boxes of 64 N × 64 K
-    st = make_map(&mb, B, DP_BF16, p.K, p.N, p.ldb, b1, p.stride_b, b2, p.stride_b2, 64, BK);
+    st = make_map(&mb, B, DP_BF16, p.K, p.N, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, 64, BK);
   else
-    st = make_map(&mb, B, DP_BF16, p.N, p.K, p.ldb, b1, p.stride_b, b2, p.stride_b2, BK, BN);
+    st = make_map(&mb, B, DP_BF16, p.N, p.K, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, BK, BN);
   if (st != DP_OK) return st;
   const int cb = dtype_bytes(p.c_dtype);
   auto al16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
@@ -590,7 +657,8 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
     if (st != DP_OK) return st;
     if ((p.epilogue & DP_EPI_RESIDUAL) && p.r_dtype == p.c_dtype && (p.ldr * cb) % 16 == 0 &&
         (p.batch == 1 || (p.stride_r * cb) % 16 == 0) && (b2 == 1 || (p.stride_r2 * cb) % 16 == 0) && al16(res)) {
-      st = make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, b1, p.stride_r, b2, p.stride_r2, 128 / cb, 32);
+      st = r_sh ? make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, 1, 0, 1, 0, 128 / cb, 32)
+                : make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, b1, p.stride_r, b2, p.stride_r2, 128 / cb, 32);
       if (st != DP_OK) return st;
       tma_res = true;
     }
@@ -612,6 +680,7 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   s.tma_store = tma_store ? 1 : 0;
   s.tma_residual = tma_res ? 1 : 0;
   s.c_bytes = cb;
+  s.bcast = (a_sh ? 1 : 0) | (b_sh ? 2 : 0) | (r_sh ? 4 : 0);
   DP_REQUIRE(p.N < (1ll << 31) && p.K < (1ll << 31), DP_ERR_UNSUPPORTED, "gemm: N or K too large");
   static bool attr_set = false;
   if (!attr_set) {

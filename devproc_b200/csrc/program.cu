@@ -124,7 +124,7 @@ extern "C" int dp_program_create(const void *plan, size_t plan_bytes, int device
   for (uint32_t i = 0; i < h.n_slots; ++i) {
     const dp_plan_slot &sl = prog->slots[i];
     if (sl.kind != DP_SLOT_BOUND && sl.kind != DP_SLOT_ARENA) return fail(DP_ERR_PLAN, "plan: bad slot kind");
-    if (sl.kind == DP_SLOT_ARENA && (sl.offset % 256 != 0 || sl.offset + sl.bytes > h.arena_bytes))
+    if (sl.kind == DP_SLOT_ARENA && (sl.offset % 16 != 0 || sl.offset + sl.bytes > h.arena_bytes))
       return fail(DP_ERR_PLAN, "plan: arena slot " + std::to_string(i) + " out of range or misaligned");
   }
   for (uint32_t r = 0; r < h.n_records; ++r) {

@@ -76,7 +76,7 @@ extern "C" int dp_program_run_noalloc(const void *plan, size_t plan_bytes, void 
     dp_plan_slot sl;
     memcpy(&sl, slots + i * sizeof(dp_plan_slot), sizeof(sl));
     if (sl.kind == DP_SLOT_ARENA) {
-      DP_REQUIRE(sl.offset % 256 == 0 && sl.offset + sl.bytes <= h.arena_bytes, DP_ERR_PLAN,
+      DP_REQUIRE(sl.offset % 16 == 0 && sl.offset + sl.bytes <= h.arena_bytes, DP_ERR_PLAN,
                  "plan: arena slot out of range");
       ptr[i] = static_cast<uint8_t *>(base) + sl.offset;
     } else {

@@ -10,13 +10,14 @@
 // The iteration space is the region's output shape; every operand carries
 // per-dim element strides (0 = broadcast, permuted strides = transpose), so
 // a transpose is just a strided load.  The host collapses contiguous dims;
-// with rank 1 and unit/zero strides each thread moves four consecutive
-// elements with vector loads.
+// each thread then works on runs of up to 8 elements along the innermost
+// dim, with 16-byte loads and stores where the run is unit-stride.
+#include <type_traits>
+
 #include "dp_common.cuh"
 
 namespace dpk_region {
 
-constexpr int E = 4;  // elements per thread
 constexpr int kThreads = 256;
 
 // Operand pointers, passed to the kernel by value.
@@ -53,60 +54,159 @@ __device__ __forceinline__ float apply_binary(int op, float a, float b) {
   }
 }
 
-// FAST: rank 1, every stride 0 or 1.
-template <bool FAST>
-__global__ void __launch_bounds__(kThreads) region_kernel(const dp_region_desc d, Ops c, int64_t total) {
-  const int64_t base = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * E;
-  const int64_t gstride = (int64_t)gridDim.x * blockDim.x * E;
-  for (int64_t i0 = base; i0 < total; i0 += gstride) {
-    int64_t coord[E][DP_REGION_MAX_RANK];
-    if (!FAST) {
+// ---------------------------------------------------------------------------
+// Iteration geometry.  The collapsed dims are right-aligned into kR slots
+// (leading slots have extent 1), so every coordinate loop is unrolled with
+// static indices.  One work item is a run of E consecutive elements along the
+// innermost dim (E divides its extent); its coordinates come from one mixed-
+// radix decomposition of the item index with magic-number division (Granlund
+// & Montgomery, "Division by invariant integers using multiplication", 1994:
+// q = (umulhi(n, m) + n) >> s with s = ⌈log2 d⌉, m = ⌊2^32 (2^s − d) / d⌋ + 1,
+// exact for n < 2^31), then each operand's offset is one dot product.
+constexpr int kR = DP_REGION_MAX_RANK;
+
+struct FastDiv {
+  uint32_t d, m, s;
+};
+
+struct Geom {
+  int64_t items;                                // work items (runs of E elements)
+  int64_t ext[kR];                              // extents; ext[kR-1] counted in runs
+  int64_t stride[DP_REGION_MAX_OPERANDS][kR];   // element strides, right-aligned
+  FastDiv fd[kR];                               // divisors of ext (32-bit path)
+  int chan_slot[DP_REGION_MAX_INSTR];           // right-aligned dim of each CHANSEL
+};
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
+  return (__umulhi(n, f.m) + n) >> f.s;
+}
+
+// E elements of one operand: a 16-byte-or-narrower vector when the run is
+// unit-stride and aligned, one broadcast load when the stride is 0.
+template <int E>
+__device__ __forceinline__ void load_run(const void *ptr, int64_t off, int64_t st, int dt, float (&v)[E]) {
+  if (st == 0) {
+    const float x = load_as_f32(ptr, off, dt);
 #pragma unroll
-      for (int e = 0; e < E; ++e) {
-        int64_t idx = i0 + e;
-        for (int k = d.rank - 1; k >= 0; --k) {
-          coord[e][k] = idx % d.shape[k];
-          idx /= d.shape[k];
+    for (int e = 0; e < E; ++e) v[e] = x;
+    return;
+  }
+  if (st == 1) {
+    const int es = dt == DP_BF16 ? 2 : 4;  // the vector paths below take bf16 and f32
+    const uintptr_t a = reinterpret_cast<uintptr_t>(ptr) + (uintptr_t)(off * es);
+    if (dt == DP_BF16 && E >= 2 && a % (2 * E < 16 ? 2 * E : 16) == 0) {
+      const __nv_bfloat162 *q = reinterpret_cast<const __nv_bfloat162 *>(a);
+      if constexpr (E == 8) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4 *>(a));
+        q = reinterpret_cast<const __nv_bfloat162 *>(&raw);
+#pragma unroll
+        for (int e = 0; e < E / 2; ++e) {
+          const float2 f = __bfloat1622float2(q[e]);
+          v[2 * e] = f.x;
+          v[2 * e + 1] = f.y;
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < E / 2; ++e) {
+          const float2 f = __bfloat1622float2(q[e]);
+          v[2 * e] = f.x;
+          v[2 * e + 1] = f.y;
         }
       }
+      return;
     }
-    const int n_live = (total - i0) < E ? (int)(total - i0) : E;
+    if (dt == DP_F32 && E >= 4 && a % 16 == 0) {
+#pragma unroll
+      for (int e = 0; e < E; e += 4) {
+        const float4 f = __ldg(reinterpret_cast<const float4 *>(a) + e / 4);
+        v[e] = f.x;
+        v[e + 1] = f.y;
+        v[e + 2] = f.z;
+        v[e + 3] = f.w;
+      }
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) v[e] = load_as_f32(ptr, off + e * st, dt);
+}
+
+template <int E>
+__device__ __forceinline__ void store_run(void *ptr, int64_t off, int64_t st, int dt, const float (&v)[E]) {
+  if (st == 1) {
+    const int es = dt == DP_BF16 ? 2 : 4;  // the vector paths below take bf16 and f32
+    const uintptr_t a = reinterpret_cast<uintptr_t>(ptr) + (uintptr_t)(off * es);
+    if (dt == DP_BF16 && E >= 2 && a % (2 * E < 16 ? 2 * E : 16) == 0) {
+      __nv_bfloat162 h[E / 2 > 0 ? E / 2 : 1];
+#pragma unroll
+      for (int e = 0; e < E / 2; ++e) h[e] = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+      if constexpr (E == 8) {
+        *reinterpret_cast<uint4 *>(a) = *reinterpret_cast<const uint4 *>(h);
+      } else {
+#pragma unroll
+        for (int e = 0; e < E / 2; ++e) reinterpret_cast<__nv_bfloat162 *>(a)[e] = h[e];
+      }
+      return;
+    }
+    if (dt == DP_F32 && E >= 4 && a % 16 == 0) {
+#pragma unroll
+      for (int e = 0; e < E; e += 4)
+        reinterpret_cast<float4 *>(a)[e / 4] = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+      return;
+    }
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) store_from_f32(ptr, off + e * st, dt, v[e]);
+}
+
+// Register-program interpreter over runs of E elements.  WIDE: 64-bit
+// item decomposition (more than 2^31 items).
+template <int E, bool WIDE>
+__global__ void __launch_bounds__(kThreads) region_kernel(const dp_region_desc d, Ops c, const Geom g) {
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < g.items; t += nthreads) {
+    int64_t coord[kR];
+    if constexpr (WIDE) {
+      int64_t rest = t;
+#pragma unroll
+      for (int k = kR - 1; k >= 0; --k) {
+        const int64_t q = rest / g.ext[k];
+        coord[k] = rest - q * g.ext[k];
+        rest = q;
+      }
+    } else {
+      uint32_t rest = (uint32_t)t;
+#pragma unroll
+      for (int k = kR - 1; k >= 0; --k) {
+        const uint32_t q = g.fd[k].d == 1 ? rest : fdiv(rest, g.fd[k]);
+        coord[k] = (int64_t)(rest - q * g.fd[k].d);
+        rest = q;
+      }
+    }
+    coord[kR - 1] *= E;  // element index of the run's first element
     float r[DP_REGION_MAX_REGS][E];
     for (int pc = 0; pc < d.n_instr; ++pc) {
       const uint32_t ins = d.instr[pc];
       const int op = ins & 0xff, dst = (ins >> 8) & 0xff, a = (ins >> 16) & 0xff, b = (ins >> 24) & 0xff;
       if (op == DP_OP_LOAD || op == DP_OP_STORE) {
-        const int operand = a;
-        void *ptr = const_cast<void *>(c.p[operand]);
-        const int dt = d.dtype[operand];
+        int64_t off = 0;
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          if (e >= n_live) break;
-          int64_t off = 0;
-          if (FAST) {
-            off = d.stride[operand][0] * (i0 + e);
-          } else {
-            for (int k = 0; k < d.rank; ++k) off += coord[e][k] * d.stride[operand][k];
-          }
-          if (op == DP_OP_LOAD)
-            r[dst][e] = load_as_f32(ptr, off, dt);
-          else
-            store_from_f32(ptr, off, dt, r[b][e]);
-        }
+        for (int k = 0; k < kR; ++k) off += coord[k] * g.stride[a][k];
+        if (op == DP_OP_LOAD)
+          load_run<E>(c.p[a], off, g.stride[a][kR - 1], d.dtype[a], r[dst]);
+        else
+          store_run<E>(const_cast<void *>(c.p[a]), off, g.stride[a][kR - 1], d.dtype[a], r[b]);
       } else if (op == DP_OP_CONST) {
 #pragma unroll
         for (int e = 0; e < E; ++e) r[dst][e] = d.consts[a];
       } else if (op == DP_OP_CHANSEL) {
+        const int slot = g.chan_slot[pc];
+        int64_t cc = 0;
 #pragma unroll
-        for (int e = 0; e < E; ++e) {
-          int64_t cc;
-          if (FAST) {
-            cc = (i0 + e) % d.shape[0];
-          } else {
-            cc = coord[e][b];
-          }
-          r[dst][e] = d.consts[a + (int)cc];
-        }
+        for (int k = 0; k < kR; ++k)
+          if (k == slot) cc = coord[k];
+#pragma unroll
+        for (int e = 0; e < E; ++e) r[dst][e] = d.consts[a + (int)(slot == kR - 1 ? cc + e : cc)];
       } else if (op >= DP_OP_ADD && op <= DP_OP_MIN) {
 #pragma unroll
         for (int e = 0; e < E; ++e) r[dst][e] = apply_binary(op, r[a][e], r[b][e]);
@@ -118,6 +218,56 @@ __global__ void __launch_bounds__(kThreads) region_kernel(const dp_region_desc d
   }
 }
 
+// Pure copies between operands of one dtype move raw elements (no float
+// round trip, so 32/64-bit integers survive), E per work item.
+template <typename T, int E, bool WIDE>
+__global__ void __launch_bounds__(kThreads) copy_kernel(const T *__restrict__ in, T *__restrict__ out, const Geom g) {
+  const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < g.items; t += nthreads) {
+    int64_t coord[kR];
+    if constexpr (WIDE) {
+      int64_t rest = t;
+#pragma unroll
+      for (int k = kR - 1; k >= 0; --k) {
+        const int64_t q = rest / g.ext[k];
+        coord[k] = rest - q * g.ext[k];
+        rest = q;
+      }
+    } else {
+      uint32_t rest = (uint32_t)t;
+#pragma unroll
+      for (int k = kR - 1; k >= 0; --k) {
+        const uint32_t q = g.fd[k].d == 1 ? rest : fdiv(rest, g.fd[k]);
+        coord[k] = (int64_t)(rest - q * g.fd[k].d);
+        rest = q;
+      }
+    }
+    coord[kR - 1] *= E;
+    int64_t io = 0, oo = 0;
+#pragma unroll
+    for (int k = 0; k < kR; ++k) {
+      io += coord[k] * g.stride[0][k];
+      oo += coord[k] * g.stride[1][k];
+    }
+    const int64_t is = g.stride[0][kR - 1], os = g.stride[1][kR - 1];
+    constexpr int kRunBytes = (int)sizeof(T) * E;
+    if constexpr (kRunBytes == 4 || kRunBytes == 8 || kRunBytes == 16) {
+      using V = std::conditional_t<kRunBytes == 16, uint4, std::conditional_t<kRunBytes == 8, uint2, uint32_t>>;
+      const T *src = in + io;
+      T *dst = out + oo;
+      if (is == 1 && os == 1 && reinterpret_cast<uintptr_t>(src) % kRunBytes == 0 &&
+          reinterpret_cast<uintptr_t>(dst) % kRunBytes == 0) {
+        *reinterpret_cast<V *>(dst) = __ldg(reinterpret_cast<const V *>(src));
+        continue;
+      }
+    }
+    T v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) v[e] = in[io + e * is];
+#pragma unroll
+    for (int e = 0; e < E; ++e) out[oo + e * os] = v[e];
+  }
+}
 
 // Tiled transpose for pure copies whose output's innermost dim is strided in
 // the input (e.g. a [.., S, D] → [.., D, S] relayout): 32×32 tiles through
@@ -245,18 +395,68 @@ int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t 
       }
     }
   }
-  bool fast = d.rank == 1;
-  for (int i = 0; i < n_ops && fast; ++i) fast = d.stride[i][0] == 0 || d.stride[i][0] == 1;
-  Ops c{};
-  for (int i = 0; i < n_ops; ++i) c.p[i] = ops[i];
-  const int64_t groups = (total + E - 1) / E;
-  int64_t blocks = (groups + kThreads - 1) / kThreads;
+  // Runs of E elements along the innermost dim.
+  const int64_t inner = d.shape[d.rank - 1];
+  const int E = inner % 8 == 0 ? 8 : inner % 4 == 0 ? 4 : inner % 2 == 0 ? 2 : 1;
+  Geom g{};
+  const int lead = kR - d.rank;
+  for (int k = 0; k < kR; ++k) {
+    g.ext[k] = k < lead ? 1 : d.shape[k - lead];
+    for (int i = 0; i < n_ops; ++i) g.stride[i][k] = k < lead ? 0 : d.stride[i][k - lead];
+  }
+  g.ext[kR - 1] /= E;
+  g.items = total / E;
+  const bool wide = g.items >= (1ll << 31);
+  for (int k = 0; k < kR; ++k) {
+    const uint32_t dv = (uint32_t)(wide ? 1 : g.ext[k]);
+    uint32_t sh = 0;
+    while ((1ull << sh) < dv) ++sh;
+    g.fd[k] = FastDiv{dv, (uint32_t)((((1ull << 32) * ((1ull << sh) - dv)) / dv) + 1), sh};
+  }
+  for (int pc = 0; pc < d.n_instr; ++pc)
+    g.chan_slot[pc] = (d.instr[pc] & 0xff) == DP_OP_CHANSEL ? (int)((d.instr[pc] >> 24) & 0xff) + lead : 0;
+  int64_t blocks = (g.items + kThreads - 1) / kThreads;
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
-  if (fast)
-    region_kernel<true><<<(int)blocks, kThreads, 0, s>>>(d, c, total);
-  else
-    region_kernel<false><<<(int)blocks, kThreads, 0, s>>>(d, c, total);
+  const bool pure_copy = d.n_in == 1 && d.n_out == 1 && d.n_instr == 2 && d.dtype[0] == d.dtype[1] &&
+                         (d.instr[0] & 0xff) == DP_OP_LOAD && (d.instr[1] & 0xff) == DP_OP_STORE;
+  const dim3 grid((unsigned)blocks), block(kThreads);
+#define DP_REGION_LAUNCH(EE)                                                                          \
+  do {                                                                                                \
+    if (pure_copy) {                                                                                  \
+      switch (dtype_bytes(d.dtype[0])) {                                                              \
+        case 1:                                                                                       \
+          if (wide) copy_kernel<uint8_t, EE, true><<<grid, block, 0, s>>>((const uint8_t *)ops[0], (uint8_t *)ops[1], g); \
+          else copy_kernel<uint8_t, EE, false><<<grid, block, 0, s>>>((const uint8_t *)ops[0], (uint8_t *)ops[1], g);    \
+          break;                                                                                      \
+        case 2:                                                                                       \
+          if (wide) copy_kernel<uint16_t, EE, true><<<grid, block, 0, s>>>((const uint16_t *)ops[0], (uint16_t *)ops[1], g); \
+          else copy_kernel<uint16_t, EE, false><<<grid, block, 0, s>>>((const uint16_t *)ops[0], (uint16_t *)ops[1], g);    \
+          break;                                                                                      \
+        case 4:                                                                                       \
+          if (wide) copy_kernel<uint32_t, EE, true><<<grid, block, 0, s>>>((const uint32_t *)ops[0], (uint32_t *)ops[1], g); \
+          else copy_kernel<uint32_t, EE, false><<<grid, block, 0, s>>>((const uint32_t *)ops[0], (uint32_t *)ops[1], g);    \
+          break;                                                                                      \
+        default:                                                                                      \
+          if (wide) copy_kernel<uint64_t, EE, true><<<grid, block, 0, s>>>((const uint64_t *)ops[0], (uint64_t *)ops[1], g); \
+          else copy_kernel<uint64_t, EE, false><<<grid, block, 0, s>>>((const uint64_t *)ops[0], (uint64_t *)ops[1], g);    \
+          break;                                                                                      \
+      }                                                                                               \
+    } else if (wide) {                                                                                \
+      region_kernel<EE, true><<<grid, block, 0, s>>>(d, c, g);                                        \
+    } else {                                                                                          \
+      region_kernel<EE, false><<<grid, block, 0, s>>>(d, c, g);                                       \
+    }                                                                                                 \
+  } while (0)
+  Ops c{};
+  for (int i = 0; i < n_ops; ++i) c.p[i] = ops[i];
+  switch (E) {
+    case 8: DP_REGION_LAUNCH(8); break;
+    case 4: DP_REGION_LAUNCH(4); break;
+    case 2: DP_REGION_LAUNCH(2); break;
+    default: DP_REGION_LAUNCH(1); break;
+  }
+#undef DP_REGION_LAUNCH
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }

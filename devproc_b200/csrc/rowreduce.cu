@@ -20,6 +20,8 @@
 // LayerNorm = (x - mean) · rsqrt(var + eps) · w + b with biased variance.
 #include <cfloat>
 
+#include <type_traits>
+
 #include "dp_common.cuh"
 
 namespace dpk_rowreduce {
@@ -451,6 +453,173 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, c
   }
 }
 
+// ---------------------------------------------------------------------------
+// layernorm / rmsnorm of 16-bit rows into the same 16-bit type.  Persistent
+// warps, one row at a time: the row is held as packed 16-byte vectors (NV per
+// lane, lane L owning columns (L + 32 i) * 8 ..), and the NEXT row's loads are
+// issued before this row's statistics, so every warp keeps two rows of loads
+// in flight.  Weight and bias (with the weight offset folded in) are staged
+// once per block in shared memory in the row's own 16-bit type.
+__device__ __forceinline__ float2 unpack2(uint32_t u, __nv_bfloat16) {
+  return make_float2(__uint_as_float(u << 16), __uint_as_float(u & 0xffff0000u));
+}
+__device__ __forceinline__ float2 unpack2(uint32_t u, __half) {
+  return __half22float2(*reinterpret_cast<const __half2 *>(&u));
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __nv_bfloat16) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b, __half) {
+  __half2 h = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <typename T, int NV>
+__device__ __forceinline__ void load_row16(uint4 (&r)[NV], const T *x, int lane, int64_t cols) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const int64_t c = (int64_t)(lane + 32 * i) * 8;
+    r[i] = c < cols ? __ldg(reinterpret_cast<const uint4 *>(x + c)) : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+template <typename T, int NV, int KIND>
+__global__ void __launch_bounds__(256) norm16_kernel(dp_rowreduce_params p, const T *__restrict__ in,
+                                                     const T *__restrict__ w, const T *__restrict__ bias,
+                                                     T *__restrict__ out) {
+  extern __shared__ uint4 wb_smem[];
+  T *ws = reinterpret_cast<T *>(wb_smem);
+  T *bs = ws + p.cols;
+  for (int64_t i = threadIdx.x; i < p.cols; i += blockDim.x) {
+    ws[i] = from_f32<T>(p.has_weight ? to_f32(w[i]) + p.weight_offset : 1.0f);
+    bs[i] = from_f32<T>(KIND == DP_RED_LAYERNORM && p.has_bias ? to_f32(bias[i]) : 0.0f);
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const float n = (float)p.cols;
+  const T tag{};
+  uint4 cur[NV];
+  if (warp0 < p.rows) load_row16<T, NV>(cur, in + warp0 * p.in_row_stride, lane, p.cols);
+  for (int64_t row = warp0; row < p.rows; row += nwarps) {
+    uint4 nxt[NV];
+    const int64_t nrow = row + nwarps;
+    if (nrow < p.rows) load_row16<T, NV>(nxt, in + nrow * p.in_row_stride, lane, p.cols);
+    // Columns past the row end were loaded as zeros: they add nothing to the
+    // sums, and only live columns enter the centred second moment.
+    float s1 = 0.0f, s2 = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const uint32_t *u = reinterpret_cast<const uint32_t *>(&cur[i]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack2(u[j], tag);
+        if constexpr (KIND == DP_RED_LAYERNORM) {
+          s1 += f.x + f.y;
+        } else {
+          s1 = fmaf(f.x, f.x, s1);
+          s2 = fmaf(f.y, f.y, s2);
+        }
+      }
+    }
+    float shift = 0.0f, scale;
+    if constexpr (KIND == DP_RED_LAYERNORM) {
+      shift = warp_sum(s1) / n;
+      float q0 = 0.0f, q1 = 0.0f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        if ((int64_t)(lane + 32 * i) * 8 >= p.cols) continue;
+        const uint32_t *u = reinterpret_cast<const uint32_t *>(&cur[i]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = unpack2(u[j], tag);
+          q0 = fmaf(f.x - shift, f.x - shift, q0);
+          q1 = fmaf(f.y - shift, f.y - shift, q1);
+        }
+      }
+      scale = rsqrtf(warp_sum(q0 + q1) / n + p.eps);
+    } else {
+      scale = rsqrtf(warp_sum(s1 + s2) / n + p.eps);
+    }
+    T *y = out + row * p.out_row_stride;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int64_t c = (int64_t)(lane + 32 * i) * 8;
+      if (c >= p.cols) continue;
+      const uint4 wr = *reinterpret_cast<const uint4 *>(ws + c);
+      const uint4 br = *reinterpret_cast<const uint4 *>(bs + c);
+      const uint32_t *u = reinterpret_cast<const uint32_t *>(&cur[i]);
+      const uint32_t *wu = reinterpret_cast<const uint32_t *>(&wr);
+      const uint32_t *bu = reinterpret_cast<const uint32_t *>(&br);
+      uint4 o;
+      uint32_t *ou = reinterpret_cast<uint32_t *>(&o);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = unpack2(u[j], tag), wf = unpack2(wu[j], tag), bf = unpack2(bu[j], tag);
+        ou[j] = pack2(fmaf((f.x - shift) * scale, wf.x, bf.x), fmaf((f.y - shift) * scale, wf.y, bf.y), tag);
+      }
+      *reinterpret_cast<uint4 *>(y + c) = o;
+    }
+#pragma unroll
+    for (int i = 0; i < NV; ++i) cur[i] = nxt[i];
+  }
+}
+
+template <typename T, int NV, int KIND>
+int launch_norm16_kind(const dp_rowreduce_params &p, const T *x, const T *w, const T *b, T *y, cudaStream_t s) {
+  const int threads = 256;
+  const size_t smem = (size_t)p.cols * 2 * sizeof(T);
+  static int per_sm = 0;  // resident blocks per SM of this instantiation (the same on every B200)
+  if (per_sm == 0) {
+    if (smem > 48 * 1024)
+      DP_CHECK_CUDA(cudaFuncSetAttribute(norm16_kernel<T, NV, KIND>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem));
+    int nb = 0;
+    DP_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, norm16_kernel<T, NV, KIND>, threads, smem));
+    per_sm = nb > 0 ? nb : 1;
+  }
+  int64_t blocks = (p.rows * 32 + threads - 1) / threads;
+  const int64_t cap = (int64_t)dp::num_sms() * per_sm;
+  if (blocks > cap) blocks = cap;
+  norm16_kernel<T, NV, KIND><<<(int)blocks, threads, smem, s>>>(p, x, w, b, y);
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
+template <typename T, int NV>
+int launch_norm16_nv(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
+                     cudaStream_t s) {
+  auto *x = static_cast<const T *>(in);
+  auto *wp = static_cast<const T *>(w);
+  auto *bp = static_cast<const T *>(b);
+  auto *y = static_cast<T *>(out);
+  if (p.kind == DP_RED_LAYERNORM) return launch_norm16_kind<T, NV, DP_RED_LAYERNORM>(p, x, wp, bp, y, s);
+  return launch_norm16_kind<T, NV, DP_RED_RMSNORM>(p, x, wp, bp, y, s);
+}
+
+// 16-bit layernorm / rmsnorm rows of up to 8 × 256 columns; returns -1 when
+// the shape or layout is not one the kernel takes.
+template <typename T>
+int launch_norm16(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
+                  cudaStream_t s) {
+  auto al = [](const void *q) { return q == nullptr || reinterpret_cast<uintptr_t>(q) % 16 == 0; };
+  if (p.kind != DP_RED_LAYERNORM && p.kind != DP_RED_RMSNORM) return -1;
+  if (p.cols % 8 || p.in_row_stride % 8 || p.out_row_stride % 8 || !al(in) || !al(out)) return -1;
+  switch ((p.cols + 255) / 256) {
+    case 1: return launch_norm16_nv<T, 1>(p, in, w, b, out, s);
+    case 2: return launch_norm16_nv<T, 2>(p, in, w, b, out, s);
+    case 3: return launch_norm16_nv<T, 3>(p, in, w, b, out, s);
+    case 4: return launch_norm16_nv<T, 4>(p, in, w, b, out, s);
+    case 5: return launch_norm16_nv<T, 5>(p, in, w, b, out, s);
+    case 6: return launch_norm16_nv<T, 6>(p, in, w, b, out, s);
+    case 7: return launch_norm16_nv<T, 7>(p, in, w, b, out, s);
+    case 8: return launch_norm16_nv<T, 8>(p, in, w, b, out, s);
+    default: return -1;
+  }
+}
+
 template <typename TIn, typename TOut, int VEC, int NV>
 int launch_norm_warp(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
                      cudaStream_t s) {
@@ -536,6 +705,12 @@ int launch_norm_vec(const dp_rowreduce_params &p, const void *in, const void *w,
   auto al = [](const void *q, size_t a) { return q == nullptr || reinterpret_cast<uintptr_t>(q) % a == 0; };
   const bool ok = vec_ok && p.cols % V == 0 && p.in_row_stride % V == 0 && p.out_row_stride % V == 0 &&
                   al(in, 16) && al(w, 16) && al(b, 16) && al(out, sizeof(TOut) * V);
+  if constexpr (std::is_same<TIn, TOut>::value && sizeof(TIn) == 2) {
+    if (p.rows > 0) {
+      const int r = launch_norm16<TIn>(p, in, w, b, out, s);
+      if (r != -1) return r;
+    }
+  }
   if (ok) {
     const int64_t per_lane = (p.cols + 32 * V - 1) / (32 * V);  // vectors per lane for a warp-per-row pass
     if (per_lane <= 4) return launch_norm_warp<TIn, TOut, V, 4>(p, in, w, b, out, s);

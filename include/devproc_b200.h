@@ -188,9 +188,11 @@ int dp_embedding(const dp_embedding_params *p, const void *ids, const void *weig
  * A plan is a little-endian blob: dp_plan_header, n_slots × dp_plan_slot,
  * n_records × dp_plan_record.  Slots of kind DP_SLOT_BOUND are caller-owned
  * buffers (inputs, weights, outputs) attached with dp_program_bind; kind
- * DP_SLOT_ARENA slots live at a fixed offset of the program's arena, which
- * dp_program_create allocates once.  dp_program_run enqueues every record in
- * order on the given stream and allocates nothing. */
+ * DP_SLOT_ARENA slots live at a fixed offset of the program's arena (a
+ * multiple of 16 bytes), which dp_program_create allocates once; two arena
+ * slots may overlap (a slot can name a column block of another slot's
+ * buffer).  dp_program_run enqueues every record in order on the given
+ * stream and allocates nothing. */
 #define DP_PLAN_MAGIC 0x32425044u /* "DPB2" */
 #define DP_PLAN_VERSION 1
 #define DP_RECORD_MAX_OPERANDS 8

@@ -188,6 +188,23 @@ def test_norms_bf16(cuda):
     assert torch.allclose(ln.float(), ref, rtol=2e-2, atol=2e-2)
 
 
+@pytest.mark.parametrize("rows,cols", [(300, 1152), (64, 264), (17, 2056), (5, 8), (1000, 2048)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_norms_16bit_row_kernel(cuda, rows, cols, dtype):
+    """16-bit layernorm / rmsnorm (persistent warps, next row prefetched, weights in
+    shared memory) against fp32 torch; rows not a multiple of 256 columns included."""
+    g = torch.Generator().manual_seed(rows + cols)
+    x = (3 * torch.randn(rows, cols, generator=g) + 1).to(dtype)
+    w = (1 + 0.1 * torch.randn(cols, generator=g)).to(dtype)
+    b = (0.1 * torch.randn(cols, generator=g)).to(dtype)
+    ln = _rr(N.DP_RED_LAYERNORM, x.to(cuda), dtype, w=w.to(cuda), b=b.to(cuda), eps=1e-6)
+    ref = torch.nn.functional.layer_norm(x.float(), (cols,), w.float(), b.float(), 1e-6)
+    assert torch.allclose(ln.float(), ref, rtol=2e-2, atol=2e-2)
+    rms = _rr(N.DP_RED_RMSNORM, x.to(cuda), dtype, w=w.to(cuda), eps=1e-6)
+    ref = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    assert torch.allclose(rms.float(), ref, rtol=2e-2, atol=2e-2)
+
+
 # ------------------------------------------------------------------- region
 def _fn_of(build, *examples):
     fn = Function("t")
@@ -261,6 +278,51 @@ def test_region_transpose_and_channel_normalize(cuda):
     _, out = _compile_run(fn, {"x0": x})
     ref = interp.run_function(fn, {"x0": x})[0]
     assert torch.equal(out[0].view(torch.int16), ref.view(torch.int16))
+
+
+@pytest.mark.parametrize("shape", [(7, 33, 64), (3, 5, 12), (9, 4, 6), (2, 3, 7)])
+def test_region_runs_of_each_width(cuda, shape):
+    """Innermost extents divisible by 8, 4, 2 and 1 (run widths), bf16 and fp32
+    vector paths, a broadcast operand and a permuted one, against the oracle."""
+    g = torch.Generator().manual_seed(sum(shape))
+    x = torch.randn(*shape, generator=g).bfloat16()
+    y = torch.randn(shape[-1], generator=g)
+    z = torch.randn(shape[1], shape[0], shape[2], generator=g)
+
+    def build(a, b, c):
+        o1 = OpBuilder.to(a, "float32")
+        o2 = OpBuilder.add(o1.outputs[0], b)
+        o3 = OpBuilder.transpose(c, (1, 0, 2))
+        o4 = OpBuilder.binary("mul", o2.outputs[0], o3.outputs[0])
+        o5 = OpBuilder.gelu(o4.outputs[0], approximate="tanh")
+        o6 = OpBuilder.to(o5.outputs[0], "bfloat16")
+        return [o1, o2, o3, o4, o5, o6]
+
+    fn = _fn_of(build, x, y, z)
+    _, out = _compile_run(fn, {"x0": x, "x1": y, "x2": z})
+    ref = interp.run_function(fn, {"x0": x, "x1": y, "x2": z})[0]
+    assert torch.allclose(out[0].float(), ref.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_region_pure_copy_moves_raw_int64(cuda):
+    """A relayout copy of int64 values above 2^24 is exact (raw element moves,
+    no float round trip)."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randint(-(1 << 40), 1 << 40, (6, 10, 16), generator=g, dtype=torch.int64)
+
+    def build(a):
+        o1 = OpBuilder.transpose(a, (1, 0, 2))
+        o2 = OpBuilder.reshape(o1.outputs[0], (60, 16))
+        return [o1, o2]
+
+    fn = _fn_of(build, x)
+    prog, out = _compile_run(fn, {"x0": x})
+    assert kernels_of(prog) == ["region"]
+    assert torch.equal(out[0], x.transpose(0, 1).reshape(60, 16))
+
+
+def kernels_of(prog):
+    return [r["kernel"] for r in prog.spec.records]
 
 
 # --------------------------------------------------------------------- GEMM
@@ -400,10 +462,34 @@ def test_gemm_bf16_b_kn_tensor_core(cuda, M, Nn, K):
     assert torch.allclose(c.cpu(), ref, rtol=1e-3, atol=1e-3 * K ** 0.5)
 
 
+def test_gemm_bf16_batch_shared_b_and_residual(cuda):
+    """Zero batch strides: one weight and one [M, N] residual shared by every
+    batch (a position embedding added in the patch GEMM's epilogue)."""
+    g = torch.Generator().manual_seed(17)
+    batch, M, Nn, K = 3, 256, 384, 192
+    a = torch.randn(batch, M, K, generator=g).bfloat16()
+    w = torch.randn(Nn, K, generator=g).bfloat16()
+    bias = torch.randn(Nn, generator=g).bfloat16()
+    res = torch.randn(M, Nn, generator=g).bfloat16()
+    for c_dtype in (torch.bfloat16, torch.float32):
+        c = torch.empty(batch, M, Nn, dtype=c_dtype, device=cuda)
+        p = N.GemmParams()
+        p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.ldr, p.batch = M, Nn, K, K, K, Nn, Nn, batch
+        p.stride_a, p.stride_b, p.stride_c, p.stride_r = M * K, 0, M * Nn, 0
+        p.a_dtype = p.b_dtype = N.DP_BF16
+        p.c_dtype, p.r_dtype, p.bias_dtype = _dt(c), N.DP_BF16, N.DP_BF16
+        p.b_layout = N.DP_B_NK
+        p.epilogue = N.DP_EPI_BIAS | N.DP_EPI_RESIDUAL
+        N.gemm(p, a.to(cuda), w.to(cuda), c, bias=bias.to(cuda), residual=res.to(cuda))
+        _sync()
+        ref = a.float() @ w.float().T + bias.float() + res.float()
+        assert torch.allclose(c.cpu().float(), ref, rtol=2e-2, atol=5e-2), c_dtype
+
+
 def test_gemm_softmax_epilogue(cuda):
     """Row softmax of alpha·A·Bᵀ fused into the tensor-core epilogue, bf16 out, N < 256 masked."""
     g = torch.Generator().manual_seed(21)
-    for (M, Nn, K) in [(256, 256, 72), (300, 200, 64)]:
+    for (M, Nn, K) in [(256, 256, 72), (300, 200, 64), (200, 104, 64), (130, 136, 136)]:
         a = torch.randn(3, M, K, generator=g).bfloat16()
         b = torch.randn(3, Nn, K, generator=g).bfloat16()
         c = torch.empty(3, M, Nn, dtype=torch.bfloat16, device=cuda)

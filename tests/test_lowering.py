@@ -129,3 +129,78 @@ def test_host_ops_are_rejected():
     fn.add_op(op)
     with pytest.raises(devproc.CompilationError):
         lower(fn)
+
+
+def _small_vit(**kw):
+    return workloads.VitClassifier(layers=1, dim=128, heads=4, mlp=256, classes=16, **kw).eval()
+
+
+def test_vit_block_lowering_fusions():
+    """q/k/v run as one GEMM over a concatenated weight, the patchify reshape is
+    one padded copy, and the position embedding rides the patch GEMM's epilogue."""
+    m = _small_vit()
+    x = torch.randn(2, 3, 224, 224).bfloat16()
+    prog = devproc.compile(m, x)
+    labels = [r["label"] for r in prog.spec.records]
+    assert labels[0].startswith("copy") and "K588->592" in labels[0]
+    patch = labels[1]
+    assert patch.startswith("gemm linear M256 N128 K588 b2")
+    assert f"epi{N.DP_EPI_BIAS | N.DP_EPI_RESIDUAL}" in patch
+    assert sum("linear x3" in lb for lb in labels) == 1
+    assert not any(lb.startswith("region add") for lb in labels)
+    # the three projection weights are replaced by their concatenation (bound once)
+    names = [c.name for c in prog.spec.consts]
+    assert not any(n.endswith("attn_modules_q_parameters_weight_") for n in names)
+    fused = [n for n in names if "+" in n and n.endswith("_v_parameters_weight_")]
+    assert len(fused) == 1
+    w = prog._constants[fused[0]]
+    ref = torch.cat([m.blocks[0].attn.q.weight, m.blocks[0].attn.k.weight, m.blocks[0].attn.v.weight])
+    assert torch.equal(w, ref)
+    # the padded patch weight is a compile-time constant
+    assert any(n.endswith("|pad592") for n in names)
+
+
+def test_sibling_linears_alias_slots_and_arena():
+    """Each fused output is a column block of one arena buffer, addressed by a
+    sub-range slot 16-byte aligned inside its root."""
+    from devproc_b200.backend.b200.lowering import Lowerer
+    m = _small_vit()
+    x = torch.randn(2, 3, 224, 224).bfloat16()
+    ir = devproc.from_torch(m, x, backend="ir")
+    low = Lowerer(ir, ir.constants.keys(), ir.constants).run()
+    subs = [b for b in low.buffers if b.base is not None]
+    assert len(subs) == 2  # k and v blocks (q starts at the root)
+    for b in subs:
+        assert b.offset == b.root.offset + b.base_off and b.offset % 16 == 0
+        assert b.base_off in (128 * 2, 256 * 2)
+        assert b.offset + b.nbytes == b.root.offset + b.root.nbytes
+    assert low.aliases == []  # arena roots need no host binding
+
+
+def test_sibling_fusion_skips_epilogue_consumers():
+    """Two linears on one input where one feeds an activation stay separate, so
+    the activation stays in that GEMM's epilogue."""
+    class Two(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.a = torch.nn.Linear(64, 32)
+            self.b = torch.nn.Linear(64, 32)
+
+        def forward(self, x):
+            return torch.relu(self.a(x)) * self.b(x)
+
+    prog = devproc.compile(Two(), torch.randn(8, 64))
+    labels = [r["label"] for r in prog.spec.records]
+    assert sum(lb.startswith("gemm") for lb in labels) == 2
+    assert any(f"epi{N.DP_EPI_BIAS | N.DP_EPI_RELU}" in lb for lb in labels)
+
+
+def test_unfused_lowering_without_constant_values():
+    """Without the constants' values (plan-only lowering) nothing is fused that
+    would need a new constant."""
+    m = _small_vit()
+    x = torch.randn(2, 3, 224, 224).bfloat16()
+    ir = devproc.from_torch(m, x, backend="ir")
+    low = lower(ir, const_names=ir.constants.keys())
+    assert not any("linear x3" in lb for lb in low.labels)
+    assert low.extra_consts == {}
