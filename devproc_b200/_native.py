@@ -87,7 +87,8 @@ class RegionDesc(ctypes.Structure):
                 ("dtype", ctypes.c_int32 * DP_REGION_MAX_OPERANDS),
                 ("stride", (ctypes.c_int64 * DP_REGION_MAX_RANK) * DP_REGION_MAX_OPERANDS),
                 ("instr", ctypes.c_uint32 * DP_REGION_MAX_INSTR),
-                ("consts", ctypes.c_float * DP_REGION_MAX_CONST)]
+                ("consts", ctypes.c_float * DP_REGION_MAX_CONST),
+                ("offset", ctypes.c_int64 * DP_REGION_MAX_OPERANDS)]
 
 
 class EmbeddingParams(ctypes.Structure):

@@ -1094,16 +1094,14 @@ class RegionBuilder:
         key = (id(v.buf), v.offset, tuple(v.shape), tuple(v.strides))
         if key in self._loaded:
             return self._loaded[key]
-        if v.offset != 0:
-            raise CompilationError("region: offset views are not supported")
-        self.operands.append((View(v.buf, v.shape, self._bstrides(v)), False))
+        self.operands.append((View(v.buf, v.shape, self._bstrides(v), v.offset), False))
         r = self._reg()
         self.instr.append(("load", r, len(self.operands) - 1, 0))
         self._loaded[key] = r
         return r
 
     def store(self, v: View, r: int) -> None:
-        self.operands.append((View(v.buf, v.shape, self._bstrides(v)), True))
+        self.operands.append((View(v.buf, v.shape, self._bstrides(v), v.offset), True))
         self.instr.append(("store", 0, len(self.operands) - 1, r))
 
     def const(self, c: float) -> int:
@@ -1157,6 +1155,7 @@ class RegionBuilder:
         for new, old in enumerate(order):
             v = self.operands[old][0]
             d.dtype[new] = N.DTYPE_CODE[v.buf.dtype]
+            d.offset[new] = v.offset
             for k in range(len(shape)):
                 d.stride[new][k] = strides[new][k]
         for pc, (name, dst, a, b) in enumerate(self.instr):

@@ -141,6 +141,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
   return ok != 0;
 }
 
+// Acquire at cluster scope: for barriers that other CTAs of the cluster arrive on.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, 100000;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
@@ -148,10 +161,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Waits at most ``timeout_ns`` of wall time (%globaltimer); false on timeout.
+template <bool kClusterScope = false>
 __device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t phase, uint64_t timeout_ns) {
-  if (mbar_try_wait(bar, phase)) return true;
+  auto probe = [&]() { return kClusterScope ? mbar_try_wait_cluster(bar, phase) : mbar_try_wait(bar, phase); };
+  if (probe()) return true;
   const uint64_t t0 = globaltimer_ns();
-  while (!mbar_try_wait(bar, phase))
+  while (!probe())
     if (globaltimer_ns() - t0 > timeout_ns) return false;
   return true;
 }

@@ -30,25 +30,57 @@
 
 namespace dpk_tcgemm {
 
-constexpr int BM = 128, BN = 256, BK = 64;
-#ifndef DP_TC_STAGES
-#define DP_TC_STAGES 3
+#ifndef DP_TC_PAIR
+#define DP_TC_PAIR 1  // build switch: 0 keeps every GEMM on single-CTA tiles
 #endif
-#ifndef DP_TC_EPI_BUFS
-#define DP_TC_EPI_BUFS 2
-#endif
-constexpr int kStages = DP_TC_STAGES;
-constexpr int kEpiBufs = DP_TC_EPI_BUFS;  // output staging chunks per epilogue warp
+constexpr int kMaxDevices = 64;
+
+constexpr int BM = 128, BN = 256, BK = 64;  // per-CTA tile rows, tile columns, K block
 constexpr int kEpiWarps = 8;   // two warps per TMEM lane quadrant, each taking half of the columns
 constexpr int kThreads = 128 + 32 * kEpiWarps;
 constexpr int kGroupM = 8;
 constexpr uint32_t kTileABytes = BM * BK * 2;  // 16 KB
-constexpr uint32_t kTileBBytes = BN * BK * 2;  // 32 KB
-constexpr uint32_t kStageBytes = kTileABytes + kTileBBytes;
 constexpr int kTmemCols = 512;                 // two 256-column fp32 accumulators
-constexpr uint32_t kEpiBufBytes = 32 * 128;     // one 32-row x 128-byte output chunk
-constexpr uint32_t kEpiBytes = kEpiWarps * kEpiBufs * kEpiBufBytes;
-constexpr size_t kSmemBytes = (size_t)kStages * kStageBytes + kEpiBytes + 1024;  // + alignment slack
+constexpr uint32_t kEpiBufBytes = 32 * 64;      // one 32-row x 64-byte output chunk (64-byte swizzle)
+
+// Per CTA-group layout.  CG = 1: one CTA computes a 128 x 256 tile and loads
+// all 256 rows of B.  CG = 2: a CTA pair computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2; each CTA loads its own 128 rows of A and half of
+// B (128 rows), so a stage is 32 KB instead of 48 KB and more stages fit.
+template <int CG>
+struct Cfg;
+// Build switches for tuning: 64-wide K boxes per pipeline stage.  The operand
+// ring is 192 KB either way (single CTA: 48 KB per box, pair: 32 KB per box),
+// so more boxes per stage means fewer, longer stages and fewer barrier
+// round trips per FLOP.
+#ifndef DP_TC_PAIR_KBOXES
+#define DP_TC_PAIR_KBOXES 2
+#endif
+#ifndef DP_TC_SINGLE_KBOXES
+#define DP_TC_SINGLE_KBOXES 1
+#endif
+template <>
+struct Cfg<1> {
+  static constexpr int kKBoxes = DP_TC_SINGLE_KBOXES;  // 64-wide K boxes per stage
+  static constexpr int kStages = 4 / DP_TC_SINGLE_KBOXES;
+  static constexpr int kEpiBufs = 1;  // output staging chunks per epilogue warp
+  static constexpr int kBRows = BN;
+};
+template <>
+struct Cfg<2> {
+  static constexpr int kKBoxes = DP_TC_PAIR_KBOXES;
+  static constexpr int kStages = 6 / DP_TC_PAIR_KBOXES;
+  static constexpr int kEpiBufs = 1;
+  static constexpr int kBRows = BN / 2;
+};
+template <int CG>
+constexpr uint32_t b_box_bytes() { return (uint32_t)Cfg<CG>::kBRows * BK * 2; }
+template <int CG>
+constexpr uint32_t stage_bytes() { return Cfg<CG>::kKBoxes * (kTileABytes + b_box_bytes<CG>()); }
+template <int CG>
+constexpr size_t smem_bytes() {  // + 1 KB slack to align the operand stages to 1024 B
+  return (size_t)Cfg<CG>::kStages * stage_bytes<CG>() + (size_t)kEpiWarps * Cfg<CG>::kEpiBufs * kEpiBufBytes + 1024;
+}
 
 struct Shape {
   int M, N, K, batch;
@@ -74,6 +106,39 @@ __device__ __forceinline__ void tma_load_4d(void *smem, const CUtensorMap *map, 
       : "memory");
 }
 
+// Pair form: the completion goes to ``bar`` given as a shared::cluster
+// address, here the leader CTA's barrier (both CTAs' bytes are counted there).
+__device__ __forceinline__ void tma_load_4d_pair(void *smem, const CUtensorMap *map, int x, int y, int z, int b2,
+                                                 uint32_t bar_cluster) {
+  const int zo = z / b2, zi = z - zo * b2;
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4, %5}], [%6];" ::"r"(smem_u32(smem)),
+      "l"(map), "r"(x), "r"(y), "r"(zi), "r"(zo), "r"(bar_cluster)
+      : "memory");
+}
+
+// shared::cluster address of the object at ``p`` in CTA ``rank`` of this cluster.
+__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_store_4d(const CUtensorMap *map, const void *smem, int x, int y, int z, int b2) {
   const int zo = z / b2, zi = z - zo * b2;
   asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(map),
@@ -86,8 +151,10 @@ __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.
 __device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
-// Byte offset of 16-byte chunk j of row r in a 128-byte-swizzled box (rows of 128 B).
-__device__ __forceinline__ uint32_t swz(int r, int j) { return (uint32_t)(r * 128 + ((j ^ (r & 7)) << 4)); }
+// Byte offset of 16-byte chunk j (0..3) of row r in a 64-byte-swizzled box
+// (rows of 64 B; address bits 4-5 XOR bits 7-8).  A warp writing one chunk
+// per row touches all 32 banks once per 8 rows.
+__device__ __forceinline__ uint32_t swz(int r, int j) { return (uint32_t)(r * 64 + ((j ^ ((r >> 1) & 3)) << 4)); }
 
 __device__ __forceinline__ void prefetch_map(const CUtensorMap *map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -125,19 +192,41 @@ __host__ __device__ constexpr uint32_t instr_desc(int m, int n, int b_mn = 0) {
          ((uint32_t)(m >> 4) << 24);
 }
 
+template <int CG>
 __device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
+  if constexpr (CG == 1) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+  }
 }
 
+// Arrive on ``bar`` once the MMAs issued so far have completed; for a pair,
+// on the barrier at the same offset in both CTAs.
+template <int CG>
 __device__ __forceinline__ void mma_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
+  if constexpr (CG == 1) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+  } else {
+    const uint16_t both = 3;
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"(both)
+        : "memory");
+  }
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
@@ -251,22 +340,28 @@ __device__ __forceinline__ bool aborted(volatile int *flag) { return *flag != 0;
 // Waits in 0.2 s slices, re-reading the CTA's abort flag between slices, for
 // at most 2 s in total; on giving up records DP_DEVERR_TIMEOUT and raises the
 // abort flag so that the other roles stop too.
+// kClusterScope: the barrier also collects arrivals from the peer CTA.
+template <bool kClusterScope = false>
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, int site, volatile int *flag) {
   for (int slice = 0; slice < 10; ++slice) {
     if (aborted(flag)) return false;
-    if (mbar_wait_for(bar, parity, 200000000ull)) return true;
+    if (mbar_wait_for<kClusterScope>(bar, parity, 200000000ull)) return true;
   }
   dp_report(DP_DEVERR_TIMEOUT, site);
   *flag = 1;
   return false;
 }
 
-template <int CB>  // bytes per element of C (4: fp32, 2: bf16 / f16)
+// CB: bytes per element of C (4: fp32, 2: bf16 / f16); CG: CTAs per tile (1 or 2).
+template <int CB, int CG>
 __global__ void __launch_bounds__(kThreads, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                    const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_r,
                    dp_gemm_params p, Shape s, void *C, const void *bias, const void *res) {
   extern __shared__ uint8_t smem_raw[];
+  constexpr int kStages = Cfg<CG>::kStages;
+  constexpr int kEpiBufs = Cfg<CG>::kEpiBufs;
+  constexpr uint32_t kStageBytes = stage_bytes<CG>();
   __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full[2], acc_empty[2], res_bar[kEpiWarps],
       sm_bar[4];
   __shared__ float2 sm_part[2][4][2][32];  // softmax (max, sum) per accumulator, quadrant, column half, row
@@ -275,6 +370,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The pair's leader (rank 0) issues the MMAs for both CTAs and owns the
+  // barriers that gather both CTAs' operand bytes and epilogue releases.
+  const uint32_t rank = CG == 2 ? cluster_rank() : 0;
+  const int cid = blockIdx.x / CG, nclusters = gridDim.x / CG;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kStages; ++i) {
@@ -283,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 32 * kEpiWarps);
+      mbar_init(&acc_empty[i], CG * kEpiWarps);  // one arrival per epilogue warp of each CTA
     }
     for (int i = 0; i < kEpiWarps; ++i) mbar_init(&res_bar[i], 1);
     for (int i = 0; i < 4; ++i) mbar_init(&sm_bar[i], 64);
@@ -295,13 +394,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     prefetch_map(&map_b);
   }
   if (warp == 2) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_slot)),
-                 "r"(kTmemCols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if constexpr (CG == 1) {
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&tmem_base_slot)),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    } else {  // warp 2 of both CTAs allocates the pair's columns together
+      asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                       smem_u32(&tmem_base_slot)),
+                   "r"(kTmemCols)
+                   : "memory");
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_slot;
   volatile int *flag = &abort_flag;
@@ -310,56 +419,83 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // ---------------- TMA producer
       int it = 0;
-      for (int t = blockIdx.x; t < s.num_tiles && !aborted(flag); t += gridDim.x) {
+      for (int t = cid; t < s.num_tiles && !aborted(flag); t += nclusters) {
         int b, tm, tn;
         tile_coords(s, t, b, tm, tn);
+        const int row0 = tm * BM * CG + (int)rank * BM;               // this CTA's A rows
+        const int col0 = tn * BN + (int)rank * Cfg<CG>::kBRows;       // this CTA's B rows (N)
+        const int ba = (s.bcast & 1) ? 0 : b, bb = (s.bcast & 2) ? 0 : b;
         for (int kb = 0; kb < s.k_blocks; ++kb, ++it) {
           const int st = it % kStages;
           if (!wait_or_abort(&empty[st], ((it / kStages) & 1) ^ 1, 300 + st, flag)) break;
+          // Stage layout: kKBoxes A boxes (128 rows x 64 K), then kKBoxes B boxes
+          // (kBRows x 64 K; MN-major: kBRows / 64 chunks of 64 N x 64 K each).
           uint8_t *sa = smem + st * kStageBytes;
-          uint8_t *sb = sa + kTileABytes;
-          mbar_arrive_expect_tx(&full[st], kStageBytes);
-          const int ba = (s.bcast & 1) ? 0 : b, bb = (s.bcast & 2) ? 0 : b;
-          tma_load_4d(sa, &map_a, kb * BK, tm * BM, ba, s.batch2, &full[st]);
-          if (s.b_mn) {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j)
-              tma_load_4d(sb + j * 8192, &map_b, tn * BN + j * 64, kb * BK, bb, s.batch2, &full[st]);
+          uint8_t *sb = sa + Cfg<CG>::kKBoxes * kTileABytes;
+          uint64_t *bar_local = &full[st];
+          uint32_t bar_pair = 0;
+          if constexpr (CG == 1) {
+            mbar_arrive_expect_tx(bar_local, kStageBytes);
           } else {
-            tma_load_4d(sb, &map_b, kb * BK, tn * BN, bb, s.batch2, &full[st]);
+            // Both CTAs' bytes complete on the leader's barrier, which expects them all.
+            if (rank == 0) mbar_arrive_expect_tx(bar_local, 2 * kStageBytes);
+            bar_pair = cluster_addr(bar_local, 0);
+          }
+          auto load = [&](void *dst, const CUtensorMap *map, int x, int y, int z) {
+            if constexpr (CG == 1)
+              tma_load_4d(dst, map, x, y, z, s.batch2, bar_local);
+            else
+              tma_load_4d_pair(dst, map, x, y, z, s.batch2, bar_pair);
+          };
+#pragma unroll
+          for (int kh = 0; kh < Cfg<CG>::kKBoxes; ++kh) {
+            const int k0 = (kb * Cfg<CG>::kKBoxes + kh) * BK;
+            load(sa + kh * kTileABytes, &map_a, k0, row0, ba);
+            uint8_t *sbk = sb + kh * b_box_bytes<CG>();
+            if (s.b_mn) {
+#pragma unroll
+              for (int j = 0; j < Cfg<CG>::kBRows / 64; ++j) load(sbk + j * 8192, &map_b, col0 + j * 64, k0, bb);
+            } else {
+              load(sbk, &map_b, k0, col0, bb);
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer
-      const uint32_t idesc = instr_desc(BM, BN, s.b_mn);
+    if (lane == 0 && rank == 0) {
+      // ---------------- MMA issuer (the leader CTA's, for a pair)
+      const uint32_t idesc = instr_desc(BM * CG, BN, s.b_mn);
       int it = 0, local = 0;
-      for (int t = blockIdx.x; t < s.num_tiles && !aborted(flag); t += gridDim.x, ++local) {
+      for (int t = cid; t < s.num_tiles && !aborted(flag); t += nclusters, ++local) {
         const int a = local & 1;
-        if (!wait_or_abort(&acc_empty[a], ((local >> 1) & 1) ^ 1, 310 + a, flag)) break;
+        if (!wait_or_abort<CG == 2>(&acc_empty[a], ((local >> 1) & 1) ^ 1, 310 + a, flag)) break;
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + (uint32_t)(a * BN);
         bool ok = true;
         for (int kb = 0; kb < s.k_blocks; ++kb, ++it) {
           const int st = it % kStages;
-          if (!wait_or_abort(&full[st], (it / kStages) & 1, 320 + st, flag)) {
+          if (!wait_or_abort<CG == 2>(&full[st], (it / kStages) & 1, 320 + st, flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + st * kStageBytes);
-          const uint32_t sb = sa + kTileABytes;
+          const uint32_t sb = sa + Cfg<CG>::kKBoxes * kTileABytes;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            const uint64_t bdesc = s.b_mn ? smem_desc_mn(sb + k * 2048) : smem_desc(sb + k * 32);
-            mma_bf16(tmem_d, smem_desc(sa + k * 32), bdesc, idesc, (kb | k) != 0);
+          for (int kh = 0; kh < Cfg<CG>::kKBoxes; ++kh) {
+            if (kh > 0 && (kb * Cfg<CG>::kKBoxes + kh) * BK >= s.K) break;  // box past K: zeros only
+            const uint32_t ak = sa + kh * kTileABytes, bk = sb + kh * b_box_bytes<CG>();
+#pragma unroll
+            for (int k = 0; k < BK / 16; ++k) {
+              const uint64_t bdesc = s.b_mn ? smem_desc_mn(bk + k * 2048) : smem_desc(bk + k * 32);
+              mma_bf16<CG>(tmem_d, smem_desc(ak + k * 32), bdesc, idesc, (kb | kh | k) != 0);
+            }
           }
-          mma_commit(&empty[st]);  // stage is free once these MMAs have read it
+          mma_commit<CG>(&empty[st]);  // stage is free (in both CTAs) once these MMAs have read it
         }
         if (!ok) break;
-        mma_commit(&acc_full[a]);  // accumulator complete
+        mma_commit<CG>(&acc_full[a]);  // accumulator complete
       }
     }
   } else if (warp >= 4) {
@@ -370,10 +506,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = e >> 2;
     const int row = q * 32 + lane;
     uint8_t *ebuf = smem + kStages * kStageBytes + e * kEpiBufs * kEpiBufBytes;
-    constexpr int chunk_cols = 128 / CB;  // 32 fp32 or 64 bf16/f16 columns
+    constexpr int chunk_cols = 64 / CB;  // 16 fp32 or 32 bf16/f16 columns
     uint32_t res_phase = 0;
     int local = 0;
-    for (int t = blockIdx.x; t < s.num_tiles; t += gridDim.x, ++local) {
+    const uint32_t acc_empty_leader[2] = {CG == 2 ? cluster_addr(&acc_empty[0], 0) : 0u,
+                                          CG == 2 ? cluster_addr(&acc_empty[1], 0) : 0u};
+    for (int t = cid; t < s.num_tiles; t += nclusters, ++local) {
       const int a = local & 1;
       // tcgen05.ld is warp-collective: the whole warp continues or stops together.
       const bool got = wait_or_abort(&acc_full[a], (local >> 1) & 1, 330 + a, flag);
@@ -381,7 +519,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       int b, tm, tn;
       tile_coords(s, t, b, tm, tn);
-      const int64_t m = (int64_t)tm * BM + row;
+      const int row0 = tm * BM * CG + (int)rank * BM;  // first accumulator row of this CTA
+      const int64_t m = (int64_t)row0 + row;
       dp::Epilogue ep(p, C, bias, res, b);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
       // Row softmax epilogue: this thread's row is all N (≤ BN) columns of
@@ -445,7 +584,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (s.tma_residual) {
             if (lane == 0) {
               mbar_arrive_expect_tx(&res_bar[e], kEpiBufBytes);
-              tma_load_4d(buf, &map_r, (int)n0, tm * BM + q * 32, (s.bcast & 4) ? 0 : b, s.batch2, &res_bar[e]);
+              tma_load_4d(buf, &map_r, (int)n0, row0 + q * 32, (s.bcast & 4) ? 0 : b, s.batch2, &res_bar[e]);
             }
             const bool ok = wait_or_abort(&res_bar[e], res_phase, 340 + e, flag);
             res_phase ^= 1u;
@@ -537,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_4d(&map_c, buf, (int)n0, tm * BM + q * 32, b, s.batch2);
+            tma_store_4d(&map_c, buf, (int)n0, row0 + q * 32, b, s.batch2);
             bulk_commit();
           }
         }
@@ -557,7 +696,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[a]);
+      __syncwarp();
+      if (lane == 0) {  // this warp has read its part of accumulator a
+        if constexpr (CG == 1)
+          mbar_arrive(&acc_empty[a]);
+        else
+          mbar_arrive_cluster(acc_empty_leader[a]);
+      }
     }
     if (lane == 0) bulk_wait_all();  // every TMA store of this warp has landed
   }
@@ -571,9 +716,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // neither CTA leaves while the pair's MMAs may touch it
   if (warp == 2) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols) : "memory");
+    if constexpr (CG == 1)
+      asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                   : "memory");
+    else
+      asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                   : "memory");
   }
 }
 
@@ -598,7 +749,8 @@ EncodeTiledFn encode_fn() {
 // outer count ``b1`` with stride ``s1``, inner count ``b2`` with stride ``s2``
 // (elements); boxes of box_cols × box_rows with 128-byte swizzle.
 int make_map(CUtensorMap *map, const void *base, int dt, int64_t rows, int64_t cols, int64_t ld, int64_t b1,
-             int64_t s1, int64_t b2, int64_t s2, int box_cols, int box_rows) {
+             int64_t s1, int64_t b2, int64_t s2, int box_cols, int box_rows,
+             CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   EncodeTiledFn fn = encode_fn();
   DP_REQUIRE(fn != nullptr, DP_ERR_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
   const int eb = dp::dtype_bytes(dt);
@@ -615,7 +767,7 @@ int make_map(CUtensorMap *map, const void *base, int dt, int64_t rows, int64_t c
   cuuint32_t box[4] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(map, t, 4, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   DP_REQUIRE(r == CUDA_SUCCESS, DP_ERR_CUDA, "gemm: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return DP_OK;
 }
@@ -642,7 +794,7 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   if (st != DP_OK) return st;
   const bool b_mn = p.b_layout == DP_B_KN;
   const int64_t mb1 = b_sh ? 1 : b1, mb2 = b_sh ? 1 : b2;
-  if (b_mn)  // [K, N], N contiguous: boxes of 64 N × 64 K
+  if (b_mn)  // [K, N], N contiguous: boxes of 64 N × 64 K (the same for a CTA pair)
     st = make_map(&mb, B, DP_BF16, p.K, p.N, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, 64, BK);
   else
     st = make_map(&mb, B, DP_BF16, p.N, p.K, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, BK, BN);
@@ -653,26 +805,31 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
                          (b2 == 1 || (p.stride_c2 * cb) % 16 == 0) && al16(C) && (cb == 4 || cb == 2);
   bool tma_res = false;
   if (tma_store) {
-    st = make_map(&mc, C, p.c_dtype, p.M, p.N, p.ldc, b1, p.stride_c, b2, p.stride_c2, 128 / cb, 32);
+    st = make_map(&mc, C, p.c_dtype, p.M, p.N, p.ldc, b1, p.stride_c, b2, p.stride_c2, 64 / cb, 32,
+                  CU_TENSOR_MAP_SWIZZLE_64B);
     if (st != DP_OK) return st;
     if ((p.epilogue & DP_EPI_RESIDUAL) && p.r_dtype == p.c_dtype && (p.ldr * cb) % 16 == 0 &&
         (p.batch == 1 || (p.stride_r * cb) % 16 == 0) && (b2 == 1 || (p.stride_r2 * cb) % 16 == 0) && al16(res)) {
-      st = r_sh ? make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, 1, 0, 1, 0, 128 / cb, 32)
-                : make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, b1, p.stride_r, b2, p.stride_r2, 128 / cb, 32);
+      st = r_sh ? make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, 1, 0, 1, 0, 64 / cb, 32, CU_TENSOR_MAP_SWIZZLE_64B)
+                : make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, b1, p.stride_r, b2, p.stride_r2, 64 / cb, 32,
+                           CU_TENSOR_MAP_SWIZZLE_64B);
       if (st != DP_OK) return st;
       tma_res = true;
     }
   }
+  // A CTA pair per 256-row tile when both operands fill more than one CTA's share.
+  const int cg = (DP_TC_PAIR && p.M > BM && p.N > BN / 2) ? 2 : 1;
   Shape s;
   s.M = (int)p.M;
   s.N = (int)p.N;
   s.K = (int)p.K;
   s.batch = (int)p.batch;
-  s.tiles_m = (int)((p.M + BM - 1) / BM);
+  s.tiles_m = (int)((p.M + BM * cg - 1) / (BM * cg));
   s.tiles_n = (int)((p.N + BN - 1) / BN);
   s.tiles_per_batch = s.tiles_m * s.tiles_n;
   s.num_tiles = s.tiles_per_batch * s.batch;
-  s.k_blocks = (int)((p.K + BK - 1) / BK);
+  const int kstep = BK * (cg == 2 ? Cfg<2>::kKBoxes : Cfg<1>::kKBoxes);  // K per stage
+  s.k_blocks = (int)((p.K + kstep - 1) / kstep);
   DP_REQUIRE(tma_store || !(p.epilogue & DP_EPI_SOFTMAX), DP_ERR_UNSUPPORTED,
              "gemm: the softmax epilogue needs a 16-byte aligned C with 16-byte row strides");
   s.batch2 = (int)b2;
@@ -682,20 +839,56 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   s.c_bytes = cb;
   s.bcast = (a_sh ? 1 : 0) | (b_sh ? 2 : 0) | (r_sh ? 4 : 0);
   DP_REQUIRE(p.N < (1ll << 31) && p.K < (1ll << 31), DP_ERR_UNSUPPORTED, "gemm: N or K too large");
-  static bool attr_set = false;
-  if (!attr_set) {
-    DP_CHECK_CUDA(
-        cudaFuncSetAttribute(tc_gemm_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    DP_CHECK_CUDA(
-        cudaFuncSetAttribute(tc_gemm_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes));
-    attr_set = true;
+  if (cg == 2 && !b_mn) {  // each CTA of the pair loads 128 rows of B
+    st = make_map(&mb, B, DP_BF16, p.N, p.K, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, BK, Cfg<2>::kBRows);
+    if (st != DP_OK) return st;
   }
-  int grid = num_sms();
-  if (grid > s.num_tiles) grid = s.num_tiles;
-  if (cb == 4)
-    tc_gemm_kernel<4><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, mr, p, s, C, bias, res);
-  else
-    tc_gemm_kernel<2><<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, mr, p, s, C, bias, res);
+  int dev = 0;
+  DP_CHECK_CUDA(cudaGetDevice(&dev));
+  DP_REQUIRE(dev >= 0 && dev < kMaxDevices, DP_ERR_UNSUPPORTED, "gemm: device ordinal out of range");
+  if (cg == 1) {
+    static bool attr_set[kMaxDevices] = {};
+    if (!attr_set[dev]) {
+      DP_CHECK_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<4, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem_bytes<1>()));
+      DP_CHECK_CUDA(cudaFuncSetAttribute(tc_gemm_kernel<2, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem_bytes<1>()));
+      attr_set[dev] = true;
+    }
+    int grid = num_sms();
+    if (grid > s.num_tiles) grid = s.num_tiles;
+    if (cb == 4)
+      tc_gemm_kernel<4, 1><<<grid, kThreads, smem_bytes<1>(), stream>>>(ma, mb, mc, mr, p, s, C, bias, res);
+    else
+      tc_gemm_kernel<2, 1><<<grid, kThreads, smem_bytes<1>(), stream>>>(ma, mb, mc, mr, p, s, C, bias, res);
+  } else {
+    auto kern = cb == 4 ? tc_gemm_kernel<4, 2> : tc_gemm_kernel<2, 2>;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = smem_bytes<2>();
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    // Co-resident pairs (clusters never straddle a GPC, so this can be below SMs / 2).
+    static int pairs[kMaxDevices][2] = {};
+    int &np = pairs[dev][cb == 4 ? 0 : 1];
+    if (np == 0) {
+      DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_bytes<2>()));
+      cfg.gridDim = dim3(2 * (num_sms() / 2));
+      int n = 0;
+      DP_CHECK_CUDA(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+      DP_REQUIRE(n > 0, DP_ERR_CUDA, "gemm: no CTA pair fits on this device");
+      np = n;
+    }
+    const int grid_pairs = np < s.num_tiles ? np : s.num_tiles;
+    cfg.gridDim = dim3(2 * grid_pairs);
+    DP_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, mr, p, s, C, bias, res));
+  }
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }

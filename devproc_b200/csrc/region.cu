@@ -71,6 +71,7 @@ struct FastDiv {
 
 struct Geom {
   int64_t items;                                // work items (runs of E elements)
+  int64_t off[DP_REGION_MAX_OPERANDS];          // element offset of each operand's first element
   int64_t ext[kR];                              // extents; ext[kR-1] counted in runs
   int64_t stride[DP_REGION_MAX_OPERANDS][kR];   // element strides, right-aligned
   FastDiv fd[kR];                               // divisors of ext (32-bit path)
@@ -189,7 +190,7 @@ __global__ void __launch_bounds__(kThreads) region_kernel(const dp_region_desc d
       const uint32_t ins = d.instr[pc];
       const int op = ins & 0xff, dst = (ins >> 8) & 0xff, a = (ins >> 16) & 0xff, b = (ins >> 24) & 0xff;
       if (op == DP_OP_LOAD || op == DP_OP_STORE) {
-        int64_t off = 0;
+        int64_t off = g.off[a];
 #pragma unroll
         for (int k = 0; k < kR; ++k) off += coord[k] * g.stride[a][k];
         if (op == DP_OP_LOAD)
@@ -243,7 +244,7 @@ __global__ void __launch_bounds__(kThreads) copy_kernel(const T *__restrict__ in
       }
     }
     coord[kR - 1] *= E;
-    int64_t io = 0, oo = 0;
+    int64_t io = g.off[0], oo = g.off[1];
 #pragma unroll
     for (int k = 0; k < kR; ++k) {
       io += coord[k] * g.stride[0][k];
@@ -277,6 +278,7 @@ __global__ void __launch_bounds__(kThreads) copy_kernel(const T *__restrict__ in
 struct TDims {
   int rank;  // of the collapsed iteration space
   int jdim;  // dim with unit input stride
+  int64_t in_base, out_base;  // element offsets of the first elements
   int64_t shape[DP_REGION_MAX_RANK];
   int64_t in_stride[DP_REGION_MAX_RANK];
   int64_t out_stride[DP_REGION_MAX_RANK];
@@ -288,7 +290,7 @@ __global__ void __launch_bounds__(256) transpose_copy_kernel(TDims d, const T *_
   const int last = d.rank - 1;
   const int64_t j0 = (int64_t)blockIdx.y * 32, l0 = (int64_t)blockIdx.x * 32;
   // offsets of the other dims
-  int64_t z = blockIdx.z, in_off = 0, out_off = 0;
+  int64_t z = blockIdx.z, in_off = d.in_base, out_off = d.out_base;
   for (int k = last; k >= 0; --k) {
     if (k == last || k == d.jdim) continue;
     const int64_t c = z % d.shape[k];
@@ -330,6 +332,7 @@ int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t 
   for (int i = 0; i < n_ops; ++i) {
     DP_REQUIRE(ops[i] != nullptr, DP_ERR_ARG, "region: null operand " + std::to_string(i));
     DP_REQUIRE(dtype_bytes(d.dtype[i]) > 0, DP_ERR_ARG, "region: bad dtype of operand " + std::to_string(i));
+    DP_REQUIRE(d.offset[i] >= 0, DP_ERR_ARG, "region: negative offset of operand " + std::to_string(i));
   }
   // Validate the program on the host so the kernel never indexes out of range.
   for (int pc = 0; pc < d.n_instr; ++pc) {
@@ -374,6 +377,8 @@ int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t 
       TDims t;
       t.rank = d.rank;
       t.jdim = jdim;
+      t.in_base = d.offset[0];
+      t.out_base = d.offset[1];
       int64_t zcount = 1;
       for (int k = 0; k < d.rank; ++k) {
         t.shape[k] = d.shape[k];
@@ -406,6 +411,7 @@ int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t 
   }
   g.ext[kR - 1] /= E;
   g.items = total / E;
+  for (int i = 0; i < n_ops; ++i) g.off[i] = d.offset[i];
   const bool wide = g.items >= (1ll << 31);
   for (int k = 0; k < kR; ++k) {
     const uint32_t dv = (uint32_t)(wide ? 1 : g.ext[k]);

@@ -146,8 +146,9 @@ int dp_gemm(const dp_gemm_params *p, const void *A, const void *B, void *C,
 /* ---- elementwise region (one kernel per fused IR dataflow region) --------
  * A small register program run per element of an iteration space of up to
  * DP_REGION_MAX_RANK dims.  Operands 0..n_in-1 are inputs, n_in.. are
- * outputs; each has a dtype and per-dim element strides (0 = broadcast).
- * Instruction word: opcode | dst << 8 | a << 16 | b << 24. */
+ * outputs; each has a dtype, per-dim element strides (0 = broadcast) and the
+ * element offset of its first element from the bound pointer (a slice of a
+ * larger buffer).  Instruction word: opcode | dst << 8 | a << 16 | b << 24. */
 #define DP_REGION_MAX_OPERANDS 8
 #define DP_REGION_MAX_RANK 6
 #define DP_REGION_MAX_INSTR 64
@@ -171,6 +172,7 @@ typedef struct dp_region_desc {
   int64_t stride[DP_REGION_MAX_OPERANDS][DP_REGION_MAX_RANK];
   uint32_t instr[DP_REGION_MAX_INSTR];
   float consts[DP_REGION_MAX_CONST];
+  int64_t offset[DP_REGION_MAX_OPERANDS];
 } dp_region_desc;
 int dp_region(const dp_region_desc *d, const void *const *operands, void *stream);
 
