@@ -55,7 +55,13 @@ mean = _ops.mean
 layer_norm = _ops.layer_norm
 rms_norm = _ops.rms_norm
 embedding = _ops.embedding
+sdpa = _ops.sdpa
+slice = _ops.slice
+cat = _ops.cat
+rope = _ops.rope
 load_vla_module = _ops.load_vla_module
+# For torch modules: a rotary embedding that capture keeps as one op.
+from .torch_ops import rope as torch_rope, rope_tables  # noqa: E402
 
 # Reference names (src/devproc/__init__.py:46-47) kept as aliases of the only backend.
 TritonCompiler = B200Compiler

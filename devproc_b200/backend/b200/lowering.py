@@ -241,6 +241,16 @@ class Lowerer:
             return us[0]
         return None
 
+    def derived_const(self, name: str, dtype: str, shape) -> Buffer:
+        """The one slot of a constant the lowering derives (a concatenated or
+        padded weight), shared by every record that reads it."""
+        for n, b in self.new_consts:
+            if n == name:
+                return b
+        buf = self.new_buffer("const", dtype, tuple(shape), name)
+        self.new_consts.append((name, buf))
+        return buf
+
     def alias(self, buf: Buffer, byte_off: int, name: str) -> Buffer:
         """A slot for the bytes of ``buf`` from ``byte_off`` (16-byte aligned) on."""
         root = buf.root
@@ -263,11 +273,27 @@ class Lowerer:
         return r
 
     def contiguous(self, value: Value) -> View:
-        """View of ``value``; a strided view is first copied to a new buffer."""
+        """Row-major view of ``value`` starting at its slot's first byte; a
+        strided view is first copied to a new buffer, a row-major slice of a
+        larger buffer gets a sub-range slot when 16-byte aligned."""
         v = self.views[value.name]
         if v.contiguous:
             return v
+        if View(v.buf, v.shape, v.strides).contiguous:
+            b = self.based(v, value.name)
+            if b is not None:
+                return b
         return self.copy_view(v, value.name + "_c")
+
+    def based(self, v: View, name: str) -> Optional[View]:
+        """``v`` with its element offset folded into a sub-range slot (offset 0),
+        or None when the offset is not a multiple of 16 bytes."""
+        if v.offset == 0:
+            return v
+        nbytes = v.offset * DTYPE_BYTES[v.buf.dtype]
+        if (v.buf.base_off + nbytes) % 16:
+            return None
+        return View(self.alias(v.buf, nbytes, name + "@%d" % v.offset), v.shape, v.strides, 0)
 
     def padded_rows(self, value: Value, K: int) -> View:
         """[rows, K] copy of ``value`` (leading dims flattened) with rows Kp = ⌈K/8⌉·8 apart."""
@@ -285,8 +311,7 @@ class Lowerer:
             if name not in self.const_tensors:
                 w = self.const_tensors[src.buf.name].reshape(-1).as_strided((rows, K), flat, src.offset)
                 self.const_tensors[name] = torch.nn.functional.pad(w, (0, Kp - K))
-            buf = self.new_buffer("const", t.dtype, (rows, Kp), name)
-            self.new_consts.append((name, buf))
+            buf = self.derived_const(name, t.dtype, (rows, Kp))
             return View(buf, (rows, K), (Kp, 1))
         if flat is None:
             src = self.contiguous(value)
@@ -435,6 +460,26 @@ class Lowerer:
             self.views[op.outputs[0].name] = View(v.buf, tuple(v.shape[d] for d in dims),
                                                   tuple(v.strides[d] for d in dims), v.offset)
             return
+        if name == "slice":
+            v = self.views[op.inputs[0].name]
+            d, st = op.attr("dim"), op.attr("step")
+            strides = list(v.strides)
+            strides[d] *= st
+            self.views[op.outputs[0].name] = View(v.buf, tuple(op.outputs[0].type.shape), tuple(strides),
+                                                  v.offset + op.attr("start") * v.strides[d])
+            return
+        if name == "expand":
+            v = self.views[op.inputs[0].name]
+            shape = tuple(op.attr("shape"))
+            lead = len(shape) - len(v.shape)
+            strides = tuple(0 if i < lead or v.shape[i - lead] != s else v.strides[i - lead]
+                            for i, s in enumerate(shape))
+            self.views[op.outputs[0].name] = View(v.buf, shape, strides, v.offset)
+            return
+        if name == "cat":
+            return self.lower_cat(op)
+        if name == "rope":
+            return self.lower_rope(op)
         if name in ELEMENTWISE:
             return self.lower_region(op)
         if name == "sdpa":
@@ -582,8 +627,7 @@ class Lowerer:
             if name not in self.const_tensors:
                 self.const_tensors[name] = torch.cat([self.const_tensors[u.inputs[idx].name].reshape(-1, *shape[1:])
                                                       for u in group], 0)
-            buf = self.new_buffer("const", group[0].inputs[idx].type.dtype, shape, name)
-            self.new_consts.append((name, buf))
+            buf = self.derived_const(name, group[0].inputs[idx].type.dtype, shape)
             return View(buf, tuple(shape), contiguous_strides(tuple(shape)))
 
         w = fused_const(1, (Ntot, K))
@@ -794,19 +838,26 @@ class Lowerer:
             dim = -1
         d = dim % rank
         xv = self.views[x_val.name]
+        cols = t.shape[d]
+        rows = t.numel // cols
+        row_stride = cols
         if d != rank - 1:
             # move the reduced dim last with a strided copy
             perm = [i for i in range(rank) if i != d] + [d]
             xv = self.copy_view(View(xv.buf, tuple(xv.shape[i] for i in perm),
                                      tuple(xv.strides[i] for i in perm), xv.offset), x_val.name + "_t")
         elif not xv.contiguous:
-            xv = self.copy_view(xv, x_val.name + "_c")
-        cols = t.shape[d]
-        rows = t.numel // cols
+            # rows of unit-stride elements a fixed distance apart are read in place
+            flat = view_reshape(xv.shape, xv.strides, (rows, cols))
+            based = self.based(xv, x_val.name) if flat is not None and (flat[1] == 1 or cols == 1) else None
+            if based is not None:
+                xv, row_stride = based, flat[0]
+            else:
+                xv = self.copy_view(xv, x_val.name + "_c")
         if t.dtype not in ("float32", "bfloat16", "float16"):
             raise CompilationError(f"{op.name}: input dtype {t.dtype} unsupported (float types only)")
         p = N.RowReduceParams()
-        p.rows, p.cols, p.in_row_stride = rows, cols, cols
+        p.rows, p.cols, p.in_row_stride = rows, cols, row_stride
         p.in_dtype = N.DTYPE_CODE[t.dtype]
         kind = {"sum": N.DP_RED_SUM, "max": N.DP_RED_MAX, "min": N.DP_RED_MIN, "mean": N.DP_RED_MEAN,
                 "argmax": N.DP_RED_ARGMAX, "softmax": N.DP_RED_SOFTMAX, "rms_norm": N.DP_RED_RMSNORM,
@@ -887,23 +938,31 @@ class Lowerer:
         dt = tq.dtype
 
         def operand(value: Value, rows_shape):
-            """(view, row stride, outer batch stride, inner batch stride) of a
-            [B, H, rows, D] operand read in place when its strides allow it."""
+            """(view, strides as [B, H, rows, D]) of an operand read in place when
+            its strides and start allow it (a slice of a fused projection)."""
             vw = self.views[value.name]
             st = view_reshape(vw.shape, vw.strides, rows_shape)
-            if st is None or st[3] != 1 or any(x % 8 for x in st[:3]):
+            based = None
+            if st is not None and st[3] == 1 and not any(x % 8 for x in st[:3]):
+                based = self.based(vw, value.name)
+            if based is None:
                 vw = self.contiguous(value)
                 st = view_reshape(vw.shape, vw.strides, rows_shape) or contiguous_strides(rows_shape)
-            return vw, st
+                return vw, st
+            return based, st
 
         if g == 1:
             qv, qst = operand(q, (B, Hq, L, D))
             q_b, q_b2, q_ld = qst[0], qst[1], qst[2]
             rows_q, batch, batch2 = L, B * Hq, Hq
         else:
-            # query heads of one group stacked as one (g·L)-row operand
-            qv = self.contiguous(q)
-            q_b, q_b2, q_ld = Hq * L * D, g * L * D, D
+            # Query heads of one group stacked as one (g·L)-row operand: in place
+            # when a group's g·L rows are evenly strided (head stride = L · row stride).
+            qv, qst = operand(q, (B, Hq, L, D))
+            if qst[1] != L * qst[2]:
+                qv = self.contiguous(q)
+                qst = contiguous_strides((B, Hq, L, D))
+            q_b, q_b2, q_ld = qst[0], g * qst[1], qst[2]
             rows_q, batch, batch2 = g * L, B * Hk, Hk
         kv, kst = operand(k, (B, Hk, S, D))
         # V is read in place as the GEMM's [K = keys, N = Dv] operand (N contiguous)
@@ -911,21 +970,25 @@ class Lowerer:
         # bf16 rows of at most 256 keys: the score GEMM's epilogue computes the row
         # softmax itself (one tensor-core tile holds a whole row) and writes bf16
         # probabilities; otherwise fp32 scores go through a separate row softmax.
-        fused = dt == "bfloat16" and S <= 256 and S % 8 == 0
-        probs = View(self.new_buffer("arena", dt, (batch, rows_q, S), op.outputs[0].name + "_p"),
-                     (batch, rows_q, S), contiguous_strides((batch, rows_q, S)))
+        fused = dt == "bfloat16" and S <= 256
+        # Score / probability rows padded to Sp = ⌈S/8⌉·8 columns so the value
+        # GEMM reads them as a tensor-core operand; the pad is never read
+        # (the operand maps end at S).
+        Sp = (S + 7) // 8 * 8
+        probs = View(self.new_buffer("arena", dt, (batch, rows_q, Sp), op.outputs[0].name + "_p"),
+                     (batch, rows_q, S), (rows_q * Sp, Sp, 1))
         if fused:
             scores = probs
         else:
-            scores = View(self.new_buffer("arena", "float32", (batch, rows_q, S), op.outputs[0].name + "_s"),
-                          (batch, rows_q, S), contiguous_strides((batch, rows_q, S)))
+            scores = View(self.new_buffer("arena", "float32", (batch, rows_q, Sp), op.outputs[0].name + "_s"),
+                          (batch, rows_q, S), (rows_q * Sp, Sp, 1))
         p = N.GemmParams()
         p.M, p.N, p.K = rows_q, S, D
-        p.lda, p.ldb, p.ldc = q_ld, kst[2], S
+        p.lda, p.ldb, p.ldc = q_ld, kst[2], Sp
         p.batch, p.batch2 = batch, batch2
         p.stride_a, p.stride_a2 = q_b, q_b2
         p.stride_b, p.stride_b2 = kst[0], kst[1]
-        p.stride_c, p.stride_c2 = batch2 * rows_q * S, rows_q * S
+        p.stride_c, p.stride_c2 = batch2 * rows_q * Sp, rows_q * Sp
         p.a_dtype = p.b_dtype = N.DTYPE_CODE[dt]
         p.c_dtype = N.DTYPE_CODE[dt] if fused else N.DP_F32
         p.b_layout = N.DP_B_NK
@@ -937,14 +1000,14 @@ class Lowerer:
         if not fused:
             r = N.RowReduceParams()
             r.kind, r.in_dtype, r.out_dtype = N.DP_RED_SOFTMAX, N.DP_F32, N.DTYPE_CODE[dt]
-            r.rows, r.cols, r.in_row_stride, r.out_row_stride = B * Hq * L, S, S, S
+            r.rows, r.cols, r.in_row_stride, r.out_row_stride = B * Hq * L, S, Sp, Sp
             self.emit(N.DP_K_ROWREDUCE, [scores.buf, None, None, probs.buf], r,
                       f"rowreduce attn-softmax {B * Hq * L}x{S}", 0, scores.buf.nbytes + probs.buf.nbytes)
         p2 = N.GemmParams()
         p2.M, p2.N, p2.K = rows_q, Dv, S
-        p2.lda, p2.ldb = S, vst[2]
+        p2.lda, p2.ldb = Sp, vst[2]
         p2.batch, p2.batch2 = batch, batch2
-        p2.stride_a, p2.stride_a2 = batch2 * rows_q * S, rows_q * S
+        p2.stride_a, p2.stride_a2 = batch2 * rows_q * Sp, rows_q * Sp
         p2.stride_b, p2.stride_b2 = vst[0], vst[1]
         p2.a_dtype = p2.b_dtype = p2.c_dtype = N.DTYPE_CODE[dt]
         p2.b_layout = N.DP_B_KN
@@ -961,6 +1024,53 @@ class Lowerer:
         self.emit(N.DP_K_GEMM, [probs.buf, vv.buf, buf, None, None], p2,
                   f"gemm attn-values b{batch} M{rows_q} N{Dv} K{S} {dt}", 2 * B * Hq * L * S * Dv,
                   probs.buf.nbytes + vv.buf.nbytes + buf.nbytes)
+
+    # ---------------------------------------------------------- cat / rope
+    def lower_cat(self, op: Op) -> None:
+        """One copy region per input into its slice of the output buffer."""
+        out = self.new_value_view(op.outputs[0])
+        d = op.attr("dim")
+        pos = 0
+        for v in op.inputs:
+            src = self.views[v.name]
+            n = v.type.shape[d]
+            if n:
+                dst = View(out.buf, src.shape, out.strides, out.offset + pos * out.strides[d])
+                rb = RegionBuilder(src.shape)
+                rb.store(dst, rb.load(src))
+                self.emit_region(rb, f"cat {v.name} -> {op.outputs[0].name}[{pos}:{pos + n}]")
+            pos += n
+
+    def lower_rope(self, op: Op) -> None:
+        """out1 = x1·c1 − x2·s1, out2 = x2·c2 + x1·s2 over the two halves of the
+        last dim, as one region over the half shape with six loads and two
+        stores (c1 = c2, s1 = s2 for half-width tables)."""
+        x_val, c_val, s_val = op.inputs
+        xv = self.views[x_val.name]
+        D = x_val.type.shape[-1]
+        h = D // 2
+        half = tuple(x_val.type.shape[:-1]) + (h,)
+
+        def halves(v: View):
+            lo = View(v.buf, tuple(v.shape[:-1]) + (h,) if v.shape[-1] == D else tuple(v.shape), v.strides,
+                      v.offset)
+            if v.shape[-1] == h:
+                return lo, lo
+            return lo, View(v.buf, lo.shape, v.strides, v.offset + h * v.strides[-1])
+
+        x1, x2 = halves(xv)
+        c1, c2 = halves(self.views[c_val.name])
+        s1, s2 = halves(self.views[s_val.name])
+        out = self.new_value_view(op.outputs[0])
+        o1, o2 = halves(out)
+        rb = RegionBuilder(half)
+        rx1, rx2 = rb.load(x1), rb.load(x2)
+        lo = rb.binary("sub", rb.binary("mul", rx1, rb.load(c1)), rb.binary("mul", rx2, rb.load(s1)))
+        rb.store(o1, lo)
+        rb.release(lo)
+        hi = rb.binary("add", rb.binary("mul", rx2, rb.load(c2)), rb.binary("mul", rx1, rb.load(s2)))
+        rb.store(o2, hi)
+        self.emit_region(rb, f"rope {half}")
 
     # ------------------------------------------------------------ embedding
     def lower_embedding(self, op: Op) -> None:
@@ -1103,6 +1213,12 @@ class RegionBuilder:
     def store(self, v: View, r: int) -> None:
         self.operands.append((View(v.buf, v.shape, self._bstrides(v), v.offset), True))
         self.instr.append(("store", 0, len(self.operands) - 1, r))
+
+    def release(self, r: int) -> None:
+        """Return temporary ``r`` (already stored) to the register pool."""
+        if r in self._temps:
+            self._temps.discard(r)
+            self._free.append(r)
 
     def const(self, c: float) -> int:
         self.consts.append(float(c))

@@ -124,12 +124,15 @@ class B200CompiledProgram(CompiledProgram):
         with torch.cuda.device(dev):
             prog = N.NativeProgram(self.spec.plan, self.device_id)
             for c in self.spec.consts:
-                t = self._constants[c.name]
-                t = t.detach().to(device=dev, dtype=TORCH_DTYPES[c.dtype]).contiguous()
+                # one device copy per constant; it stays referenced for as long as a slot points at it
+                t = self._dev_consts.get(c.name)
+                if t is None:
+                    t = self._constants[c.name]
+                    t = t.detach().to(device=dev, dtype=TORCH_DTYPES[c.dtype]).contiguous()
+                    self._dev_consts[c.name] = t
                 if list(t.shape) != list(c.shape):
                     raise N.DevProcError(N.DP_ERR_SHAPE, f"constant {c.name}: shape {tuple(t.shape)} != "
                                                          f"{tuple(c.shape)}")
-                self._dev_consts[c.name] = t
                 self._bind_slot(prog, c.slot, t.data_ptr(), t.numel() * t.element_size())
             for o in self.spec.outputs:
                 t = torch.empty(o.shape, dtype=TORCH_DTYPES[o.dtype], device=dev)

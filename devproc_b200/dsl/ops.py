@@ -173,6 +173,26 @@ def embedding(ids: KernelTensor, weight: KernelTensor) -> KernelTensor:
     return _emit(OpBuilder.embedding(ids.ir_value, weight.ir_value))
 
 
+def sdpa(q: KernelTensor, k: KernelTensor, v: KernelTensor, scale: Optional[float] = None) -> KernelTensor:
+    """new: softmax(q·kᵀ·scale)·v; k / v may have fewer heads (grouped-query)."""
+    return _emit(OpBuilder.sdpa(q.ir_value, k.ir_value, v.ir_value, scale))
+
+
+def slice(tensor: KernelTensor, dim: int, start: int, end: int, step: int = 1) -> KernelTensor:
+    """new: tensor[..., start:end:step, ...] along ``dim`` (a view)."""
+    return _emit(OpBuilder.slice(tensor.ir_value, dim, start, end, step))
+
+
+def cat(tensors: Sequence[KernelTensor], dim: int = 0) -> KernelTensor:
+    """new: concatenation along ``dim``."""
+    return _emit(OpBuilder.cat([t.ir_value for t in tensors], dim))
+
+
+def rope(tensor: KernelTensor, cos: KernelTensor, sin: KernelTensor) -> KernelTensor:
+    """new: rotate-half rotary embedding, tensor·cos + [-x2, x1]·sin."""
+    return _emit(OpBuilder.rope(tensor.ir_value, cos.ir_value, sin.ir_value))
+
+
 # ------------------------------------------------ host-side value kinds
 class _HostHandle:
     def __init__(self, ir_value: Value, name: Optional[str] = None):

@@ -58,6 +58,7 @@ def _target_name(target) -> str:
 class FXToIRConverter:
     op_map: Dict[str, str] = field(default_factory=get_fx_op_map)
     value_map: Dict[Any, Value] = field(default_factory=dict)
+    tuple_map: Dict[Any, List[Value]] = field(default_factory=dict)  # split / chunk results
     gm: Optional[torch.fx.GraphModule] = field(default=None, init=False)
     example_inputs: Tuple[Any, ...] = field(default_factory=tuple, init=False)
 
@@ -65,6 +66,7 @@ class FXToIRConverter:
         self.gm = gm
         self.example_inputs = tuple(example_inputs)
         self.value_map = {}
+        self.tuple_map = {}
         self.fn = Function(type(gm).__name__ if gm is not None else "fx_graph")
         self.fn.constants = {}
         self._ph_index = 0
@@ -174,9 +176,59 @@ class FXToIRConverter:
     def _on_call_function(self, node) -> None:
         t = node.target
         if t is operator.getitem:
-            src = node.args[0]
-            raise ValueError(f"Unsupported FX function: getitem of {getattr(src, 'name', src)}")
+            return self._getitem(node)
         self._dispatch(node, _target_name(t), node.args, node.kwargs)
+
+    def _getitem(self, node) -> None:
+        """``tuple[i]`` of a split/chunk result, or tensor indexing with ints,
+        slices, ``None`` and ``...`` (basic indexing: views, no gathers)."""
+        src, idx = node.args
+        if src in self.tuple_map:
+            self.value_map[node] = self.tuple_map[src][idx]
+            return
+        x = self._v(src)
+        items = list(idx) if isinstance(idx, tuple) else [idx]
+        rank = len(x.type.shape)
+        n_real = sum(1 for it in items if it is not None and it is not Ellipsis)
+        if n_real > rank:
+            raise ValueError(f"getitem {node.name}: too many indices")
+        if Ellipsis in items:
+            e = items.index(Ellipsis)
+            items = items[:e] + [slice(None)] * (rank - n_real) + items[e + 1:]
+        items += [slice(None)] * (rank - sum(1 for it in items if it is not None))
+        cur, d = x, 0
+        squeeze, unsqueeze = [], []
+        out_pos = 0
+        for it in items:
+            if it is None:
+                unsqueeze.append(out_pos)
+                out_pos += 1
+                continue
+            if isinstance(it, int):
+                size = cur.type.shape[d]
+                i = it + size if it < 0 else it
+                if not 0 <= i < size:
+                    raise ValueError(f"getitem {node.name}: index {it} out of range")
+                op = OpBuilder.slice(cur, d, i, i + 1)
+                self.fn.block.add_op(op)
+                cur = op.outputs[0]
+                squeeze.append(d)
+            elif isinstance(it, slice):
+                if not (it.start is None and it.stop is None and it.step in (None, 1)):
+                    if any(isinstance(b, torch.fx.Node) for b in (it.start, it.stop, it.step)):
+                        raise ValueError(f"getitem {node.name}: data-dependent slice bounds")
+                    op = OpBuilder.slice(cur, d, 0 if it.start is None else it.start,
+                                         cur.type.shape[d] if it.stop is None else it.stop, it.step or 1)
+                    self.fn.block.add_op(op)
+                    cur = op.outputs[0]
+                out_pos += 1
+            else:
+                raise ValueError(f"getitem {node.name}: unsupported index {it!r} (tensor indexing)")
+            d += 1
+        shape = self._ex_shape(node)
+        if tuple(cur.type.shape) != shape:
+            cur = self._reshape_value(cur, shape)
+        self.value_map[node] = cur
 
     def _on_output(self, node) -> None:
         res = node.args[0]
@@ -405,6 +457,51 @@ class FXToIRConverter:
         self.fn.block.add_op(lin)
         y = self._reshape_value(lin.outputs[0], (B, gh, gw, O))
         self._emit(node, OpBuilder.transpose(y, (0, 3, 1, 2)))
+
+    def _op_narrow(self, node, args, kwargs):
+        x = self._v(args[0])
+        dim, start, length = self._arg(node, 1, "dim"), self._arg(node, 2, "start"), self._arg(node, 3, "length")
+        self._emit(node, OpBuilder.slice(x, dim, start, start + length))
+
+    def _slices(self, node, x: Value, dim: int, sizes) -> None:
+        outs, pos = [], 0
+        for n in sizes:
+            op = OpBuilder.slice(x, dim, pos, pos + n)
+            self.fn.block.add_op(op)
+            outs.append(op.outputs[0])
+            pos += n
+        self.tuple_map[node] = outs
+
+    def _op_chunk(self, node, args, kwargs):
+        x = self._v(args[0])
+        chunks, dim = self._arg(node, 1, "chunks"), self._arg(node, 2, "dim", 0)
+        size = x.type.shape[dim]
+        step = -(-size // chunks)
+        self._slices(node, x, dim, [min(step, size - i) for i in range(0, size, step)])
+
+    def _op_split(self, node, args, kwargs):
+        x = self._v(args[0])
+        sz, dim = self._arg(node, 1, "split_size_or_sections", self._arg(node, 1, "split_size")), \
+            self._arg(node, 2, "dim", 0)
+        size = x.type.shape[dim]
+        if isinstance(sz, int):
+            sizes = [min(sz, size - i) for i in range(0, size, sz)]
+        else:
+            sizes = list(sz)
+        self._slices(node, x, dim, sizes)
+
+    def _op_cat(self, node, args, kwargs):
+        xs = self._arg(node, 0, "tensors")
+        dim = self._arg(node, 1, "dim", 0)
+        self._emit(node, OpBuilder.cat([self._v(t) for t in xs], dim))
+
+    def _op_expand(self, node, args, kwargs):
+        x = self._v(args[0])
+        self._emit(node, OpBuilder.expand(x, self._ex_shape(node)))
+
+    def _op_rope(self, node, args, kwargs):
+        x, c, s_ = (self._v(a) for a in args[:3])
+        self._emit(node, OpBuilder.rope(x, c, s_))
 
     def _op_sdpa(self, node, args, kwargs):
         q, k, v = (self._v(a) for a in args[:3])

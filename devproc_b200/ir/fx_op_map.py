@@ -31,5 +31,8 @@ def get_fx_op_map() -> Dict[str, str]:
         "view": "reshape", "reshape": "reshape", "flatten": "reshape", "unsqueeze": "reshape",
         "squeeze": "reshape", "permute": "permute", "transpose": "transpose", "t": "transpose",
         "interpolate": "interpolate",
+        # slicing and joining
+        "narrow": "narrow", "chunk": "chunk", "split": "split", "cat": "cat", "concat": "cat",
+        "concatenate": "cat", "expand": "expand", "rope": "rope",
     }
     return m

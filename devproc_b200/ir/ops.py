@@ -17,15 +17,19 @@ got wrong for the pipelines this backend runs:
   integer type (the reference kept uint8 at ops.py:235-238).
 
 New ops needed by the pipelines: gelu, tanh, silu, exp, neg, sum, max, mean,
-layer_norm, rms_norm, embedding, reshape, sdpa.
+layer_norm, rms_norm, embedding, reshape, sdpa, slice, expand, cat, rope.
 """
 
+import builtins
 from typing import Optional, Sequence, Tuple
 
 from .base import Op, Value
 from .function import Function
 from .types import (FLOAT_DTYPES, DictType, ScalarType, StringType, TensorType,
                     TokenizerType, Type)
+
+
+builtins_slice = builtins.slice
 
 
 def _tensor(v: Value, opname: str) -> TensorType:
@@ -145,6 +149,66 @@ class OpBuilder:
             raise ValueError(f"transpose: {dims} is not a permutation of rank {rank}")
         shape = tuple(t.shape[d] for d in dims)
         return Op("transpose", [x], [_new(TensorType(shape, t.dtype, t.device))], {"dims": dims})
+
+    @staticmethod
+    def slice(x: Value, dim: int, start: int, end: int, step: int = 1) -> Op:
+        """x[..., start:end:step, ...] along ``dim`` (Python slice bounds, clamped)."""
+        t = _tensor(x, "slice")
+        d = _norm_dim(dim, len(t.shape))
+        if step < 1:
+            raise ValueError("slice: step must be positive")
+        start, end, step = builtins_slice(start, end, step).indices(t.shape[d])
+        n = len(range(start, end, step))
+        shape = tuple(n if i == d else s for i, s in enumerate(t.shape))
+        return Op("slice", [x], [_new(TensorType(shape, t.dtype, t.device))],
+                  {"dim": d, "start": start, "end": end, "step": step})
+
+    @staticmethod
+    def expand(x: Value, shape: Tuple[int, ...]) -> Op:
+        """Broadcast ``x`` to ``shape`` (torch ``expand``; -1 keeps a dim)."""
+        t = _tensor(x, "expand")
+        shape = tuple(int(s) for s in shape)
+        lead = len(shape) - len(t.shape)
+        if lead < 0:
+            raise ValueError("expand: fewer dims than the input")
+        full = []
+        for i, s in enumerate(shape):
+            src = t.shape[i - lead] if i >= lead else 1
+            s = src if s == -1 else s
+            if src != s and src != 1:
+                raise ValueError(f"expand: {t.shape} cannot expand to {shape}")
+            full.append(s)
+        return Op("expand", [x], [_new(TensorType(tuple(full), t.dtype, t.device))], {"shape": tuple(full)})
+
+    @staticmethod
+    def cat(xs: Sequence[Value], dim: int = 0) -> Op:
+        """Concatenate along ``dim``; all inputs share the other dims and the dtype."""
+        ts = [_tensor(v, "cat") for v in xs]
+        if not ts:
+            raise ValueError("cat: no inputs")
+        d = _norm_dim(dim, len(ts[0].shape))
+        for t in ts[1:]:
+            if len(t.shape) != len(ts[0].shape) or t.dtype != ts[0].dtype or any(
+                    a != b for i, (a, b) in enumerate(zip(t.shape, ts[0].shape)) if i != d):
+                raise ValueError("cat: inputs differ outside the cat dim")
+        shape = tuple(sum(t.shape[d] for t in ts) if i == d else s for i, s in enumerate(ts[0].shape))
+        return Op("cat", list(xs), [_new(TensorType(shape, ts[0].dtype, ts[0].device))], {"dim": d})
+
+    @staticmethod
+    def rope(x: Value, cos: Value, sin: Value) -> Op:
+        """Rotary position embedding, rotate-half form: with x = [x1, x2] split
+        in halves along the last dim, out = x·cos + [-x2, x1]·sin.  ``cos`` and
+        ``sin`` broadcast to x and hold either the full last dim D or its half."""
+        t = _tensor(x, "rope")
+        tc, ts = _tensor(cos, "rope"), _tensor(sin, "rope")
+        D = t.shape[-1]
+        if D % 2:
+            raise ValueError("rope: the last dim must be even")
+        for tt in (tc, ts):
+            if tt.shape[-1] not in (D, D // 2):
+                raise ValueError(f"rope: cos/sin last dim {tt.shape[-1]} is neither {D} nor {D // 2}")
+            broadcast_shapes(t.shape[:-1], tt.shape[:-1])
+        return Op("rope", [x, cos, sin], [_new(TensorType(t.shape, t.dtype, t.device))])
 
     @staticmethod
     def to(x: Value, dtype: str, device: Optional[str] = None) -> Op:

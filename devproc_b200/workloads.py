@@ -11,6 +11,8 @@ seed 1), and models are random-init modules of the stated architecture.
   argmax → int32 (the fp32 token pipeline).
 """
 
+import math
+
 import torch
 
 from .dsl import ops as dp
@@ -149,12 +151,16 @@ class VitClassifier(torch.nn.Module):
                     prm.copy_(torch.randn(prm.shape, generator=g) * 0.02)
         self.to(dtype)
 
-    def forward(self, pixels):
+    def encode(self, pixels):
+        """Token features [B, tokens, dim] after the final LayerNorm."""
         x = self.patch(pixels).flatten(2).transpose(1, 2)
         x = x + self.pos
         for blk in self.blocks:
             x = blk(x)
-        x = self.post_ln(x)
+        return self.post_ln(x)
+
+    def forward(self, pixels):
+        x = self.encode(pixels)
         y = self.head(x.mean(dim=1))
         return y if self.logits else y.argmax(-1)
 
@@ -162,3 +168,156 @@ class VitClassifier(torch.nn.Module):
 def vit_flops_per_image(layers=27, dim=1152, mlp=4304, tokens=256, heads=16, classes=1000, patch_k=588):
     per_layer = 2 * tokens * dim * dim * 4 + 2 * tokens * dim * mlp * 2 + 2 * 2 * tokens * tokens * dim
     return layers * per_layer + 2 * tokens * patch_k * dim + 2 * dim * classes
+
+
+# --------------------------------------------------------------- pi0.5-shaped
+class DecoderBlock(torch.nn.Module):
+    """Pre-norm decoder block of the Gemma family: RMSNorm → grouped-query
+    attention with rotary embeddings → RMSNorm → GeGLU MLP (tanh GELU).
+    ``forward`` returns the new hidden state and this layer's post-rotary
+    keys and values; given ``prefix_kv`` the queries attend to the prefix
+    keys / values followed by the block's own (bidirectionally)."""
+
+    def __init__(self, dim: int, heads: int, kv_heads: int, head_dim: int, mlp: int, eps: float = 1e-6):
+        super().__init__()
+        self.heads, self.kv_heads, self.head_dim = heads, kv_heads, head_dim
+        self.ln1 = torch.nn.RMSNorm(dim, eps=eps)
+        self.q = torch.nn.Linear(dim, heads * head_dim, bias=False)
+        self.k = torch.nn.Linear(dim, kv_heads * head_dim, bias=False)
+        self.v = torch.nn.Linear(dim, kv_heads * head_dim, bias=False)
+        self.o = torch.nn.Linear(heads * head_dim, dim, bias=False)
+        self.ln2 = torch.nn.RMSNorm(dim, eps=eps)
+        self.gate = torch.nn.Linear(dim, mlp, bias=False)
+        self.up = torch.nn.Linear(dim, mlp, bias=False)
+        self.down = torch.nn.Linear(mlp, dim, bias=False)
+
+    def forward(self, x, cos, sin, prefix_k=None, prefix_v=None):
+        from .torch_ops import rope
+        b, n, _ = x.shape
+        h = self.ln1(x)
+        q = rope(self.q(h).view(b, n, self.heads, self.head_dim).transpose(1, 2), cos, sin)
+        k = rope(self.k(h).view(b, n, self.kv_heads, self.head_dim).transpose(1, 2), cos, sin)
+        v = self.v(h).view(b, n, self.kv_heads, self.head_dim).transpose(1, 2)
+        ka, va = k, v
+        if prefix_k is not None:
+            ka = torch.cat([prefix_k, k], dim=2)
+            va = torch.cat([prefix_v, v], dim=2)
+        a = torch.nn.functional.scaled_dot_product_attention(q, ka, va, enable_gqa=True)
+        x = x + self.o(a.transpose(1, 2).reshape(b, n, self.heads * self.head_dim))
+        h = self.ln2(x)
+        x = x + self.down(torch.nn.functional.gelu(self.gate(h), approximate="tanh") * self.up(h))
+        return x, k, v
+
+
+class Pi05Policy(torch.nn.Module):
+    """pi0.5-shaped vision-language-action policy with random-init weights.
+
+    Per sample: ``cams`` camera images (already preprocessed, bf16
+    [3, 224, 224]) → the SigLIP-shaped encoder (no head) → projection to the
+    language width; ``text`` token ids → embedding · √width; one prefill over
+    image + text tokens through the Gemma-2B-shaped decoder (18 layers, width
+    2048, 8 query heads sharing 1 key/value head of 256, GeGLU 16384) whose
+    per-layer keys / values the action expert reads; then ``steps`` flow-
+    matching denoise steps from N(0, 1) noise [horizon, action_dim] through
+    the action expert (18 layers, width 1024, same heads, MLP 4096), each
+    step x ← x − v(x, t) / steps with t = 1, 1 − 1/steps, …  Time enters as a
+    sinusoidal embedding through a SiLU MLP added to the action tokens.
+    Returns the denoised actions (fp32).
+    """
+
+    def __init__(self, cams: int = 3, text: int = 48, vocab: int = 257152, width: int = 2048, layers: int = 18,
+                 heads: int = 8, kv_heads: int = 1, head_dim: int = 256, mlp: int = 16384,
+                 expert_width: int = 1024, expert_layers: int = 18, expert_mlp: int = 4096,
+                 horizon: int = 50, action_dim: int = 32, steps: int = 10, vit: dict = None, seed: int = 1,
+                 dtype=torch.bfloat16):
+        super().__init__()
+        from .torch_ops import rope_tables
+        vit = dict(vit or {})
+        self.cams, self.steps = cams, steps
+        self.width = width
+        self.vision = VitClassifier(seed=seed, dtype=torch.float32, logits=True, **vit)
+        vdim = self.vision.post_ln.normalized_shape[0]
+        self.vision.head = torch.nn.Identity()
+        self.img_tokens = cams * self.vision.pos.shape[1]
+        self.proj = torch.nn.Linear(vdim, width)
+        self.embed = torch.nn.Embedding(vocab, width)
+        self.blocks = torch.nn.ModuleList([DecoderBlock(width, heads, kv_heads, head_dim, mlp) for _ in range(layers)])
+        self.expert = torch.nn.ModuleList([DecoderBlock(expert_width, heads, kv_heads, head_dim, expert_mlp)
+                                           for _ in range(expert_layers)])
+        self.action_in = torch.nn.Linear(action_dim, expert_width)
+        self.time_mlp = torch.nn.Sequential(torch.nn.Linear(expert_width, expert_width), torch.nn.SiLU(),
+                                            torch.nn.Linear(expert_width, expert_width))
+        self.final_ln = torch.nn.RMSNorm(expert_width, eps=1e-6)
+        self.action_out = torch.nn.Linear(expert_width, action_dim)
+        prefix = self.img_tokens + text
+        cos, sin = rope_tables(prefix + horizon, head_dim)
+        self.register_buffer("cos", cos)
+        self.register_buffer("sin", sin)
+        # sinusoidal embedding of t = 1, 1 - 1/steps, ..., 1/steps
+        t = 1.0 - torch.arange(steps, dtype=torch.float64) / steps
+        freq = torch.exp(-math.log(10000.0) * torch.arange(expert_width // 2, dtype=torch.float64) /
+                         (expert_width // 2))
+        ang = t[:, None] * 1000.0 * freq[None, :]
+        self.register_buffer("t_emb", torch.cat([torch.sin(ang), torch.cos(ang)], -1).float())
+        self.prefix = prefix
+        g = torch.Generator().manual_seed(seed + 1)
+        with torch.no_grad():
+            for name, prm in self.named_parameters():
+                if name.startswith("vision."):
+                    continue
+                if name.endswith("bias"):
+                    prm.zero_()
+                elif ".ln" in name or name.startswith("final_ln"):
+                    prm.fill_(1.0)
+                else:
+                    prm.copy_(torch.randn(prm.shape, generator=g) * 0.02)
+        self.to(dtype)
+        self.t_emb.data = self.t_emb.data.to(dtype)
+
+    def forward(self, pixels, text_ids, noise):
+        b = text_ids.shape[0]
+        vis = self.vision.encode(pixels)  # [b * cams, tokens, vdim]
+        img = self.proj(vis.reshape(b, self.img_tokens, -1))
+        txt = self.embed(text_ids) * math.sqrt(self.width)
+        x = torch.cat([img, txt], dim=1)
+        cos_p, sin_p = self.cos[: self.prefix], self.sin[: self.prefix]
+        cos_e, sin_e = self.cos[self.prefix:], self.sin[self.prefix:]
+        kv = []
+        for blk in self.blocks:
+            x, k, v = blk(x, cos_p, sin_p)
+            kv.append((k, v))
+        a = noise
+        for s in range(self.steps):
+            h = self.action_in(a.to(self.action_in.weight.dtype)) + self.time_mlp(self.t_emb[s])
+            for blk, (k, v) in zip(self.expert, kv):
+                h, _, _ = blk(h, cos_e, sin_e, k, v)
+            vel = self.action_out(self.final_ln(h)).float()
+            a = a - vel * (1.0 / self.steps)
+        return a
+
+
+def pi05_inputs(batch: int = 64, cams: int = 3, text: int = 48, vocab: int = 257152, horizon: int = 50,
+                action_dim: int = 32, seed: int = 0):
+    """(uint8 camera images [batch·cams, 480, 640, 3], int32 ids [batch, text], fp32 noise)."""
+    g = torch.Generator().manual_seed(seed)
+    imgs = torch.randint(0, 256, (batch * cams, PREPROC_IN_H, PREPROC_IN_W, 3), generator=g, dtype=torch.uint8)
+    ids = torch.randint(0, vocab, (batch, text), generator=g, dtype=torch.int32)
+    noise = torch.randn(batch, horizon, action_dim, generator=g)
+    return imgs, ids, noise
+
+
+def pi05_flops_per_sample(cams=3, text=48, width=2048, layers=18, heads=8, kv_heads=1, head_dim=256, mlp=16384,
+                          expert_width=1024, expert_layers=18, expert_mlp=4096, horizon=50, action_dim=32, steps=10):
+    """Multiply-add FLOPs (2 per MAC) of one sample: vision, projection,
+    prefill and the denoise steps (GEMMs and attention)."""
+    img = cams * 256
+    prefix = img + text
+    vision = cams * vit_flops_per_image(classes=0)
+    proj = 2 * img * 1152 * width
+    qkvo = 2 * width * head_dim * (2 * heads + 2 * kv_heads)
+    prefill = layers * (prefix * (qkvo + 2 * 3 * width * mlp) + 2 * 2 * heads * prefix * prefix * head_dim)
+    eq = 2 * expert_width * head_dim * (2 * heads + 2 * kv_heads)
+    per_step = expert_layers * (horizon * (eq + 2 * 3 * expert_width * expert_mlp)
+                                + 2 * 2 * heads * horizon * (prefix + horizon) * head_dim)
+    per_step += 2 * horizon * (action_dim * expert_width * 2) + 2 * 2 * expert_width * expert_width
+    return vision + proj + prefill + steps * per_step

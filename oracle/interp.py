@@ -97,6 +97,23 @@ def _eval(op, x, out_v):
         return x[0].permute(*a["dims"]).contiguous()
     if n == "reshape":
         return x[0].reshape(a["shape"])
+    if n == "slice":
+        idx = [slice(None)] * x[0].dim()
+        idx[a["dim"]] = slice(a["start"], a["end"], a["step"])
+        return x[0][tuple(idx)].contiguous()
+    if n == "expand":
+        return x[0].expand(a["shape"]).contiguous()
+    if n == "cat":
+        return torch.cat(x, dim=a["dim"])
+    if n == "rope":  # out = x*cos + rotate_half(x)*sin, rotate_half(x) = [-x2, x1]
+        xf, c, s_ = x[0].float(), x[1].float(), x[2].float()
+        half = xf.shape[-1] // 2
+        if c.shape[-1] == half:
+            c = torch.cat([c, c], -1)
+        if s_.shape[-1] == half:
+            s_ = torch.cat([s_, s_], -1)
+        rot = torch.cat([-xf[..., half:], xf[..., :half]], -1)
+        return _cast(xf * c + rot * s_, out_v)
     if n == "matmul":  # reference test_triton.py:104 (torch.matmul), fp32 accumulate
         return _cast(torch.matmul(x[0].float(), x[1].float()), out_v)
     if n == "linear":  # reference linear_kernel, templates/matmul.py:152-156; test_triton.py:124

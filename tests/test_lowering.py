@@ -204,3 +204,55 @@ def test_unfused_lowering_without_constant_values():
     low = lower(ir, const_names=ir.constants.keys())
     assert not any("linear x3" in lb for lb in low.labels)
     assert low.extra_consts == {}
+
+
+def test_small_policy_lowering():
+    """The scaled-down pi0.5 policy captures and lowers: one rope region per
+    rotated tensor, fused q/k/v, grouped-query attention with padded score
+    rows, and expert keys / values joined to the prefix ones by cat copies."""
+    m = workloads.Pi05Policy(cams=2, text=8, vocab=1000, width=128, layers=2, heads=4, kv_heads=1, head_dim=32,
+                             mlp=256, expert_width=64, expert_layers=2, expert_mlp=128, horizon=10, action_dim=8,
+                             steps=3, vit=dict(layers=1, dim=64, heads=2, mlp=128, image=56)).eval()
+    pix = torch.randn(4, 3, 56, 56).bfloat16()
+    ids = torch.randint(0, 1000, (2, 8), dtype=torch.int32)
+    noise = torch.randn(2, 10, 8)
+    prog = devproc.compile(m, pix, ids, noise)
+    labels = [r["label"] for r in prog.spec.records]
+    assert sum(lb.startswith("rope") for lb in labels) == 2 * (2 + 3 * 2)
+    assert sum("linear x3" in lb for lb in labels) == 1 + 2 + 3 * 2
+    assert any("attn-scores+softmax b2 M40 N50" in lb for lb in labels)
+    assert sum(lb.startswith("cat") for lb in labels) >= 4 * 3 * 2
+    assert prog.spec.outputs[0].shape == [2, 10, 8] and prog.spec.outputs[0].dtype == "float32"
+
+
+def test_fx_slicing_and_joining():
+    """Indexing with slices / ints / None / ..., chunk, split, narrow and cat
+    through the FX frontend agree with eager on the oracle."""
+    from oracle import interp
+
+    class M(torch.nn.Module):
+        def forward(self, x):
+            a, b = x.chunk(2, dim=-1)
+            c = x[..., 1:7:2, None, :4]
+            d = torch.narrow(x, 1, 2, 3)
+            e, f, _ = torch.split(x, [3, 4, 1], dim=1)
+            return torch.cat([a * b, d.sum(-1, keepdim=True).expand(-1, -1, 4)], 1), c, e + f[:, :3]
+
+    x = torch.randn(2, 8, 8)
+    ir = devproc.from_torch(M(), x, backend="ir")
+    got = interp.run_function(ir, {ir.inputs[0].name: x})
+    ref = M()(x)
+    for g_, r_ in zip(got, ref):
+        assert torch.allclose(g_, r_, atol=1e-5), (g_.shape, r_.shape)
+
+
+def test_derived_constants_have_one_slot_each():
+    """A fused weight that several records read (the action expert's q/k/v in
+    every denoise step) is one constant slot, bound once."""
+    m = workloads.Pi05Policy(cams=2, text=8, vocab=1000, width=128, layers=2, heads=4, kv_heads=1, head_dim=32,
+                             mlp=256, expert_width=64, expert_layers=2, expert_mlp=128, horizon=10, action_dim=8,
+                             steps=3, vit=dict(layers=1, dim=64, heads=2, mlp=128, image=56)).eval()
+    prog = devproc.compile(m, torch.randn(4, 3, 56, 56).bfloat16(), torch.randint(0, 1000, (2, 8), dtype=torch.int32),
+                           torch.randn(2, 10, 8))
+    names = [c.name for c in prog.spec.consts]
+    assert len(names) == len(set(names))
