@@ -49,7 +49,8 @@ def parse():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--cpu-sample", type=int, default=64, help="images in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=["preprocess", "gemm", "reduce", "token", "vit"], default="preprocess",
+    ap.add_argument("--workload", choices=["preprocess", "gemm", "reduce", "token", "vit", "vla"],
+                    default="preprocess",
                     help="preprocess = the headline pipeline; gemm / reduce / token = template microbenches "
                          "and the fp32 token pipeline")
     return ap.parse_args()
@@ -186,6 +187,50 @@ def micro_vit(args, dev):
             "config": {"workload": "preprocess 128x480x640x3 u8 -> SigLIP-So400m/14-shaped ViT (27 layers, width "
                                    "1152, 16 heads, MLP 4304) -> mean-pool -> Linear 1152->1000 -> argmax, bf16, "
                                    "random-init weights N(0, 0.02)"}}
+
+
+def micro_vla(args, dev):
+    """pi0.5-shaped policy at batch 64: 192 camera images (uint8 480x640) preprocessed, the SigLIP-shaped
+    encoder, a Gemma-2B-shaped prefill over 816 tokens and 10 action-expert denoise steps, bf16."""
+    import devproc
+    from devproc_b200 import workloads
+    B = 64
+    t0 = time.time()
+    m = workloads.Pi05Policy(device=dev).eval()
+    build_s = time.time() - t0
+    imgs, ids, noise = workloads.pi05_inputs(B)
+    pre = devproc.compile(workloads.vision_preprocess, imgs)
+    t0 = time.time()
+    pol = devproc.compile(m, torch.zeros(B * 3, 3, 224, 224, dtype=torch.bfloat16, device=dev),
+                          ids.to(dev), noise.to(dev))
+    compile_s = time.time() - t0
+    d_imgs, d_ids, d_noise = imgs.to(dev), ids.to(dev), noise.to(dev)
+    names = {v.name: v for v in pol.ir_function.inputs}
+    order = [i.name for i in pol.spec.inputs]
+    feed = {n: (d_ids if "ids" in n else d_noise if "noise" in n else None) for n in order}
+    pix_name = [n for n in order if "pixels" in n][0]
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        x = pre.run(images=d_imgs, to_cpu=False)[0]
+        feed[pix_name] = x
+        return pol.run(**feed, to_cpu=False)[0]
+
+    ms = time_region(step, min(args.steps, 3), args.warmup, stream)
+    flops = workloads.pi05_flops_per_sample() * B
+    peak, kind = tensor_peak()
+    tf = flops / (ms / 1e3) / 1e12
+    return {"metric": "policy samples/sec (pi0.5-shaped VLA)", "value": B / (ms / 1e3), "unit": "samples/s",
+            "higher_is_better": True, "dtype": "bf16", "ms_per_step": ms, "tflops": tf,
+            "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s", "frac": tf / peak,
+                         "peak_kind": kind},
+            "launches_per_step": len(pre.spec.records) + len(pol.spec.records), "build_s": build_s,
+            "compile_s": compile_s, "arena_gib": pol.spec.arena_bytes / 2 ** 30,
+            "config": {"workload": "pi0.5-shaped policy, batch 64: 3 cameras 480x640 u8 -> SigLIP-So400m/14-shaped "
+                                   "encoder (768 tokens) -> proj 1152->2048; 48 text ids; Gemma-2B-shaped prefill "
+                                   "(18 layers, width 2048, 8q/1kv heads of 256, GeGLU 16384, RMSNorm, RoPE) over "
+                                   "816 tokens; action expert (18 layers, width 1024, MLP 4096) x 10 flow-matching "
+                                   "steps on 50x32 noise; bf16, random-init weights N(0, 0.02)"}}
 
 
 def micro_token(args, dev):
@@ -332,7 +377,8 @@ def main():
     from devproc_b200 import workloads
 
     if args.workload != "preprocess":
-        fn = {"gemm": micro_gemm, "reduce": micro_reduce, "token": micro_token, "vit": micro_vit}[args.workload]
+        fn = {"gemm": micro_gemm, "reduce": micro_reduce, "token": micro_token, "vit": micro_vit,
+              "vla": micro_vla}[args.workload]
         line = fn(args, dev)
         line.update({"n_gpus": world, "data": "synthetic"})
         if rank == 0:

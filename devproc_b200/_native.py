@@ -39,6 +39,7 @@ DP_LAYOUT_NHWC, DP_LAYOUT_NCHW = 0, 1
 DP_B_NK, DP_B_KN = 0, 1
 DP_EPI_BIAS, DP_EPI_RELU, DP_EPI_GELU_ERF, DP_EPI_GELU_TANH, DP_EPI_RESIDUAL, DP_EPI_SILU = 1, 2, 4, 8, 16, 32
 DP_EPI_SOFTMAX = 64
+DP_EPI_MUL = 128
 
 DP_REGION_MAX_OPERANDS, DP_REGION_MAX_RANK, DP_REGION_MAX_INSTR = 8, 6, 64
 DP_REGION_MAX_CONST, DP_REGION_MAX_REGS = 32, 8

@@ -783,6 +783,16 @@ class Lowerer:
                 else:
                     break
                 c_dtype = nxt.outputs[0].type.dtype
+            elif nxt.name == "mul" and residual is None and not shared_rows:
+                # a gated unit: this GEMM times an already computed same-shape operand
+                # (gelu(gate) · up of a GeGLU MLP, with the gate GEMM lowered first)
+                other = nxt.inputs[1] if nxt.inputs[0] is cur else nxt.inputs[0]
+                if (other is cur or tuple(other.type.shape) != shp or other.type.dtype not in FLOAT_DTYPES
+                        or tuple(nxt.outputs[0].type.shape) != shp or not self.ready(other)):
+                    break
+                residual = self.contiguous(other)
+                epi |= N.DP_EPI_MUL
+                c_dtype = nxt.outputs[0].type.dtype
             elif nxt.name in ("relu", "gelu", "silu") and not act_done and residual is None:
                 if nxt.name == "relu":
                     epi |= N.DP_EPI_RELU

@@ -1,5 +1,5 @@
 // GEMM epilogue shared by the FFMA and tcgen05 GEMMs:
-//   v = acc (+ bias[n]) → activation → (+ residual[m, n]) → cast → C[m, n].
+//   v = acc (+ bias[n]) → activation → (+ or × residual[m, n]) → cast → C[m, n].
 #pragma once
 
 #include "dp_common.cuh"
@@ -36,6 +36,7 @@ struct Epilogue {
     if (p.epilogue & DP_EPI_GELU_TANH) v = act_gelu_tanh(v);
     if (p.epilogue & DP_EPI_SILU) v = v / (1.0f + expf(-v));
     if (p.epilogue & DP_EPI_RESIDUAL) v += load_as_f32(res, r_off + m * p.ldr + n, p.r_dtype);
+    if (p.epilogue & DP_EPI_MUL) v *= load_as_f32(res, r_off + m * p.ldr + n, p.r_dtype);
     return v;
   }
 

@@ -18,7 +18,9 @@ int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C, 
   DP_REQUIRE(p.c_dtype == DP_F32 || p.c_dtype == DP_BF16 || p.c_dtype == DP_F16, DP_ERR_ARG,
              "gemm: C must be f32/bf16/f16");
   if (p.epilogue & DP_EPI_BIAS) DP_REQUIRE(bias != nullptr && dtype_bytes(p.bias_dtype) > 0, DP_ERR_ARG, "gemm: bias");
-  if (p.epilogue & DP_EPI_RESIDUAL) {
+  DP_REQUIRE(!((p.epilogue & DP_EPI_RESIDUAL) && (p.epilogue & DP_EPI_MUL)), DP_ERR_ARG,
+             "gemm: the residual is either added or multiplied, not both");
+  if (p.epilogue & (DP_EPI_RESIDUAL | DP_EPI_MUL)) {
     DP_REQUIRE(res != nullptr && dtype_bytes(p.r_dtype) > 0, DP_ERR_ARG, "gemm: residual");
     DP_REQUIRE(p.ldr >= p.N, DP_ERR_SHAPE, "gemm: ldr < N");
   }

@@ -529,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // swaps them through shared memory, guarded by a per-quadrant mbarrier.
       float sm_max = 0.0f, sm_inv = 1.0f, sm_l2 = 0.0f;
       const bool softmax = (p.epilogue & DP_EPI_SOFTMAX) != 0;
+      const bool res_mul = (p.epilogue & DP_EPI_MUL) != 0;
       const int col_lo = half * (BN / 2);
       const int col_hi = col_lo + BN / 2;
       if (softmax) {
@@ -612,10 +613,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               if (p.epilogue)
                 epi16(x, nb, s.N, p.epilogue, bias, p.bias_dtype, CB == 2);
             }
-            if ((p.epilogue & DP_EPI_RESIDUAL) && !s.tma_residual) {
+            if ((p.epilogue & (DP_EPI_RESIDUAL | DP_EPI_MUL)) && !s.tma_residual) {
 #pragma unroll
               for (int e = 0; e < 16; ++e)
-                if (m < s.M && nb + e < s.N) x[e] += load_as_f32(res, ep.r_off + m * p.ldr + nb + e, p.r_dtype);
+                if (m < s.M && nb + e < s.N) {
+                  const float rv = load_as_f32(res, ep.r_off + m * p.ldr + nb + e, p.r_dtype);
+                  x[e] = res_mul ? x[e] * rv : x[e] + rv;
+                }
             }
             // This step's 16 columns are 16-byte chunks step*2.. (16-bit C) or step*4.. (fp32 C).
             if constexpr (CB == 4) {
@@ -625,10 +629,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float4 f = make_float4(x[4 * h], x[4 * h + 1], x[4 * h + 2], x[4 * h + 3]);
                 if (s.tma_residual) {
                   const float4 rr = *slot;
-                  f.x += rr.x;
-                  f.y += rr.y;
-                  f.z += rr.z;
-                  f.w += rr.w;
+                  f.x = res_mul ? f.x * rr.x : f.x + rr.x;
+                  f.y = res_mul ? f.y * rr.y : f.y + rr.y;
+                  f.z = res_mul ? f.z * rr.z : f.z + rr.z;
+                  f.w = res_mul ? f.w * rr.w : f.w + rr.w;
                 }
                 *slot = f;
               }
@@ -647,8 +651,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                       const float2 f = __bfloat1622float2(rb[e]);
-                      w[2 * e] += f.x;
-                      w[2 * e + 1] += f.y;
+                      w[2 * e] = res_mul ? w[2 * e] * f.x : w[2 * e] + f.x;
+                      w[2 * e + 1] = res_mul ? w[2 * e + 1] * f.y : w[2 * e + 1] + f.y;
                     }
                   }
                   __nv_bfloat162 *pb = reinterpret_cast<__nv_bfloat162 *>(&packed);
@@ -661,8 +665,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                       const float2 f = __half22float2(rh[e]);
-                      w[2 * e] += f.x;
-                      w[2 * e + 1] += f.y;
+                      w[2 * e] = res_mul ? w[2 * e] * f.x : w[2 * e] + f.x;
+                      w[2 * e + 1] = res_mul ? w[2 * e + 1] * f.y : w[2 * e + 1] + f.y;
                     }
                   }
                   __half2 *ph = reinterpret_cast<__half2 *>(&packed);
@@ -788,7 +792,7 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   // its map has no batch extent and the kernel reads it at batch 0.
   auto shared = [&](int64_t s1, int64_t s2) { return p.batch > 1 && s1 == 0 && (b2 == 1 || s2 == 0); };
   const bool a_sh = shared(p.stride_a, p.stride_a2), b_sh = shared(p.stride_b, p.stride_b2);
-  const bool r_sh = (p.epilogue & DP_EPI_RESIDUAL) && shared(p.stride_r, p.stride_r2);
+  const bool r_sh = (p.epilogue & (DP_EPI_RESIDUAL | DP_EPI_MUL)) && shared(p.stride_r, p.stride_r2);
   int st = a_sh ? make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, 1, 0, 1, 0, BK, BM)
                 : make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, b1, p.stride_a, b2, p.stride_a2, BK, BM);
   if (st != DP_OK) return st;
@@ -808,7 +812,7 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
     st = make_map(&mc, C, p.c_dtype, p.M, p.N, p.ldc, b1, p.stride_c, b2, p.stride_c2, 64 / cb, 32,
                   CU_TENSOR_MAP_SWIZZLE_64B);
     if (st != DP_OK) return st;
-    if ((p.epilogue & DP_EPI_RESIDUAL) && p.r_dtype == p.c_dtype && (p.ldr * cb) % 16 == 0 &&
+    if ((p.epilogue & (DP_EPI_RESIDUAL | DP_EPI_MUL)) && p.r_dtype == p.c_dtype && (p.ldr * cb) % 16 == 0 &&
         (p.batch == 1 || (p.stride_r * cb) % 16 == 0) && (b2 == 1 || (p.stride_r2 * cb) % 16 == 0) && al16(res)) {
       st = r_sh ? make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, 1, 0, 1, 0, 64 / cb, 32, CU_TENSOR_MAP_SWIZZLE_64B)
                 : make_map(&mr, res, p.r_dtype, p.M, p.N, p.ldr, b1, p.stride_r, b2, p.stride_r2, 64 / cb, 32,

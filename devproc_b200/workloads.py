@@ -131,7 +131,8 @@ class VitClassifier(torch.nn.Module):
     """
 
     def __init__(self, layers: int = 27, dim: int = 1152, heads: int = 16, mlp: int = 4304, classes: int = 1000,
-                 patch: int = 14, image: int = 224, seed: int = 1, dtype=torch.bfloat16, logits: bool = False):
+                 patch: int = 14, image: int = 224, seed: int = 1, dtype=torch.bfloat16, logits: bool = False,
+                 device=None):
         super().__init__()
         self.logits = logits
         self.patch = torch.nn.Conv2d(3, dim, kernel_size=patch, stride=patch)
@@ -140,7 +141,7 @@ class VitClassifier(torch.nn.Module):
         self.blocks = torch.nn.ModuleList([VitBlock(dim, heads, mlp, 1e-6) for _ in range(layers)])
         self.post_ln = torch.nn.LayerNorm(dim, eps=1e-6)
         self.head = torch.nn.Linear(dim, classes)
-        g = torch.Generator().manual_seed(seed)
+        g = torch.Generator(device=device or "cpu").manual_seed(seed)
         with torch.no_grad():
             for name, prm in self.named_parameters():
                 if name.endswith("bias"):
@@ -148,7 +149,7 @@ class VitClassifier(torch.nn.Module):
                 elif ".ln" in name or name.startswith("post_ln"):
                     prm.fill_(1.0)
                 else:
-                    prm.copy_(torch.randn(prm.shape, generator=g) * 0.02)
+                    prm.copy_(torch.randn(prm.shape, generator=g, dtype=torch.float32, device=g.device) * 0.02)
         self.to(dtype)
 
     def encode(self, pixels):
@@ -229,13 +230,24 @@ class Pi05Policy(torch.nn.Module):
                  heads: int = 8, kv_heads: int = 1, head_dim: int = 256, mlp: int = 16384,
                  expert_width: int = 1024, expert_layers: int = 18, expert_mlp: int = 4096,
                  horizon: int = 50, action_dim: int = 32, steps: int = 10, vit: dict = None, seed: int = 1,
-                 dtype=torch.bfloat16):
+                 dtype=torch.bfloat16, device=None):
         super().__init__()
+        prev = torch.get_default_dtype()
+        torch.set_default_dtype(dtype)  # build in the target dtype: no fp32 copy of ~3 B weights
+        try:
+            with torch.device(device or "cpu"):
+                self._build(cams, text, vocab, width, layers, heads, kv_heads, head_dim, mlp, expert_width,
+                            expert_layers, expert_mlp, horizon, action_dim, steps, dict(vit or {}), seed, dtype,
+                            device)
+        finally:
+            torch.set_default_dtype(prev)
+
+    def _build(self, cams, text, vocab, width, layers, heads, kv_heads, head_dim, mlp, expert_width, expert_layers,
+               expert_mlp, horizon, action_dim, steps, vit, seed, dtype, device):
         from .torch_ops import rope_tables
-        vit = dict(vit or {})
         self.cams, self.steps = cams, steps
         self.width = width
-        self.vision = VitClassifier(seed=seed, dtype=torch.float32, logits=True, **vit)
+        self.vision = VitClassifier(seed=seed, dtype=dtype, logits=True, device=device, **vit)
         vdim = self.vision.post_ln.normalized_shape[0]
         self.vision.head = torch.nn.Identity()
         self.img_tokens = cams * self.vision.pos.shape[1]
@@ -251,16 +263,18 @@ class Pi05Policy(torch.nn.Module):
         self.action_out = torch.nn.Linear(expert_width, action_dim)
         prefix = self.img_tokens + text
         cos, sin = rope_tables(prefix + horizon, head_dim)
-        self.register_buffer("cos", cos)
-        self.register_buffer("sin", sin)
+        self.register_buffer("cos", cos.to(dtype))
+        self.register_buffer("sin", sin.to(dtype))
         # sinusoidal embedding of t = 1, 1 - 1/steps, ..., 1/steps
         t = 1.0 - torch.arange(steps, dtype=torch.float64) / steps
         freq = torch.exp(-math.log(10000.0) * torch.arange(expert_width // 2, dtype=torch.float64) /
                          (expert_width // 2))
         ang = t[:, None] * 1000.0 * freq[None, :]
-        self.register_buffer("t_emb", torch.cat([torch.sin(ang), torch.cos(ang)], -1).float())
+        self.register_buffer("t_emb", torch.cat([torch.sin(ang), torch.cos(ang)], -1).to(dtype))
         self.prefix = prefix
-        g = torch.Generator().manual_seed(seed + 1)
+        # With ``device`` the draws come from that device's generator (a different
+        # stream than the CPU default, which keeps building on a GPU fast).
+        g = torch.Generator(device=device or "cpu").manual_seed(seed + 1)
         with torch.no_grad():
             for name, prm in self.named_parameters():
                 if name.startswith("vision."):
@@ -269,10 +283,8 @@ class Pi05Policy(torch.nn.Module):
                     prm.zero_()
                 elif ".ln" in name or name.startswith("final_ln"):
                     prm.fill_(1.0)
-                else:
-                    prm.copy_(torch.randn(prm.shape, generator=g) * 0.02)
-        self.to(dtype)
-        self.t_emb.data = self.t_emb.data.to(dtype)
+                else:  # N(0, 0.02), drawn in fp32 one tensor at a time
+                    prm.copy_(torch.randn(prm.shape, generator=g, dtype=torch.float32, device=g.device) * 0.02)
 
     def forward(self, pixels, text_ids, noise):
         b = text_ids.shape[0]

@@ -118,7 +118,8 @@ int dp_rowreduce(const dp_rowreduce_params *p, const void *in, const void *weigh
  * bf16 × bf16 runs on tcgen05 tensor cores (TMEM accumulator, TMA loads);
  * fp32 × fp32 runs an exact-fp32 FFMA kernel.
  * Epilogue order: × alpha (0 means 1) → + bias[n] → activation →
- * + residual[m, n] → cast to C. */
+ * + residual[m, n] (or × residual[m, n] with DP_EPI_MUL: a gated unit whose
+ * other half is already computed) → cast to C. */
 enum { DP_B_NK = 0, DP_B_KN = 1 };
 enum {
   DP_EPI_BIAS = 1, DP_EPI_RELU = 2, DP_EPI_GELU_ERF = 4, DP_EPI_GELU_TANH = 8,
@@ -126,7 +127,10 @@ enum {
   /* Row softmax of alpha·(A·Bᵀ) over the N columns (exp via __expf); needs
    * N ≤ 256 (one tensor-core tile holds a whole row), bf16 operands on the
    * tensor-core path and no other epilogue flag. */
-  DP_EPI_SOFTMAX = 64
+  DP_EPI_SOFTMAX = 64,
+  /* Multiply by the residual operand instead of adding it (excludes
+   * DP_EPI_RESIDUAL). */
+  DP_EPI_MUL = 128
 };
 typedef struct dp_gemm_params {
   int64_t M, N, K;

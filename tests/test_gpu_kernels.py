@@ -462,6 +462,29 @@ def test_gemm_bf16_b_kn_tensor_core(cuda, M, Nn, K):
     assert torch.allclose(c.cpu(), ref, rtol=1e-3, atol=1e-3 * K ** 0.5)
 
 
+@pytest.mark.parametrize("c_dtype", [torch.bfloat16, torch.float32])
+def test_gemm_multiply_epilogue(cuda, c_dtype):
+    """C = (A·Bᵀ) ⊙ G with G an already computed operand (the up projection of
+    a GeGLU times gelu(gate)), on the tensor-core path and the fp32 FFMA path."""
+    g = torch.Generator().manual_seed(23)
+    M, Nn, K = 300, 520, 256
+    gate = torch.randn(M, Nn, generator=g).to(c_dtype)
+    for in_dtype in (torch.bfloat16, torch.float32):
+        a = torch.randn(M, K, generator=g).to(in_dtype)
+        w = torch.randn(Nn, K, generator=g).to(in_dtype)
+        c = torch.empty(M, Nn, dtype=c_dtype, device=cuda)
+        p = N.GemmParams()
+        p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.ldr, p.batch = M, Nn, K, K, K, Nn, Nn, 1
+        p.a_dtype = p.b_dtype = _dt(a)
+        p.c_dtype, p.r_dtype = _dt(c), _dt(gate)
+        p.b_layout, p.epilogue = N.DP_B_NK, N.DP_EPI_MUL
+        N.gemm(p, a.to(cuda), w.to(cuda), c, residual=gate.to(cuda))
+        _sync()
+        ref = (a.float() @ w.float().T) * gate.float()
+        tol = 2e-2 if c_dtype == torch.bfloat16 or in_dtype == torch.bfloat16 else 1e-4
+        assert torch.allclose(c.cpu().float(), ref, rtol=tol, atol=tol * ref.abs().max().item()), (in_dtype, c_dtype)
+
+
 def test_gemm_bf16_batch_shared_b_and_residual(cuda):
     """Zero batch strides: one weight and one [M, N] residual shared by every
     batch (a position embedding added in the patch GEMM's epilogue)."""
