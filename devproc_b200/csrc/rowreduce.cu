@@ -364,6 +364,8 @@ template <typename TIn, typename TOut, int VEC, int NV, int KIND>
 __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, const TIn *__restrict__ in,
                                                         const TIn *__restrict__ w, const TIn *__restrict__ bias,
                                                         TOut *__restrict__ out) {
+  // Rows need not hold a whole number of vectors: the one vector that
+  // straddles the row end is read and written element by element.
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -376,11 +378,11 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, c
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = lane * VEC + i * step;
-      if (c < p.cols) {
+      if (c + VEC <= p.cols) {
         load_vec<TIn, VEC>(x + c, v[i]);
       } else {
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) v[i][j] = 0.0f;
+        for (int j = 0; j < VEC; ++j) v[i][j] = c + j < p.cols ? to_f32(x[c + j]) : 0.0f;
       }
     }
     float scale = 1.0f, shift = 0.0f;
@@ -388,16 +390,16 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, c
       float m = -INFINITY;
 #pragma unroll
       for (int i = 0; i < NV; ++i)
-        if (lane * VEC + i * step < p.cols)
 #pragma unroll
-          for (int j = 0; j < VEC; ++j) m = nan_max(m, v[i][j]);
+        for (int j = 0; j < VEC; ++j)
+          if (lane * VEC + i * step + j < p.cols) m = nan_max(m, v[i][j]);
       m = warp_max(m);
       float sum = 0.0f;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
-        const bool live = lane * VEC + i * step < p.cols;
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
+          const bool live = lane * VEC + i * step + j < p.cols;
           v[i][j] = live ? __expf(v[i][j] - m) : 0.0f;
           sum += v[i][j];
         }
@@ -420,9 +422,9 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, c
       float q = 0.0f;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
-        const bool live = lane * VEC + i * step < p.cols;
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
+          const bool live = lane * VEC + i * step + j < p.cols;
           const float d = live ? v[i][j] - mean : 0.0f;
           q = fmaf(d, d, q);
         }
@@ -434,9 +436,24 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, c
     for (int i = 0; i < NV; ++i) {
       const int c = lane * VEC + i * step;
       if (c >= p.cols) continue;
+      const bool full = c + VEC <= p.cols;
       float o[VEC], wv[VEC], bv[VEC];
-      if (KIND != DP_RED_SOFTMAX && p.has_weight) load_vec<TIn, VEC>(w + c, wv);
-      if (KIND == DP_RED_LAYERNORM && p.has_bias) load_vec<TIn, VEC>(bias + c, bv);
+      if (KIND != DP_RED_SOFTMAX && p.has_weight) {
+        if (full) {
+          load_vec<TIn, VEC>(w + c, wv);
+        } else {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) wv[j] = c + j < p.cols ? to_f32(w[c + j]) : 0.0f;
+        }
+      }
+      if (KIND == DP_RED_LAYERNORM && p.has_bias) {
+        if (full) {
+          load_vec<TIn, VEC>(bias + c, bv);
+        } else {
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) bv[j] = c + j < p.cols ? to_f32(bias[c + j]) : 0.0f;
+        }
+      }
 #pragma unroll
       for (int j = 0; j < VEC; ++j) {
         if constexpr (KIND == DP_RED_SOFTMAX) {
@@ -448,7 +465,13 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, c
           o[j] = t;
         }
       }
-      store_vec<TOut, VEC>(y + c, o);
+      if (full) {
+        store_vec<TOut, VEC>(y + c, o);
+      } else {
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          if (c + j < p.cols) y[c + j] = from_f32<TOut>(o[j]);
+      }
     }
   }
 }
@@ -703,21 +726,24 @@ int launch_norm_vec(const dp_rowreduce_params &p, const void *in, const void *w,
   constexpr int VO = 16 / (int)sizeof(TOut);
   const bool vec_ok = V == VO || sizeof(TOut) * V <= 16;
   auto al = [](const void *q, size_t a) { return q == nullptr || reinterpret_cast<uintptr_t>(q) % a == 0; };
-  const bool ok = vec_ok && p.cols % V == 0 && p.in_row_stride % V == 0 && p.out_row_stride % V == 0 &&
-                  al(in, 16) && al(w, 16) && al(b, 16) && al(out, sizeof(TOut) * V);
+  // Whole vectors per row are needed only by the CTA-per-row kernel; the warp
+  // kernel reads a row's last partial vector element by element.
+  const bool aligned = vec_ok && p.in_row_stride % V == 0 && p.out_row_stride % V == 0 && al(in, 16) &&
+                       al(w, 16) && al(b, 16) && al(out, sizeof(TOut) * V);
+  const bool ok = aligned && p.cols % V == 0;
   if constexpr (std::is_same<TIn, TOut>::value && sizeof(TIn) == 2) {
     if (p.rows > 0) {
       const int r = launch_norm16<TIn>(p, in, w, b, out, s);
       if (r != -1) return r;
     }
   }
-  if (ok) {
+  if (aligned) {
     const int64_t per_lane = (p.cols + 32 * V - 1) / (32 * V);  // vectors per lane for a warp-per-row pass
     if (per_lane <= 4) return launch_norm_warp<TIn, TOut, V, 4>(p, in, w, b, out, s);
     if (per_lane <= 8) return launch_norm_warp<TIn, TOut, V, 8>(p, in, w, b, out, s);
     if (per_lane <= 16 && sizeof(TIn) == 4) return launch_norm_warp<TIn, TOut, V, 16>(p, in, w, b, out, s);
     if (per_lane <= 32 && sizeof(TIn) == 4) return launch_norm_warp<TIn, TOut, V, 32>(p, in, w, b, out, s);
-    return launch_norm<TIn, TOut, V>(p, in, w, b, out, s);
+    if (ok) return launch_norm<TIn, TOut, V>(p, in, w, b, out, s);
   }
   return launch_norm<TIn, TOut, 1>(p, in, w, b, out, s);
 }

@@ -156,7 +156,7 @@ def test_argmax_golden_vectors(cuda, golden):
         assert torch.equal(out, torch.from_numpy(golden[f"{case}/y"])), case
 
 
-@pytest.mark.parametrize("rows,cols", [(1024, 4096), (37, 1000), (64, 512), (16, 20000), (3, 7)])
+@pytest.mark.parametrize("rows,cols", [(1024, 4096), (37, 1000), (64, 512), (16, 20000), (3, 7), (300, 866), (64, 1003), (9, 3)])
 def test_softmax_and_norms_fp32(cuda, rows, cols):
     g = torch.Generator().manual_seed(7 * rows + cols)
     x = torch.randn(rows, cols, generator=g) * 3
@@ -170,6 +170,23 @@ def test_softmax_and_norms_fp32(cuda, rows, cols):
     assert torch.allclose(rn, ref, rtol=1e-4, atol=1e-5)
     ln = _rr(N.DP_RED_LAYERNORM, xd, torch.float32, w=w.to(cuda), b=b.to(cuda), eps=1e-5)
     assert torch.allclose(ln, torch.nn.functional.layer_norm(x, (cols,), w, b, 1e-5), rtol=1e-4, atol=1e-5)
+
+
+@pytest.mark.parametrize("cols", [866, 50, 3, 1003])
+def test_softmax_padded_rows_partial_vector(cuda, cols):
+    """Attention-style rows: fp32 scores with rows padded to a multiple of 8,
+    a column count that is not a whole number of vectors, bf16 output."""
+    g = torch.Generator().manual_seed(cols)
+    rows, stride = 257, (cols + 7) // 8 * 8
+    x = torch.randn(rows, stride, generator=g) * 4
+    out = torch.full((rows, stride), float("nan"), dtype=torch.bfloat16, device=cuda)
+    p = N.RowReduceParams(N.DP_RED_SOFTMAX, N.DP_F32, N.DP_BF16, 0, 0, 0, rows, cols, stride, stride, 0.0, 0.0)
+    N.rowreduce(p, x.to(cuda), out)
+    _sync()
+    ref = torch.softmax(x[:, :cols], -1)
+    got = out.cpu()
+    assert torch.allclose(got[:, :cols].float(), ref, rtol=1e-2, atol=1e-3)
+    assert torch.isnan(got[:, cols:].float()).all()  # the pad is not written
 
 
 def test_softmax_golden_vector(cuda, golden):
