@@ -29,6 +29,7 @@ STATUS_NAMES = {0: "DP_OK", 1: "DP_ERR_ARG", 2: "DP_ERR_SHAPE", 3: "DP_ERR_CUDA"
 
 # element types
 DP_U8, DP_I8, DP_I16, DP_I32, DP_I64, DP_F16, DP_BF16, DP_F32, DP_F64, DP_BOOL = range(10)
+DP_TF32 = 10  # GEMM operands: fp32 storage, TF32 tensor-core math
 DTYPE_CODE = {"uint8": DP_U8, "int8": DP_I8, "int16": DP_I16, "int32": DP_I32, "int64": DP_I64,
               "float16": DP_F16, "bfloat16": DP_BF16, "float32": DP_F32, "float64": DP_F64, "bool": DP_BOOL}
 
@@ -45,7 +46,7 @@ DP_REGION_MAX_OPERANDS, DP_REGION_MAX_RANK, DP_REGION_MAX_INSTR = 8, 6, 64
 DP_REGION_MAX_CONST, DP_REGION_MAX_REGS = 32, 8
 OP = {"load": 1, "store": 2, "const": 3, "chansel": 4, "add": 10, "sub": 11, "mul": 12, "div": 13,
       "max": 14, "min": 15, "neg": 20, "abs": 21, "relu": 22, "sigmoid": 23, "tanh": 24, "exp": 25,
-      "gelu_erf": 26, "gelu_tanh": 27, "silu": 28, "mov": 29}
+      "gelu_erf": 26, "gelu_tanh": 27, "silu": 28, "mov": 29, "tf32": 30}
 
 DP_PLAN_MAGIC, DP_PLAN_VERSION = 0x32425044, 1
 DP_NOALLOC_ARENA_BYTES = 64 << 20

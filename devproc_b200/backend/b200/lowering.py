@@ -664,14 +664,67 @@ class Lowerer:
             col += n
             self.done.add(id(u))
 
+    # fp32 linears on the tensor cores: x·w = x_hi·w_hi + x_hi·w_lo + x_lo·w_hi
+    # with *_hi the TF32-grid part (10 mantissa bits) and *_lo = * − *_hi,
+    # run as ONE TF32 GEMM over K' = 3K on [x_hi | x_hi | x_lo] · [w_hi | w_lo | w_hi]ᵀ.
+    # The dropped x_lo·w_lo term and the TF32 rounding of the lo parts are
+    # ~2^-20 relative: fp32-level results (3xTF32).
+    TF32_MIN_WORK = 1 << 24
+
+    def tf32_split_ok(self, op: Op) -> bool:
+        x, w = op.inputs[0], op.inputs[1]
+        if x.type.dtype != "float32" or w.type.dtype != "float32" or len(w.type.shape) != 2:
+            return False
+        K = x.type.shape[-1]
+        M = _prod(x.type.shape[:-1])
+        src = self.views[w.name]
+        const = (src.buf.kind == "const" and src.buf.base is None and src.buf.name in self.const_tensors)
+        return const and K % 4 == 0 and M >= 64 and M * w.type.shape[0] * K >= self.TF32_MIN_WORK
+
+    def tf32_split_weight(self, value: Value, K: int) -> View:
+        import torch
+        src = self.views[value.name]
+        name = src.buf.name + "|3xtf32"
+        if name not in self.const_tensors:
+            rows = value.type.shape[0]
+            flat = view_reshape(src.shape, src.strides, (rows, K)) or contiguous_strides((rows, K))
+            w = self.const_tensors[src.buf.name].reshape(-1).as_strided((rows, K), flat, src.offset).float()
+            hi = (w.contiguous().view(torch.int32) & -8192).view(torch.float32)
+            self.const_tensors[name] = torch.cat([hi, w - hi, hi], dim=1).contiguous()
+        buf = self.derived_const(name, "float32", (value.type.shape[0], 3 * K))
+        return View(buf, (value.type.shape[0], 3 * K), (3 * K, 1))
+
+    def tf32_split_rows(self, value: Value, K: int) -> View:
+        """[rows, 3K] = [x_hi | x_hi | x_lo] in one region."""
+        rows = _prod(value.type.shape[:-1])
+        src = self.views[value.name]
+        flat = view_reshape(src.shape, src.strides, (rows, K))
+        if flat is None:
+            src = self.contiguous(value)
+            flat = contiguous_strides((rows, K))
+        out = self.new_buffer("arena", "float32", (rows, 3 * K), value.name + "_3xtf32")
+        rb = RegionBuilder((rows, K))
+        xr = rb.load(View(src.buf, (rows, K), flat, src.offset))
+        hi = rb.unary("tf32", xr)
+        rb.store(View(out, (rows, K), (3 * K, 1), 0), hi)
+        rb.store(View(out, (rows, K), (3 * K, 1), K), hi)
+        rb.store(View(out, (rows, K), (3 * K, 1), 2 * K), rb.binary("sub", xr, hi))
+        self.emit_region(rb, f"split {value.name} 3xtf32")
+        return View(out, (rows, 3 * K), (3 * K, 1))
+
     def lower_gemm(self, op: Op) -> None:
         p = N.GemmParams()
+        tf32 = False
         if op.name == "linear":
             group = self.sibling_linears(op)
             if len(group) > 1:
                 return self.lower_linear_group(group)
             K = op.inputs[0].type.shape[-1]
-            if op.inputs[0].type.dtype == "bfloat16" and K % 8:
+            tf32 = self.tf32_split_ok(op)
+            if tf32:
+                x = self.tf32_split_rows(op.inputs[0], K)
+                w = self.tf32_split_weight(op.inputs[1], K)
+            elif op.inputs[0].type.dtype == "bfloat16" and K % 8:
                 # tensor-core operands need 16-byte row strides: rows padded to Kp
                 x = self.padded_rows(op.inputs[0], K)
                 w = self.padded_rows(op.inputs[1], K)
@@ -680,8 +733,8 @@ class Lowerer:
                 w = self.contiguous(op.inputs[1])
             M = _prod(x.shape[:-1])
             Nn = w.shape[0]
-            p.M, p.N, p.K = M, Nn, K
-            p.lda, p.ldb = x.strides[-2] if len(x.shape) > 1 else K, w.strides[0]
+            p.M, p.N, p.K = M, Nn, x.shape[-1]
+            p.lda, p.ldb = x.strides[-2] if len(x.shape) > 1 else x.shape[-1], w.strides[0]
             p.b_layout = N.DP_B_NK
             p.batch, p.stride_a, p.stride_b = 1, 0, 0
             a_dtype, b_dtype = x.buf.dtype, w.buf.dtype
@@ -721,7 +774,7 @@ class Lowerer:
         if a_dtype != b_dtype or a_dtype not in ("float32", "bfloat16"):
             raise CompilationError(f"{op.name}: operand dtypes {a_dtype} x {b_dtype}; supported: "
                                    "float32 x float32, bfloat16 x bfloat16")
-        p.a_dtype = p.b_dtype = N.DTYPE_CODE[a_dtype]
+        p.a_dtype = p.b_dtype = N.DP_TF32 if tf32 else N.DTYPE_CODE[a_dtype]
         epi = 0
         residual = None
         shared_rows = 0
@@ -835,7 +888,10 @@ class Lowerer:
         ops_ = [a_buf.buf, b_buf.buf, out.buf, bias.buf if bias is not None else None,
                 residual.buf if residual is not None else None]
         nb = sum(b.nbytes for b in ops_ if b is not None)
-        self.emit(N.DP_K_GEMM, ops_, p, f"gemm {op.name} M{p.M} N{p.N} K{p.K} b{p.batch} {a_dtype} epi{epi}",
+        kind = "3xtf32" if tf32 else a_dtype
+        if tf32:
+            flops = 2 * p.M * p.N * (p.K // 3) * p.batch  # the work of the fp32 product
+        self.emit(N.DP_K_GEMM, ops_, p, f"gemm {op.name} M{p.M} N{p.N} K{p.K} b{p.batch} {kind} epi{epi}",
                   flops, nb)
 
     # ------------------------------------------------------ row reductions

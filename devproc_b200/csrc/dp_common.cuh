@@ -33,7 +33,7 @@ inline int dtype_bytes(int dt) {
   switch (dt) {
     case DP_U8: case DP_I8: case DP_BOOL: return 1;
     case DP_I16: case DP_F16: case DP_BF16: return 2;
-    case DP_I32: case DP_F32: return 4;
+    case DP_I32: case DP_F32: case DP_TF32: return 4;
     case DP_I64: case DP_F64: return 8;
     default: return 0;
   }

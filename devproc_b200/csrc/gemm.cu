@@ -1,8 +1,8 @@
 // GEMM entry point: validates the request and picks the kernel.
-// bf16 × bf16 goes to the tcgen05 tensor-core kernel when its TMA alignment
-// rules hold (row and batch strides multiples of 8 elements, 16-byte aligned
-// bases), with B either [N, K] or [K, N]; everything else (fp32, or bf16 with
-// odd strides) runs the FFMA kernel.  Both share one epilogue.
+// bf16 × bf16 (B either [N, K] or [K, N]) and TF32 × TF32 (B as [N, K]) go
+// to the tcgen05 tensor-core kernel when its TMA alignment rules hold (row
+// and batch strides multiples of 16 bytes, 16-byte aligned bases); everything
+// else (fp32, or odd strides) runs the FFMA kernel.  Both share one epilogue.
 #include "dp_gemm_epilogue.cuh"
 
 namespace dp {
@@ -32,10 +32,13 @@ int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C, 
     DP_REQUIRE(p.epilogue == DP_EPI_SOFTMAX, DP_ERR_ARG, "gemm: the softmax epilogue takes no other epilogue flag");
     DP_REQUIRE(p.N <= 256, DP_ERR_UNSUPPORTED, "gemm: the softmax epilogue needs N <= 256");
   }
-  if (p.a_dtype == DP_BF16 && p.b_dtype == DP_BF16) {
+  const bool tf32 = p.a_dtype == DP_TF32 && p.b_dtype == DP_TF32;
+  if ((p.a_dtype == DP_BF16 && p.b_dtype == DP_BF16) || (tf32 && p.b_layout == DP_B_NK)) {
+    // operand rows and batch strides must be 16-byte multiples for TMA
+    const int64_t v = tf32 ? 4 : 8;
     auto al = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
-    const bool tc_ok = p.lda % 8 == 0 && p.ldb % 8 == 0 && p.stride_a % 8 == 0 &&
-                       p.stride_b % 8 == 0 && p.stride_a2 % 8 == 0 && p.stride_b2 % 8 == 0 && al(A) && al(B);
+    const bool tc_ok = p.lda % v == 0 && p.ldb % v == 0 && p.stride_a % v == 0 && p.stride_b % v == 0 &&
+                       p.stride_a2 % v == 0 && p.stride_b2 % v == 0 && al(A) && al(B);
     if (tc_ok) return launch_gemm_tc(p, A, B, C, bias, res, s);
   }
   DP_REQUIRE(!(p.epilogue & DP_EPI_SOFTMAX), DP_ERR_UNSUPPORTED,

@@ -168,7 +168,8 @@ namespace dp {
 
 int launch_gemm_simt(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias,
                      const void *res, cudaStream_t s) {
-  if (p.a_dtype == DP_F32 && p.b_dtype == DP_F32)
+  // TF32 operands that cannot go to the tensor cores run in full fp32 here.
+  if ((p.a_dtype == DP_F32 || p.a_dtype == DP_TF32) && (p.b_dtype == DP_F32 || p.b_dtype == DP_TF32))
     return dpk_sgemm::launch_typed<float, float>(p, A, B, C, bias, res, s);
   if (p.a_dtype == DP_BF16 && p.b_dtype == DP_BF16)
     return dpk_sgemm::launch_typed<__nv_bfloat16, __nv_bfloat16>(p, A, B, C, bias, res, s);

@@ -91,6 +91,8 @@ struct Shape {
   int tma_residual;  // residual read by TMA into the same chunks (same dtype as C)
   int c_bytes;       // element size of C
   int bcast;         // operands shared by every batch (zero batch strides): 1 A, 2 B, 4 residual
+  int tf32;          // operands are fp32 multiplied as TF32 (kind::tf32); else bf16 (kind::f16)
+  int box_k;         // K elements per 128-byte operand box: 64 bf16 or 32 fp32
 };
 
 // ------------------------------------------------------------------ PTX
@@ -185,30 +187,47 @@ __device__ __forceinline__ uint64_t smem_desc_mn(uint32_t addr) {
   return d;
 }
 
-// Instruction descriptor, kind::f16: fp32 accumulate, bf16 A and B, A K-major,
-// B K-major (b_mn = 0) or MN-major (b_mn = 1).
-__host__ __device__ constexpr uint32_t instr_desc(int m, int n, int b_mn = 0) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) |
+// Instruction descriptor: fp32 accumulate, A K-major, B K-major (b_mn = 0)
+// or MN-major (b_mn = 1); operand format 1 = BF16 (kind::f16) or 2 = TF32
+// (kind::tf32) in both the A and B fields.
+__host__ __device__ constexpr uint32_t instr_desc(int m, int n, int b_mn = 0, uint32_t fmt = 1) {
+  return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) |
          ((uint32_t)(m >> 4) << 24);
 }
 
 template <int CG>
-__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
+__device__ __forceinline__ void mma_issue(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate, bool tf32) {
   if constexpr (CG == 1) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
+    if (tf32)
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "setp.ne.b32 p, %4, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+          "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+          : "memory");
+    else
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "setp.ne.b32 p, %4, 0;\n\t"
+          "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+          "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+          : "memory");
   } else {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-        : "memory");
+    if (tf32)
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "setp.ne.b32 p, %4, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+          "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+          : "memory");
+    else
+      asm volatile(
+          "{\n\t.reg .pred p;\n\t"
+          "setp.ne.b32 p, %4, 0;\n\t"
+          "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+          "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+          : "memory");
   }
 }
 
@@ -449,7 +468,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           };
 #pragma unroll
           for (int kh = 0; kh < Cfg<CG>::kKBoxes; ++kh) {
-            const int k0 = (kb * Cfg<CG>::kKBoxes + kh) * BK;
+            const int k0 = (kb * Cfg<CG>::kKBoxes + kh) * s.box_k;
             load(sa + kh * kTileABytes, &map_a, k0, row0, ba);
             uint8_t *sbk = sb + kh * b_box_bytes<CG>();
             if (s.b_mn) {
@@ -465,7 +484,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------- MMA issuer (the leader CTA's, for a pair)
-      const uint32_t idesc = instr_desc(BM * CG, BN, s.b_mn);
+      const uint32_t idesc = instr_desc(BM * CG, BN, s.b_mn, s.tf32 ? 2u : 1u);
+      const bool tf32 = s.tf32 != 0;
       int it = 0, local = 0;
       for (int t = cid; t < s.num_tiles && !aborted(flag); t += nclusters, ++local) {
         const int a = local & 1;
@@ -484,12 +504,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sb = sa + Cfg<CG>::kKBoxes * kTileABytes;
 #pragma unroll
           for (int kh = 0; kh < Cfg<CG>::kKBoxes; ++kh) {
-            if (kh > 0 && (kb * Cfg<CG>::kKBoxes + kh) * BK >= s.K) break;  // box past K: zeros only
+            if (kh > 0 && (kb * Cfg<CG>::kKBoxes + kh) * s.box_k >= s.K) break;  // box past K: zeros only
             const uint32_t ak = sa + kh * kTileABytes, bk = sb + kh * b_box_bytes<CG>();
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
               const uint64_t bdesc = s.b_mn ? smem_desc_mn(bk + k * 2048) : smem_desc(bk + k * 32);
-              mma_bf16<CG>(tmem_d, smem_desc(ak + k * 32), bdesc, idesc, (kb | kh | k) != 0);
+              mma_issue<CG>(tmem_d, smem_desc(ak + k * 32), bdesc, idesc, (kb | kh | k) != 0, tf32);
             }
           }
           mma_commit<CG>(&empty[st]);  // stage is free (in both CTAs) once these MMAs have read it
@@ -793,15 +813,18 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   auto shared = [&](int64_t s1, int64_t s2) { return p.batch > 1 && s1 == 0 && (b2 == 1 || s2 == 0); };
   const bool a_sh = shared(p.stride_a, p.stride_a2), b_sh = shared(p.stride_b, p.stride_b2);
   const bool r_sh = (p.epilogue & (DP_EPI_RESIDUAL | DP_EPI_MUL)) && shared(p.stride_r, p.stride_r2);
-  int st = a_sh ? make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, 1, 0, 1, 0, BK, BM)
-                : make_map(&ma, A, DP_BF16, p.M, p.K, p.lda, b1, p.stride_a, b2, p.stride_a2, BK, BM);
+  const bool tf32 = p.a_dtype == DP_TF32;
+  const int ab_dt = tf32 ? DP_F32 : DP_BF16;
+  const int box_k = tf32 ? 32 : 64;  // K elements per 128-byte box
+  int st = a_sh ? make_map(&ma, A, ab_dt, p.M, p.K, p.lda, 1, 0, 1, 0, box_k, BM)
+                : make_map(&ma, A, ab_dt, p.M, p.K, p.lda, b1, p.stride_a, b2, p.stride_a2, box_k, BM);
   if (st != DP_OK) return st;
   const bool b_mn = p.b_layout == DP_B_KN;
   const int64_t mb1 = b_sh ? 1 : b1, mb2 = b_sh ? 1 : b2;
   if (b_mn)  // [K, N], N contiguous: boxes of 64 N × 64 K (the same for a CTA pair)
     st = make_map(&mb, B, DP_BF16, p.K, p.N, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, 64, BK);
   else
-    st = make_map(&mb, B, DP_BF16, p.N, p.K, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, BK, BN);
+    st = make_map(&mb, B, ab_dt, p.N, p.K, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, box_k, BN);
   if (st != DP_OK) return st;
   const int cb = dtype_bytes(p.c_dtype);
   auto al16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
@@ -832,7 +855,7 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   s.tiles_n = (int)((p.N + BN - 1) / BN);
   s.tiles_per_batch = s.tiles_m * s.tiles_n;
   s.num_tiles = s.tiles_per_batch * s.batch;
-  const int kstep = BK * (cg == 2 ? Cfg<2>::kKBoxes : Cfg<1>::kKBoxes);  // K per stage
+  const int kstep = box_k * (cg == 2 ? Cfg<2>::kKBoxes : Cfg<1>::kKBoxes);  // K per stage
   s.k_blocks = (int)((p.K + kstep - 1) / kstep);
   DP_REQUIRE(tma_store || !(p.epilogue & DP_EPI_SOFTMAX), DP_ERR_UNSUPPORTED,
              "gemm: the softmax epilogue needs a 16-byte aligned C with 16-byte row strides");
@@ -842,9 +865,11 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   s.tma_residual = tma_res ? 1 : 0;
   s.c_bytes = cb;
   s.bcast = (a_sh ? 1 : 0) | (b_sh ? 2 : 0) | (r_sh ? 4 : 0);
+  s.tf32 = tf32 ? 1 : 0;
+  s.box_k = box_k;
   DP_REQUIRE(p.N < (1ll << 31) && p.K < (1ll << 31), DP_ERR_UNSUPPORTED, "gemm: N or K too large");
   if (cg == 2 && !b_mn) {  // each CTA of the pair loads 128 rows of B
-    st = make_map(&mb, B, DP_BF16, p.N, p.K, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, BK, Cfg<2>::kBRows);
+    st = make_map(&mb, B, ab_dt, p.N, p.K, p.ldb, mb1, p.stride_b, mb2, p.stride_b2, box_k, Cfg<2>::kBRows);
     if (st != DP_OK) return st;
   }
   int dev = 0;

@@ -39,6 +39,7 @@ __device__ __forceinline__ float apply_unary(int op, float x) {
       return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
     }
     case DP_OP_SILU: return x / (1.0f + expf(-x));
+    case DP_OP_TF32: return __uint_as_float(__float_as_uint(x) & 0xffffe000u);
     default: return x;  // MOV
   }
 }
@@ -357,7 +358,7 @@ int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t 
         if (op >= DP_OP_ADD && op <= DP_OP_MIN) {
           DP_REQUIRE(dst < DP_REGION_MAX_REGS && a < DP_REGION_MAX_REGS && b < DP_REGION_MAX_REGS, DP_ERR_ARG,
                      where + " bad registers");
-        } else if (op >= DP_OP_NEG && op <= DP_OP_MOV) {
+        } else if (op >= DP_OP_NEG && op <= DP_OP_TF32) {
           DP_REQUIRE(dst < DP_REGION_MAX_REGS && a < DP_REGION_MAX_REGS, DP_ERR_ARG, where + " bad registers");
         } else {
           return set_error(DP_ERR_ARG, where + " unknown opcode " + std::to_string(op));

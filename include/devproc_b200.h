@@ -54,7 +54,11 @@ enum {
 /* ---- element types ---------------------------------------------------- */
 enum {
   DP_U8 = 0, DP_I8 = 1, DP_I16 = 2, DP_I32 = 3, DP_I64 = 4,
-  DP_F16 = 5, DP_BF16 = 6, DP_F32 = 7, DP_F64 = 8, DP_BOOL = 9
+  DP_F16 = 5, DP_BF16 = 6, DP_F32 = 7, DP_F64 = 8, DP_BOOL = 9,
+  /* GEMM operands only: fp32 in memory, multiplied as TF32 on the tensor
+   * cores (the low 13 mantissa bits are not used).  Split x = hi + lo
+   * operands give fp32-level products (3xTF32). */
+  DP_TF32 = 10
 };
 
 /* ---- device error word codes (read with dp_device_error) -------------- */
@@ -167,7 +171,8 @@ enum {
   DP_OP_MAX = 14, DP_OP_MIN = 15,
   DP_OP_NEG = 20, DP_OP_ABS = 21, DP_OP_RELU = 22, DP_OP_SIGMOID = 23,
   DP_OP_TANH = 24, DP_OP_EXP = 25, DP_OP_GELU_ERF = 26, DP_OP_GELU_TANH = 27,
-  DP_OP_SILU = 28, DP_OP_MOV = 29
+  DP_OP_SILU = 28, DP_OP_MOV = 29,
+  DP_OP_TF32 = 30    /* keep the 10 mantissa bits a TF32 operand uses (truncate) */
 };
 typedef struct dp_region_desc {
   int32_t rank, n_in, n_out, n_instr;

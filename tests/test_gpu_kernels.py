@@ -479,6 +479,35 @@ def test_gemm_bf16_b_kn_tensor_core(cuda, M, Nn, K):
     assert torch.allclose(c.cpu(), ref, rtol=1e-3, atol=1e-3 * K ** 0.5)
 
 
+@pytest.mark.parametrize("M,Nn,K", [(1024, 2048, 512), (300, 520, 128), (64, 32000, 512)])
+def test_gemm_3xtf32_matches_fp32(cuda, M, Nn, K):
+    """fp32 product on the tensor cores: one TF32 GEMM over [a_hi|a_hi|a_lo]·[b_hi|b_lo|b_hi]ᵀ
+    agrees with an fp64 reference to fp32-level error (plain TF32 would not)."""
+    g = torch.Generator().manual_seed(M + Nn)
+    a = torch.randn(M, K, generator=g)
+    b = torch.randn(Nn, K, generator=g)
+
+    def split(x):
+        hi = (x.view(torch.int32) & -8192).view(torch.float32)
+        return hi, x - hi
+
+    ah, al = split(a)
+    bh, bl = split(b)
+    a3 = torch.cat([ah, ah, al], 1).contiguous()
+    b3 = torch.cat([bh, bl, bh], 1).contiguous()
+    c = torch.empty(M, Nn, dtype=torch.float32, device=cuda)
+    p = N.GemmParams()
+    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.batch = M, Nn, 3 * K, 3 * K, 3 * K, Nn, 1
+    p.a_dtype = p.b_dtype = N.DP_TF32
+    p.c_dtype = N.DP_F32
+    p.b_layout = N.DP_B_NK
+    N.gemm(p, a3.to(cuda), b3.to(cuda), c)
+    _sync()
+    ref = a.double() @ b.double().T
+    err = (c.cpu().double() - ref).abs() / (a.double().abs() @ b.double().abs().T)
+    assert err.max() < 1e-5, err.max()  # plain TF32 (10-bit mantissas) gives ~1e-3
+
+
 @pytest.mark.parametrize("c_dtype", [torch.bfloat16, torch.float32])
 def test_gemm_multiply_epilogue(cuda, c_dtype):
     """C = (A·Bᵀ) ⊙ G with G an already computed operand (the up projection of

@@ -26,9 +26,14 @@ def test_token_pipeline_fuses_epilogues_and_argmax_cast():
     m = workloads.TokenPipeline()
     prog = devproc.compile(m, workloads.token_ids())
     labels = [r["label"] for r in prog.spec.records]
-    assert kernels(prog) == ["embedding", "gemm", "gemm", "rowreduce", "gemm", "rowreduce"]
-    assert f"epi{N.DP_EPI_BIAS | N.DP_EPI_GELU_ERF}" in labels[1]
-    assert "argmax" in labels[5] and "int32" in labels[5]
+    # each fp32 linear is one 3xTF32 tensor-core GEMM fed by a [hi | hi | lo] split region
+    assert kernels(prog) == ["embedding", "region", "gemm", "region", "gemm", "rowreduce", "region", "gemm",
+                             "rowreduce"]
+    assert all("3xtf32" in lb for lb in labels if lb.startswith("gemm"))
+    assert f"epi{N.DP_EPI_BIAS | N.DP_EPI_GELU_ERF}" in labels[2]
+    assert "argmax" in labels[8] and "int32" in labels[8]
+    w3 = [c for c in prog.spec.consts if c.name.endswith("|3xtf32")]
+    assert len(w3) == 3 and w3[0].shape[1] == 3 * 512
     assert prog.spec.outputs[0].dtype == "int32"
     # constants are bound once; one runtime input
     assert [i.name for i in prog.spec.inputs] == ["l_ids_"]
@@ -133,6 +138,23 @@ def test_host_ops_are_rejected():
 
 def _small_vit(**kw):
     return workloads.VitClassifier(layers=1, dim=128, heads=4, mlp=256, classes=16, **kw).eval()
+
+
+def test_tf32_split_is_exact():
+    """hi carries the TF32 grid part (low 13 mantissa bits zero) and hi + lo
+    reproduces every fp32 weight exactly."""
+    from devproc_b200.backend.b200.lowering import Lowerer
+    m = workloads.TokenPipeline()
+    ir = devproc.from_torch(m, workloads.token_ids(), backend="ir")
+    low = Lowerer(ir, ir.constants.keys(), ir.constants).run()
+    name = [n for n in low.extra_consts if n.endswith("|3xtf32")][0]
+    w3 = low.extra_consts[name]
+    K = w3.shape[1] // 3
+    hi, lo, hi2 = w3[:, :K], w3[:, K:2 * K], w3[:, 2 * K:]
+    assert torch.equal(hi, hi2)
+    assert ((hi.view(torch.int32) & 8191) == 0).all()
+    orig = ir.constants[name.split("|")[0]].float()
+    assert torch.equal(hi + lo, orig)
 
 
 def test_vit_block_lowering_fusions():
