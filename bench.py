@@ -449,6 +449,46 @@ def main():
     h2d = images_host.numel() * images_host.element_size()
     d2h = sum(o.numel() * o.element_size() for o in outs)
 
+    # ---- with the optional final gather: every step's bf16 output is all-gathered over NCCL on a side
+    # stream, overlapped with the next step's preprocessing (two programs, so two output buffers alternate)
+    gather = None
+    if world > 1:
+        import torch.distributed as dist
+        progs = [prog, devproc.compile(workloads.vision_preprocess, images_host, device_id=local_rank)]
+        outs_g = [pg.run(images=dev_in[j], to_cpu=False)[0] for j, pg in enumerate(progs)]
+        gbuf = torch.empty((world,) + tuple(outs_g[0].shape), dtype=outs_g[0].dtype, device=dev)
+        comm = torch.cuda.Stream(dev)
+        done = [torch.cuda.Event() for _ in range(2)]
+        freed = [torch.cuda.Event() for _ in range(2)]
+        dist.all_gather_into_tensor(gbuf, outs_g[0])
+        torch.cuda.synchronize()
+        barrier()
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record(stream)
+        for i in range(K):
+            j = i % 2
+            if i >= 2:
+                stream.wait_event(freed[j])  # the gather that read this output buffer is done
+            progs[j].run(images=dev_in[j], to_cpu=False)
+            done[j].record(stream)
+            comm.wait_event(done[j])
+            with torch.cuda.stream(comm):
+                dist.all_gather_into_tensor(gbuf, outs_g[j])
+            freed[j].record(comm)
+        stream.wait_stream(comm)
+        g1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        g_ms = max_over_ranks(g0.elapsed_time(g1))
+        ingress = (world - 1) * outs_g[0].numel() * outs_g[0].element_size()
+        link = 770.0  # measured peer copy GB/s per direction per GPU on this machine type
+        gather = {"value": B * world * K / (g_ms / 1e3), "unit": "images/s", "ms_per_step": g_ms / K,
+                  "collective": "all_gather_into_tensor of each rank's bf16 output (NCCL), overlapped with the "
+                                "next step on a side stream",
+                  "nvlink_ingress_bytes_per_step_per_gpu": ingress,
+                  "nvlink_bound_ms_per_step": ingress / (link * 1e9) * 1e3,
+                  "nvlink_frac": (ingress / (link * 1e9) * 1e3) / (g_ms / K)}
+
     # ---- roofline of the preprocessing kernel (one launch per step)
     bytes_per_launch = B * workloads.PREPROC_BYTES_PER_IMAGE
     launch_ms = statistics.mean(per_step) / n_launch_per_step
@@ -479,6 +519,7 @@ def main():
                          "kernel": "preproc_u8c3_kernel<bf16> (NHWC u8 -> NCHW bf16)",
                          "algorithmic_bytes_per_launch": bytes_per_launch},
             "cpu_baseline": cpu,
+            "with_gather": gather,
             "clocks": clocks,
             "gpu_launches": K * n_launch_per_step,
         }

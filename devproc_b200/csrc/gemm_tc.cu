@@ -66,11 +66,17 @@ struct Cfg<1> {
   static constexpr int kEpiBufs = 1;  // output staging chunks per epilogue warp
   static constexpr int kBRows = BN;
 };
+#ifndef DP_TC_PAIR_STAGES
+#define DP_TC_PAIR_STAGES (6 / DP_TC_PAIR_KBOXES)
+#endif
+#ifndef DP_TC_PAIR_EPI_BUFS
+#define DP_TC_PAIR_EPI_BUFS 1
+#endif
 template <>
 struct Cfg<2> {
   static constexpr int kKBoxes = DP_TC_PAIR_KBOXES;
-  static constexpr int kStages = 6 / DP_TC_PAIR_KBOXES;
-  static constexpr int kEpiBufs = 1;
+  static constexpr int kStages = DP_TC_PAIR_STAGES;
+  static constexpr int kEpiBufs = DP_TC_PAIR_EPI_BUFS;
   static constexpr int kBRows = BN / 2;
 };
 template <int CG>
