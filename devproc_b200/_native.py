@@ -52,8 +52,8 @@ DP_PLAN_MAGIC, DP_PLAN_VERSION = 0x32425044, 1
 DP_NOALLOC_ARENA_BYTES = 64 << 20
 DP_RECORD_MAX_OPERANDS, DP_RECORD_PARAM_BYTES = 8, 1280
 DP_SLOT_BOUND, DP_SLOT_ARENA = 0, 1
-DP_K_PREPROC, DP_K_ROWREDUCE, DP_K_GEMM, DP_K_REGION, DP_K_EMBEDDING, DP_K_COPY = 1, 2, 3, 4, 5, 6
-KERNEL_NAMES = {1: "preproc", 2: "rowreduce", 3: "gemm", 4: "region", 5: "embedding", 6: "copy"}
+DP_K_PREPROC, DP_K_ROWREDUCE, DP_K_GEMM, DP_K_REGION, DP_K_EMBEDDING, DP_K_COPY, DP_K_ATTENTION = range(1, 8)
+KERNEL_NAMES = {1: "preproc", 2: "rowreduce", 3: "gemm", 4: "region", 5: "embedding", 6: "copy", 7: "attention"}
 
 
 class PreprocParams(ctypes.Structure):
@@ -98,6 +98,16 @@ class EmbeddingParams(ctypes.Structure):
                 ("id_dtype", ctypes.c_int32), ("w_dtype", ctypes.c_int32)]
 
 
+class AttentionParams(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("heads_kv", ctypes.c_int64), ("group", ctypes.c_int64),
+                ("L", ctypes.c_int64), ("S", ctypes.c_int64), ("D", ctypes.c_int64), ("Dv", ctypes.c_int64),
+                ("q_sb", ctypes.c_int64), ("q_sh", ctypes.c_int64), ("q_sl", ctypes.c_int64),
+                ("k_sb", ctypes.c_int64), ("k_sh", ctypes.c_int64), ("k_ss", ctypes.c_int64),
+                ("v_sb", ctypes.c_int64), ("v_sh", ctypes.c_int64), ("v_ss", ctypes.c_int64),
+                ("o_sb", ctypes.c_int64), ("o_sh", ctypes.c_int64), ("o_sl", ctypes.c_int64),
+                ("scale", ctypes.c_float), ("dtype", ctypes.c_int32)]
+
+
 class PlanHeader(ctypes.Structure):
     _fields_ = [("magic", ctypes.c_uint32), ("version", ctypes.c_uint32), ("n_slots", ctypes.c_uint32),
                 ("n_records", ctypes.c_uint32), ("arena_bytes", ctypes.c_uint64), ("reserved", ctypes.c_uint64)]
@@ -115,7 +125,7 @@ class PlanRecord(ctypes.Structure):
 
 
 PARAM_STRUCTS = {DP_K_PREPROC: PreprocParams, DP_K_ROWREDUCE: RowReduceParams, DP_K_GEMM: GemmParams,
-                 DP_K_REGION: RegionDesc, DP_K_EMBEDDING: EmbeddingParams}
+                 DP_K_REGION: RegionDesc, DP_K_EMBEDDING: EmbeddingParams, DP_K_ATTENTION: AttentionParams}
 
 # (symbol, argtypes) of every exported function, in header order.
 _VP = ctypes.c_void_p
@@ -129,6 +139,7 @@ EXPORTS = {
     "dp_gemm": [ctypes.POINTER(GemmParams), _VP, _VP, _VP, _VP, _VP, _VP],
     "dp_region": [ctypes.POINTER(RegionDesc), ctypes.POINTER(_VP), _VP],
     "dp_embedding": [ctypes.POINTER(EmbeddingParams), _VP, _VP, _VP, _VP],
+    "dp_attention": [ctypes.POINTER(AttentionParams), _VP, _VP, _VP, _VP, _VP],
     "dp_program_create": [_VP, ctypes.c_size_t, ctypes.c_int, ctypes.POINTER(_VP)],
     "dp_program_bind": [_VP, ctypes.c_int, _VP, ctypes.c_size_t],
     "dp_program_run": [_VP, _VP],
@@ -216,6 +227,11 @@ def gemm(p: GemmParams, a, b, c, bias=None, residual=None, stream=None) -> None:
 def region(d: RegionDesc, operands, stream=None) -> None:
     arr = (_VP * len(operands))(*[_ptr(o) for o in operands])
     check(lib().dp_region(ctypes.byref(d), arr, _stream(stream)), "dp_region")
+
+
+def attention(p: AttentionParams, q, k, v, o, stream=None) -> None:
+    check(lib().dp_attention(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _stream(stream)),
+          "dp_attention")
 
 
 def embedding(p: EmbeddingParams, ids, weight, out, stream=None) -> None:

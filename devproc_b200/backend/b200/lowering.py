@@ -187,6 +187,8 @@ class Lowered:
 
 
 class Lowerer:
+    use_fused_attention = True  # bf16 sdpa as one fused tensor-core kernel (else GEMM + softmax + GEMM)
+
     def __init__(self, fn: Function, const_names=(), const_tensors=None):
         self.fn = fn
         self.const_names = set(const_names)
@@ -1033,6 +1035,10 @@ class Lowerer:
         kv, kst = operand(k, (B, Hk, S, D))
         # V is read in place as the GEMM's [K = keys, N = Dv] operand (N contiguous)
         vv, vst = operand(v, (B, Hk, S, Dv))
+        if self.use_fused_attention and dt == "bfloat16" and D <= 256 and Dv <= 256 and D % 8 == 0 \
+                and Dv % 8 == 0:
+            return self.lower_attention_fused(op, qv, (q_b, q_b2 // g if g > 1 else q_b2, q_ld), kv, kst, vv, vst,
+                                              B, Hq, Hk, g, L, S, D, Dv)
         # bf16 rows of at most 256 keys: the score GEMM's epilogue computes the row
         # softmax itself (one tensor-core tile holds a whole row) and writes bf16
         # probabilities; otherwise fp32 scores go through a separate row softmax.
@@ -1137,6 +1143,34 @@ class Lowerer:
         hi = rb.binary("add", rb.binary("mul", rx2, rb.load(c2)), rb.binary("mul", rx1, rb.load(s2)))
         rb.store(o2, hi)
         self.emit_region(rb, f"rope {half}")
+
+    def lower_attention_fused(self, op: Op, qv: View, qst, kv: View, kst, vv: View, vst, B, Hq, Hk, g, L, S, D,
+                              Dv) -> None:
+        """One fused tcgen05 attention record (scores stay on chip).  The query
+        operand arrives as (view, (batch, head, row) strides); the output is
+        token-major [B, L, H, Dv] for one query head per key head (so the usual
+        transpose(1, 2).reshape that follows is free) and [B, H, L, Dv]
+        otherwise (a group's heads stacked, as the kernel needs)."""
+        out_v = op.outputs[0]
+        p = N.AttentionParams()
+        p.batch, p.heads_kv, p.group = B, Hk, g
+        p.L, p.S, p.D, p.Dv = L, S, D, Dv
+        p.q_sb, p.q_sh, p.q_sl = qst
+        p.k_sb, p.k_sh, p.k_ss = kst[0], kst[1], kst[2]
+        p.v_sb, p.v_sh, p.v_ss = vst[0], vst[1], vst[2]
+        if g == 1 and len(out_v.type.shape) == 4:
+            buf = self.new_buffer("arena", "bfloat16", (B, L, Hq, Dv), out_v.name)
+            self.views[out_v.name] = View(buf, (B, Hq, L, Dv), (L * Hq * Dv, Dv, Hq * Dv, 1))
+            p.o_sb, p.o_sh, p.o_sl = L * Hq * Dv, Dv, Hq * Dv
+        else:
+            buf = self.new_value_view(out_v).buf
+            p.o_sb, p.o_sh, p.o_sl = Hq * L * Dv, L * Dv, Dv
+        p.scale = float(op.attr("scale"))
+        p.dtype = N.DP_BF16
+        flops = 2 * B * Hq * L * S * (D + Dv)
+        self.emit(N.DP_K_ATTENTION, [qv.buf, kv.buf, vv.buf, buf], p,
+                  f"attention b{B} hkv{Hk} g{g} L{L} S{S} D{D} Dv{Dv}", flops,
+                  qv.buf.nbytes + kv.buf.nbytes + vv.buf.nbytes + buf.nbytes)
 
     # ------------------------------------------------------------ embedding
     def lower_embedding(self, op: Op) -> None:

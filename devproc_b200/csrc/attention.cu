@@ -1,0 +1,552 @@
+// Fused attention on the 5th-generation tensor cores:
+//   O = softmax(scale · Q·Kᵀ) · V, bf16 operands, fp32 scores and accumulation,
+// the scores never leave the SM.
+//
+// One persistent CTA per SM works through items of 128 query rows of one
+// (batch, key/value head); the query heads that share a key/value head are
+// stacked rows (grouped-query attention), so every item reads one K / V
+// stream.  Per item the key/value blocks of 64 keys stream through a TMA
+// ring, and four roles run concurrently:
+//   warp 0   TMA producer: the Q tile once per item, then K and V blocks;
+//   warp 1   MMA issuer (one thread): S_j = Q·K_jᵀ into one of two TMEM
+//            score buffers, issued one block ahead, then O += P_j·V_j into
+//            the TMEM output accumulator; Q is released right after the
+//            item's last Q·Kᵀ so the next item's Q loads under the tail;
+//   warp 2   allocates / frees the 512 TMEM columns;
+//   warps 4-7 softmax and epilogue, one query row per thread: read S_j from
+//            TMEM, keep the row's running max m and sum l in log2 units,
+//            write P_j = 2^(s − m) as bf16 into one of two 128-byte-swizzled
+//            shared tiles (so P_{j+1} is written while P_j·V_j runs), and at
+//            the end O / l → bf16 → global.
+// The running max is raised lazily (only when a block's max exceeds it by
+// more than 2^8): P then stays ≤ 256, exact in bf16's exponent range, and O
+// and l are rescaled by 2^(m_old − m_new) only on those rare blocks.
+//
+// Every mbarrier wait is bounded (%globaltimer); on a timeout the kernel
+// records DP_DEVERR_TIMEOUT, all roles stop, in-flight copies and MMAs get a
+// bounded time to drain, TMEM is freed and the kernel returns.
+#include <cuda.h>
+#include <cstring>
+
+#include "dp_common.cuh"
+
+namespace dpk_attn {
+
+constexpr int BM = 128;        // query rows per item
+constexpr int BKV = 64;        // keys per block
+constexpr int kThreads = 256;
+constexpr int kMaxStages = 4;
+constexpr int kTmemCols = 512;
+constexpr int kSCols = BKV;    // one score buffer: 64 fp32 columns
+constexpr uint32_t kQBox = BM * 128;    // 16 KB: 128 rows × 64 bf16
+constexpr uint32_t kKVBox = BKV * 128;  // 8 KB: 64 rows × 64 bf16
+constexpr uint32_t kPBytes = BM * 128;  // 16 KB: 128 rows × 64 bf16 keys
+
+struct Shape {
+  int R;        // query rows per (batch, kv head): group · L
+  int L, S, D, Dv;
+  int nd, ndv;  // 64-wide boxes of D (Q, K) and of Dv (V)
+  int ks;       // K = 16 MMA steps covering D
+  int dvp;      // PV MMA N: Dv rounded up to 16
+  int stages;
+  int tiles_r, items, kv_blocks, heads_kv, group;
+  uint32_t stage_bytes, q_bytes;
+  float scale_log2;
+  int64_t o_sb, o_sh, o_sl;
+};
+
+__device__ __forceinline__ uint32_t su32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void tma_load(void *dst, const CUtensorMap *map, int x, int y, int z, int w,
+                                         uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+      "%5}], [%6];" ::"r"(su32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(su32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ uint64_t desc_k(uint32_t addr) {  // K-major, 128-byte swizzle, 8-row groups 1024 B
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__device__ __forceinline__ uint64_t desc_mn(uint32_t addr) {  // MN-major, 64-element N chunks 8 KB apart
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(8192 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+__host__ __device__ constexpr uint32_t idesc(int m, int n, int b_mn) {  // bf16 × bf16 → fp32
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)b_mn << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+__device__ __forceinline__ void mma(uint32_t d, uint64_t a, uint64_t b, uint32_t id, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(id), "r"(acc)
+      : "memory");
+}
+__device__ __forceinline__ void commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+// tcgen05.ld without the wait: several loads in flight, one tcgen05.wait::ld after them
+__device__ __forceinline__ void tld16_async(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+__device__ __forceinline__ void tst16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ bool aborted(volatile int *f) { return *f != 0; }
+// 0.2 s slices re-reading the abort flag, 2 s in total; on giving up records
+// DP_DEVERR_TIMEOUT and raises the abort flag.
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, int site, volatile int *flag) {
+  for (int slice = 0; slice < 10; ++slice) {
+    if (aborted(flag)) return false;
+    if (mbar_wait_for(bar, parity, 200000000ull)) return true;
+  }
+  dp_report(DP_DEVERR_TIMEOUT, site);
+  *flag = 1;
+  return false;
+}
+
+__device__ __forceinline__ void item_coords(const Shape &s, int item, int &b, int &hk, int &rt) {
+  rt = item % s.tiles_r;
+  const int bh = item / s.tiles_r;
+  hk = bh % s.heads_kv;
+  b = bh / s.heads_kv;
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                const __grid_constant__ CUtensorMap map_v, const Shape s, __nv_bfloat16 *__restrict__ out) {
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t q_full, q_empty, kv_full[kMaxStages], kv_empty[kMaxStages], s_full[2],
+      s_free[2], p_full[2], p_free[2], o_full, o_free;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sq = smem;
+  uint8_t *sp = sq + s.q_bytes;
+  uint8_t *skv = sp + 2 * kPBytes;  // two P tiles: softmax writes P_{j+1} while P_j is still being read
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    mbar_init(&q_empty, 1);
+    for (int i = 0; i < kMaxStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_free[i], 1);
+    }
+    mbar_init(&o_full, 1);
+    mbar_init(&o_free, 4);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_q) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_k) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_v) : "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = tmem_slot;
+  const uint32_t t_o = tmem + 2 * kSCols;  // output accumulator columns
+  volatile int *flag = &abort_flag;
+  const int nb = s.kv_blocks;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------- TMA producer
+      int it = 0, local = 0;
+      for (int item = blockIdx.x; item < s.items && !aborted(flag); item += gridDim.x, ++local) {
+        int b, hk, rt;
+        item_coords(s, item, b, hk, rt);
+        if (!wait_or_abort(&q_empty, (local & 1) ^ 1, 500, flag)) break;
+        mbar_arrive_expect_tx(&q_full, s.q_bytes);
+        for (int x = 0; x < s.nd; ++x) tma_load(sq + x * kQBox, &map_q, x * 64, rt * BM, hk, b, &q_full);
+        bool ok = true;
+        for (int j = 0; j < nb; ++j, ++it) {
+          const int st = it % s.stages;
+          if (!wait_or_abort(&kv_empty[st], ((it / s.stages) & 1) ^ 1, 510 + st, flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sk = skv + st * s.stage_bytes;
+          uint8_t *sv = sk + s.nd * kKVBox;
+          mbar_arrive_expect_tx(&kv_full[st], s.stage_bytes);
+          for (int x = 0; x < s.nd; ++x) tma_load(sk + x * kKVBox, &map_k, x * 64, j * BKV, hk, b, &kv_full[st]);
+          for (int x = 0; x < s.ndv; ++x) tma_load(sv + x * kKVBox, &map_v, x * 64, j * BKV, hk, b, &kv_full[st]);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------- MMA issuer
+      const uint32_t id_s = idesc(BM, BKV, 0), id_pv = idesc(BM, s.dvp, 1);
+      int it = 0, jg = 0, local = 0;
+      bool ok = true;
+      for (int item = blockIdx.x; item < s.items && ok && !aborted(flag); item += gridDim.x, ++local) {
+        if (!wait_or_abort(&q_full, local & 1, 520, flag)) break;
+        fence_after();
+        const uint32_t aq = su32(sq);
+        auto issue_s = [&](int j) -> bool {  // S_j into score buffer (jg + j) % 2
+          const int itj = it + j, jgj = jg + j, st = itj % s.stages, sb = jgj & 1;
+          if (!wait_or_abort(&kv_full[st], (itj / s.stages) & 1, 530 + st, flag)) return false;
+          if (!wait_or_abort(&s_free[sb], ((jgj >> 1) & 1) ^ 1, 540 + sb, flag)) return false;
+          fence_after();
+          const uint32_t ak = su32(skv + st * s.stage_bytes);
+          for (int k = 0; k < s.ks; ++k) {
+            const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;  // 64-wide box, 16-wide step
+            mma(tmem + sb * kSCols, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
+                k > 0 ? 1u : 0u);
+          }
+          commit(&s_full[sb]);
+          if (j == nb - 1) commit(&q_empty);  // the item's last read of Q: the next Q may load now
+          return true;
+        };
+        if (!issue_s(0)) break;
+        for (int j = 0; j < nb; ++j) {
+          if (j + 1 < nb && !issue_s(j + 1)) {
+            ok = false;
+            break;
+          }
+          const int itj = it + j, jgj = jg + j, st = itj % s.stages, pb = jgj & 1;
+          // the previous item's epilogue has read O before this item's first P·V overwrites it
+          if (j == 0 && !wait_or_abort(&o_free, (local & 1) ^ 1, 521, flag)) {
+            ok = false;
+            break;
+          }
+          if (!wait_or_abort(&p_full[pb], (jgj >> 1) & 1, 550 + pb, flag)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          const uint32_t ap = su32(sp + pb * kPBytes), av = su32(skv + st * s.stage_bytes + s.nd * kKVBox);
+          for (int k = 0; k < BKV / 16; ++k)
+            mma(t_o, desc_k(ap + k * 32), desc_mn(av + k * 2048), id_pv, (j > 0 || k > 0) ? 1u : 0u);
+          commit(&kv_empty[st]);  // K_j and V_j are read
+          commit(&p_free[pb]);    // P_j is read and O holds blocks ≤ j
+        }
+        it += nb;
+        jg += nb;
+        if (!ok) break;
+        commit(&o_full);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax + epilogue: thread = query row (warp - 4)·32 + lane
+    const int q4 = warp - 4;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    int jg = 0, local = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < s.items && ok; item += gridDim.x, ++local) {
+      int b, hk, rt;
+      item_coords(s, item, b, hk, rt);
+      float m = -INFINITY, l = 0.0f;
+      for (int j = 0; j < nb; ++j, ++jg) {
+        const int sb = jg & 1;
+        const bool got = wait_or_abort(&s_full[sb], (jg >> 1) & 1, 560 + sb, flag);
+        if (!__all_sync(0xffffffffu, got)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        float v[BKV];
+        {
+          uint32_t r[BKV / 16][16];
+#pragma unroll
+          for (int c = 0; c < BKV / 16; ++c) tld16_async(tmem + lane_off + sb * kSCols + c * 16, r[c]);
+          tld_wait();  // all four loads in flight together
+#pragma unroll
+          for (int c = 0; c < BKV / 16; ++c)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[c * 16 + e] = __uint_as_float(r[c][e]);
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[sb]);  // this score buffer may take S_{j+2}
+        const int k0 = j * BKV;
+        float t8[8];
+#pragma unroll
+        for (int e = 0; e < BKV; ++e) v[e] = (k0 + e < s.S) ? v[e] * s.scale_log2 : -INFINITY;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {  // tree max: short dependency chains
+          const float a = fmaxf(fmaxf(v[e], v[e + 8]), fmaxf(v[e + 16], v[e + 24]));
+          const float b2 = fmaxf(fmaxf(v[e + 32], v[e + 40]), fmaxf(v[e + 48], v[e + 56]));
+          t8[e] = fmaxf(a, b2);
+        }
+        const float mx = fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
+                               fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
+        // This block's P tile is free once the P·V of block jg − 2 is complete.
+        const int pb = jg & 1;
+        if (jg >= 2) {
+          const bool pf = wait_or_abort(&p_free[pb], ((jg >> 1) & 1) ^ 1, 570 + pb, flag);
+          if (!__all_sync(0xffffffffu, pf)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+        }
+        if (j == 0) {
+          m = mx;
+        } else if (__any_sync(0xffffffffu, mx > m + 8.0f)) {
+          // O must hold every issued block (P·V of block jg − 1 complete) before it is
+          // rescaled.  tcgen05.ld / st are warp-collective: the whole warp rescales its
+          // rows, rows whose max did not grow by more than 2^8 by a factor of 1.
+          const int prev = jg - 1;
+          const bool pv = wait_or_abort(&p_free[prev & 1], (prev >> 1) & 1, 575, flag);
+          if (!__all_sync(0xffffffffu, pv)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          float alpha = 1.0f;
+          if (mx > m + 8.0f) {
+            alpha = ex2(m - mx);
+            l *= alpha;
+            m = mx;
+          }
+          for (int c = 0; c < s.dvp / 16; ++c) {
+            uint32_t r[16];
+            tld16(t_o + lane_off + c * 16, r);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tst16(t_o + lane_off + c * 16, r);
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+        // P_j row as bf16 into the 128-byte-swizzled K-major tile
+        uint8_t *prow = sp + pb * kPBytes + row * 128;
+        float part[8];
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          uint32_t w[4];
+          float acc = 0.0f;
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float p0 = ex2(v[ch * 8 + 2 * h] - m), p1 = ex2(v[ch * 8 + 2 * h + 1] - m);
+            acc += p0 + p1;
+            __nv_bfloat162 bb = __floats2bfloat162_rn(p0, p1);
+            w[h] = *reinterpret_cast<uint32_t *>(&bb);
+          }
+          part[ch] = acc;  // eight independent partial sums
+          *reinterpret_cast<uint4 *>(prow + ((ch ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        l += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[pb]);
+      }
+      if (!ok) break;
+      // ---------------- epilogue: O / l → bf16 → global
+      const bool of = wait_or_abort(&o_full, local & 1, 580, flag);
+      if (!__all_sync(0xffffffffu, of)) break;
+      fence_after();
+      const int r = rt * BM + row;
+      const float inv = 1.0f / l;
+      __nv_bfloat16 *orow = nullptr;
+      if (r < s.R) {
+        const int hq = hk * s.group + r / s.L, pos = r % s.L;
+        orow = out + (int64_t)b * s.o_sb + (int64_t)hq * s.o_sh + (int64_t)pos * s.o_sl;
+      }
+      for (int c = 0; c < s.dvp / 16; ++c) {
+        uint32_t rr[16];
+        tld16(t_o + lane_off + c * 16, rr);
+        if (orow) {
+          __nv_bfloat162 h[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            h[e] = __floats2bfloat162_rn(__uint_as_float(rr[2 * e]) * inv, __uint_as_float(rr[2 * e + 1]) * inv);
+          const int c0 = c * 16;
+          if (c0 + 16 <= s.Dv) {
+            uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+            dst[0] = *reinterpret_cast<const uint4 *>(&h[0]);
+            dst[1] = *reinterpret_cast<const uint4 *>(&h[4]);
+          } else {
+            const __nv_bfloat16 *hv = reinterpret_cast<const __nv_bfloat16 *>(h);
+            for (int e = 0; c0 + e < s.Dv; ++e) orow[c0 + e] = hv[e];
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free);
+    }
+  }
+
+  __syncthreads();
+  if (aborted(flag) && threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer_ns();  // let copies and MMAs in flight drain (bounded)
+    while (globaltimer_ns() - t0 < 2000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 2) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// bf16 tensor (cols, rows, d2, d3) with element strides (row, s2, s3), boxes of 64 × box_rows.
+int make_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t d2, int64_t d3, int64_t rs,
+             int64_t s2, int64_t s3, int box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  DP_REQUIRE(fn != nullptr, DP_ERR_CUDA, "attention: cuTensorMapEncodeTiled unavailable");
+  if (d2 <= 1) s2 = rows * rs;
+  if (d3 <= 1) s3 = d2 * s2;
+  cuuint64_t dims[4] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)d2, (cuuint64_t)d3};
+  cuuint64_t strides[3] = {(cuuint64_t)(rs * 2), (cuuint64_t)(s2 * 2), (cuuint64_t)(s3 * 2)};
+  cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  DP_REQUIRE(r == CUDA_SUCCESS, DP_ERR_CUDA,
+             "attention: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return DP_OK;
+}
+
+}  // namespace dpk_attn
+
+namespace dp {
+
+int launch_attention(const dp_attention_params &p, const void *q, const void *k, const void *v, void *o,
+                     cudaStream_t stream) {
+  using namespace dpk_attn;
+  DP_REQUIRE(q && k && v && o, DP_ERR_ARG, "attention: null operand");
+  DP_REQUIRE(p.dtype == DP_BF16, DP_ERR_UNSUPPORTED, "attention: bf16 operands only");
+  DP_REQUIRE(p.batch > 0 && p.heads_kv > 0 && p.group > 0 && p.L > 0 && p.S > 0 && p.D > 0 && p.Dv > 0,
+             DP_ERR_SHAPE, "attention: sizes must be positive");
+  DP_REQUIRE(p.D <= 256 && p.Dv <= 256 && p.D % 8 == 0 && p.Dv % 8 == 0, DP_ERR_UNSUPPORTED,
+             "attention: head dims must be multiples of 8, at most 256");
+  const int64_t strides[] = {p.q_sb, p.q_sh, p.q_sl, p.k_sb, p.k_sh, p.k_ss,
+                             p.v_sb, p.v_sh, p.v_ss, p.o_sb, p.o_sh, p.o_sl};
+  for (int64_t x : strides)
+    DP_REQUIRE(x >= 0 && x % 8 == 0, DP_ERR_UNSUPPORTED, "attention: strides must be multiples of 8 elements");
+  auto al = [](const void *ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; };
+  DP_REQUIRE(al(q) && al(k) && al(v) && al(o), DP_ERR_UNSUPPORTED, "attention: 16-byte aligned bases needed");
+  DP_REQUIRE(p.group == 1 || (p.q_sh == p.L * p.q_sl && p.o_sh == p.L * p.o_sl), DP_ERR_UNSUPPORTED,
+             "attention: a group's query heads must be stacked rows");
+  DP_REQUIRE(p.group * p.L < (1ll << 30) && p.S < (1ll << 30), DP_ERR_UNSUPPORTED, "attention: too many rows");
+  Shape s{};
+  s.L = (int)p.L;
+  s.R = (int)(p.group * p.L);
+  s.S = (int)p.S;
+  s.D = (int)p.D;
+  s.Dv = (int)p.Dv;
+  s.nd = (int)((p.D + 63) / 64);
+  s.ndv = (int)((p.Dv + 63) / 64);
+  s.ks = (int)((p.D + 15) / 16);
+  s.dvp = (int)((p.Dv + 15) / 16 * 16);
+  s.q_bytes = (uint32_t)s.nd * kQBox;
+  s.stage_bytes = (uint32_t)(s.nd + s.ndv) * kKVBox;
+  const size_t budget = 224 * 1024;  // dynamic shared memory for tiles (the 1 KB alignment slack comes on top)
+  int stages = (int)((budget - s.q_bytes - 2 * kPBytes) / s.stage_bytes);
+  if (stages > kMaxStages) stages = kMaxStages;
+  DP_REQUIRE(stages >= 2, DP_ERR_UNSUPPORTED, "attention: head dims too large for the shared-memory ring");
+  s.stages = stages;
+  s.tiles_r = (s.R + BM - 1) / BM;
+  s.heads_kv = (int)p.heads_kv;
+  s.group = (int)p.group;
+  s.kv_blocks = (s.S + BKV - 1) / BKV;
+  const int64_t items = p.batch * p.heads_kv * s.tiles_r;
+  DP_REQUIRE(items < (1ll << 31), DP_ERR_UNSUPPORTED, "attention: too many work items");
+  s.items = (int)items;
+  s.scale_log2 = p.scale * 1.4426950408889634f;
+  s.o_sb = p.o_sb;
+  s.o_sh = p.o_sh;
+  s.o_sl = p.o_sl;
+  CUtensorMap mq, mk, mv;
+  // Q as (D, group rows R, kv heads, batch): a group's stacked query heads are one row range
+  int st = make_map(&mq, q, p.D, s.R, p.heads_kv, p.batch, p.q_sl, p.group * p.q_sh, p.q_sb, BM);
+  if (st != DP_OK) return st;
+  st = make_map(&mk, k, p.D, p.S, p.heads_kv, p.batch, p.k_ss, p.k_sh, p.k_sb, BKV);
+  if (st != DP_OK) return st;
+  st = make_map(&mv, v, p.Dv, p.S, p.heads_kv, p.batch, p.v_ss, p.v_sh, p.v_sb, BKV);
+  if (st != DP_OK) return st;
+  const size_t smem = (size_t)s.q_bytes + 2 * kPBytes + (size_t)stages * s.stage_bytes + 1024;
+  int dev = 0;
+  DP_CHECK_CUDA(cudaGetDevice(&dev));
+  static size_t attr_bytes[64] = {};
+  DP_REQUIRE(dev >= 0 && dev < 64, DP_ERR_UNSUPPORTED, "attention: device ordinal out of range");
+  if (smem > attr_bytes[dev]) {
+    DP_CHECK_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_bytes[dev] = smem;
+  }
+  int grid = num_sms();
+  if (grid > s.items) grid = s.items;
+  attn_kernel<<<grid, kThreads, smem, stream>>>(mq, mk, mv, s, static_cast<__nv_bfloat16 *>(o));
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
+}  // namespace dp
+
+extern "C" int dp_attention(const dp_attention_params *p, const void *q, const void *k, const void *v, void *o,
+                            void *stream) {
+  if (!p) return dp::set_error(DP_ERR_ARG, "dp_attention: null params");
+  return dp::launch_attention(*p, q, k, v, o, dp::as_stream(stream));
+}

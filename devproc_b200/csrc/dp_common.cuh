@@ -48,6 +48,8 @@ int launch_rowreduce(const dp_rowreduce_params &p, const void *in, const void *w
 int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C,
                 const void *bias, const void *res, cudaStream_t s);
 int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t s);
+int launch_attention(const dp_attention_params &p, const void *q, const void *k, const void *v, void *o,
+                     cudaStream_t s);
 int launch_embedding(const dp_embedding_params &p, const void *ids, const void *w,
                      void *out, cudaStream_t s);
 

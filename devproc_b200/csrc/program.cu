@@ -75,6 +75,12 @@ int run_records(dp_program *prog, cudaStream_t s) {
         st = dp::launch_embedding(p, ops[0], ops[1], const_cast<void *>(ops[2]), s);
         break;
       }
+      case DP_K_ATTENTION: {
+        dp_attention_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_attention(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
+        break;
+      }
       case DP_K_COPY: {
         uint64_t bytes;
         memcpy(&bytes, rec.params, sizeof(bytes));

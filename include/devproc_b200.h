@@ -195,6 +195,32 @@ typedef struct dp_embedding_params {
 int dp_embedding(const dp_embedding_params *p, const void *ids, const void *weight,
                  void *out, void *stream);
 
+/* ---- fused attention ----------------------------------------------------------
+ * O = softmax(scale · Q·Kᵀ) · V per (batch, key/value head), bf16 in and out,
+ * fp32 scores and accumulation, never materialising the scores (one tcgen05
+ * kernel: Q·Kᵀ into tensor memory, an online row softmax, P·V accumulated in
+ * tensor memory).  Replaces the reference's missing attention (its FX
+ * converter had no lowering for scaled_dot_product_attention,
+ * src/devproc/ir/fx_converter.py:443-448).
+ * Q[b, h, l, :] sits at q + b·q_sb + h·q_sh + l·q_sl (elements), likewise K
+ * [b, hk, s], V [b, hk, s] and O [b, h, l].  Query head h uses key/value
+ * head h / group; with group > 1 a group's query heads must be stacked rows
+ * (q_sh = L·q_sl and o_sh = L·o_sl).  D, Dv ≤ 256, multiples of 8; every
+ * row stride and batch / head stride a multiple of 8 elements; bases
+ * 16-byte aligned. */
+typedef struct dp_attention_params {
+  int64_t batch, heads_kv, group;  /* query heads = heads_kv · group */
+  int64_t L, S, D, Dv;
+  int64_t q_sb, q_sh, q_sl;
+  int64_t k_sb, k_sh, k_ss;
+  int64_t v_sb, v_sh, v_ss;
+  int64_t o_sb, o_sh, o_sl;
+  float scale;
+  int32_t dtype;  /* DP_BF16 */
+} dp_attention_params;
+int dp_attention(const dp_attention_params *p, const void *q, const void *k, const void *v, void *o,
+                 void *stream);
+
 /* ---- compiled program ------------------------------------------------------
  * A plan is a little-endian blob: dp_plan_header, n_slots × dp_plan_slot,
  * n_records × dp_plan_record.  Slots of kind DP_SLOT_BOUND are caller-owned
@@ -211,7 +237,7 @@ int dp_embedding(const dp_embedding_params *p, const void *ids, const void *weig
 enum { DP_SLOT_BOUND = 0, DP_SLOT_ARENA = 1 };
 enum {
   DP_K_PREPROC = 1, DP_K_ROWREDUCE = 2, DP_K_GEMM = 3, DP_K_REGION = 4,
-  DP_K_EMBEDDING = 5, DP_K_COPY = 6
+  DP_K_EMBEDDING = 5, DP_K_COPY = 6, DP_K_ATTENTION = 7
 };
 typedef struct dp_plan_header {
   uint32_t magic, version, n_slots, n_records;

@@ -242,7 +242,10 @@ def test_small_policy_lowering():
     labels = [r["label"] for r in prog.spec.records]
     assert sum(lb.startswith("rope") for lb in labels) == 2 * (2 + 3 * 2)
     assert sum("linear x3" in lb for lb in labels) == 1 + 2 + 3 * 2
-    assert any("attn-scores+softmax b2 M40 N50" in lb for lb in labels)
+    # grouped-query attention (4 query heads per key/value head) as fused attention records;
+    # the expert's queries see the 40 prefix keys plus their own 10
+    assert any(lb.startswith("attention b2 hkv1 g4 L10 S50 D32") for lb in labels)
+    assert sum(lb.startswith("attention") for lb in labels) == 1 + 2 + 3 * 2
     assert sum(lb.startswith("cat") for lb in labels) >= 4 * 3 * 2
     assert prog.spec.outputs[0].shape == [2, 10, 8] and prog.spec.outputs[0].dtype == "float32"
 
