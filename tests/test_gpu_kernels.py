@@ -601,7 +601,8 @@ def _attn_ref(q, k, v, scale):
 
 @pytest.mark.parametrize("B,Hk,g,L,S,D,Dv", [(2, 1, 8, 24, 50, 64, 64), (2, 1, 8, 50, 866, 256, 256),
                                               (1, 2, 4, 200, 300, 128, 128), (3, 4, 1, 256, 256, 72, 72),
-                                              (1, 1, 1, 1, 1, 64, 64), (2, 2, 1, 130, 70, 256, 128)])
+                                              (1, 1, 1, 1, 1, 64, 64), (2, 2, 1, 130, 70, 256, 128),
+                                              (32, 16, 1, 256, 256, 72, 72)])
 def test_fused_attention(cuda, B, Hk, g, L, S, D, Dv):
     """Fused tcgen05 attention against fp32 torch: grouped-query heads stacked as rows,
     key counts not a multiple of the 64-key block, partial 128-row query tiles, head dims
