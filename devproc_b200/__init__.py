@@ -20,7 +20,8 @@ from .dsl.kernel import kernel, KernelTensor, parse_ir
 from .dsl import ops as _ops
 from .dsl.types import (String, Tensor, Float32, Float16, BFloat16, Int32, Int64, UInt8, Bool, Tokenizer,
                         TorchModel, KVCache, IRFunction)
-from .ir.from_torch import from_torch
+from .ir.from_torch import from_export, from_torch
+from .ir.export_importer import TorchExportImporter
 from .runtime import Runtime
 from .backend.base import Backend, CompiledProgram, BackendError, UnsupportedOpError, CompilationError
 from .backend.b200 import B200Compiler, B200CompiledProgram
@@ -86,19 +87,23 @@ def compile(target, *example_inputs, backend: str = "b200", **kwargs):
 
     ``target`` may be an IR ``Function``; a ``@kernel`` wrapper or plain
     function (called with ``example_inputs`` to build the IR, as in the
-    reference, __init__.py:55-85); or a ``torch.nn.Module``, which is captured
-    with the FX frontend.  ``kwargs``: ``device_id``, ``use_graph``,
-    ``constants`` (name → tensor bound once, e.g. weights).
+    reference, __init__.py:55-85); a ``torch.nn.Module``, captured with
+    Dynamo (``method="dynamo"``) or ``torch.export`` (``method="export"``);
+    or a ``torch.export.ExportedProgram``.  ``kwargs``: ``device_id``,
+    ``use_graph``, ``constants`` (name → tensor bound once, e.g. weights).
     """
     if backend not in _BACKENDS:
         raise ValueError(f"Unknown backend: {backend}")
     constants = kwargs.pop("constants", None)
+    method = kwargs.pop("method", "dynamo")
     if hasattr(target, "ir_function"):
         fn = target.ir_function
     elif isinstance(target, Function):
         fn = target
+    elif isinstance(target, __import__("torch").export.ExportedProgram):
+        fn = from_export(target, backend="ir")
     elif isinstance(target, __import__("torch").nn.Module):
-        fn = from_torch(target, *example_inputs, backend="ir")
+        fn = from_torch(target, *example_inputs, backend="ir", method=method)
     else:
         fn = target(*example_inputs)
     return B200Compiler(**kwargs).compile(fn, constants=constants)
@@ -125,5 +130,5 @@ __all__ = [
     "mean", "layer_norm", "rms_norm", "embedding", "load_vla_module",
     "Backend", "CompiledProgram", "BackendError", "UnsupportedOpError", "CompilationError",
     "B200Compiler", "B200CompiledProgram", "TritonCompiler", "TritonCompiledProgram", "TritonRuntime",
-    "DevProcError", "Runtime", "compile", "save", "load", "from_torch",
+    "DevProcError", "Runtime", "compile", "save", "load", "from_torch", "from_export", "TorchExportImporter",
 ]

@@ -12,6 +12,7 @@ from typing import Any, Callable, Optional, Tuple, Union
 import torch
 
 from .function import Function
+from .export_importer import TorchExportImporter, export_module
 from .fx_converter import FXToIRConverter
 
 
@@ -80,13 +81,29 @@ def capture(target: Union[torch.nn.Module, Callable], *example_inputs) -> Tuple[
 
 
 def from_torch(target: Union[torch.nn.Module, Callable], *example_inputs: Any, backend: str = "devproc",
-               device_id: int = 0):
-    """Convert ``target`` to IR (``backend="ir"``) or to a compiled program (``"devproc"``)."""
+               device_id: int = 0, method: str = "dynamo"):
+    """Convert ``target`` to IR (``backend="ir"``) or to a compiled program (``"devproc"``).
+
+    ``method="dynamo"`` captures with ``torch.compile`` (the reference's FX
+    path); ``method="export"`` goes through ``torch.export.export`` and the
+    ATen importer.  ``target`` may also be an ``ExportedProgram``."""
     if backend not in ("ir", "devproc"):
         raise ValueError(f"Unknown backend: {backend}")
-    gm, ex = capture(target, *example_inputs)
-    fn = FXToIRConverter().convert(gm, ex)
+    if method not in ("dynamo", "export"):
+        raise ValueError(f"Unknown capture method: {method}")
+    if isinstance(target, torch.export.ExportedProgram):
+        fn = TorchExportImporter().import_program(target)
+    elif method == "export":
+        fn = TorchExportImporter().import_program(export_module(target, *example_inputs))
+    else:
+        gm, ex = capture(target, *example_inputs)
+        fn = FXToIRConverter().convert(gm, ex)
     if backend == "ir":
         return fn
     from ..backend.b200 import B200Compiler
     return DevProcCompiledProgram(B200Compiler(device_id).compile(fn))
+
+
+def from_export(ep: "torch.export.ExportedProgram", backend: str = "devproc", device_id: int = 0):
+    """IR (``backend="ir"``) or compiled program of a ``torch.export`` result."""
+    return from_torch(ep, backend=backend, device_id=device_id)

@@ -45,9 +45,17 @@ def _ttype(t: torch.Tensor) -> TensorType:
     return TensorType(tuple(int(s) for s in t.shape), _DT[t.dtype], "cuda" if t.is_cuda else "cpu")
 
 
+def _meta_val(node):
+    """The node's example result: Dynamo's ``example_value``, or ``val`` in a torch.export graph."""
+    ev = node.meta.get("example_value")
+    return node.meta.get("val") if ev is None else ev
+
+
 def _target_name(target) -> str:
     if isinstance(target, str):
         return target
+    if isinstance(target, torch._ops.OpOverload):  # aten.add.Tensor → "add"
+        return target.overloadpacket.__name__
     name = getattr(target, "__name__", None) or str(target)
     if name.endswith(".default"):
         name = name[:-8]
@@ -88,7 +96,7 @@ class FXToIRConverter:
     def _emit(self, node: torch.fx.Node, op) -> Value:
         self.fn.block.add_op(op)
         out = op.outputs[0]
-        ev = node.meta.get("example_value") if node is not None else None
+        ev = _meta_val(node) if node is not None else None
         if isinstance(ev, torch.Tensor) and isinstance(out.type, TensorType):
             if tuple(ev.shape) != out.type.shape:
                 raise ValueError(f"shape rule mismatch at {node.name} ({op.name}): IR {out.type.shape} vs "
@@ -112,7 +120,7 @@ class FXToIRConverter:
         return node.kwargs.get(key, default)
 
     def _ex_shape(self, node) -> Tuple[int, ...]:
-        ev = node.meta.get("example_value")
+        ev = _meta_val(node)
         if isinstance(ev, torch.Tensor):
             return tuple(int(s) for s in ev.shape)
         raise ValueError(f"{node.name}: no example_value to take the result shape from")
@@ -123,7 +131,7 @@ class FXToIRConverter:
         self._ph_index += 1
         example = self.example_inputs[idx] if idx < len(self.example_inputs) else None
         if not isinstance(example, torch.Tensor):
-            ev = node.meta.get("example_value")
+            ev = _meta_val(node)
             if not isinstance(ev, torch.Tensor):
                 raise ValueError(f"placeholder {node.name}: no tensor example")
             example = ev
@@ -257,7 +265,7 @@ class FXToIRConverter:
 
     def _op_matmul(self, node, args, kwargs):
         a, b = self._v(args[0]), self._v(args[1])
-        ev = node.meta.get("example_value")
+        ev = _meta_val(node)
         out = _DT[ev.dtype] if isinstance(ev, torch.Tensor) else "float32"
         self._emit(node, OpBuilder.matmul(a, b, out_dtype=out))
 
@@ -333,7 +341,7 @@ class FXToIRConverter:
         if dim is None:
             x = self._reshape_value(x, (x.type.numel,))
             dim = 0
-        ev = node.meta.get("example_value")
+        ev = _meta_val(node)
         self._emit(node, OpBuilder.argmax(x, dim, dtype=_DT[ev.dtype] if isinstance(ev, torch.Tensor)
                                           else "int64", keepdim=keepdim))
 
@@ -374,12 +382,12 @@ class FXToIRConverter:
         w = self._arg(node, 2, "weight")
         eps = self._arg(node, 3, "eps", None)
         if eps is None:
-            eps = torch.finfo(node.meta["example_value"].dtype).eps
+            eps = torch.finfo(_meta_val(node).dtype).eps
         self._emit(node, OpBuilder.rms_norm(self._v(args[0]), self._v(w) if w is not None else None, eps))
 
     def _op_to(self, node, args, kwargs):
         x = self._v(args[0])
-        ev = node.meta.get("example_value")
+        ev = _meta_val(node)
         dtype = _DT[ev.dtype] if isinstance(ev, torch.Tensor) else x.type.dtype
         if dtype == x.type.dtype:
             self.value_map[node] = x
@@ -505,8 +513,8 @@ class FXToIRConverter:
 
     def _op_sdpa(self, node, args, kwargs):
         q, k, v = (self._v(a) for a in args[:3])
-        if kwargs.get("attn_mask") is not None or (len(args) > 3 and args[3] is not None):
+        if self._arg(node, 3, "attn_mask") is not None:
             raise ValueError("scaled_dot_product_attention with a mask is not supported")
-        if kwargs.get("dropout_p", 0.0):
+        if self._arg(node, 4, "dropout_p", 0.0):
             raise ValueError("scaled_dot_product_attention with dropout is not supported")
-        self._emit(node, OpBuilder.sdpa(q, k, v, kwargs.get("scale"), kwargs.get("is_causal", False)))
+        self._emit(node, OpBuilder.sdpa(q, k, v, self._arg(node, 6, "scale"), self._arg(node, 5, "is_causal", False)))
