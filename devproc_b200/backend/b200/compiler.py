@@ -17,6 +17,7 @@ from ...ir.verifier import IRVerifier
 from ..base import Backend, CompilationError
 from .lowering import lower
 from .program import B200CompiledProgram, ProgramSpec
+from .rebatch import batch_factors, rebatch
 
 
 class B200Compiler(Backend):
@@ -48,4 +49,38 @@ class B200Compiler(Backend):
         low = lower(ir_function, const_names=consts.keys(), const_tensors=consts)
         consts.update(low.extra_consts)
         spec = ProgramSpec.from_lowered(low)
-        return B200CompiledProgram(spec, consts, self.device_id, ir_function, self.use_graph)
+        prog = B200CompiledProgram(spec, consts, self.device_id, ir_function, self.use_graph)
+        chunk = stream_chunk(ir_function, low, consts)
+        if chunk is not None:
+            sub_fn = rebatch(ir_function, chunk, consts.keys())
+            sub = lower(sub_fn, const_names=consts.keys(), const_tensors=consts)
+            consts.update(sub.extra_consts)
+            prog.set_stream(chunk, ProgramSpec.from_lowered(sub))
+        return prog
+
+
+# Streaming a program in chunks pays when its run is dominated by moving
+# host data: only memory-bound records (no GEMM or attention), and enough
+# input bytes that each chunk's copy is still long next to a launch.
+_STREAM_MIN_BYTES = 16 << 20
+_STREAM_MIN_CHUNK_BYTES = 4 << 20
+_STREAM_MAX_CHUNKS = 16
+
+
+def stream_chunk(fn: Function, low, consts) -> Optional[int]:
+    """Chunk batch for overlapped host transfers, or None: the program must be
+    batch-separable and memory-bound, with at least 16 MiB of input."""
+    from ... import _native as N
+    if any(r.kernel in (N.DP_K_GEMM, N.DP_K_ATTENTION) for r in low.records):
+        return None
+    B, _, _ = batch_factors(fn, consts.keys())
+    if B is None:
+        return None
+    in_bytes = sum(b.nbytes for _, b in low.inputs)
+    if in_bytes < _STREAM_MIN_BYTES:
+        return None
+    n = min(_STREAM_MAX_CHUNKS, B, in_bytes // _STREAM_MIN_CHUNK_BYTES)
+    for chunk in range(-(-B // n), B):
+        if B % chunk == 0:
+            return chunk
+    return None

@@ -91,6 +91,10 @@ class B200CompiledProgram(CompiledProgram):
         self._host_out: List[Optional[torch.Tensor]] = []
         self._bound: Dict[int, int] = {}
         self._checks_index = any(r["kernel"] == "embedding" for r in spec.records)
+        # chunked execution for host inputs (see set_stream)
+        self.stream_chunk: Optional[int] = None
+        self._chunk: Optional["B200CompiledProgram"] = None
+        self._side: Optional[tuple] = None
 
     # reference-compatible attributes ----------------------------------
     @property
@@ -151,13 +155,7 @@ class B200CompiledProgram(CompiledProgram):
 
     def _bind_input(self, io: IOSlot, t: torch.Tensor) -> None:
         want = TORCH_DTYPES[io.dtype]
-        if not isinstance(t, torch.Tensor):
-            raise TypeError(f"input {io.name}: expected a torch.Tensor, got {type(t).__name__}")
-        if t.numel() != io.numel:
-            raise N.DevProcError(N.DP_ERR_SHAPE, f"input {io.name}: shape {tuple(t.shape)} does not match "
-                                                 f"the compiled shape {tuple(io.shape)}")
-        if t.dtype != want:
-            raise N.DevProcError(N.DP_ERR_SHAPE, f"input {io.name}: dtype {t.dtype} != compiled {want}")
+        t = self._check_input(io, t)
         dev = self._device()
         if t.is_cuda and t.device == dev and t.is_contiguous():
             src = t
@@ -172,6 +170,90 @@ class B200CompiledProgram(CompiledProgram):
         if self._bound.get(io.slot) != ptr:
             self._bind_slot(self._native, io.slot, ptr, max(1, src.numel()) * src.element_size())
             self._bound[io.slot] = ptr
+
+    def set_stream(self, chunk: int, chunk_spec: ProgramSpec) -> None:
+        """Attach the same program compiled for a batch of ``chunk`` samples.
+        ``run`` with host inputs then executes it on successive chunks of the
+        batch: chunk i+1's inputs cross PCIe on one stream while chunk i runs
+        and chunk i-1's outputs come back on another, instead of one whole
+        copy in, the launches, and one whole copy out."""
+        batch = self.spec.inputs[0].shape[0]
+        if batch % chunk or chunk_spec.inputs[0].shape[0] != chunk:
+            raise ValueError(f"chunk {chunk} does not divide batch {batch}")
+        self.stream_chunk = chunk
+        self._chunk = B200CompiledProgram(chunk_spec, self._constants, self.device_id, use_graph=False)
+        self._chunk._dev_consts = self._dev_consts  # one upload per constant, shared
+
+    def _run_streamed(self, given: Dict[str, torch.Tensor], to_cpu: bool) -> List[torch.Tensor]:
+        sub = self._chunk
+        sub._ensure_ready()
+        dev = self._device()
+        cur = torch.cuda.current_stream(dev)
+        if self._side is None:
+            self._side = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        h2d, d2h = self._side
+        batch, b = self.spec.inputs[0].shape[0], self.stream_chunk
+        start = torch.cuda.Event()
+        start.record(cur)
+        h2d.wait_event(start)
+        rows = []  # (chunk IOSlot, full-batch source [batch, -1], host source or None)
+        for io, cio in zip(self.spec.inputs, sub.spec.inputs):
+            t = self._check_input(io, given[io.name])
+            if t.is_cuda and t.device == dev and t.is_contiguous():
+                rows.append((cio, t.view(batch, -1), None))
+                continue
+            st = self._staging.get(io.name)
+            if st is None:
+                st = torch.empty(io.shape, dtype=t.dtype, device=dev)
+                self._staging[io.name] = st
+            rows.append((cio, st.view(batch, -1), t.reshape(batch, -1)))
+        outs = [o.view(batch, -1) for o in self._outputs]
+        host = []
+        if to_cpu:
+            d2h.wait_event(start)
+            for i, t in enumerate(self._outputs):
+                if self._host_out[i] is None:
+                    self._host_out[i] = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                host.append(self._host_out[i].view(batch, -1))
+        for i in range(batch // b):
+            lo, hi = i * b, (i + 1) * b
+            staged = torch.cuda.Event()
+            with torch.cuda.stream(h2d):
+                for _, dst, src in rows:
+                    if src is not None:
+                        dst[lo:hi].copy_(src[lo:hi], non_blocking=True)
+                staged.record(h2d)
+            cur.wait_event(staged)
+            for cio, dst, _ in rows:
+                part = dst[lo:hi]
+                sub._bind_slot(sub._native, cio.slot, part.data_ptr(), max(1, part.numel()) * part.element_size())
+            for cio, o in zip(sub.spec.outputs, outs):
+                part = o[lo:hi]
+                sub._bind_slot(sub._native, cio.slot, part.data_ptr(), max(1, part.numel()) * part.element_size())
+            sub._native.run(cur.cuda_stream)
+            if to_cpu:
+                done = torch.cuda.Event()
+                done.record(cur)
+                d2h.wait_event(done)
+                with torch.cuda.stream(d2h):
+                    for h, o in zip(host, outs):
+                        h[lo:hi].copy_(o[lo:hi], non_blocking=True)
+        if to_cpu:
+            back = torch.cuda.Event()
+            back.record(d2h)
+            cur.wait_event(back)
+        return [self._host_out[i] for i in range(len(outs))] if to_cpu else list(self._outputs)
+
+    def _check_input(self, io: IOSlot, t) -> torch.Tensor:
+        want = TORCH_DTYPES[io.dtype]
+        if not isinstance(t, torch.Tensor):
+            raise TypeError(f"input {io.name}: expected a torch.Tensor, got {type(t).__name__}")
+        if t.numel() != io.numel:
+            raise N.DevProcError(N.DP_ERR_SHAPE, f"input {io.name}: shape {tuple(t.shape)} does not match "
+                                                 f"the compiled shape {tuple(io.shape)}")
+        if t.dtype != want:
+            raise N.DevProcError(N.DP_ERR_SHAPE, f"input {io.name}: dtype {t.dtype} != compiled {want}")
+        return t
 
     def run(self, *args, to_cpu: bool = True, reuse_host_buffers: bool = False, **kwargs) -> List[torch.Tensor]:
         """Execute once.  Inputs by IR name (positional args fill the inputs in
@@ -195,21 +277,28 @@ class B200CompiledProgram(CompiledProgram):
             for io in self.spec.inputs:
                 if io.name not in given:
                     raise TypeError(f"missing input {io.name}")
-                self._bind_input(io, given[io.name])
             stream = torch.cuda.current_stream(self._device())
-            self._native.run(stream.cuda_stream)
-            if not to_cpu:
-                return list(self._outputs)
-            outs = []
-            for i, t in enumerate(self._outputs):
-                h = self._host_out[i]
-                if h is None:
-                    h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
-                    self._host_out[i] = h
-                h.copy_(t, non_blocking=True)
-                outs.append(h)
+            if self._chunk is not None and any(not given[io.name].is_cuda for io in self.spec.inputs
+                                               if isinstance(given[io.name], torch.Tensor)):
+                outs = self._run_streamed(given, to_cpu)
+                if not to_cpu:
+                    return outs
+            else:
+                for io in self.spec.inputs:
+                    self._bind_input(io, given[io.name])
+                self._native.run(stream.cuda_stream)
+                if not to_cpu:
+                    return list(self._outputs)
+                outs = []
+                for i, t in enumerate(self._outputs):
+                    h = self._host_out[i]
+                    if h is None:
+                        h = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                        self._host_out[i] = h
+                    h.copy_(t, non_blocking=True)
+                    outs.append(h)
             stream.synchronize()
-            if self._checks_index:
+            if self._checks_index or (self._chunk is not None and self._chunk._checks_index):
                 code, info = N.device_error()
                 if code == N.DP_DEVERR_INDEX:
                     raise IndexError(f"embedding id out of range at flat position {info}")
@@ -227,9 +316,13 @@ class B200CompiledProgram(CompiledProgram):
             f.write(self.spec.plan)
         offset = 0
         consts = []
-        if self.spec.consts:
+        to_write = list(self.spec.consts)
+        if self._chunk is not None:
+            have = {c.name for c in to_write}
+            to_write += [c for c in self._chunk.spec.consts if c.name not in have]
+        if to_write:
             with open(path + ".weights", "wb") as f:
-                for c in self.spec.consts:
+                for c in to_write:
                     t = self._constants[c.name].detach().to("cpu", TORCH_DTYPES[c.dtype]).contiguous()
                     raw = t.view(torch.uint8).numpy().tobytes() if t.numel() else b""
                     pad = (-offset) % 256
@@ -243,11 +336,20 @@ class B200CompiledProgram(CompiledProgram):
             "plan_bytes": len(self.spec.plan), "arena_bytes": self.spec.arena_bytes,
             "inputs": [asdict(i) for i in self.spec.inputs],
             "consts": [asdict(c) for c in consts],
+            "n_consts": len(self.spec.consts),
             "outputs": [asdict(o) for o in self.spec.outputs],
             "kernels": self.spec.records,
             "aliases": self.spec.aliases,
             "tensor_allocations": {o.name: {"shape": o.shape, "dtype": o.dtype} for o in self.spec.outputs},
         }
+        if self._chunk is not None:
+            cs = self._chunk.spec
+            with open(path + ".chunk", "wb") as f:
+                f.write(cs.plan)
+            meta["stream"] = {"chunk": self.stream_chunk, "plan_bytes": len(cs.plan), "arena_bytes": cs.arena_bytes,
+                              "inputs": [asdict(i) for i in cs.inputs], "consts": [asdict(c) for c in cs.consts],
+                              "outputs": [asdict(o) for o in cs.outputs], "kernels": cs.records,
+                              "aliases": cs.aliases}
         with open(path + ".meta.json", "w") as f:
             json.dump(meta, f, indent=1)
 
@@ -271,10 +373,23 @@ class B200CompiledProgram(CompiledProgram):
                 raw = bytearray(blob[c.offset:c.offset + nbytes])
                 t = torch.frombuffer(raw, dtype=torch.uint8) if nbytes else torch.empty(0, dtype=torch.uint8)
                 constants[c.name] = t.view(TORCH_DTYPES[c.dtype]).reshape(c.shape)
-        spec = ProgramSpec(meta["name"], plan, [IOSlot(**i) for i in meta["inputs"]], consts,
+        # the weights file may also hold constants only the chunk program reads (after the first n_consts)
+        spec = ProgramSpec(meta["name"], plan, [IOSlot(**i) for i in meta["inputs"]],
+                           consts[:meta.get("n_consts", len(consts))],
                            [IOSlot(**o) for o in meta["outputs"]], meta["arena_bytes"], meta["kernels"],
                            meta.get("aliases", []))
-        return B200CompiledProgram(spec, constants, device_id)
+        prog = B200CompiledProgram(spec, constants, device_id)
+        st = meta.get("stream")
+        if st:
+            with open(path + ".chunk", "rb") as f:
+                cplan = f.read()
+            if len(cplan) != st["plan_bytes"]:
+                raise ValueError(f"{path}.chunk: plan size {len(cplan)} != {st['plan_bytes']}")
+            prog.set_stream(st["chunk"], ProgramSpec(meta["name"], cplan, [IOSlot(**i) for i in st["inputs"]],
+                                                     [IOSlot(**c) for c in st["consts"]],
+                                                     [IOSlot(**o) for o in st["outputs"]], st["arena_bytes"],
+                                                     st["kernels"], st.get("aliases", [])))
+        return prog
 
     def close(self) -> None:
         if self._native is not None:
