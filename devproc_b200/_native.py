@@ -52,8 +52,10 @@ DP_PLAN_MAGIC, DP_PLAN_VERSION = 0x32425044, 1
 DP_NOALLOC_ARENA_BYTES = 64 << 20
 DP_RECORD_MAX_OPERANDS, DP_RECORD_PARAM_BYTES = 8, 1280
 DP_SLOT_BOUND, DP_SLOT_ARENA = 0, 1
-DP_K_PREPROC, DP_K_ROWREDUCE, DP_K_GEMM, DP_K_REGION, DP_K_EMBEDDING, DP_K_COPY, DP_K_ATTENTION = range(1, 8)
-KERNEL_NAMES = {1: "preproc", 2: "rowreduce", 3: "gemm", 4: "region", 5: "embedding", 6: "copy", 7: "attention"}
+DP_K_PREPROC, DP_K_ROWREDUCE, DP_K_GEMM, DP_K_REGION, DP_K_EMBEDDING, DP_K_COPY, DP_K_ATTENTION, DP_K_ROPE = \
+    range(1, 9)
+KERNEL_NAMES = {1: "preproc", 2: "rowreduce", 3: "gemm", 4: "region", 5: "embedding", 6: "copy", 7: "attention",
+                8: "rope"}
 
 
 class PreprocParams(ctypes.Structure):
@@ -108,6 +110,16 @@ class AttentionParams(ctypes.Structure):
                 ("scale", ctypes.c_float), ("dtype", ctypes.c_int32)]
 
 
+class RopeParams(ctypes.Structure):
+    _fields_ = [("batch", ctypes.c_int64), ("heads", ctypes.c_int64), ("rows", ctypes.c_int64),
+                ("dim", ctypes.c_int64),
+                ("x_sb", ctypes.c_int64), ("x_sh", ctypes.c_int64), ("x_sr", ctypes.c_int64),
+                ("o_sb", ctypes.c_int64), ("o_sh", ctypes.c_int64), ("o_sr", ctypes.c_int64),
+                ("t_sb", ctypes.c_int64), ("t_sh", ctypes.c_int64), ("t_sr", ctypes.c_int64),
+                ("half_table", ctypes.c_int32), ("x_dtype", ctypes.c_int32), ("t_dtype", ctypes.c_int32),
+                ("reserved", ctypes.c_int32)]
+
+
 class PlanHeader(ctypes.Structure):
     _fields_ = [("magic", ctypes.c_uint32), ("version", ctypes.c_uint32), ("n_slots", ctypes.c_uint32),
                 ("n_records", ctypes.c_uint32), ("arena_bytes", ctypes.c_uint64), ("reserved", ctypes.c_uint64)]
@@ -125,7 +137,8 @@ class PlanRecord(ctypes.Structure):
 
 
 PARAM_STRUCTS = {DP_K_PREPROC: PreprocParams, DP_K_ROWREDUCE: RowReduceParams, DP_K_GEMM: GemmParams,
-                 DP_K_REGION: RegionDesc, DP_K_EMBEDDING: EmbeddingParams, DP_K_ATTENTION: AttentionParams}
+                 DP_K_REGION: RegionDesc, DP_K_EMBEDDING: EmbeddingParams, DP_K_ATTENTION: AttentionParams,
+                 DP_K_ROPE: RopeParams}
 
 # (symbol, argtypes) of every exported function, in header order.
 _VP = ctypes.c_void_p
@@ -140,6 +153,7 @@ EXPORTS = {
     "dp_region": [ctypes.POINTER(RegionDesc), ctypes.POINTER(_VP), _VP],
     "dp_embedding": [ctypes.POINTER(EmbeddingParams), _VP, _VP, _VP, _VP],
     "dp_attention": [ctypes.POINTER(AttentionParams), _VP, _VP, _VP, _VP, _VP],
+    "dp_rope": [ctypes.POINTER(RopeParams), _VP, _VP, _VP, _VP, _VP],
     "dp_program_create": [_VP, ctypes.c_size_t, ctypes.c_int, ctypes.POINTER(_VP)],
     "dp_program_bind": [_VP, ctypes.c_int, _VP, ctypes.c_size_t],
     "dp_program_run": [_VP, _VP],
@@ -232,6 +246,10 @@ def region(d: RegionDesc, operands, stream=None) -> None:
 def attention(p: AttentionParams, q, k, v, o, stream=None) -> None:
     check(lib().dp_attention(ctypes.byref(p), _ptr(q), _ptr(k), _ptr(v), _ptr(o), _stream(stream)),
           "dp_attention")
+
+
+def rope(p: RopeParams, x, cos, sin, out, stream=None) -> None:
+    check(lib().dp_rope(ctypes.byref(p), _ptr(x), _ptr(cos), _ptr(sin), _ptr(out), _stream(stream)), "dp_rope")
 
 
 def embedding(p: EmbeddingParams, ids, weight, out, stream=None) -> None:

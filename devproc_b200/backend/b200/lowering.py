@@ -1119,6 +1119,8 @@ class Lowerer:
         stores (c1 = c2, s1 = s2 for half-width tables)."""
         x_val, c_val, s_val = op.inputs
         xv = self.views[x_val.name]
+        if self.lower_rope_kernel(op):
+            return
         D = x_val.type.shape[-1]
         h = D // 2
         half = tuple(x_val.type.shape[:-1]) + (h,)
@@ -1143,6 +1145,71 @@ class Lowerer:
         hi = rb.binary("add", rb.binary("mul", rx2, rb.load(c2)), rb.binary("mul", rx1, rb.load(s2)))
         rb.store(o2, hi)
         self.emit_region(rb, f"rope {half}")
+
+    def lower_rope_kernel(self, op: Op) -> bool:
+        """One ``dp_rope`` record when x is at most 4-d with a contiguous last
+        dim, the two tables share one broadcast layout, and every base, stride
+        and half width is 16-byte vector aligned; False leaves the region."""
+        x_val, c_val, s_val = op.inputs
+        xv, cv, sv = (self.views[v.name] for v in op.inputs)
+        dt, tdt = x_val.type.dtype, c_val.type.dtype
+        if dt not in ("bfloat16", "float16", "float32") or tdt != s_val.type.dtype or \
+                tdt not in ("bfloat16", "float16", "float32"):
+            return False
+        rank, D = len(xv.shape), xv.shape[-1]
+        if rank > 4 or D % 2 or xv.strides[-1] != 1:
+            return False
+        vec = 16 // DTYPE_BYTES[dt]
+        tb = DTYPE_BYTES[tdt]
+        t_align = 16 // tb if vec * tb >= 16 else vec
+        if (D // 2) % vec:
+            return False
+
+        def table(v: View):
+            """(strides over x's 4 dims, half_table) of a table broadcast to x."""
+            if v.shape[-1] not in (D, D // 2) or v.strides[-1] != 1:
+                return None
+            lead = rank - len(v.shape)
+            if lead < 0:
+                return None
+            st = []
+            for k in range(rank - 1):
+                j = k - lead
+                if j < 0 or v.shape[j] == 1:
+                    st.append(0)
+                elif v.shape[j] == xv.shape[k]:
+                    st.append(v.strides[j])
+                else:
+                    return None
+            return [0] * (4 - rank) + st, v.shape[-1] == D // 2
+
+        tc, ts = table(cv), table(sv)
+        if tc is None or tc != ts:
+            return False
+        t_st, half_table = tc
+        pad = [0] * (4 - rank)
+        x_st = pad + list(xv.strides[:-1])
+        o_st = pad + list(contiguous_strides(tuple(xv.shape))[:-1])
+        if any(s % vec for s in x_st + o_st) or any(s % t_align for s in t_st):
+            return False
+        if any((v.buf.base_off + v.offset * DTYPE_BYTES[v.buf.dtype]) % 16 for v in (xv, cv, sv)):
+            return False
+        bx, bc, bs = (self.based(v, n) for v, n in ((xv, x_val.name), (cv, c_val.name), (sv, s_val.name)))
+        out = self.new_value_view(op.outputs[0])
+        dims = [1] * (4 - rank) + list(xv.shape[:-1])
+        p = N.RopeParams()
+        p.batch, p.heads, p.rows, p.dim = dims[0], dims[1], dims[2], D
+        p.x_sb, p.x_sh, p.x_sr = x_st
+        p.o_sb, p.o_sh, p.o_sr = o_st
+        p.t_sb, p.t_sh, p.t_sr = t_st
+        p.half_table = int(half_table)
+        p.x_dtype = N.DTYPE_CODE[dt]
+        p.t_dtype = N.DTYPE_CODE[tdt]
+        n = _prod(xv.shape)
+        nbytes = 2 * n * DTYPE_BYTES[dt] + 2 * _prod(cv.shape) * tb  # x, out, and the two tables once
+        self.emit(N.DP_K_ROPE, [bx.buf, bc.buf, bs.buf, out.buf], p, f"rope {tuple(xv.shape)} kernel",
+                  6 * n, nbytes)
+        return True
 
     def lower_attention_fused(self, op: Op, qv: View, qst, kv: View, kst, vv: View, vst, B, Hq, Hk, g, L, S, D,
                               Dv) -> None:

@@ -52,8 +52,28 @@ int launch_attention(const dp_attention_params &p, const void *q, const void *k,
                      cudaStream_t s);
 int launch_embedding(const dp_embedding_params &p, const void *ids, const void *w,
                      void *out, cudaStream_t s);
+int launch_rope(const dp_rope_params &p, const void *x, const void *cos, const void *sin, void *out,
+                cudaStream_t s);
 
 }  // namespace dp
+
+// Division by a run-time invariant d with one multiply-high, add and shift
+// (Granlund & Montgomery, "Division by invariant integers using
+// multiplication", 1994): q = (umulhi(n, m) + n) >> s with s = ceil(log2 d),
+// m = floor(2^32 (2^s - d) / d) + 1, exact for n < 2^31.
+struct FastDiv {
+  uint32_t d, m, s;
+};
+
+inline FastDiv make_fastdiv(uint32_t d) {
+  uint32_t s = 0;
+  while ((1ull << s) < d) ++s;
+  return FastDiv{d, (uint32_t)((((1ull << 32) * ((1ull << s) - d)) / d) + 1), s};
+}
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
+  return (__umulhi(n, f.m) + n) >> f.s;
+}
 
 // -------------------------------------------------------------- device side
 // Device error word: first failure wins (code, info); read and cleared by

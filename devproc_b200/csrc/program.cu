@@ -81,6 +81,12 @@ int run_records(dp_program *prog, cudaStream_t s) {
         st = dp::launch_attention(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
         break;
       }
+      case DP_K_ROPE: {
+        dp_rope_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_rope(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
+        break;
+      }
       case DP_K_COPY: {
         uint64_t bytes;
         memcpy(&bytes, rec.params, sizeof(bytes));

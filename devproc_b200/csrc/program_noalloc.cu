@@ -139,6 +139,12 @@ extern "C" int dp_program_run_noalloc(const void *plan, size_t plan_bytes, void 
         st = dp::launch_attention(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
         break;
       }
+      case DP_K_ROPE: {
+        dp_rope_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_rope(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
+        break;
+      }
       case DP_K_COPY: {
         uint64_t bytes;
         memcpy(&bytes, rec.params, sizeof(bytes));

@@ -60,15 +60,10 @@ __device__ __forceinline__ float apply_binary(int op, float a, float b) {
 // (leading slots have extent 1), so every coordinate loop is unrolled with
 // static indices.  One work item is a run of E consecutive elements along the
 // innermost dim (E divides its extent); its coordinates come from one mixed-
-// radix decomposition of the item index with magic-number division (Granlund
-// & Montgomery, "Division by invariant integers using multiplication", 1994:
-// q = (umulhi(n, m) + n) >> s with s = ⌈log2 d⌉, m = ⌊2^32 (2^s − d) / d⌋ + 1,
-// exact for n < 2^31), then each operand's offset is one dot product.
+// radix decomposition of the item index with magic-number division
+// (FastDiv, exact for indices below 2^31), then each operand's offset is one
+// dot product.
 constexpr int kR = DP_REGION_MAX_RANK;
-
-struct FastDiv {
-  uint32_t d, m, s;
-};
 
 struct Geom {
   int64_t items;                                // work items (runs of E elements)
@@ -78,10 +73,6 @@ struct Geom {
   FastDiv fd[kR];                               // divisors of ext (32-bit path)
   int chan_slot[DP_REGION_MAX_INSTR];           // right-aligned dim of each CHANSEL
 };
-
-__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
-  return (__umulhi(n, f.m) + n) >> f.s;
-}
 
 // E elements of one operand: a 16-byte-or-narrower vector when the run is
 // unit-stride and aligned, one broadcast load when the stride is 0.
@@ -415,10 +406,7 @@ int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t 
   for (int i = 0; i < n_ops; ++i) g.off[i] = d.offset[i];
   const bool wide = g.items >= (1ll << 31);
   for (int k = 0; k < kR; ++k) {
-    const uint32_t dv = (uint32_t)(wide ? 1 : g.ext[k]);
-    uint32_t sh = 0;
-    while ((1ull << sh) < dv) ++sh;
-    g.fd[k] = FastDiv{dv, (uint32_t)((((1ull << 32) * ((1ull << sh) - dv)) / dv) + 1), sh};
+    g.fd[k] = make_fastdiv((uint32_t)(wide ? 1 : g.ext[k]));
   }
   for (int pc = 0; pc < d.n_instr; ++pc)
     g.chan_slot[pc] = (d.instr[pc] & 0xff) == DP_OP_CHANSEL ? (int)((d.instr[pc] >> 24) & 0xff) + lead : 0;

@@ -221,6 +221,29 @@ typedef struct dp_attention_params {
 int dp_attention(const dp_attention_params *p, const void *q, const void *k, const void *v, void *o,
                  void *stream);
 
+/* ---- rotary embedding ----------------------------------------------------------
+ * Rotate-half rotary position embedding over x viewed as [batch, heads, rows,
+ * dim] (element strides; the last dim contiguous), for i < dim/2:
+ *   out[.., i]         = x[.., i]·cos[.., i]                 − x[.., i + dim/2]·sin[.., i]
+ *   out[.., i + dim/2] = x[.., i + dim/2]·cos[.., i + dim/2] + x[.., i]·sin[.., i + dim/2]
+ * each product and sum rounded in fp32, then rounded once to x's type — the
+ * torch-level ``devproc::rope`` op.  cos and sin share the strides t_s*
+ * (0 broadcasts a dim) and hold dim columns, or dim/2 with half_table (column
+ * i serves both halves).  Replaces the slice / neg / cat / mul / add chain the
+ * reference's FX converter could not lower (src/devproc/ir/fx_converter.py:
+ * 443-448).  x and out: bf16, f16 or f32 (same type); tables bf16, f16 or
+ * f32.  dim/2 a multiple of 16 / sizeof(x); strides multiples of that too;
+ * bases 16-byte aligned.  out must not overlap x. */
+typedef struct dp_rope_params {
+  int64_t batch, heads, rows, dim;
+  int64_t x_sb, x_sh, x_sr;
+  int64_t o_sb, o_sh, o_sr;
+  int64_t t_sb, t_sh, t_sr;
+  int32_t half_table, x_dtype, t_dtype, reserved;
+} dp_rope_params;
+int dp_rope(const dp_rope_params *p, const void *x, const void *cos, const void *sin, void *out,
+            void *stream);
+
 /* ---- compiled program ------------------------------------------------------
  * A plan is a little-endian blob: dp_plan_header, n_slots × dp_plan_slot,
  * n_records × dp_plan_record.  Slots of kind DP_SLOT_BOUND are caller-owned
@@ -237,7 +260,7 @@ int dp_attention(const dp_attention_params *p, const void *q, const void *k, con
 enum { DP_SLOT_BOUND = 0, DP_SLOT_ARENA = 1 };
 enum {
   DP_K_PREPROC = 1, DP_K_ROWREDUCE = 2, DP_K_GEMM = 3, DP_K_REGION = 4,
-  DP_K_EMBEDDING = 5, DP_K_COPY = 6, DP_K_ATTENTION = 7
+  DP_K_EMBEDDING = 5, DP_K_COPY = 6, DP_K_ATTENTION = 7, DP_K_ROPE = 8
 };
 typedef struct dp_plan_header {
   uint32_t magic, version, n_slots, n_records;

@@ -68,7 +68,7 @@ def _run(fn, *xs):
 
 
 @pytest.mark.parametrize("half_tables", [False, True])
-def test_rope_region(cuda, half_tables):
+def test_rope_program(cuda, half_tables):
     g = torch.Generator().manual_seed(1)
     x = torch.randn(2, 3, 20, 64, generator=g).bfloat16()
     from devproc_b200.torch_ops import rope_tables
@@ -77,6 +77,48 @@ def test_rope_region(cuda, half_tables):
         c, s = c[:, :32].contiguous(), s[:, :32].contiguous()
     got, ref = _run(_fn(lambda a, b, d: [OpBuilder.rope(a, b, d)], x, c, s), x, c, s)
     _close(got, ref)
+
+
+@pytest.mark.parametrize("xdt,tdt,half,bcast", [
+    (torch.bfloat16, torch.bfloat16, False, False),
+    (torch.bfloat16, torch.float32, True, False),
+    (torch.float16, torch.float16, False, True),
+    (torch.float32, torch.bfloat16, False, False),
+    (torch.float32, torch.float32, True, True),
+])
+def test_rope_kernel_bit_exact(cuda, xdt, tdt, half, bcast):
+    """``dp_rope`` through the C ABI on a token-major column block of a fused
+    projection (x[b, h, r] at b·R·W + r·W + off + h·D), against the torch-level
+    op on the CPU: the same fp32 products and sums, so the bits agree."""
+    from devproc_b200 import _native as N
+    from devproc_b200.torch_ops import rope, rope_tables
+    B, H, R, D, W, off = 3, 4, 37, 64, 7 * 64, 64
+    g = torch.Generator().manual_seed(5)
+    proj = torch.randn(B, R, W, generator=g).to(xdt)
+    x = proj[:, :, off:off + H * D].view(B, R, H, D).transpose(1, 2)  # [B, H, R, D], strided
+    c, s_ = rope_tables(R, D)
+    if half:
+        c, s_ = c[:, :D // 2].contiguous(), s_[:, :D // 2].contiguous()
+    c, s_ = c.to(tdt), s_.to(tdt)
+    if bcast:  # a per-sample table, broadcast over heads
+        c = torch.stack([c.roll(i, 0) for i in range(B)])[:, None]
+        s_ = torch.stack([s_.roll(i, 0) for i in range(B)])[:, None]
+    ref = rope(x, c, s_)
+    dproj, dc, ds = proj.to(cuda), c.to(cuda).contiguous(), s_.to(cuda).contiguous()
+    out = torch.empty(B, H, R, D, dtype=xdt, device=cuda)
+    es = proj.element_size()
+    p = N.RopeParams()
+    p.batch, p.heads, p.rows, p.dim = B, H, R, D
+    p.x_sb, p.x_sh, p.x_sr = R * W, D, W
+    p.o_sb, p.o_sh, p.o_sr = H * R * D, R * D, D
+    cols = c.shape[-1]
+    p.t_sb, p.t_sh, p.t_sr = (R * cols if bcast else 0), 0, cols
+    p.half_table = int(half)
+    p.x_dtype = N.DTYPE_CODE[str(xdt).replace("torch.", "")]
+    p.t_dtype = N.DTYPE_CODE[str(tdt).replace("torch.", "")]
+    N.rope(p, dproj.data_ptr() + off * es, dc, ds, out)
+    torch.cuda.synchronize()
+    assert torch.equal(out.cpu(), ref)
 
 
 def test_slice_cat_expand_regions(cuda):
