@@ -198,8 +198,8 @@ __global__ void __launch_bounds__(kMaxThreads) preproc_plain_kernel(Geo g, const
 // multiple of 16 (so every staged row is 16-byte aligned), planar output.
 // Each thread produces two adjacent output columns of one output row for all
 // three channels; a block covers R output rows per unit.  Per output element
-// the kernel spends ~24 full-rate instructions:
-//   * the 6 bytes of an (x0, x0+1) pixel pair come from two 8-byte shared
+// the kernel spends ~16 full-rate instructions:
+//   * the 6 bytes of an (x0, x0+1) pixel pair come from three 4-byte shared
 //     loads plus funnel shifts; byte → float is exact via the 2^23 magic
 //     number (byte | 0x4B000000 reinterpreted, minus 2^23) instead of I2F;
 //   * the three interpolation FMAs are the generic path's, unchanged;
@@ -216,6 +216,7 @@ constexpr int kFastStages = 2;
 struct FastGeo {
   int B, H, W, OH, OW;
   int R, tpr, upi;     // rows per unit, threads per row, units per image
+  int split, rps;      // thread groups sharing a unit's rows, rows per group
   int row_bytes;       // W * 3
   int slot_bytes;      // shared bytes per output row: 2 input rows + 16 B slack, 16-B rounded
   float sy, sx;
@@ -224,13 +225,15 @@ struct FastGeo {
 };
 
 
-// Window of one output column: the 8-byte aligned 16-byte span of the row
-// holding pixels x0 and x1, and how to shift it so that pixel x0 starts at
-// byte 0.  ``edge`` marks the clamped right edge (x1 == x0).
+// Window of one output column: the three 4-byte words of the row holding
+// pixels x0 and x1 (from the word containing x0's first byte), and how to
+// shift them so that pixel x0 starts at byte 0.  ``edge`` marks the clamped
+// right edge (x1 == x0).  Three 32-bit shared loads and two funnel shifts per
+// pixel pair: no selects, and the 16 bytes of slack after each staged row
+// cover the last word.
 struct ColWin {
   int ws;
   int sh;
-  bool hi;
   bool edge;
   float l0, l1;
 };
@@ -238,10 +241,8 @@ struct ColWin {
 __device__ __forceinline__ ColWin make_win(const Coef &c) {
   ColWin w;
   const int b0 = 3 * c.i0;
-  w.ws = b0 & ~7;
-  const int o = b0 - w.ws;  // 0..7
-  w.hi = o >= 4;
-  w.sh = 8 * (o & 3);
+  w.ws = b0 & ~3;
+  w.sh = 8 * (b0 & 3);
   w.edge = c.i1 == c.i0;
   w.l0 = c.l0;
   w.l1 = c.l1;
@@ -251,9 +252,8 @@ __device__ __forceinline__ ColWin make_win(const Coef &c) {
 // Bytes of pixels x0 and x0+1 (3 channels each) as a0 = [x0.c0 x0.c1 x0.c2 x1.c0],
 // a1 = [x1.c1 x1.c2 . .].
 __device__ __forceinline__ void fetch_pair(const uint8_t *row, const ColWin &w, uint32_t &a0, uint32_t &a1) {
-  const uint2 lo = *reinterpret_cast<const uint2 *>(row + w.ws);
-  const uint2 hi = *reinterpret_cast<const uint2 *>(row + w.ws + 8);
-  const uint32_t w0 = w.hi ? lo.y : lo.x, w1 = w.hi ? hi.x : lo.y, w2 = w.hi ? hi.y : hi.x;
+  const uint32_t *q = reinterpret_cast<const uint32_t *>(row + w.ws);
+  const uint32_t w0 = q[0], w1 = q[1], w2 = q[2];
   a0 = __funnelshift_r(w0, w1, w.sh);
   a1 = __funnelshift_r(w1, w2, w.sh);
 }
@@ -355,12 +355,16 @@ __device__ __forceinline__ void compute_two_cols(const uint8_t *row0, const uint
 }
 
 constexpr int kMaxFastOH = 2048;
-constexpr int kFastRowsPerThread = 4;  // output rows a thread computes per unit
+constexpr int kFastRowsPerThread = 8;  // output rows a thread computes per unit
 
 // Warp-specialised pipeline: warp 0 lane 0 is the producer (bulk copies into
 // kFastStages stages, each guarded by a "full" and an "empty" mbarrier);
 // warps 1.. are consumers, one column pair per lane, walking the R output
-// rows of each unit.  Consumers never wait for each other: a warp releases a
+// rows of each unit.  When the column pairs of a row fill a whole number of
+// warps only when doubled (224 output columns: 112 pairs, 3.5 warps), two
+// thread groups split each unit's rows (R/2 each), so every consumer lane
+// works (7 full warps instead of 4 with 16 idle lanes).  Consumers never wait
+// for each other: a warp releases a
 // stage with one arrive on its "empty" barrier.  Every wait is bounded; a
 // timeout sets the device error word and a shared abort flag, after which
 // all warps stop and the producer waits (bounded) for the copies it issued.
@@ -374,7 +378,7 @@ __global__ void __launch_bounds__(kMaxThreads + 32) preproc_u8c3_kernel(FastGeo 
   const int stage_bytes = g.R * g.slot_bytes;
   const uint32_t copy_bytes = (uint32_t)(2 * g.row_bytes);
   RowCoef *rows = reinterpret_cast<RowCoef *>(smem_raw + kFastStages * stage_bytes);
-  const int n_consumer_warps = (g.tpr + 31) / 32;
+  const int n_consumer_warps = (g.split * g.tpr + 31) / 32;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFastStages; ++s) {
@@ -430,8 +434,10 @@ __global__ void __launch_bounds__(kMaxThreads + 32) preproc_u8c3_kernel(FastGeo 
   }
 
   // Consumers: one column pair per lane.
-  const int j = threadIdx.x - 32;
-  const bool active = j < g.tpr;
+  const int jj = threadIdx.x - 32;
+  const int part = jj / g.tpr;
+  const int j = jj - part * g.tpr;
+  const bool active = part < g.split;
   const int ox = 2 * j;
   const ColWin c0 = make_win(src_coef(active ? ox : 0, g.W, g.OW, g.sx));
   const ColWin c1 = make_win(src_coef(active ? ox + 1 : 0, g.W, g.OW, g.sx));
@@ -446,10 +452,12 @@ __global__ void __launch_bounds__(kMaxThreads + 32) preproc_u8c3_kernel(FastGeo 
     const int oy0 = cur_u * g.R;
     if (active) {
       const int nrows = min(g.R, g.OH - oy0);
+      const int r_lo = part * g.rps;
+      const int r_hi = min(r_lo + g.rps, nrows);
       const uint8_t *stage = smem_raw + s * stage_bytes;
-      TOut *o = out + ((int64_t)cur_b * 3 * g.OH + oy0) * g.OW + ox;
+      TOut *o = out + ((int64_t)cur_b * 3 * g.OH + oy0 + r_lo) * g.OW + ox;
 #pragma unroll 2
-      for (int rr = 0; rr < nrows; ++rr) {
+      for (int rr = r_lo; rr < r_hi; ++rr) {
         const RowCoef rc = rows[oy0 + rr];
         const uint8_t *base = stage + rr * g.slot_bytes;
         const uint8_t *row0 = base + (rc.r01 & 0xff) * g.row_bytes;
@@ -495,7 +503,9 @@ int launch_fast(const dp_preproc_params &p, const void *in, void *out, cudaStrea
     g.stdv[c] = p.normalize ? p.stdv[c] : 1.0f;
     g.rcp[c] = 1.0f / g.stdv[c];
   }
-  const int threads = 32 + ((g.tpr + 31) / 32) * 32;
+  g.split = (g.tpr % 32 != 0 && (2 * g.tpr) % 32 == 0 && g.R % 2 == 0 && 2 * g.tpr <= kMaxThreads) ? 2 : 1;
+  g.rps = g.R / g.split;
+  const int threads = 32 + ((g.split * g.tpr + 31) / 32) * 32;
   const size_t smem = (size_t)kFastStages * g.R * g.slot_bytes + (size_t)g.OH * sizeof(RowCoef);
   const int n_units = g.B * g.upi;
   auto kern = preproc_u8c3_kernel<TOut>;
