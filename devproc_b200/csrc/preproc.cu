@@ -21,7 +21,7 @@
 //   row = fma(x[i0], l0, x[i1] * l1); out = fma(row0, h0, row1 * h1).
 #include "dp_common.cuh"
 
-namespace {
+namespace dpk_preproc {
 
 constexpr int kStages = 4;
 constexpr int kMaxThreads = 256;
@@ -582,7 +582,9 @@ int launch_out(const Geo &g, int out_dtype, bool in_nchw, bool out_nchw, const v
   }
 }
 
-}  // namespace
+}  // namespace dpk_preproc
+
+using namespace dpk_preproc;
 
 namespace dp {
 

@@ -17,7 +17,7 @@
 // its coordinates come from three FastDiv divisions (items < 2^31).
 #include "dp_common.cuh"
 
-namespace {
+namespace dpk_rope {
 
 constexpr int kThreads = 256;
 
@@ -126,7 +126,7 @@ int launch_tables(const RopeGeo &g, int t_dtype, const void *x, const void *c, c
   }
 }
 
-}  // namespace
+}  // namespace dpk_rope
 
 namespace dp {
 
@@ -156,7 +156,7 @@ int launch_rope(const dp_rope_params &p, const void *x, const void *cosv, const 
   const int64_t jn = p.dim / 2 / vec;
   const int64_t items = p.batch * p.heads * p.rows * jn;
   DP_REQUIRE(items < (1ll << 31), DP_ERR_UNSUPPORTED, "rope: more than 2^31 work items");
-  RopeGeo g;
+  dpk_rope::RopeGeo g;
   g.x_sb = p.x_sb; g.x_sh = p.x_sh; g.x_sr = p.x_sr;
   g.o_sb = p.o_sb; g.o_sh = p.o_sh; g.o_sr = p.o_sr;
   g.t_sb = p.t_sb; g.t_sh = p.t_sh; g.t_sr = p.t_sr;
@@ -167,9 +167,9 @@ int launch_rope(const dp_rope_params &p, const void *x, const void *cosv, const 
   g.rows = make_fastdiv((uint32_t)p.rows);
   g.heads = make_fastdiv((uint32_t)p.heads);
   switch (p.x_dtype) {
-    case DP_BF16: return launch_tables<__nv_bfloat16>(g, p.t_dtype, x, cosv, sinv, out, s);
-    case DP_F16: return launch_tables<__half>(g, p.t_dtype, x, cosv, sinv, out, s);
-    default: return launch_tables<float>(g, p.t_dtype, x, cosv, sinv, out, s);
+    case DP_BF16: return dpk_rope::launch_tables<__nv_bfloat16>(g, p.t_dtype, x, cosv, sinv, out, s);
+    case DP_F16: return dpk_rope::launch_tables<__half>(g, p.t_dtype, x, cosv, sinv, out, s);
+    default: return dpk_rope::launch_tables<float>(g, p.t_dtype, x, cosv, sinv, out, s);
   }
 }
 
