@@ -148,20 +148,72 @@ __global__ void __launch_bounds__(256) reduce_warp_kernel(dp_rowreduce_params p,
     float acc = (KIND == DP_RED_MAX) ? -INFINITY : (KIND == DP_RED_MIN ? INFINITY : 0.0f);
     ArgVal best{-INFINITY, (long long)p.cols};
     int64_t c = (int64_t)lane * VEC;
-    for (; c + (kUnroll - 1) * step < p.cols; c += kUnroll * step) {
-      float v[kUnroll][VEC];
+    if constexpr (KIND == DP_RED_ARGMAX) {
+      // One running (value, index) per vector slot: VEC independent compare
+      // chains instead of one.  A lane visits its columns in increasing order,
+      // so a later column only wins with a larger value, or as the first NaN;
+      // ties keep the earlier index.  The slots and lanes are then combined
+      // with the full (value, index) order, so the first maximal index wins.
+      float bv[VEC];
+      long long bi[VEC];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) load_vec<TIn, VEC>(x + c + u * step, v[u]);
+      for (int j = 0; j < VEC; ++j) {
+        bv[j] = -INFINITY;
+        bi[j] = (long long)p.cols;
+      }
+      auto upd = [&](int j, float v, long long idx) {
+        if (v > bv[j] || (isnan(v) && !isnan(bv[j]))) {
+          bv[j] = v;
+          bi[j] = idx;
+        }
+      };
+      if (c < p.cols) {  // each slot starts at the lane's first column of it (an all -inf row keeps index 0)
+        float v0[VEC];
+        load_vec<TIn, VEC>(x + c, v0);
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
+        for (int j = 0; j < VEC; ++j) {
+          bv[j] = v0[j];
+          bi[j] = c + j;
+        }
+        c += step;
+      }
+      for (; c + (kUnroll - 1) * step < p.cols; c += kUnroll * step) {
+        float v[kUnroll][VEC];
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) acc_step<KIND>(acc, best, v[u][j], c + u * step + j);
-    }
-    for (; c < p.cols; c += step) {
-      float v[VEC];
-      load_vec<TIn, VEC>(x + c, v);
+        for (int u = 0; u < kUnroll; ++u) load_vec<TIn, VEC>(x + c + u * step, v[u]);
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) acc_step<KIND>(acc, best, v[j], c + j);
+        for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) upd(j, v[u][j], c + u * step + j);
+      }
+      for (; c < p.cols; c += step) {
+        float v[VEC];
+        load_vec<TIn, VEC>(x + c, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) upd(j, v[j], c + j);
+      }
+#pragma unroll
+      for (int j = 0; j < VEC; ++j)
+        if (bi[j] < p.cols && arg_better(bv[j], bi[j], best.v, best.i)) {
+          best.v = bv[j];
+          best.i = bi[j];
+        }
+    } else {
+      for (; c + (kUnroll - 1) * step < p.cols; c += kUnroll * step) {
+        float v[kUnroll][VEC];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) load_vec<TIn, VEC>(x + c + u * step, v[u]);
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u)
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) acc_step<KIND>(acc, best, v[u][j], c + u * step + j);
+      }
+      for (; c < p.cols; c += step) {
+        float v[VEC];
+        load_vec<TIn, VEC>(x + c, v);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc_step<KIND>(acc, best, v[j], c + j);
+      }
     }
     if constexpr (KIND == DP_RED_ARGMAX) {
 #pragma unroll
@@ -385,6 +437,13 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, c
         for (int j = 0; j < VEC; ++j) v[i][j] = c + j < p.cols ? to_f32(x[c + j]) : 0.0f;
       }
     }
+    // RMSNorm / LayerNorm statistics use VEC independent partial accumulators
+    // per lane (one per vector slot): dependency chains of NV steps instead of
+    // NV·VEC.  A lane whose columns all lie inside the row skips the
+    // per-element checks.  (Softmax keeps one running max and sum: split
+    // accumulators measured no faster there.)
+    const bool full = lane * VEC + (NV - 1) * step + VEC <= p.cols;
+    auto live = [&](int i, int j) { return full || lane * VEC + i * step + j < p.cols; };
     float scale = 1.0f, shift = 0.0f;
     if constexpr (KIND == DP_RED_SOFTMAX) {
       float m = -INFINITY;
@@ -392,43 +451,55 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, c
       for (int i = 0; i < NV; ++i)
 #pragma unroll
         for (int j = 0; j < VEC; ++j)
-          if (lane * VEC + i * step + j < p.cols) m = nan_max(m, v[i][j]);
+          if (live(i, j)) m = nan_max(m, v[i][j]);
       m = warp_max(m);
       float sum = 0.0f;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-          const bool live = lane * VEC + i * step + j < p.cols;
-          v[i][j] = live ? __expf(v[i][j] - m) : 0.0f;
+          v[i][j] = live(i, j) ? __expf(v[i][j] - m) : 0.0f;
           sum += v[i][j];
         }
       }
       scale = 1.0f / warp_sum(sum);
     } else if constexpr (KIND == DP_RED_RMSNORM) {
-      float ss = 0.0f;
+      float sp[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) sp[j] = 0.0f;
 #pragma unroll
       for (int i = 0; i < NV; ++i)
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) ss = fmaf(v[i][j], v[i][j], ss);
+        for (int j = 0; j < VEC; ++j) sp[j] = fmaf(v[i][j], v[i][j], sp[j]);
+      float ss = sp[0];
+#pragma unroll
+      for (int j = 1; j < VEC; ++j) ss += sp[j];
       scale = rsqrtf(warp_sum(ss) / n + p.eps);
     } else {
-      float sum = 0.0f;
+      float sp[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) sp[j] = 0.0f;
 #pragma unroll
       for (int i = 0; i < NV; ++i)
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) sum += v[i][j];
+        for (int j = 0; j < VEC; ++j) sp[j] += v[i][j];
+      float sum = sp[0];
+#pragma unroll
+      for (int j = 1; j < VEC; ++j) sum += sp[j];
       const float mean = warp_sum(sum) / n;
-      float q = 0.0f;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) sp[j] = 0.0f;
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-          const bool live = lane * VEC + i * step + j < p.cols;
-          const float d = live ? v[i][j] - mean : 0.0f;
-          q = fmaf(d, d, q);
+          const float d = live(i, j) ? v[i][j] - mean : 0.0f;
+          sp[j] = fmaf(d, d, sp[j]);
         }
       }
+      float q = sp[0];
+#pragma unroll
+      for (int j = 1; j < VEC; ++j) q += sp[j];
       scale = rsqrtf(warp_sum(q) / n + p.eps);
       shift = mean;
     }

@@ -149,6 +149,18 @@ def test_argmax_ties_and_nan_first_index(cuda):
     assert torch.isnan(mx[1]) and mx[0] == 3.0
 
 
+def test_argmax_infinities_and_ties_across_slots(cuda):
+    """All -inf rows give index 0; equal maxima in different vector slots and
+    lanes give the first index; +inf beats finite values."""
+    x = torch.full((4, 4096), float("-inf"))
+    x[1, 7], x[1, 2], x[1, 4000] = 5.0, 5.0, 5.0
+    x[2] = torch.randn(4096)
+    x[2, 129], x[2, 3] = float("inf"), float("inf")
+    x[3] = 1.0
+    out = _rr(N.DP_RED_ARGMAX, x.to(cuda), torch.int64)
+    assert out.tolist() == torch.argmax(x, -1).tolist() == [0, 2, 3, 0]
+
+
 def test_argmax_golden_vectors(cuda, golden):
     for case in ("argmax_small", "argmax_wide", "argmax_ties"):
         x = torch.from_numpy(golden[f"{case}/x"])
