@@ -714,6 +714,136 @@ int launch_norm16(const dp_rowreduce_params &p, const void *in, const void *w, c
   }
 }
 
+// ---------------------------------------------------------------------------
+// fp32 softmax / rmsnorm / layernorm, one warp per row, rows staged in shared
+// memory by the TMA engine (cp.async.bulk, one 1-D copy per row) into two
+// buffers per warp: while a warp computes row k from one buffer, row k + 1
+// is already landing in the other, so the memory pipe never waits for the
+// statistics.  The register-resident kernel above keeps 128 floats per lane
+// for a 4096-wide row (about 250 registers, 8 warps per SM) and loads the next
+// row only after this one is written.  Each lane reads float4 i at column
+// 4·lane + 128·i (conflict-free), once for the statistics and once for the
+// output.  Every wait is bounded; a warp that gives up records the timeout,
+// stops, and waits (bounded) for the copy it still has in flight.
+constexpr int kStagedWarps = 7;
+
+template <int KIND>
+__global__ void __launch_bounds__(32 * kStagedWarps) norm_staged_kernel(dp_rowreduce_params p,
+                                                                        const float *__restrict__ in,
+                                                                        const float *__restrict__ w,
+                                                                        const float *__restrict__ bias,
+                                                                        float *__restrict__ out, int row_floats) {
+  extern __shared__ __align__(16) float srow[];
+  __shared__ __align__(8) uint64_t bars[kStagedWarps][2];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float *buf0 = srow + (size_t)wid * 2 * row_floats;
+  const int64_t nw = (int64_t)gridDim.x * kStagedWarps;
+  const int64_t first = (int64_t)blockIdx.x * kStagedWarps + wid;
+  const uint32_t bytes = (uint32_t)(p.cols * 4);
+  const int nvec = (int)(p.cols / 4);
+  const float n = (float)p.cols;
+  if (lane == 0) {
+    mbar_init(&bars[wid][0], 1);
+    mbar_init(&bars[wid][1], 1);
+    fence_barrier_init();
+  }
+  __syncwarp();
+  auto issue = [&](int64_t row, int b) {
+    mbar_arrive_expect_tx(&bars[wid][b], bytes);
+    bulk_g2s(buf0 + b * row_floats, in + row * p.in_row_stride, bytes, &bars[wid][b]);
+  };
+  if (lane == 0 && first < p.rows) issue(first, 0);
+  int k = 0;
+  bool pending = first < p.rows;  // a copy of this warp is in flight
+  for (int64_t row = first; row < p.rows; row += nw, ++k) {
+    const int b = k & 1;
+    const int64_t next = row + nw;
+    bool ok = true;
+    if (lane == 0) ok = mbar_wait_bounded(&bars[wid][b], (uint32_t)(k >> 1) & 1u, 700);
+    ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+    if (!ok) break;  // the copy into buffer b is what timed out; nothing else is in flight
+    pending = false;
+    if (next < p.rows) {
+      // buffer b ^ 1 was last read in the previous iteration (all lanes passed __syncwarp)
+      if (lane == 0) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        issue(next, b ^ 1);
+      }
+      pending = true;
+    }
+    const float4 *xs = reinterpret_cast<const float4 *>(buf0 + b * row_floats);
+    float scale = 1.0f, shift = 0.0f;
+    if constexpr (KIND == DP_RED_SOFTMAX) {
+      float m0 = -INFINITY, m1 = -INFINITY;
+      for (int i = lane; i < nvec; i += 32) {
+        const float4 v = xs[i];
+        m0 = nan_max(m0, nan_max(v.x, v.y));
+        m1 = nan_max(m1, nan_max(v.z, v.w));
+      }
+      const float m = warp_max(nan_max(m0, m1));
+      float s0 = 0.0f, s1 = 0.0f;
+      for (int i = lane; i < nvec; i += 32) {
+        const float4 v = xs[i];
+        s0 += __expf(v.x - m) + __expf(v.y - m);
+        s1 += __expf(v.z - m) + __expf(v.w - m);
+      }
+      scale = 1.0f / warp_sum(s0 + s1);
+      shift = m;
+    } else if constexpr (KIND == DP_RED_RMSNORM) {
+      float s0 = 0.0f, s1 = 0.0f;
+      for (int i = lane; i < nvec; i += 32) {
+        const float4 v = xs[i];
+        s0 = fmaf(v.x, v.x, fmaf(v.y, v.y, s0));
+        s1 = fmaf(v.z, v.z, fmaf(v.w, v.w, s1));
+      }
+      scale = rsqrtf(warp_sum(s0 + s1) / n + p.eps);
+    } else {
+      float s0 = 0.0f, s1 = 0.0f;
+      for (int i = lane; i < nvec; i += 32) {
+        const float4 v = xs[i];
+        s0 += v.x + v.y;
+        s1 += v.z + v.w;
+      }
+      const float mean = warp_sum(s0 + s1) / n;
+      float q0 = 0.0f, q1 = 0.0f;
+      for (int i = lane; i < nvec; i += 32) {
+        const float4 v = xs[i];
+        q0 = fmaf(v.x - mean, v.x - mean, fmaf(v.y - mean, v.y - mean, q0));
+        q1 = fmaf(v.z - mean, v.z - mean, fmaf(v.w - mean, v.w - mean, q1));
+      }
+      scale = rsqrtf(warp_sum(q0 + q1) / n + p.eps);
+      shift = mean;
+    }
+    float4 *y = reinterpret_cast<float4 *>(out + row * p.out_row_stride);
+    const float4 *wv = reinterpret_cast<const float4 *>(w);
+    const float4 *bv = reinterpret_cast<const float4 *>(bias);
+    for (int i = lane; i < nvec; i += 32) {
+      const float4 v = xs[i];
+      float4 o;
+      if constexpr (KIND == DP_RED_SOFTMAX) {
+        o = make_float4(__expf(v.x - shift) * scale, __expf(v.y - shift) * scale, __expf(v.z - shift) * scale,
+                        __expf(v.w - shift) * scale);
+      } else {
+        o = make_float4((v.x - shift) * scale, (v.y - shift) * scale, (v.z - shift) * scale, (v.w - shift) * scale);
+        if (p.has_weight) {
+          const float4 g = __ldg(wv + i);
+          o = make_float4(o.x * (g.x + p.weight_offset), o.y * (g.y + p.weight_offset), o.z * (g.z + p.weight_offset),
+                          o.w * (g.w + p.weight_offset));
+        }
+        if (KIND == DP_RED_LAYERNORM && p.has_bias) {
+          const float4 c = __ldg(bv + i);
+          o = make_float4(o.x + c.x, o.y + c.y, o.z + c.z, o.w + c.w);
+        }
+      }
+      y[i] = o;
+    }
+    __syncwarp();
+  }
+  // Leave no copy in flight into shared memory that is about to go away.
+  if (lane == 0 && pending) mbar_wait_bounded(&bars[wid][k & 1], (uint32_t)(k >> 1) & 1u, 701);
+  __syncwarp();
+}
+
 template <typename TIn, typename TOut, int VEC, int NV>
 int launch_norm_warp(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
                      cudaStream_t s) {
@@ -790,6 +920,35 @@ int launch_norm(const dp_rowreduce_params &p, const void *in, const void *w, con
   return DP_OK;
 }
 
+int launch_norm_staged(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
+                       cudaStream_t s) {
+  const int row_floats = (int)((p.cols + 3) / 4 * 4);
+  const size_t smem = (size_t)kStagedWarps * 2 * row_floats * 4;
+  // shared-memory opt-in already granted, per kernel (softmax, rmsnorm, layernorm) and device
+  static size_t attr[3][64] = {};
+  auto launch = [&](auto kern, int which) -> int {
+    int dev = 0;
+    DP_CHECK_CUDA(cudaGetDevice(&dev));
+    DP_REQUIRE(dev >= 0 && dev < 64, DP_ERR_UNSUPPORTED, "rowreduce: device ordinal out of range");
+    if (smem > attr[which][dev]) {
+      DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      attr[which][dev] = smem;
+    }
+    int64_t blocks = (p.rows + kStagedWarps - 1) / kStagedWarps;
+    if (blocks > dp::num_sms()) blocks = dp::num_sms();
+    kern<<<(int)blocks, 32 * kStagedWarps, smem, s>>>(p, static_cast<const float *>(in),
+                                                      static_cast<const float *>(w), static_cast<const float *>(b),
+                                                      static_cast<float *>(out), row_floats);
+    DP_CHECK_CUDA(cudaGetLastError());
+    return DP_OK;
+  };
+  switch (p.kind) {
+    case DP_RED_SOFTMAX: return launch(norm_staged_kernel<DP_RED_SOFTMAX>, 0);
+    case DP_RED_RMSNORM: return launch(norm_staged_kernel<DP_RED_RMSNORM>, 1);
+    default: return launch(norm_staged_kernel<DP_RED_LAYERNORM>, 2);
+  }
+}
+
 template <typename TIn, typename TOut>
 int launch_norm_vec(const dp_rowreduce_params &p, const void *in, const void *w, const void *b, void *out,
                     cudaStream_t s) {
@@ -807,6 +966,13 @@ int launch_norm_vec(const dp_rowreduce_params &p, const void *in, const void *w,
       const int r = launch_norm16<TIn>(p, in, w, b, out, s);
       if (r != -1) return r;
     }
+  }
+  if constexpr (std::is_same<TIn, float>::value && std::is_same<TOut, float>::value) {
+    // Staged rows: whole float4 vectors, 16-byte aligned rows, two rows of a
+    // warp within the shared-memory budget.
+    if (ok && p.cols % 4 == 0 && p.cols >= 1024 && p.cols * 4 * 2 * kStagedWarps <= 224 * 1024 &&
+        p.in_row_stride % 4 == 0 && p.out_row_stride % 4 == 0 && p.rows >= 4 * dp::num_sms())
+      return launch_norm_staged(p, in, w, b, out, s);
   }
   if (aligned) {
     const int64_t per_lane = (p.cols + 32 * V - 1) / (32 * V);  // vectors per lane for a warp-per-row pass

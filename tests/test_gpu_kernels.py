@@ -168,7 +168,8 @@ def test_argmax_golden_vectors(cuda, golden):
         assert torch.equal(out, torch.from_numpy(golden[f"{case}/y"])), case
 
 
-@pytest.mark.parametrize("rows,cols", [(1024, 4096), (37, 1000), (64, 512), (16, 20000), (3, 7), (300, 866), (64, 1003), (9, 3)])
+@pytest.mark.parametrize("rows,cols", [(1024, 4096), (37, 1000), (64, 512), (16, 20000), (3, 7), (300, 866), (64, 1003), (9, 3),
+                                       (600, 1024), (1200, 2052), (700, 4092)])
 def test_softmax_and_norms_fp32(cuda, rows, cols):
     g = torch.Generator().manual_seed(7 * rows + cols)
     x = torch.randn(rows, cols, generator=g) * 3
@@ -182,6 +183,31 @@ def test_softmax_and_norms_fp32(cuda, rows, cols):
     assert torch.allclose(rn, ref, rtol=1e-4, atol=1e-5)
     ln = _rr(N.DP_RED_LAYERNORM, xd, torch.float32, w=w.to(cuda), b=b.to(cuda), eps=1e-5)
     assert torch.allclose(ln, torch.nn.functional.layer_norm(x, (cols,), w, b, 1e-5), rtol=1e-4, atol=1e-5)
+
+
+def test_staged_rows_with_padded_strides(cuda):
+    """fp32 rows staged through shared memory (enough rows for every SM),
+    with input and output row strides larger than the row: each kind against
+    torch, and the output padding left untouched."""
+    g = torch.Generator().manual_seed(11)
+    rows, cols, si, so = 900, 2048, 2056, 2064
+    x = torch.randn(rows, si, generator=g) * 3
+    w, b = torch.randn(cols, generator=g), torch.randn(cols, generator=g)
+    xs = x[:, :cols]
+    refs = {N.DP_RED_SOFTMAX: torch.softmax(xs, -1),
+            N.DP_RED_RMSNORM: xs * torch.rsqrt(xs.pow(2).mean(-1, keepdim=True) + 1e-6) * w,
+            N.DP_RED_LAYERNORM: torch.nn.functional.layer_norm(xs, (cols,), w, b, 1e-5)}
+    for kind, ref in refs.items():
+        out = torch.full((rows, so), float("nan"), device=cuda)
+        has_w = int(kind != N.DP_RED_SOFTMAX)
+        has_b = int(kind == N.DP_RED_LAYERNORM)
+        eps = 1e-6 if kind == N.DP_RED_RMSNORM else 1e-5
+        p = N.RowReduceParams(kind, N.DP_F32, N.DP_F32, has_w, has_b, 0, rows, cols, si, so, eps, 0.0)
+        N.rowreduce(p, x.to(cuda), out, weight=w.to(cuda) if has_w else None, bias=b.to(cuda) if has_b else None)
+        _sync()
+        got = out.cpu()
+        assert torch.allclose(got[:, :cols], ref, rtol=1e-4, atol=1e-5), kind
+        assert torch.isnan(got[:, cols:]).all(), kind
 
 
 @pytest.mark.parametrize("cols", [866, 50, 3, 1003])
