@@ -47,6 +47,7 @@ def parse():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--rows", type=int, default=65536, help="rows of the reduce workload (4096 fp32 columns)")
     ap.add_argument("--cpu-sample", type=int, default=64, help="images in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--workload", choices=["preprocess", "gemm", "reduce", "token", "vit", "vla"],
@@ -121,10 +122,10 @@ def micro_gemm(args, dev):
 
 
 def micro_reduce(args, dev):
-    """Row reductions over fp32 [65536, 4096]."""
+    """Row reductions over fp32 [rows, 4096] (65536 rows by default)."""
     from devproc_b200 import _native as N
     peak, kind = peaks()
-    rows, cols = 65536, 4096
+    rows, cols = args.rows, 4096
     g = torch.Generator(device=dev).manual_seed(0)
     x = torch.randn(rows, cols, device=dev, generator=g)
     ones = torch.ones(cols, device=dev)
@@ -147,11 +148,11 @@ def micro_reduce(args, dev):
         gbs = nbytes / (ms / 1e3) / 1e9
         res[name] = {"ms": ms, "gbs": gbs, "frac": gbs / peak}
     worst = min(v["frac"] for v in res.values())
-    return {"metric": "row reduction HBM GB/s, fp32 [65536, 4096]", "value": res["sum"]["gbs"], "unit": "GB/s",
+    return {"metric": f"row reduction HBM GB/s, fp32 [{rows}, {cols}]", "value": res["sum"]["gbs"], "unit": "GB/s",
             "higher_is_better": True, "dtype": "f32", "kinds": res,
             "roofline": {"bound": "hbm", "achieved": res["softmax"]["gbs"], "peak": peak, "unit": "GB/s",
                          "frac": res["softmax"]["gbs"] / peak, "peak_kind": kind, "worst_frac": worst},
-            "config": {"workload": "rowreduce fp32 65536x4096 (inputs 1 GiB > L2)"}}
+            "config": {"workload": f"rowreduce fp32 {rows}x{cols} (inputs {rows * cols * 4 / 2**30:.2f} GiB > L2)"}}
 
 
 def micro_vit(args, dev):
