@@ -5,9 +5,11 @@
 // One persistent CTA per SM works through items of 128 query rows of one
 // (batch, key/value head); the query heads that share a key/value head are
 // stacked rows (grouped-query attention), so every item reads one K / V
-// stream.  Per item the key/value blocks of 64 keys stream through a TMA
-// ring, and four roles run concurrently:
-//   warp 0   TMA producer: the Q tile once per item, then K and V blocks;
+// stream.  Per item the key/value blocks of 64 keys stream through two TMA
+// rings (K and V, so a K slot frees as soon as its Q·Kᵀ is done), and five
+// roles run concurrently:
+//   warp 0   TMA producer: the Q tile once per item, then K blocks;
+//   warp 3   TMA producer of the V blocks;
 //   warp 1   MMA issuer (one thread): S_j = Q·K_jᵀ into one of two TMEM
 //            score buffers, issued one block ahead, then O += P_j·V_j into
 //            the TMEM output accumulator; Q is released right after the
@@ -149,22 +151,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_v, const Shape s, __nv_bfloat16 *__restrict__ out) {
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t q_full, q_empty, kv_full[kMaxStages], kv_empty[kMaxStages], s_full[2],
-      s_free[2], p_full[2], p_free[2], o_full, o_free;
+  __shared__ __align__(8) uint64_t q_full, q_empty, k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages],
+      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2], p_free[2], o_full, o_free;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sq = smem;
   uint8_t *sp = sq + s.q_bytes;
-  uint8_t *skv = sp + 2 * kPBytes;  // two P tiles: softmax writes P_{j+1} while P_j is still being read
+  uint8_t *sk_ring = sp + 2 * kPBytes;  // two P tiles: softmax writes P_{j+1} while P_j is still being read
+  uint8_t *sv_ring = sk_ring + (size_t)s.stages * s.nd * kKVBox;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
     mbar_init(&q_empty, 1);
     for (int i = 0; i < kMaxStages; ++i) {
-      mbar_init(&kv_full[i], 1);
-      mbar_init(&kv_empty[i], 1);
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
@@ -211,15 +216,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int j = 0; j < nb; ++j, ++it) {
           const int st = it % s.stages;
-          if (!wait_or_abort(&kv_empty[st], ((it / s.stages) & 1) ^ 1, 510 + st, flag)) {
+          if (!wait_or_abort(&k_empty[st], ((it / s.stages) & 1) ^ 1, 510 + st, flag)) {
             ok = false;
             break;
           }
-          uint8_t *sk = skv + st * s.stage_bytes;
-          uint8_t *sv = sk + s.nd * kKVBox;
-          mbar_arrive_expect_tx(&kv_full[st], s.stage_bytes);
-          for (int x = 0; x < s.nd; ++x) tma_load(sk + x * kKVBox, &map_k, x * 64, j * BKV, hk, b, &kv_full[st]);
-          for (int x = 0; x < s.ndv; ++x) tma_load(sv + x * kKVBox, &map_v, x * 64, j * BKV, hk, b, &kv_full[st]);
+          uint8_t *sk = sk_ring + (size_t)st * s.nd * kKVBox;
+          mbar_arrive_expect_tx(&k_full[st], (uint32_t)s.nd * kKVBox);
+          for (int x = 0; x < s.nd; ++x) tma_load(sk + x * kKVBox, &map_k, x * 64, j * BKV, hk, b, &k_full[st]);
+        }
+        if (!ok) break;
+      }
+    }
+  } else if (warp == 3) {
+    if (lane == 0) {
+      // ---------------- TMA producer of V: its own ring, so a K slot frees as
+      // soon as its Q·Kᵀ is done instead of waiting for the block's P·V
+      int it = 0;
+      for (int item = blockIdx.x; item < s.items && !aborted(flag); item += gridDim.x) {
+        int b, hk, rt;
+        item_coords(s, item, b, hk, rt);
+        bool ok = true;
+        for (int j = 0; j < nb; ++j, ++it) {
+          const int st = it % s.stages;
+          if (!wait_or_abort(&v_empty[st], ((it / s.stages) & 1) ^ 1, 515 + st, flag)) {
+            ok = false;
+            break;
+          }
+          uint8_t *sv = sv_ring + (size_t)st * s.ndv * kKVBox;
+          mbar_arrive_expect_tx(&v_full[st], (uint32_t)s.ndv * kKVBox);
+          for (int x = 0; x < s.ndv; ++x) tma_load(sv + x * kKVBox, &map_v, x * 64, j * BKV, hk, b, &v_full[st]);
         }
         if (!ok) break;
       }
@@ -236,16 +261,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t aq = su32(sq);
         auto issue_s = [&](int j) -> bool {  // S_j into score buffer (jg + j) % 2
           const int itj = it + j, jgj = jg + j, st = itj % s.stages, sb = jgj & 1;
-          if (!wait_or_abort(&kv_full[st], (itj / s.stages) & 1, 530 + st, flag)) return false;
+          if (!wait_or_abort(&k_full[st], (itj / s.stages) & 1, 530 + st, flag)) return false;
           if (!wait_or_abort(&s_free[sb], ((jgj >> 1) & 1) ^ 1, 540 + sb, flag)) return false;
           fence_after();
-          const uint32_t ak = su32(skv + st * s.stage_bytes);
+          const uint32_t ak = su32(sk_ring + (size_t)st * s.nd * kKVBox);
           for (int k = 0; k < s.ks; ++k) {
             const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;  // 64-wide box, 16-wide step
             mma(tmem + sb * kSCols, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
                 k > 0 ? 1u : 0u);
           }
           commit(&s_full[sb]);
+          commit(&k_empty[st]);               // K_j is read once S_j is complete
           if (j == nb - 1) commit(&q_empty);  // the item's last read of Q: the next Q may load now
           return true;
         };
@@ -265,11 +291,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if (!wait_or_abort(&v_full[st], (itj / s.stages) & 1, 535 + st, flag)) {
+            ok = false;
+            break;
+          }
           fence_after();
-          const uint32_t ap = su32(sp + pb * kPBytes), av = su32(skv + st * s.stage_bytes + s.nd * kKVBox);
+          const uint32_t ap = su32(sp + pb * kPBytes), av = su32(sv_ring + (size_t)st * s.ndv * kKVBox);
           for (int k = 0; k < BKV / 16; ++k)
             mma(t_o, desc_k(ap + k * 32), desc_mn(av + k * 2048), id_pv, (j > 0 || k > 0) ? 1u : 0u);
-          commit(&kv_empty[st]);  // K_j and V_j are read
+          commit(&v_empty[st]);   // V_j is read
           commit(&p_free[pb]);    // P_j is read and O holds blocks ≤ j
         }
         it += nb;
