@@ -35,14 +35,20 @@
 namespace dpk_attn {
 
 constexpr int BM = 128;        // query rows per item
-constexpr int BKV = 64;        // keys per block
 constexpr int kThreads = 256;
 constexpr int kMaxStages = 4;
 constexpr int kTmemCols = 512;
-constexpr int kSCols = BKV;    // one score buffer: 64 fp32 columns
 constexpr uint32_t kQBox = BM * 128;    // 16 KB: 128 rows × 64 bf16
-constexpr uint32_t kKVBox = BKV * 128;  // 8 KB: 64 rows × 64 bf16
-constexpr uint32_t kPBytes = BM * 128;  // 16 KB: 128 rows × 64 bf16 keys
+constexpr uint32_t kPBox = BM * 128;    // 16 KB: 128 rows × 64 bf16 keys of P
+// Keys per block: 64, or 128 for head dims ≤ 128 (half the per-block
+// hand-offs; two 128-column score buffers and a ≤ 128-column output still fit
+// the 512 TMEM columns, and two stages still fit shared memory).
+template <int BKV>
+struct Blk {
+  static constexpr int kSCols = BKV;                    // one score buffer: BKV fp32 columns
+  static constexpr uint32_t kKVBox = BKV * 128;         // one 64-column box of K or V: BKV rows × 128 B
+  static constexpr uint32_t kPBytes = (BKV / 64) * kPBox;  // one P tile: BKV / 64 swizzle atoms along the keys
+};
 
 struct Shape {
   int R;        // query rows per (batch, kv head): group · L
@@ -72,8 +78,9 @@ __device__ __forceinline__ uint64_t desc_k(uint32_t addr) {  // K-major, 128-byt
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-__device__ __forceinline__ uint64_t desc_mn(uint32_t addr) {  // MN-major, 64-element N chunks 8 KB apart
-  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(8192 >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
+// MN-major, 64-element N chunks (V boxes) ``chunk`` bytes apart
+__device__ __forceinline__ uint64_t desc_mn(uint32_t addr, uint32_t chunk) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)(chunk >> 4) << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 __host__ __device__ constexpr uint32_t idesc(int m, int n, int b_mn) {  // bf16 × bf16 → fp32
@@ -147,9 +154,13 @@ __device__ __forceinline__ void item_coords(const Shape &s, int item, int &b, in
   b = bh / s.heads_kv;
 }
 
+template <int BKV>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_v, const Shape s, __nv_bfloat16 *__restrict__ out) {
+  constexpr int kSCols = Blk<BKV>::kSCols;
+  constexpr uint32_t kKVBox = Blk<BKV>::kKVBox;
+  constexpr uint32_t kPBytes = Blk<BKV>::kPBytes;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, q_empty, k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages],
       v_empty[kMaxStages], s_full[2], s_free[2], p_full[2], p_free[2], o_full, o_free;
@@ -297,8 +308,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_after();
           const uint32_t ap = su32(sp + pb * kPBytes), av = su32(sv_ring + (size_t)st * s.ndv * kKVBox);
-          for (int k = 0; k < BKV / 16; ++k)
-            mma(t_o, desc_k(ap + k * 32), desc_mn(av + k * 2048), id_pv, (j > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BKV / 16; ++k)  // 16 keys per step: P atom k / 4, V rows k·16
+            mma(t_o, desc_k(ap + (uint32_t)(k >> 2) * kPBox + (uint32_t)(k & 3) * 32), desc_mn(av + k * 2048, kKVBox),
+                id_pv, (j > 0 || k > 0) ? 1u : 0u);
           commit(&v_empty[st]);   // V_j is read
           commit(&p_free[pb]);    // P_j is read and O holds blocks ≤ j
         }
@@ -350,6 +362,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float a = fmaxf(fmaxf(v[e], v[e + 8]), fmaxf(v[e + 16], v[e + 24]));
           const float b2 = fmaxf(fmaxf(v[e + 32], v[e + 40]), fmaxf(v[e + 48], v[e + 56]));
           t8[e] = fmaxf(a, b2);
+          if constexpr (BKV == 128) {
+            const float c = fmaxf(fmaxf(v[e + 64], v[e + 72]), fmaxf(v[e + 80], v[e + 88]));
+            const float d = fmaxf(fmaxf(v[e + 96], v[e + 104]), fmaxf(v[e + 112], v[e + 120]));
+            t8[e] = fmaxf(t8[e], fmaxf(c, d));
+          }
         }
         const float mx = fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
                                fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
@@ -392,10 +409,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
         // P_j row as bf16 into the 128-byte-swizzled K-major tile
+        // (BKV / 64 swizzle atoms of 64 keys, each 128 rows × 128 B)
         uint8_t *prow = sp + pb * kPBytes + row * 128;
-        float part[8];
+        float part[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
-        for (int ch = 0; ch < 8; ++ch) {
+        for (int ch = 0; ch < BKV / 8; ++ch) {
           uint32_t w[4];
           float acc = 0.0f;
 #pragma unroll
@@ -405,8 +423,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             __nv_bfloat162 bb = __floats2bfloat162_rn(p0, p1);
             w[h] = *reinterpret_cast<uint32_t *>(&bb);
           }
-          part[ch] = acc;  // eight independent partial sums
-          *reinterpret_cast<uint4 *>(prow + ((ch ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          part[ch & 7] += acc;  // eight independent partial sums
+          *reinterpret_cast<uint4 *>(prow + (ch >> 3) * kPBox + (((ch & 7) ^ (row & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
         }
         l += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -499,6 +518,49 @@ int make_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int
   return DP_OK;
 }
 
+
+template <int BKV>
+int stages_for(const Shape &s) {
+  const size_t budget = 224 * 1024;  // dynamic shared memory for tiles (the 1 KB alignment slack comes on top)
+  const size_t stage = (size_t)(s.nd + s.ndv) * Blk<BKV>::kKVBox;
+  const size_t fixed = (size_t)s.q_bytes + 2 * Blk<BKV>::kPBytes;
+  if (fixed >= budget) return 0;
+  int stages = (int)((budget - fixed) / stage);
+  return stages > kMaxStages ? kMaxStages : stages;
+}
+
+template <int BKV>
+int launch_blocks(const dp_attention_params &p, Shape s, const void *q, const void *k, const void *v, void *o,
+                  cudaStream_t stream) {
+  const int stages = stages_for<BKV>(s);
+  DP_REQUIRE(stages >= 2, DP_ERR_UNSUPPORTED, "attention: head dims too large for the shared-memory ring");
+  s.stages = stages;
+  s.stage_bytes = (uint32_t)(s.nd + s.ndv) * Blk<BKV>::kKVBox;
+  s.kv_blocks = (s.S + BKV - 1) / BKV;
+  CUtensorMap mq, mk, mv;
+  // Q as (D, group rows R, kv heads, batch): a group's stacked query heads are one row range
+  int st = make_map(&mq, q, p.D, s.R, p.heads_kv, p.batch, p.q_sl, p.group * p.q_sh, p.q_sb, BM);
+  if (st != DP_OK) return st;
+  st = make_map(&mk, k, p.D, p.S, p.heads_kv, p.batch, p.k_ss, p.k_sh, p.k_sb, BKV);
+  if (st != DP_OK) return st;
+  st = make_map(&mv, v, p.Dv, p.S, p.heads_kv, p.batch, p.v_ss, p.v_sh, p.v_sb, BKV);
+  if (st != DP_OK) return st;
+  const size_t smem = (size_t)s.q_bytes + 2 * Blk<BKV>::kPBytes + (size_t)stages * s.stage_bytes + 1024;
+  int dev = 0;
+  DP_CHECK_CUDA(cudaGetDevice(&dev));
+  static size_t attr_bytes[64] = {};  // one per kernel instantiation (BKV) and device
+  DP_REQUIRE(dev >= 0 && dev < 64, DP_ERR_UNSUPPORTED, "attention: device ordinal out of range");
+  if (smem > attr_bytes[dev]) {
+    DP_CHECK_CUDA(cudaFuncSetAttribute(attn_kernel<BKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_bytes[dev] = smem;
+  }
+  int grid = dp::num_sms();
+  if (grid > s.items) grid = s.items;
+  attn_kernel<BKV><<<grid, kThreads, smem, stream>>>(mq, mk, mv, s, static_cast<__nv_bfloat16 *>(o));
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
 }  // namespace dpk_attn
 
 namespace dp {
@@ -532,16 +594,9 @@ int launch_attention(const dp_attention_params &p, const void *q, const void *k,
   s.ks = (int)((p.D + 15) / 16);
   s.dvp = (int)((p.Dv + 15) / 16 * 16);
   s.q_bytes = (uint32_t)s.nd * kQBox;
-  s.stage_bytes = (uint32_t)(s.nd + s.ndv) * kKVBox;
-  const size_t budget = 224 * 1024;  // dynamic shared memory for tiles (the 1 KB alignment slack comes on top)
-  int stages = (int)((budget - s.q_bytes - 2 * kPBytes) / s.stage_bytes);
-  if (stages > kMaxStages) stages = kMaxStages;
-  DP_REQUIRE(stages >= 2, DP_ERR_UNSUPPORTED, "attention: head dims too large for the shared-memory ring");
-  s.stages = stages;
   s.tiles_r = (s.R + BM - 1) / BM;
   s.heads_kv = (int)p.heads_kv;
   s.group = (int)p.group;
-  s.kv_blocks = (s.S + BKV - 1) / BKV;
   const int64_t items = p.batch * p.heads_kv * s.tiles_r;
   DP_REQUIRE(items < (1ll << 31), DP_ERR_UNSUPPORTED, "attention: too many work items");
   s.items = (int)items;
@@ -549,28 +604,10 @@ int launch_attention(const dp_attention_params &p, const void *q, const void *k,
   s.o_sb = p.o_sb;
   s.o_sh = p.o_sh;
   s.o_sl = p.o_sl;
-  CUtensorMap mq, mk, mv;
-  // Q as (D, group rows R, kv heads, batch): a group's stacked query heads are one row range
-  int st = make_map(&mq, q, p.D, s.R, p.heads_kv, p.batch, p.q_sl, p.group * p.q_sh, p.q_sb, BM);
-  if (st != DP_OK) return st;
-  st = make_map(&mk, k, p.D, p.S, p.heads_kv, p.batch, p.k_ss, p.k_sh, p.k_sb, BKV);
-  if (st != DP_OK) return st;
-  st = make_map(&mv, v, p.Dv, p.S, p.heads_kv, p.batch, p.v_ss, p.v_sh, p.v_sb, BKV);
-  if (st != DP_OK) return st;
-  const size_t smem = (size_t)s.q_bytes + 2 * kPBytes + (size_t)stages * s.stage_bytes + 1024;
-  int dev = 0;
-  DP_CHECK_CUDA(cudaGetDevice(&dev));
-  static size_t attr_bytes[64] = {};
-  DP_REQUIRE(dev >= 0 && dev < 64, DP_ERR_UNSUPPORTED, "attention: device ordinal out of range");
-  if (smem > attr_bytes[dev]) {
-    DP_CHECK_CUDA(cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_bytes[dev] = smem;
-  }
-  int grid = num_sms();
-  if (grid > s.items) grid = s.items;
-  attn_kernel<<<grid, kThreads, smem, stream>>>(mq, mk, mv, s, static_cast<__nv_bfloat16 *>(o));
-  DP_CHECK_CUDA(cudaGetLastError());
-  return DP_OK;
+  // 128-key blocks when the score and output columns fit TMEM (2·128 + dvp ≤ 512) and two stages fit
+  if (p.D <= 128 && p.Dv <= 128 && stages_for<128>(s) >= 2)
+    return launch_blocks<128>(p, s, q, k, v, o, stream);
+  return launch_blocks<64>(p, s, q, k, v, o, stream);
 }
 
 }  // namespace dp
