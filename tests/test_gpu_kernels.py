@@ -640,7 +640,8 @@ def _attn_ref(q, k, v, scale):
 @pytest.mark.parametrize("B,Hk,g,L,S,D,Dv", [(2, 1, 8, 24, 50, 64, 64), (2, 1, 8, 50, 866, 256, 256),
                                               (1, 2, 4, 200, 300, 128, 128), (3, 4, 1, 256, 256, 72, 72),
                                               (1, 1, 1, 1, 1, 64, 64), (2, 2, 1, 130, 70, 256, 128),
-                                              (32, 16, 1, 256, 256, 72, 72)])
+                                              (32, 16, 1, 256, 256, 72, 72), (1, 1, 2, 64, 385, 96, 40),
+                                              (2, 1, 1, 128, 129, 128, 8)])
 def test_fused_attention(cuda, B, Hk, g, L, S, D, Dv):
     """Fused tcgen05 attention against fp32 torch: grouped-query heads stacked as rows,
     key counts not a multiple of the 64-key block, partial 128-row query tiles, head dims
@@ -664,6 +665,31 @@ def test_fused_attention(cuda, B, Hk, g, L, S, D, Dv):
     ref = _attn_ref(q, k, v, scale)
     got = o.cpu().float()
     assert torch.allclose(got, ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item()), (got - ref).abs().max()
+
+
+@pytest.mark.parametrize("D", [72, 256])
+def test_fused_attention_rising_scores(cuda, D):
+    """Scores that grow block after block (keys scaled up with their position),
+    so the running max is raised and O / l rescaled on many blocks, with
+    128-key blocks (D 72) and 64-key blocks (D 256)."""
+    torch.manual_seed(D)
+    B, H, L, S = 2, 2, 130, 700
+    q = torch.randn(B, H, L, D).abs().bfloat16()
+    k = (torch.randn(B, H, S, D).abs() * torch.linspace(0.1, 3.0, S)[:, None]).bfloat16()
+    v = torch.randn(B, H, S, D).bfloat16()
+    scale = D ** -0.5
+    o = torch.empty(B, H, L, D, dtype=torch.bfloat16, device=cuda)
+    p = N.AttentionParams()
+    p.batch, p.heads_kv, p.group, p.L, p.S, p.D, p.Dv = B, H, 1, L, S, D, D
+    p.q_sb, p.q_sh, p.q_sl = H * L * D, L * D, D
+    p.k_sb, p.k_sh, p.k_ss = H * S * D, S * D, D
+    p.v_sb, p.v_sh, p.v_ss = H * S * D, S * D, D
+    p.o_sb, p.o_sh, p.o_sl = H * L * D, L * D, D
+    p.scale, p.dtype = scale, N.DP_BF16
+    N.attention(p, q.to(cuda), k.to(cuda), v.to(cuda), o)
+    _sync()
+    ref = _attn_ref(q, k, v, scale)
+    assert torch.allclose(o.cpu().float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
 
 
 def test_fused_attention_token_major_output(cuda):
