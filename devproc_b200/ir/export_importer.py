@@ -15,11 +15,18 @@ handlers (the overload's packet name is the handler key) and adds the ATen
 forms the Dynamo graph does not have: ``embedding(weight, indices)``,
 ``select.int``, ``slice.Tensor``, ``upsample_bilinear2d.vec``,
 ``_to_copy``, ``dropout`` in eval mode, and the metadata asserts (dropped).
+Graphs lowered to core ATen (``ep.run_decompositions()``) import too for
+``addmm`` (a linear when its right operand is a transposed weight),
+``native_layer_norm`` (its normalised output), ``_softmax``, patchify
+``convolution`` and ``_unsafe_view``; the math form of attention that
+decomposition produces (with boolean guards for fully masked rows) does not:
+export without decompositions keeps ``scaled_dot_product_attention`` whole.
 Lifted parameters, buffers and constants become ``fn.constants``, so the
 compiled program uploads them once; only the user inputs stay run-time
 inputs, named after the exported function's arguments.
 """
 
+import operator
 from typing import Any, Dict, Optional
 
 import torch
@@ -133,6 +140,60 @@ class TorchExportImporter(FXToIRConverter):
         shape = self._ex_shape(node)
         layout = "NCHW" if len(shape) == 4 else "CHW"
         self._emit(node, OpBuilder.resize(self._v(args[0]), (shape[-2], shape[-1]), layout=layout))
+
+    # -------------------------------------- core-ATen forms (run_decompositions)
+    def _aten_addmm(self, node, args, kwargs):
+        """aten.addmm(bias, x, w.t()) → linear(x, w, bias) when the right operand
+        is the transpose of a weight [N, K]; else matmul + add."""
+        if self._arg(node, 3, "beta", 1) != 1 or self._arg(node, 4, "alpha", 1) != 1:
+            raise ValueError("addmm with beta or alpha other than 1 is not supported")
+        bias, x, m2 = args[0], args[1], args[2]
+        src = self._transposed_source(m2)
+        if src is not None:
+            self._emit(node, OpBuilder.linear(self._v(x), self._v(src), self._v(bias)))
+            return
+        mm = OpBuilder.matmul(self._v(x), self._v(m2), out_dtype=self._v(x).type.dtype)
+        self.fn.block.add_op(mm)
+        self._emit(node, OpBuilder.binary("add", mm.outputs[0], self._v(bias)))
+
+    @staticmethod
+    def _transposed_source(n):
+        """The [N, K] node that ``n`` transposes (aten.t / permute [1, 0]), if any."""
+        if not isinstance(n, torch.fx.Node) or n.op != "call_function":
+            return None
+        t = n.target
+        name = t.overloadpacket.__name__ if isinstance(t, torch._ops.OpOverload) else ""
+        if name == "t" or (name == "permute" and list(n.args[1]) == [1, 0]) or \
+                (name == "transpose" and sorted(a % 2 for a in n.args[1:3]) == [0, 1]):
+            return n.args[0]
+        return None
+
+    def _aten_native_layer_norm(self, node, args, kwargs):
+        """aten.native_layer_norm(x, shape, w, b, eps) → (out, mean, rstd); only out is used."""
+        shape = args[1]
+        if len(shape) != 1:
+            raise ValueError("layer_norm over more than the last dim is not supported")
+        w, b, eps = args[2], args[3], args[4]
+        op = OpBuilder.layer_norm(self._v(args[0]), self._v(w) if w is not None else None,
+                                  self._v(b) if b is not None else None, eps)
+        self.fn.block.add_op(op)
+        self.tuple_map[node] = [op.outputs[0], None, None]
+        for user in node.users:
+            if not (user.target is operator.getitem and user.args[1] == 0):
+                raise ValueError("native_layer_norm: only the normalised output may be used")
+
+    def _aten__softmax(self, node, args, kwargs):
+        """aten._softmax(x, dim, half_to_float)."""
+        self._emit(node, OpBuilder.softmax(self._v(args[0]), args[1]))
+
+    def _aten_convolution(self, node, args, kwargs):
+        """aten.convolution(x, w, b, stride, padding, dilation, transposed, output_padding, groups)."""
+        if args[6] or any(args[7]):
+            raise ValueError("transposed convolution is not supported")
+        self._patchify(node, args[1], args[2], args[3], args[4], args[5], args[8])
+
+    def _aten__unsafe_view(self, node, args, kwargs):
+        self._op_reshape(node, args, kwargs)
 
     def _aten__to_copy(self, node, args, kwargs):
         self._op_to(node, args, kwargs)

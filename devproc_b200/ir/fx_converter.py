@@ -438,13 +438,12 @@ class FXToIRConverter:
 
     def _op_conv2d(self, node, args, kwargs):
         """Patchify convolution (stride == kernel, no padding) as reshape → permute → linear."""
-        x = self._v(args[0])
-        w_node = self._arg(node, 1, "weight")
-        b_node = self._arg(node, 2, "bias")
-        stride = self._arg(node, 3, "stride", 1)
-        padding = self._arg(node, 4, "padding", 0)
-        dilation = self._arg(node, 5, "dilation", 1)
-        groups = self._arg(node, 6, "groups", 1)
+        self._patchify(node, self._arg(node, 1, "weight"), self._arg(node, 2, "bias"), self._arg(node, 3, "stride", 1),
+                       self._arg(node, 4, "padding", 0), self._arg(node, 5, "dilation", 1),
+                       self._arg(node, 6, "groups", 1))
+
+    def _patchify(self, node, w_node, b_node, stride, padding, dilation, groups):
+        x = self._v(node.args[0])
         w = self._v(w_node)
         O, C, kh, kw = w.type.shape
         st = tuple(stride) if isinstance(stride, (tuple, list)) else (stride, stride)

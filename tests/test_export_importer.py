@@ -127,3 +127,42 @@ def test_state_mutation_is_rejected():
     ep = torch.export.export(Counter(), (torch.randn(4),))
     with pytest.raises(ValueError, match="mutates state"):
         devproc.from_export(ep, backend="ir")
+
+
+def test_decomposed_core_aten_token_pipeline():
+    """``ep.run_decompositions()`` (core ATen: addmm over a transposed weight,
+    native_layer_norm with its tuple result, permute, _to_copy) imports to the
+    same plan as the high-level export, and the oracle matches eager."""
+    m = workloads.TokenPipeline().eval()
+    ids = workloads.token_ids()
+    ep = torch.export.export(m, (ids,))
+    dec = ep.run_decompositions()
+    fn = devproc.from_export(dec, backend="ir")
+    assert "linear" in [op.name for op in fn.block.ops]
+    assert torch.equal(_run_ir(fn, ids)[0], m(ids))
+    assert _labels(devproc.compile(ep)) == _labels(devproc.compile(dec))
+
+
+def test_decomposed_core_aten_patchify_softmax():
+    """convolution (patchify), _softmax, addmm without a transposed weight."""
+
+    class M(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.patch = torch.nn.Conv2d(3, 16, kernel_size=4, stride=4)
+            self.w = torch.nn.Parameter(torch.randn(16, 5))
+            self.b = torch.nn.Parameter(torch.randn(5))
+
+        def forward(self, x):
+            y = self.patch(x).flatten(2).transpose(1, 2)       # [B, 16 patches, 16]
+            z = torch.addmm(self.b, y.reshape(-1, 16), self.w)  # weight used as [K, N]
+            return torch.softmax(z, -1)
+
+    m = M().eval()
+    x = torch.randn(2, 3, 16, 16)
+    ep = torch.export.export(m, (x,)).run_decompositions()
+    fn = devproc.from_export(ep, backend="ir")
+    got = _run_ir(fn, x)[0]
+    with torch.no_grad():
+        ref = m(x)
+    assert torch.allclose(got, ref, rtol=1e-4, atol=1e-5)
