@@ -147,6 +147,9 @@ EXPORTS = {
     "dp_last_error": [ctypes.c_char_p, ctypes.c_size_t],
     "dp_device_init": [ctypes.c_int],
     "dp_device_error": [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int64)],
+    "dp_device_error_pending": [ctypes.c_int, ctypes.POINTER(ctypes.c_int)],
+    "dp_set_wait_limit": [ctypes.c_int, ctypes.c_uint64],
+    "dp_test_withhold_copies": [ctypes.c_int, ctypes.c_int],
     "dp_preproc": [ctypes.POINTER(PreprocParams), _VP, _VP, _VP],
     "dp_rowreduce": [ctypes.POINTER(RowReduceParams), _VP, _VP, _VP, _VP, _VP],
     "dp_gemm": [ctypes.POINTER(GemmParams), _VP, _VP, _VP, _VP, _VP, _VP],
@@ -207,6 +210,40 @@ def device_error():
     code, info = ctypes.c_int(0), ctypes.c_int64(0)
     check(lib().dp_device_error(ctypes.byref(code), ctypes.byref(info)), "dp_device_error")
     return code.value, info.value
+
+
+def device_error_pending(device: int) -> int:
+    """DP_DEVERR_* code recorded on ``device`` since the last clear (no CUDA call;
+    meaningful once the work that may have failed has been synchronised)."""
+    code = ctypes.c_int(0)
+    check(lib().dp_device_error_pending(device, ctypes.byref(code)), "dp_device_error_pending")
+    return code.value
+
+
+def raise_device_error(device: int, where: str) -> None:
+    """Raise if a kernel on ``device`` recorded an error: IndexError for an
+    out-of-range embedding id, DevProcError(DP_ERR_DEVICE) for a wait that
+    gave up (with its site).  Reads and clears the word."""
+    if device_error_pending(device) == DP_DEVERR_NONE:
+        return
+    import torch
+    with torch.cuda.device(device):
+        code, info = device_error()
+    if code == DP_DEVERR_INDEX:
+        raise IndexError(f"{where}: embedding id out of range at flat position {info}")
+    if code == DP_DEVERR_TIMEOUT:
+        raise DevProcError(DP_ERR_DEVICE, f"{where}: a bounded wait inside a kernel gave up (site {info}); "
+                                          "the outputs of this run are incomplete")
+    if code != DP_DEVERR_NONE:
+        raise DevProcError(DP_ERR_DEVICE, f"{where}: device error {code} (info {info})")
+
+
+def set_wait_limit(device: int, limit_ns: int) -> None:
+    check(lib().dp_set_wait_limit(device, limit_ns), "dp_set_wait_limit")
+
+
+def test_withhold_copies(device: int, enable: bool) -> None:
+    check(lib().dp_test_withhold_copies(device, 1 if enable else 0), "dp_test_withhold_copies")
 
 
 def _ptr(x):

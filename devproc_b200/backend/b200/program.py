@@ -90,7 +90,6 @@ class B200CompiledProgram(CompiledProgram):
         self._staging: Dict[str, torch.Tensor] = {}
         self._host_out: List[Optional[torch.Tensor]] = []
         self._bound: Dict[int, int] = {}
-        self._checks_index = any(r["kernel"] == "embedding" for r in spec.records)
         # chunked execution for host inputs (see set_stream)
         self.stream_chunk: Optional[int] = None
         self._chunk: Optional["B200CompiledProgram"] = None
@@ -261,7 +260,13 @@ class B200CompiledProgram(CompiledProgram):
         behaviour); with ``reuse_host_buffers`` the program's pinned host
         output buffers themselves (no host copy; the next run overwrites
         them); with ``to_cpu=False`` the device output buffers (likewise
-        overwritten by the next run)."""
+        overwritten by the next run), enqueued without waiting.
+
+        A run that returns host tensors synchronises and then raises if a
+        kernel reported an error through the device error word: IndexError
+        for an embedding id out of range, DevProcError (DP_ERR_DEVICE) for a
+        bounded wait that gave up.  After ``to_cpu=False`` runs,
+        ``synchronize()`` does the same check."""
         self._ensure_ready()
         if len(args) > len(self.spec.inputs):
             raise TypeError(f"{len(args)} positional inputs for {len(self.spec.inputs)} program inputs")
@@ -298,13 +303,17 @@ class B200CompiledProgram(CompiledProgram):
                     h.copy_(t, non_blocking=True)
                     outs.append(h)
             stream.synchronize()
-            if self._checks_index or (self._chunk is not None and self._chunk._checks_index):
-                code, info = N.device_error()
-                if code == N.DP_DEVERR_INDEX:
-                    raise IndexError(f"embedding id out of range at flat position {info}")
-                if code != N.DP_DEVERR_NONE:
-                    raise N.DevProcError(N.DP_ERR_DEVICE, f"device error {code} (info {info})")
+            N.raise_device_error(self.device_id, f"program {self.spec.name}")
             return outs if reuse_host_buffers else [h.clone() for h in outs]
+
+    def synchronize(self) -> None:
+        """Wait for the work ``run(to_cpu=False)`` enqueued on the current
+        stream and raise if one of its kernels reported an error (an embedding
+        id out of range, a bounded wait that gave up).  ``run`` with host
+        results does this itself after every call."""
+        with torch.cuda.device(self._device()):
+            torch.cuda.current_stream(self._device()).synchronize()
+        N.raise_device_error(self.device_id, f"program {self.spec.name}")
 
     def __call__(self, *args, **kwargs):
         return self.run(*args, **kwargs)

@@ -17,6 +17,12 @@ namespace dp {
 int set_error(int code, const std::string &msg);
 int cuda_status(cudaError_t e, const char *what);
 int num_sms();  // SM count of the current device (cached per device)
+// Resident blocks per SM of kernel ``func`` at (threads, smem) on the current
+// device.  The first call per (device, kernel, threads, smem) grants the
+// dynamic shared-memory opt-in (and, with ``max_carveout``, prefers the
+// largest shared-memory carveout) and queries the occupancy; later calls are
+// a cache lookup, so launchers make no attribute or occupancy call per launch.
+int kernel_blocks_per_sm(const void *func, int threads, size_t smem, bool max_carveout, int *per_sm);
 
 #define DP_CHECK_CUDA(expr)                                   \
   do {                                                        \
@@ -77,12 +83,25 @@ __device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv &f) {
 
 // -------------------------------------------------------------- device side
 // Device error word: first failure wins (code, info); read and cleared by
-// dp_device_error().  Defined once in dp_api.cu.
+// dp_device_error().  The winning code is also stored to a pinned, mapped
+// host word (g_dp_err_host, set up by dp_device_init), so the host can see
+// after a stream synchronisation that something failed without a CUDA call
+// (dp_device_error_pending).  Defined once in dp_api.cu.
 extern __device__ unsigned int g_dp_err_code;
 extern __device__ long long g_dp_err_info;
+extern __device__ int *g_dp_err_host;
+// Wall-time limit of the waits that take the device-wide limit (2 s unless
+// dp_set_wait_limit changed it), and the failure-detection switch that makes
+// the staged row kernel arm its barriers without issuing the copies.
+extern __device__ unsigned long long g_dp_wait_limit_ns;
+extern __device__ unsigned int g_dp_withhold_copies;
 
 __device__ __forceinline__ void dp_report(unsigned code, long long info) {
-  if (atomicCAS(&g_dp_err_code, 0u, code) == 0u) g_dp_err_info = info;
+  if (atomicCAS(&g_dp_err_code, 0u, code) == 0u) {
+    g_dp_err_info = info;
+    int *h = g_dp_err_host;
+    if (h) *reinterpret_cast<volatile int *>(h) = (int)code;
+  }
 }
 
 template <typename T> __device__ __forceinline__ float to_f32(T v);
@@ -193,12 +212,17 @@ __device__ __forceinline__ bool mbar_wait_for(uint64_t *bar, uint32_t phase, uin
   return true;
 }
 
-// Bounded wait: gives up once ``timeout_ns`` of wall time has passed,
-// records DP_DEVERR_TIMEOUT with ``site`` and returns false.  No wait in
-// this library can spin forever.
+// Bounded wait: gives up once ``timeout_ns`` of wall time has passed (0 =
+// the device-wide limit, g_dp_wait_limit_ns, read only when the first probe
+// fails), records DP_DEVERR_TIMEOUT with ``site`` and returns false.  No wait
+// in this library can spin forever.  Waits that drain copies still in flight
+// before a CTA exits pass their own fixed limit, so a short device-wide limit
+// never lets a CTA leave while a copy can still land in its shared memory.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, int site,
-                                                  uint64_t timeout_ns = 2000000000ull) {
-  if (mbar_wait_for(bar, phase, timeout_ns)) return true;
+                                                  uint64_t timeout_ns = 0) {
+  if (mbar_try_wait(bar, phase)) return true;
+  const uint64_t limit = timeout_ns ? timeout_ns : *reinterpret_cast<volatile unsigned long long *>(&g_dp_wait_limit_ns);
+  if (mbar_wait_for(bar, phase, limit)) return true;
   dp_report(DP_DEVERR_TIMEOUT, site);
   return false;
 }

@@ -509,12 +509,9 @@ int launch_fast(const dp_preproc_params &p, const void *in, void *out, cudaStrea
   const size_t smem = (size_t)kFastStages * g.R * g.slot_bytes + (size_t)g.OH * sizeof(RowCoef);
   const int n_units = g.B * g.upi;
   auto kern = preproc_u8c3_kernel<TOut>;
-  DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-  DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                     (int)cudaSharedmemCarveoutMaxShared));
   int per_sm = 0;
-  DP_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem));
-  if (per_sm < 1) per_sm = 1;
+  int st = dp::kernel_blocks_per_sm((const void *)kern, threads, smem, true, &per_sm);
+  if (st != DP_OK) return st;
   int grid = dp::num_sms() * per_sm;
   if (grid > n_units) grid = n_units;
   kern<<<grid, threads, smem, s>>>(g, static_cast<const uint8_t *>(in), static_cast<TOut *>(out), n_units);
@@ -538,10 +535,9 @@ int launch_typed(const Geo &g, const void *in, void *out, cudaStream_t s) {
   if (bulk) {
     auto kern = preproc_bulk_kernel<TIn, TOut, IN_NCHW, OUT_NCHW>;
     const size_t smem = stage_bytes * kStages;
-    DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;
-    DP_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem));
-    if (per_sm < 1) per_sm = 1;
+    int st = dp::kernel_blocks_per_sm((const void *)kern, threads, smem, false, &per_sm);
+    if (st != DP_OK) return st;
     int grid = sms * per_sm;
     if (grid > n_units) grid = n_units;
     kern<<<grid, threads, smem, s>>>(g, static_cast<const TIn *>(in), static_cast<TOut *>(out), n_units);
@@ -549,10 +545,9 @@ int launch_typed(const Geo &g, const void *in, void *out, cudaStream_t s) {
     auto kern = preproc_plain_kernel<TIn, TOut, IN_NCHW, OUT_NCHW>;
     const size_t smem = stage_bytes;
     DP_REQUIRE(smem <= 200 * 1024, DP_ERR_UNSUPPORTED, "preproc: input rows too wide for shared memory");
-    DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int per_sm = 0;
-    DP_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, threads, smem));
-    if (per_sm < 1) per_sm = 1;
+    int st = dp::kernel_blocks_per_sm((const void *)kern, threads, smem, false, &per_sm);
+    if (st != DP_OK) return st;
     int grid = sms * per_sm;
     if (grid > n_units) grid = n_units;
     kern<<<grid, threads, smem, s>>>(g, static_cast<const TIn *>(in), static_cast<TOut *>(out), n_units);

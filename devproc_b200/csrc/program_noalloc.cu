@@ -10,6 +10,8 @@
 // library's own device memory (DP_NOALLOC_ARENA_BYTES on every GPU that loads
 // the library, held until the process exits).  The caller still passes every
 // input, weight and output buffer.
+#include <cuda.h>
+
 #include <cstring>
 #include <mutex>
 
@@ -22,25 +24,104 @@ namespace {
 constexpr int kMaxDevices = 64;
 constexpr int kMaxSlots = 1024;
 
+struct ArenaAddress {
+  unsigned long long ctx_id = 0;  // context the address was looked up in
+  void *ptr = nullptr;
+};
 std::mutex g_noalloc_mu;
-void *g_noalloc_base[kMaxDevices] = {nullptr};
+ArenaAddress g_noalloc_base[kMaxDevices];
 
-// Device address of g_noalloc_arena on the current device (looked up once per
-// device; in host code the symbol itself is only a host-side stand-in).
+// Device address of g_noalloc_arena on the current device.  In host code the
+// symbol itself is only a host-side stand-in, so the address is looked up with
+// cudaGetSymbolAddress once per device, with that device current, and cached
+// with the id of the context it belongs to: after a cudaDeviceReset the
+// device has a new context (and the module a new address), so the lookup is
+// made again.  No call here allocates.
 int noalloc_base(void **out) {
   int dev = 0;
   DP_CHECK_CUDA(cudaGetDevice(&dev));
   DP_REQUIRE(dev >= 0 && dev < kMaxDevices, DP_ERR_UNSUPPORTED, "dp_program_run_noalloc: device index too large");
+  DP_CHECK_CUDA(cudaSetDevice(dev));  // makes the device's primary context current
+  // Driver entry points through the runtime, so the library does not link libcuda.
+  using GetCurrentFn = CUresult (*)(CUcontext *);
+  using GetIdFn = CUresult (*)(CUcontext, unsigned long long *);
+  static GetCurrentFn get_current = nullptr;
+  static GetIdFn get_id = nullptr;
+  if (!get_current || !get_id) {
+    void *a = nullptr, *b = nullptr;
+    cudaDriverEntryPointQueryResult qa, qb;
+    DP_REQUIRE(cudaGetDriverEntryPoint("cuCtxGetCurrent", &a, cudaEnableDefault, &qa) == cudaSuccess &&
+                   qa == cudaDriverEntryPointSuccess &&
+                   cudaGetDriverEntryPoint("cuCtxGetId", &b, cudaEnableDefault, &qb) == cudaSuccess &&
+                   qb == cudaDriverEntryPointSuccess,
+               DP_ERR_CUDA, "dp_program_run_noalloc: cuCtxGetCurrent / cuCtxGetId unavailable");
+    get_current = reinterpret_cast<GetCurrentFn>(a);
+    get_id = reinterpret_cast<GetIdFn>(b);
+  }
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  DP_REQUIRE(get_current(&ctx) == CUDA_SUCCESS && ctx != nullptr && get_id(ctx, &id) == CUDA_SUCCESS,
+             DP_ERR_CUDA, "dp_program_run_noalloc: no current CUDA context");
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_base[dev]) {
+  ArenaAddress &a = g_noalloc_base[dev];
+  if (!a.ptr || a.ctx_id != id) {
     void *p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_arena);
     if (e != cudaSuccess) return dp::cuda_status(e, "cudaGetSymbolAddress(g_noalloc_arena)");
     DP_REQUIRE(p != nullptr, DP_ERR_CUDA, "dp_program_run_noalloc: null arena address");
-    g_noalloc_base[dev] = p;
+    a.ptr = p;
+    a.ctx_id = id;
   }
-  *out = g_noalloc_base[dev];
+  *out = a.ptr;
   return DP_OK;
+}
+
+int launch_record(const dp_plan_record &rec, const void *const *ops, cudaStream_t s) {
+  switch (rec.kernel) {
+    case DP_K_PREPROC: {
+      dp_preproc_params p;
+      memcpy(&p, rec.params, sizeof(p));
+      return dp::launch_preproc(p, ops[0], const_cast<void *>(ops[1]), s);
+    }
+    case DP_K_ROWREDUCE: {
+      dp_rowreduce_params p;
+      memcpy(&p, rec.params, sizeof(p));
+      return dp::launch_rowreduce(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
+    }
+    case DP_K_GEMM: {
+      dp_gemm_params p;
+      memcpy(&p, rec.params, sizeof(p));
+      return dp::launch_gemm(p, ops[0], ops[1], const_cast<void *>(ops[2]), ops[3], ops[4], s);
+    }
+    case DP_K_REGION: {
+      dp_region_desc d;
+      memcpy(&d, rec.params, sizeof(d));
+      return dp::launch_region(d, ops, s);
+    }
+    case DP_K_EMBEDDING: {
+      dp_embedding_params p;
+      memcpy(&p, rec.params, sizeof(p));
+      return dp::launch_embedding(p, ops[0], ops[1], const_cast<void *>(ops[2]), s);
+    }
+    case DP_K_ATTENTION: {
+      dp_attention_params p;
+      memcpy(&p, rec.params, sizeof(p));
+      return dp::launch_attention(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
+    }
+    case DP_K_ROPE: {
+      dp_rope_params p;
+      memcpy(&p, rec.params, sizeof(p));
+      return dp::launch_rope(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
+    }
+    case DP_K_COPY: {
+      uint64_t bytes;
+      memcpy(&bytes, rec.params, sizeof(bytes));
+      cudaError_t e = cudaMemcpyAsync(const_cast<void *>(ops[1]), ops[0], bytes, cudaMemcpyDeviceToDevice, s);
+      return e == cudaSuccess ? DP_OK : dp::cuda_status(e, "copy");
+    }
+    default:
+      return dp::set_error(DP_ERR_PLAN, "unknown record kind " + std::to_string(rec.kernel));
+  }
 }
 
 }  // namespace
@@ -61,9 +142,44 @@ extern "C" int dp_program_run_noalloc(const void *plan, size_t plan_bytes, void 
   DP_REQUIRE(h.arena_bytes <= (uint64_t)DP_NOALLOC_ARENA_BYTES, DP_ERR_UNSUPPORTED,
              "dp_program_run_noalloc: the plan needs " + std::to_string(h.arena_bytes) +
                  " bytes of intermediates; the static arena holds " + std::to_string(DP_NOALLOC_ARENA_BYTES));
-  const uint8_t *cur = static_cast<const uint8_t *>(plan) + sizeof(h);
-  const uint8_t *slots = cur;
-  const uint8_t *records = cur + (size_t)h.n_slots * sizeof(dp_plan_slot);
+  const uint8_t *slots = static_cast<const uint8_t *>(plan) + sizeof(h);
+  const uint8_t *records = slots + (size_t)h.n_slots * sizeof(dp_plan_slot);
+
+  // Validate the whole plan and the caller's buffers before anything is
+  // enqueued, so a malformed plan writes nothing.
+  int n_bound_slots = 0;
+  for (uint32_t i = 0; i < h.n_slots; ++i) {
+    dp_plan_slot sl;
+    memcpy(&sl, slots + i * sizeof(dp_plan_slot), sizeof(sl));
+    if (sl.kind == DP_SLOT_ARENA) {
+      DP_REQUIRE(sl.offset % 16 == 0 && sl.offset + sl.bytes <= h.arena_bytes, DP_ERR_PLAN,
+                 "plan: arena slot " + std::to_string(i) + " out of range or misaligned");
+      continue;
+    }
+    DP_REQUIRE(sl.kind == DP_SLOT_BOUND, DP_ERR_PLAN, "plan: bad kind of slot " + std::to_string(i));
+    DP_REQUIRE(bound_ptrs != nullptr && n_bound_slots < n_bound, DP_ERR_ARG,
+               "dp_program_run_noalloc: fewer buffers than the plan's bound slots");
+    DP_REQUIRE(bound_ptrs[n_bound_slots] != nullptr, DP_ERR_ARG,
+               "dp_program_run_noalloc: null buffer " + std::to_string(n_bound_slots));
+    DP_REQUIRE(bound_bytes == nullptr || bound_bytes[n_bound_slots] >= sl.bytes, DP_ERR_SHAPE,
+               "dp_program_run_noalloc: buffer " + std::to_string(n_bound_slots) + " (slot " + std::to_string(i) +
+                   ") is smaller than its slot");
+    ++n_bound_slots;
+  }
+  DP_REQUIRE(n_bound_slots == n_bound, DP_ERR_ARG,
+             "dp_program_run_noalloc: " + std::to_string(n_bound) + " buffers for " + std::to_string(n_bound_slots) +
+                 " bound slots");
+  for (uint32_t r = 0; r < h.n_records; ++r) {
+    dp_plan_record rec;
+    memcpy(&rec, records + (size_t)r * sizeof(dp_plan_record), sizeof(rec));
+    DP_REQUIRE(rec.kernel >= DP_K_PREPROC && rec.kernel <= DP_K_ROPE, DP_ERR_PLAN,
+               "program record " + std::to_string(r) + ": unknown record kind " + std::to_string(rec.kernel));
+    DP_REQUIRE(rec.n_operands <= DP_RECORD_MAX_OPERANDS, DP_ERR_PLAN,
+               "program record " + std::to_string(r) + ": too many operands");
+    for (uint32_t i = 0; i < rec.n_operands; ++i)
+      DP_REQUIRE(rec.operand[i] >= -1 && rec.operand[i] < (int32_t)h.n_slots, DP_ERR_PLAN,
+                 "program record " + std::to_string(r) + ": operand out of range");
+  }
 
   void *base = nullptr;
   int st = noalloc_base(&base);
@@ -75,87 +191,21 @@ extern "C" int dp_program_run_noalloc(const void *plan, size_t plan_bytes, void 
   for (uint32_t i = 0; i < h.n_slots; ++i) {
     dp_plan_slot sl;
     memcpy(&sl, slots + i * sizeof(dp_plan_slot), sizeof(sl));
-    if (sl.kind == DP_SLOT_ARENA) {
-      DP_REQUIRE(sl.offset % 16 == 0 && sl.offset + sl.bytes <= h.arena_bytes, DP_ERR_PLAN,
-                 "plan: arena slot out of range");
-      ptr[i] = static_cast<uint8_t *>(base) + sl.offset;
-    } else {
-      DP_REQUIRE(sl.kind == DP_SLOT_BOUND, DP_ERR_PLAN, "plan: bad slot kind");
-      DP_REQUIRE(bound_ptrs != nullptr && next_bound < n_bound, DP_ERR_ARG,
-                 "dp_program_run_noalloc: fewer buffers than the plan's bound slots");
-      DP_REQUIRE(bound_ptrs[next_bound] != nullptr, DP_ERR_ARG, "dp_program_run_noalloc: null buffer");
-      DP_REQUIRE(bound_bytes == nullptr || bound_bytes[next_bound] >= sl.bytes, DP_ERR_SHAPE,
-                 "dp_program_run_noalloc: buffer " + std::to_string(next_bound) + " is smaller than its slot");
-      ptr[i] = bound_ptrs[next_bound++];
-    }
+    ptr[i] = sl.kind == DP_SLOT_ARENA ? static_cast<uint8_t *>(base) + sl.offset : bound_ptrs[next_bound++];
   }
-  DP_REQUIRE(next_bound == n_bound, DP_ERR_ARG, "dp_program_run_noalloc: more buffers than bound slots");
 
   cudaStream_t s = dp::as_stream(stream);
   for (uint32_t r = 0; r < h.n_records; ++r) {
     dp_plan_record rec;
     memcpy(&rec, records + (size_t)r * sizeof(dp_plan_record), sizeof(rec));
-    DP_REQUIRE(rec.n_operands <= DP_RECORD_MAX_OPERANDS, DP_ERR_PLAN, "plan: too many operands");
     const void *ops[DP_RECORD_MAX_OPERANDS] = {nullptr};
-    for (uint32_t i = 0; i < rec.n_operands; ++i) {
-      DP_REQUIRE(rec.operand[i] >= -1 && rec.operand[i] < (int32_t)h.n_slots, DP_ERR_PLAN,
-                 "plan: operand out of range");
-      ops[i] = rec.operand[i] >= 0 ? ptr[rec.operand[i]] : nullptr;
+    for (uint32_t i = 0; i < rec.n_operands; ++i) ops[i] = rec.operand[i] >= 0 ? ptr[rec.operand[i]] : nullptr;
+    st = launch_record(rec, ops, s);
+    if (st != DP_OK) {
+      char buf[512];
+      dp_last_error(buf, sizeof(buf));
+      return dp::set_error(st, "program record " + std::to_string(r) + ": " + buf);
     }
-    switch (rec.kernel) {
-      case DP_K_PREPROC: {
-        dp_preproc_params p;
-        memcpy(&p, rec.params, sizeof(p));
-        st = dp::launch_preproc(p, ops[0], const_cast<void *>(ops[1]), s);
-        break;
-      }
-      case DP_K_ROWREDUCE: {
-        dp_rowreduce_params p;
-        memcpy(&p, rec.params, sizeof(p));
-        st = dp::launch_rowreduce(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
-        break;
-      }
-      case DP_K_GEMM: {
-        dp_gemm_params p;
-        memcpy(&p, rec.params, sizeof(p));
-        st = dp::launch_gemm(p, ops[0], ops[1], const_cast<void *>(ops[2]), ops[3], ops[4], s);
-        break;
-      }
-      case DP_K_REGION: {
-        dp_region_desc d;
-        memcpy(&d, rec.params, sizeof(d));
-        st = dp::launch_region(d, ops, s);
-        break;
-      }
-      case DP_K_EMBEDDING: {
-        dp_embedding_params p;
-        memcpy(&p, rec.params, sizeof(p));
-        st = dp::launch_embedding(p, ops[0], ops[1], const_cast<void *>(ops[2]), s);
-        break;
-      }
-      case DP_K_ATTENTION: {
-        dp_attention_params p;
-        memcpy(&p, rec.params, sizeof(p));
-        st = dp::launch_attention(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
-        break;
-      }
-      case DP_K_ROPE: {
-        dp_rope_params p;
-        memcpy(&p, rec.params, sizeof(p));
-        st = dp::launch_rope(p, ops[0], ops[1], ops[2], const_cast<void *>(ops[3]), s);
-        break;
-      }
-      case DP_K_COPY: {
-        uint64_t bytes;
-        memcpy(&bytes, rec.params, sizeof(bytes));
-        cudaError_t e = cudaMemcpyAsync(const_cast<void *>(ops[1]), ops[0], bytes, cudaMemcpyDeviceToDevice, s);
-        st = e == cudaSuccess ? DP_OK : dp::cuda_status(e, "noalloc copy record");
-        break;
-      }
-      default:
-        st = dp::set_error(DP_ERR_PLAN, "plan: unknown record kind " + std::to_string(rec.kernel));
-    }
-    if (st != DP_OK) return st;
   }
   return DP_OK;
 }

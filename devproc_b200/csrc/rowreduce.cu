@@ -748,9 +748,12 @@ __global__ void __launch_bounds__(32 * kStagedWarps) norm_staged_kernel(dp_rowre
     fence_barrier_init();
   }
   __syncwarp();
+  // With g_dp_withhold_copies set (failure-detection tests only) the barrier
+  // is armed but no copy is issued: its wait can end only by the limit.
+  const bool withhold = *reinterpret_cast<volatile unsigned int *>(&g_dp_withhold_copies) != 0u;
   auto issue = [&](int64_t row, int b) {
     mbar_arrive_expect_tx(&bars[wid][b], bytes);
-    bulk_g2s(buf0 + b * row_floats, in + row * p.in_row_stride, bytes, &bars[wid][b]);
+    if (!withhold) bulk_g2s(buf0 + b * row_floats, in + row * p.in_row_stride, bytes, &bars[wid][b]);
   };
   if (lane == 0 && first < p.rows) issue(first, 0);
   int k = 0;
@@ -839,8 +842,9 @@ __global__ void __launch_bounds__(32 * kStagedWarps) norm_staged_kernel(dp_rowre
     }
     __syncwarp();
   }
-  // Leave no copy in flight into shared memory that is about to go away.
-  if (lane == 0 && pending) mbar_wait_bounded(&bars[wid][k & 1], (uint32_t)(k >> 1) & 1u, 701);
+  // Leave no copy in flight into shared memory that is about to go away
+  // (a fixed 100 ms limit, independent of the device-wide one).
+  if (lane == 0 && pending) mbar_wait_bounded(&bars[wid][k & 1], (uint32_t)(k >> 1) & 1u, 701, 100000000ull);
   __syncwarp();
 }
 

@@ -183,8 +183,16 @@ class TorchExportImporter(FXToIRConverter):
                 raise ValueError("native_layer_norm: only the normalised output may be used")
 
     def _aten__softmax(self, node, args, kwargs):
-        """aten._softmax(x, dim, half_to_float)."""
-        self._emit(node, OpBuilder.softmax(self._v(args[0]), args[1]))
+        """aten._softmax(x, dim, half_to_float).  With half_to_float a 16-bit
+        input gives an fp32 result: the input is cast to fp32 first (the
+        softmax itself runs in fp32 either way)."""
+        x = self._v(args[0])
+        half_to_float = len(args) > 2 and bool(args[2])
+        if half_to_float and x.type.dtype in ("float16", "bfloat16"):
+            cast = OpBuilder.to(x, "float32")
+            self.fn.block.add_op(cast)
+            x = cast.outputs[0]
+        self._emit(node, OpBuilder.softmax(x, args[1]))
 
     def _aten_convolution(self, node, args, kwargs):
         """aten.convolution(x, w, b, stride, padding, dilation, transposed, output_padding, groups)."""

@@ -76,6 +76,24 @@ int dp_device_init(int device);               /* sets the device, checks it is s
  * the device).  *code receives a DP_DEVERR_* value, *info the first bad index
  * or wait site recorded. */
 int dp_device_error(int *code, int64_t *info);
+/* The DP_DEVERR_* code a kernel recorded on ``device`` since the word was last
+ * cleared, read from a pinned host mirror that dp_device_init sets up: no CUDA
+ * call and no synchronisation, so call it after synchronising the stream the
+ * work ran on; then dp_device_error for the site and to clear.  The reference
+ * reported no kernel failure at all: it warned and skipped ops
+ * (src/devproc/backend/triton/compiler.py:70-74, 302-304, 343-346). */
+int dp_device_error_pending(int device, int *code);
+/* Wall-time limit of the bounded waits of the row-reduction and preprocessing
+ * kernels on ``device`` (0 restores the default, 2 s).  Waits that drain copies
+ * in flight before a CTA exits keep their own fixed limit.  No reference
+ * counterpart (the reference has no device-side waits). */
+int dp_set_wait_limit(int device, uint64_t limit_ns);
+/* Failure-detection test switch, off by default: while enabled, the staged
+ * fp32 softmax / RMSNorm / LayerNorm kernel on ``device`` arms its row
+ * barriers but issues no copy, so its waits can only end by their limit and
+ * the kernel reports DP_DEVERR_TIMEOUT (site 700) and returns.  No reference
+ * counterpart. */
+int dp_test_withhold_copies(int device, int enable);
 
 /* ---- fused preprocessing region ------------------------------------------
  * out[b, c, y, x] (or out[b, y, x, c]) =
@@ -295,11 +313,15 @@ int dp_program_destroy(dp_program *prog);
  * the library's own device memory, present on every GPU that loads the
  * library until the process exits.  ``bound_ptrs`` (and optionally
  * ``bound_bytes``, checked against the slot sizes) give one caller buffer per
- * DP_SLOT_BOUND slot, in slot order: inputs, weights and outputs.  A plan that
+ * DP_SLOT_BOUND slot, in slot order: inputs, weights and outputs, and also
+ * every sub-range slot of such a buffer (a slice of a weight or an input,
+ * listed in the program's meta.json "aliases" as [slot, root slot, byte
+ * offset]), which takes the root buffer's pointer plus that offset.  The
+ * whole plan and the buffer list are checked before anything is enqueued.  A plan that
  * needs more intermediate bytes than the limit is rejected with
  * DP_ERR_UNSUPPORTED.  No cudaMalloc or cudaFree is called.  The first call on
- * a device looks up the array's device address, so make it before any stream
- * capture.  Every call shares the one array, which keeps the last call's
+ * a device (and the first after a cudaDeviceReset) looks up the array's device
+ * address, so make it before any stream capture.  Every call shares the one array, which keeps the last call's
  * contents; each intermediate is written before it is read, so nothing needs
  * clearing, but calls that overlap on the GPU (other streams or threads) race
  * on it. */

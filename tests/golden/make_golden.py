@@ -1,6 +1,6 @@
 """Generate golden vectors from the reference's own kernels (run here, on the CPU).
 
-The reference (DevProc, read from /root/reference/src) implements every
+The reference (DevProc, read from its ``src`` folder) implements every
 tensor op as a Triton template.  Triton's interpreter (TRITON_INTERPRET=1)
 executes those templates with numpy on the CPU, so their outputs can be
 recorded without a GPU.  Each case runs in its own subprocess because the
@@ -13,9 +13,11 @@ in ``templates.npz``; plus ``ir_ops.json`` with the op lists the reference's
 DSL and FX frontend build for the test programs of its own test-suite.
 
 Usage (in a container that has the reference tree):
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py --ref-src <DevProc checkout>/src
+or with DEVPROC_REF_SRC set to that folder.
 """
 
+import argparse
 import json
 import os
 import subprocess
@@ -25,7 +27,7 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF_SRC = "/root/reference/src"
+REF_SRC = os.environ.get("DEVPROC_REF_SRC")
 
 CASES = ["normalize_f32", "normalize_u8", "relu", "sigmoid", "add", "to_i32", "softmax", "argmax_small",
          "argmax_wide", "argmax_ties", "sum", "matmul", "linear"]
@@ -81,6 +83,12 @@ np.savez(sys.argv[2], **{k: v.numpy() for k, v in out.items()})
 
 
 def main() -> None:
+    global REF_SRC
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref-src", default=REF_SRC, help="the reference's src folder (default: $DEVPROC_REF_SRC)")
+    REF_SRC = ap.parse_args().ref_src
+    if not REF_SRC or not (Path(REF_SRC) / "devproc").is_dir():
+        raise SystemExit("give the reference's src folder with --ref-src or DEVPROC_REF_SRC")
     arrays = {}
     skipped = {}
     for case in CASES:

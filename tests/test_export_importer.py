@@ -166,3 +166,19 @@ def test_decomposed_core_aten_patchify_softmax():
     with torch.no_grad():
         ref = m(x)
     assert torch.allclose(got, ref, rtol=1e-4, atol=1e-5)
+
+
+def test_aten_softmax_half_to_float_gives_fp32():
+    """aten._softmax(x, dim, half_to_float=True) on bf16 x returns fp32."""
+
+    class M(torch.nn.Module):
+        def forward(self, x):
+            return torch.ops.aten._softmax(x, -1, True)
+
+    x = torch.randn(4, 40).bfloat16()
+    ep = torch.export.export(M(), (x,))
+    fn = devproc.from_export(ep, backend="ir")
+    assert [op.name for op in fn.block.ops] == ["to", "softmax"]
+    got = _run_ir(fn, x)[0]
+    assert got.dtype == torch.float32
+    assert torch.allclose(got, torch.softmax(x.float(), -1), rtol=1e-5, atol=1e-7)

@@ -54,7 +54,9 @@ def test_token_pipeline_end_to_end(cuda):
     ir = devproc.from_torch(m, ids, backend="ir")
     ref = interp.run_function(ir, {"l_ids_": ids})[0]
     assert ref.dtype == torch.int32
-    assert (got == ref).float().mean().item() > 0.95
+    top2 = logits.topk(2, dim=-1).values
+    decided = (top2[..., 0] - top2[..., 1]) > tol
+    assert torch.equal(got[decided], ref[decided])
 
 
 def test_save_load_runtime_roundtrip(cuda, tmp_path):
