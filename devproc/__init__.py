@@ -15,7 +15,7 @@ from devproc_b200 import __all__, __version__  # noqa: F401
 _SUBMODULES = [
     "ir", "ir.types", "ir.base", "ir.function", "ir.ops", "ir.verifier", "ir.from_torch", "ir.fx_converter",
     "ir.fx_op_map", "dsl", "dsl.kernel", "dsl.ops", "dsl.types", "runtime", "backend", "backend.base",
-    "backend.b200", "backend.b200.compiler", "backend.b200.program", "backend.b200.lowering",
+    "backend.b200", "backend.b200.compiler", "backend.b200.program", "backend.b200.lowering", "sharded",
 ]
 for _name in _SUBMODULES:
     sys.modules[f"{__name__}.{_name}"] = importlib.import_module(f"devproc_b200.{_name}")

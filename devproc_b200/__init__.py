@@ -109,6 +109,9 @@ def compile(target, *example_inputs, backend: str = "b200", **kwargs):
     return B200Compiler(**kwargs).compile(fn, constants=constants)
 
 
+from .sharded import ShardedRuntime, shard_batch, shard_range  # noqa: E402
+
+
 def save(compiled_program, path: str) -> None:
     """Write ``path`` (plan), ``path.meta.json`` and, with constants, ``path.weights``."""
     compiled_program.export(path)
@@ -131,4 +134,5 @@ __all__ = [
     "Backend", "CompiledProgram", "BackendError", "UnsupportedOpError", "CompilationError",
     "B200Compiler", "B200CompiledProgram", "TritonCompiler", "TritonCompiledProgram", "TritonRuntime",
     "DevProcError", "Runtime", "compile", "save", "load", "from_torch", "from_export", "TorchExportImporter",
+    "ShardedRuntime", "shard_batch", "shard_range",
 ]

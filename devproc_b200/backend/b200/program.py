@@ -170,6 +170,15 @@ class B200CompiledProgram(CompiledProgram):
             self._bind_slot(self._native, io.slot, ptr, max(1, src.numel()) * src.element_size())
             self._bound[io.slot] = ptr
 
+    def clone(self) -> "B200CompiledProgram":
+        """The same plan and constants with its own arena and output buffers;
+        the device copies of the constants are shared, not uploaded again."""
+        c = B200CompiledProgram(self.spec, self._constants, self.device_id, self.ir_function, self.use_graph)
+        c._dev_consts = self._dev_consts
+        if self._chunk is not None:
+            c.set_stream(self.stream_chunk, self._chunk.spec)
+        return c
+
     def set_stream(self, chunk: int, chunk_spec: ProgramSpec) -> None:
         """Attach the same program compiled for a batch of ``chunk`` samples.
         ``run`` with host inputs then executes it on successive chunks of the

@@ -81,10 +81,12 @@ int kernel_blocks_per_sm(const void *func, int threads, size_t smem, bool max_ca
     *per_sm = it->second;
     return DP_OK;
   }
-  // The opt-in only ever grows, so a smaller launch never revokes a larger one's.
+  // The opt-in only ever grows, so a smaller launch never revokes a larger
+  // one's.  It is granted for every size: static shared memory (barriers)
+  // counts against the same 48 KB default as the dynamic bytes.
   static std::map<std::pair<int, const void *>, size_t> granted;
   size_t &g = granted[{dev, func}];
-  if (smem > 48 * 1024 && smem > g) {
+  if (smem > g) {
     DP_CHECK_CUDA(cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     g = smem;
   }

@@ -319,12 +319,13 @@ def pi05_inputs(batch: int = 64, cams: int = 3, text: int = 48, vocab: int = 257
 
 
 def pi05_flops_per_sample(cams=3, text=48, width=2048, layers=18, heads=8, kv_heads=1, head_dim=256, mlp=16384,
-                          expert_width=1024, expert_layers=18, expert_mlp=4096, horizon=50, action_dim=32, steps=10):
+                          expert_width=1024, expert_layers=18, expert_mlp=4096, horizon=50, action_dim=32, steps=10,
+                          vit_layers=27):
     """Multiply-add FLOPs (2 per MAC) of one sample: vision, projection,
     prefill and the denoise steps (GEMMs and attention)."""
     img = cams * 256
     prefix = img + text
-    vision = cams * vit_flops_per_image(classes=0)
+    vision = cams * vit_flops_per_image(layers=vit_layers, classes=0)
     proj = 2 * img * 1152 * width
     qkvo = 2 * width * head_dim * (2 * heads + 2 * kv_heads)
     prefill = layers * (prefix * (qkvo + 2 * 3 * width * mlp) + 2 * 2 * heads * prefix * prefix * head_dim)

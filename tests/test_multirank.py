@@ -1,11 +1,13 @@
-"""Batch sharding across ranks (host side, 2 gloo ranks on the CPU).
+"""Batch sharding and the final gather of ``ShardedRuntime`` on 2 gloo ranks (CPU).
 
-Each rank of the weak-scaled pipeline compiles the same program and runs its
-own shard of images; results are combined only for checking.  Here the ranks
-run the compile step and the CPU oracle on their shard and gather through
-gloo: the union of the shards must equal the single-process result, a rank
-that fails must surface as an error on the others, and no data-path
-collective is needed for correctness.
+Each rank builds ``devproc.ShardedRuntime`` for its shard of a global batch of
+images, exactly as a GPU job does, and runs several steps through ``run``:
+the product's shard selection, double-buffered program alternation and
+gather-to-rank-0 code.  On the CPU the compiled plan cannot execute, so the
+runtime wraps a stand-in program that evaluates the same IR with the CPU
+oracle; everything else is the product's code.  Rank 0's gathered result of
+every step must equal the single-process oracle result of the global batch;
+a rank that fails must surface as an error instead of a hang.
 """
 
 import os
@@ -27,9 +29,30 @@ def _free_port():
     return port
 
 
-def _shard(total, rank, world):
-    per = total // world
-    return rank * per, (rank + 1) * per
+class _OracleProgram:
+    """CPU stand-in for a compiled program: same spec, the oracle computes."""
+
+    def __init__(self, prog, ir):
+        self.spec, self.ir, self.device_id = prog.spec, ir, None
+        self.runs = 0
+
+    def run(self, *args, to_cpu=True, **kwargs):
+        from oracle import interp
+        self.runs += 1
+        return interp.run_function(self.ir, kwargs)
+
+    def clone(self):
+        return _OracleProgram(self, self.ir)
+
+    def synchronize(self):
+        pass
+
+    def close(self):
+        pass
+
+
+def _global_batch(step):
+    return workloads.preprocess_images(8, 48, 64, seed=100 + step)
 
 
 def _worker(rank, world, port, fail_rank, q):
@@ -39,20 +62,24 @@ def _worker(rank, world, port, fail_rank, q):
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
     try:
         import devproc
-        from oracle import interp
-        imgs = workloads.preprocess_images(8, 48, 64, seed=0)
-        lo, hi = _shard(8, rank, world)
-        mine = imgs[lo:hi]
-        ir = devproc.parse_ir(workloads.vision_preprocess, mine)
-        prog = devproc.compile(workloads.vision_preprocess, mine)
+        mine0 = devproc.shard_batch(_global_batch(0), rank, world)
+        assert mine0.shape[0] == 8 // world
+        prog = devproc.compile(workloads.vision_preprocess, mine0)  # host-only: the plan this rank would run
         assert [r["kernel"] for r in prog.spec.records] == ["preproc"]
+        ir = devproc.parse_ir(workloads.vision_preprocess, mine0)
+        rt = devproc.ShardedRuntime(program=_OracleProgram(prog, ir), gather=True)
+        assert (rt.rank, rt.world_size) == (rank, world) and rt.global_batch() == 8
         if rank == fail_rank:
             raise RuntimeError("injected failure on rank %d" % rank)
-        out = interp.run_function(ir, {"images": mine})[0].float()
-        gathered = [torch.empty_like(out) for _ in range(world)]
-        dist.all_gather(gathered, out)
+        results = []
+        for step in range(3):
+            out = rt.run(images=rt.shard_batch(_global_batch(step)))
+            if rank == 0:
+                results.append(out[0].float().numpy().copy())
+        rt.synchronize()
+        assert [p.runs for p in rt._progs] == [2, 1]  # the two program copies alternate
         if rank == 0:
-            q.put(("ok", torch.cat(gathered).numpy().copy()))
+            q.put(("ok", results))
     except Exception as e:  # report, then let the process group time out on the others
         q.put(("err", f"rank {rank}: {e}"))
     finally:
@@ -86,19 +113,29 @@ def _run(world, fail_rank=-1):
     return out
 
 
-def test_two_rank_shards_equal_single_process():
+def test_sharded_runtime_gathers_every_step_to_rank0():
     results = _run(2)
     oks = [r for r in results if r[0] == "ok"]
     assert len(oks) == 1, results
     import devproc
     from oracle import interp
-    imgs = workloads.preprocess_images(8, 48, 64, seed=0)
-    ir = devproc.parse_ir(workloads.vision_preprocess, imgs)
-    full = interp.run_function(ir, {"images": imgs})[0].float()
-    assert torch.equal(torch.from_numpy(oks[0][1]), full)
+    for step, got in enumerate(oks[0][1]):
+        imgs = _global_batch(step)
+        ir = devproc.parse_ir(workloads.vision_preprocess, imgs)
+        full = interp.run_function(ir, {"images": imgs})[0].float()
+        assert torch.equal(torch.from_numpy(got), full), f"step {step}"
 
 
 def test_failing_rank_is_reported_not_hung():
     results = _run(2, fail_rank=1)
     errs = [r for r in results if r[0] == "err"]
     assert any("injected failure on rank 1" in e[1] for e in errs), results
+
+
+def test_shard_ranges():
+    import devproc
+    assert [devproc.shard_range(256, r, 8) for r in (0, 7)] == [(0, 32), (224, 256)]
+    with pytest.raises(ValueError):
+        devproc.shard_range(10, 0, 4)
+    with pytest.raises(ValueError):
+        devproc.shard_range(8, 2, 2)
