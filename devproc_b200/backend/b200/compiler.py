@@ -15,6 +15,8 @@ import torch
 from ...ir.function import Function
 from ...ir.verifier import IRVerifier
 from ..base import Backend, CompilationError
+from ..host_ops import split_host_ops
+from .host_program import HostDeviceProgram
 from .lowering import lower
 from .program import B200CompiledProgram, ProgramSpec
 from .rebatch import batch_factors, rebatch
@@ -44,6 +46,11 @@ class B200Compiler(Backend):
             v = IRVerifier(ir_function)
             if not v.verify():
                 raise CompilationError("IR verification failed: " + "; ".join(v.get_errors()))
+        split = split_host_ops(ir_function)
+        if split is not None:  # tokenizer / string / dict ops run on the host around one device plan
+            prologue, sub, epilogue, dev_in, dev_out = split
+            device = self.compile(sub, constants) if sub.block.ops else None
+            return HostDeviceProgram.from_split(ir_function, prologue, device, epilogue, dev_in, dev_out)
         consts = dict(getattr(ir_function, "constants", {}) or {})
         consts.update(constants or {})
         low = lower(ir_function, const_names=consts.keys(), const_tensors=consts)

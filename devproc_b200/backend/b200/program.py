@@ -372,12 +372,17 @@ class B200CompiledProgram(CompiledProgram):
             json.dump(meta, f, indent=1)
 
     @staticmethod
-    def load(path: str, device_id: int = 0) -> "B200CompiledProgram":
+    def load(path: str, device_id: int = 0, host_ok: bool = True):
+        """Rebuild a saved program; one saved with host steps (tokenizer, string
+        or dict ops) comes back as a HostDeviceProgram around its device plan."""
         path = str(path)
         with open(path + ".meta.json") as f:
             meta = json.load(f)
         if meta.get("format") != FORMAT or meta.get("version") != FORMAT_VERSION:
             raise ValueError(f"{path}: not a {FORMAT} v{FORMAT_VERSION} program")
+        if host_ok and "host" in meta:
+            from .host_program import HostDeviceProgram
+            return HostDeviceProgram.from_meta(path, meta, device_id)
         with open(path, "rb") as f:
             plan = f.read()
         if len(plan) != meta["plan_bytes"]:

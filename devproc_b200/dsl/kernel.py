@@ -110,14 +110,19 @@ def kernel(func: Callable) -> Callable:
                     ctx.ir_function.add_input(v)
                     ctx.param_map[pname] = v
                     wrapped.append(KernelTensor(v, pname))
+                elif isinstance(a, str):
+                    # a host string input (the text a tokenizer step encodes); the example's value is unused
+                    from .ops import string_input
+                    wrapped.append(string_input(pname))
                 else:
-                    raise TypeError(f"Expected torch.Tensor, got {type(a)}")
+                    raise TypeError(f"Expected torch.Tensor or str, got {type(a)}")
             result = func(*wrapped, **kwargs)
             if isinstance(result, KernelTensor):
                 ctx.set_output(result)
                 ctx.ir_function.output = result.ir_value
-            elif isinstance(result, (tuple, list)) and result and all(
-                    isinstance(r, KernelTensor) for r in result):
+            elif hasattr(result, "ir_value"):  # a host value (string, dict) returned by the kernel
+                ctx.ir_function.output = result.ir_value
+            elif isinstance(result, (tuple, list)) and result and all(hasattr(r, "ir_value") for r in result):
                 ctx.ir_function.outputs = [r.ir_value for r in result]
             return ctx.ir_function
         finally:
