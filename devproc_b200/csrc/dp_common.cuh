@@ -170,11 +170,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// try_wait may suspend the thread until the phase completes or a time hint
+// passes; DP_MBAR_HINT selects the hint form (build switch for tuning).
+#ifndef DP_MBAR_HINT
+#define DP_MBAR_HINT ", 100000"
+#endif
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2" DP_MBAR_HINT ";\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(phase)
@@ -187,7 +192,7 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t ph
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, 100000;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2" DP_MBAR_HINT ";\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(smem_u32(bar)), "r"(phase)

@@ -99,6 +99,7 @@ struct Shape {
   int bcast;         // operands shared by every batch (zero batch strides): 1 A, 2 B, 4 residual
   int tf32;          // operands are fp32 multiplied as TF32 (kind::tf32); else bf16 (kind::f16)
   int box_k;         // K elements per 128-byte operand box: 64 bf16 or 32 fp32
+  int last_boxes;    // boxes of the last K stage that lie inside K (the rest are zero fill)
 };
 
 // ------------------------------------------------------------------ PTX
@@ -254,6 +255,20 @@ __device__ __forceinline__ void mma_commit(uint64_t *bar) {
   }
 }
 
+// One lane of a converged warp (the lowest), as elect.sync picks it.  The
+// producer and MMA roles run their loops on the whole warp and issue each
+// TMA / tcgen05 instruction from the elected lane, so every value the
+// instructions take is warp-uniform.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t.reg .b32 R;\n\t"
+      "elect.sync R|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -366,8 +381,33 @@ __device__ __forceinline__ bool aborted(volatile int *flag) { return *flag != 0;
 // at most 2 s in total; on giving up records DP_DEVERR_TIMEOUT and raises the
 // abort flag so that the other roles stop too.
 // kClusterScope: the barrier also collects arrivals from the peer CTA.
+// Non-blocking probe of a barrier phase (no suspension of the thread).
+template <bool kClusterScope>
+__device__ __forceinline__ bool mbar_test(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  if constexpr (kClusterScope)
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  else
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+  return ok != 0;
+}
+
 template <bool kClusterScope = false>
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, int site, volatile int *flag) {
+  // Fast path first: a phase that is already complete needs no abort-flag read.
+  if (mbar_test<kClusterScope>(bar, parity)) return true;
   for (int slice = 0; slice < 10; ++slice) {
     if (aborted(flag)) return false;
     if (mbar_wait_for<kClusterScope>(bar, parity, 200000000ull)) return true;
@@ -441,8 +481,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int *flag = &abort_flag;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer
+    {
+      // ---------------- TMA producer (whole warp; the elected lane issues)
       int it = 0;
       for (int t = cid; t < s.num_tiles && !aborted(flag); t += nclusters) {
         int b, tm, tn;
@@ -459,39 +499,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t *sb = sa + Cfg<CG>::kKBoxes * kTileABytes;
           uint64_t *bar_local = &full[st];
           uint32_t bar_pair = 0;
-          if constexpr (CG == 1) {
-            mbar_arrive_expect_tx(bar_local, kStageBytes);
-          } else {
-            // Both CTAs' bytes complete on the leader's barrier, which expects them all.
-            if (rank == 0) mbar_arrive_expect_tx(bar_local, 2 * kStageBytes);
-            bar_pair = cluster_addr(bar_local, 0);
-          }
+          if constexpr (CG == 2) bar_pair = cluster_addr(bar_local, 0);
           auto load = [&](void *dst, const CUtensorMap *map, int x, int y, int z) {
             if constexpr (CG == 1)
               tma_load_4d(dst, map, x, y, z, s.batch2, bar_local);
             else
               tma_load_4d_pair(dst, map, x, y, z, s.batch2, bar_pair);
           };
-#pragma unroll
-          for (int kh = 0; kh < Cfg<CG>::kKBoxes; ++kh) {
-            const int k0 = (kb * Cfg<CG>::kKBoxes + kh) * s.box_k;
-            load(sa + kh * kTileABytes, &map_a, k0, row0, ba);
-            uint8_t *sbk = sb + kh * b_box_bytes<CG>();
-            if (s.b_mn) {
-#pragma unroll
-              for (int j = 0; j < Cfg<CG>::kBRows / 64; ++j) load(sbk + j * 8192, &map_b, col0 + j * 64, k0, bb);
+          if (elect_one()) {
+            if constexpr (CG == 1) {
+              mbar_arrive_expect_tx(bar_local, kStageBytes);
             } else {
-              load(sbk, &map_b, k0, col0, bb);
+              // Both CTAs' bytes complete on the leader's barrier, which expects them all.
+              if (rank == 0) mbar_arrive_expect_tx(bar_local, 2 * kStageBytes);
+            }
+#pragma unroll
+            for (int kh = 0; kh < Cfg<CG>::kKBoxes; ++kh) {
+              const int k0 = (kb * Cfg<CG>::kKBoxes + kh) * s.box_k;
+              load(sa + kh * kTileABytes, &map_a, k0, row0, ba);
+              uint8_t *sbk = sb + kh * b_box_bytes<CG>();
+              if (s.b_mn) {
+#pragma unroll
+                for (int j = 0; j < Cfg<CG>::kBRows / 64; ++j) load(sbk + j * 8192, &map_b, col0 + j * 64, k0, bb);
+              } else {
+                load(sbk, &map_b, k0, col0, bb);
+              }
             }
           }
+          __syncwarp();
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0 && rank == 0) {
-      // ---------------- MMA issuer (the leader CTA's, for a pair)
+    if (rank == 0) {
+      // ---------------- MMA issuer (the leader CTA's, for a pair; whole warp, the elected lane issues)
       const uint32_t idesc = instr_desc(BM * CG, BN, s.b_mn, s.tf32 ? 2u : 1u);
       const bool tf32 = s.tf32 != 0;
+      const bool b_mn = s.b_mn != 0;
+      const uint32_t b_kstep = b_mn ? 2048u : 32u;  // bytes per 16-deep K step of B (MN-major: 16 rows of 128 B)
       int it = 0, local = 0;
       for (int t = cid; t < s.num_tiles && !aborted(flag); t += nclusters, ++local) {
         const int a = local & 1;
@@ -506,22 +551,28 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
+          // Descriptors of the stage's first K step; later steps add their byte
+          // offset >> 4 to the 14-bit address field (shared addresses stay
+          // below 256 KB, so the field never carries).
           const uint32_t sa = smem_u32(smem + st * kStageBytes);
           const uint32_t sb = sa + Cfg<CG>::kKBoxes * kTileABytes;
+          const uint64_t a_desc0 = smem_desc(sa);
+          const uint64_t b_desc0 = b_mn ? smem_desc_mn(sb) : smem_desc(sb);
+          const int kh_end = kb + 1 == s.k_blocks ? s.last_boxes : Cfg<CG>::kKBoxes;  // boxes past K hold zeros only
 #pragma unroll
           for (int kh = 0; kh < Cfg<CG>::kKBoxes; ++kh) {
-            if (kh > 0 && (kb * Cfg<CG>::kKBoxes + kh) * s.box_k >= s.K) break;  // box past K: zeros only
-            const uint32_t ak = sa + kh * kTileABytes, bk = sb + kh * b_box_bytes<CG>();
+            if (kh >= kh_end) break;
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k) {
-              const uint64_t bdesc = s.b_mn ? smem_desc_mn(bk + k * 2048) : smem_desc(bk + k * 32);
-              mma_issue<CG>(tmem_d, smem_desc(ak + k * 32), bdesc, idesc, (kb | kh | k) != 0, tf32);
+              const uint64_t adesc = a_desc0 + (uint64_t)((kh * kTileABytes + k * 32) >> 4);
+              const uint64_t bdesc = b_desc0 + (uint64_t)((kh * b_box_bytes<CG>() + k * b_kstep) >> 4);
+              if (elect_one()) mma_issue<CG>(tmem_d, adesc, bdesc, idesc, (kb | kh | k) != 0, tf32);
             }
           }
-          mma_commit<CG>(&empty[st]);  // stage is free (in both CTAs) once these MMAs have read it
+          if (elect_one()) mma_commit<CG>(&empty[st]);  // stage is free (in both CTAs) once these MMAs have read it
         }
         if (!ok) break;
-        mma_commit<CG>(&acc_full[a]);  // accumulator complete
+        if (elect_one()) mma_commit<CG>(&acc_full[a]);  // accumulator complete
       }
     }
   } else if (warp >= 4) {
@@ -863,6 +914,7 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   s.num_tiles = s.tiles_per_batch * s.batch;
   const int kstep = box_k * (cg == 2 ? Cfg<2>::kKBoxes : Cfg<1>::kKBoxes);  // K per stage
   s.k_blocks = (int)((p.K + kstep - 1) / kstep);
+  s.last_boxes = (int)((p.K - (int64_t)(s.k_blocks - 1) * kstep + box_k - 1) / box_k);
   DP_REQUIRE(tma_store || !(p.epilogue & DP_EPI_SOFTMAX), DP_ERR_UNSUPPORTED,
              "gemm: the softmax epilogue needs a 16-byte aligned C with 16-byte row strides");
   s.batch2 = (int)b2;
