@@ -52,10 +52,10 @@ DP_PLAN_MAGIC, DP_PLAN_VERSION = 0x32425044, 1
 DP_NOALLOC_ARENA_BYTES = 64 << 20
 DP_RECORD_MAX_OPERANDS, DP_RECORD_PARAM_BYTES = 8, 1280
 DP_SLOT_BOUND, DP_SLOT_ARENA = 0, 1
-DP_K_PREPROC, DP_K_ROWREDUCE, DP_K_GEMM, DP_K_REGION, DP_K_EMBEDDING, DP_K_COPY, DP_K_ATTENTION, DP_K_ROPE = \
-    range(1, 9)
+DP_K_PREPROC, DP_K_ROWREDUCE, DP_K_GEMM, DP_K_REGION, DP_K_EMBEDDING, DP_K_COPY, DP_K_ATTENTION, DP_K_ROPE, \
+    DP_K_SPLITK = range(1, 10)
 KERNEL_NAMES = {1: "preproc", 2: "rowreduce", 3: "gemm", 4: "region", 5: "embedding", 6: "copy", 7: "attention",
-                8: "rope"}
+                8: "rope", 9: "splitk"}
 
 
 class PreprocParams(ctypes.Structure):
@@ -83,6 +83,10 @@ class GemmParams(ctypes.Structure):
                 ("bias_dtype", ctypes.c_int32), ("alpha", ctypes.c_float),
                 ("batch2", ctypes.c_int64), ("stride_a2", ctypes.c_int64), ("stride_b2", ctypes.c_int64),
                 ("stride_c2", ctypes.c_int64), ("stride_r2", ctypes.c_int64)]
+
+
+class SplitKParams(ctypes.Structure):
+    _fields_ = [("gemm", GemmParams), ("splits", ctypes.c_int64), ("slice_stride", ctypes.c_int64)]
 
 
 class RegionDesc(ctypes.Structure):
@@ -138,7 +142,7 @@ class PlanRecord(ctypes.Structure):
 
 PARAM_STRUCTS = {DP_K_PREPROC: PreprocParams, DP_K_ROWREDUCE: RowReduceParams, DP_K_GEMM: GemmParams,
                  DP_K_REGION: RegionDesc, DP_K_EMBEDDING: EmbeddingParams, DP_K_ATTENTION: AttentionParams,
-                 DP_K_ROPE: RopeParams}
+                 DP_K_ROPE: RopeParams, DP_K_SPLITK: SplitKParams}
 
 # (symbol, argtypes) of every exported function, in header order.
 _VP = ctypes.c_void_p
@@ -153,6 +157,7 @@ EXPORTS = {
     "dp_preproc": [ctypes.POINTER(PreprocParams), _VP, _VP, _VP],
     "dp_rowreduce": [ctypes.POINTER(RowReduceParams), _VP, _VP, _VP, _VP, _VP],
     "dp_gemm": [ctypes.POINTER(GemmParams), _VP, _VP, _VP, _VP, _VP, _VP],
+    "dp_gemm_splitk_reduce": [ctypes.POINTER(SplitKParams), _VP, _VP, _VP, _VP, _VP],
     "dp_region": [ctypes.POINTER(RegionDesc), ctypes.POINTER(_VP), _VP],
     "dp_embedding": [ctypes.POINTER(EmbeddingParams), _VP, _VP, _VP, _VP],
     "dp_attention": [ctypes.POINTER(AttentionParams), _VP, _VP, _VP, _VP, _VP],
@@ -273,6 +278,11 @@ def rowreduce(p: RowReduceParams, x, out, weight=None, bias=None, stream=None) -
 def gemm(p: GemmParams, a, b, c, bias=None, residual=None, stream=None) -> None:
     check(lib().dp_gemm(ctypes.byref(p), _ptr(a), _ptr(b), _ptr(c), _ptr(bias), _ptr(residual),
                         _stream(stream)), "dp_gemm")
+
+
+def gemm_splitk_reduce(p: SplitKParams, workspace, c, bias=None, residual=None, stream=None) -> None:
+    check(lib().dp_gemm_splitk_reduce(ctypes.byref(p), _ptr(workspace), _ptr(c), _ptr(bias), _ptr(residual),
+                                      _stream(stream)), "dp_gemm_splitk_reduce")
 
 
 def region(d: RegionDesc, operands, stream=None) -> None:

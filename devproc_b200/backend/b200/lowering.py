@@ -186,6 +186,43 @@ class Lowered:
         return b"".join(out)
 
 
+# ------------------------------------------------------------- split-K
+_SMS = 148  # B200
+
+
+def splitk_factor(M: int, N: int, K: int, tf32: bool, b_layout: int) -> int:
+    """Number of K slices for a tensor-core GEMM, 1 = no split.
+
+    Tiles: 256 x 256 on CTA pairs (74 per GPU) when M and N exceed one CTA's
+    share, else 128 x 256 on single CTAs; a stage covers 128 bf16 or 64 TF32
+    K.  A GEMM with fewer tiles than half the pairs and at least 8 stages is
+    split when the modelled time - waves x (stages per slice + 3 for pipeline
+    fill and epilogue) at 1 us per stage, plus 3 us and the workspace traffic
+    at 5 TB/s for the reduction - drops by 10 % or more.  Slices are whole
+    stages (S divides the stage count) so every slice's K is the same.
+    """
+    cg = 2 if (M > 128 and N > 128) else 1
+    pairs = _SMS // cg
+    tiles = -(-M // (128 * cg)) * -(-N // 256)
+    box_k = 32 if tf32 else 64
+    kstep = box_k * (2 if cg == 2 else 1)
+    if K % kstep or tiles * 2 > pairs:
+        return 1
+    kb = K // kstep
+    if kb < 8:
+        return 1
+
+    def cost(S):
+        t = -(-tiles * S // pairs) * (kb / S + 3.0)
+        return t + (3.0 + (S + 1) * M * N * 4 / 5e6 if S > 1 else 0.0)
+
+    best, best_s = cost(1), 1
+    for S in range(2, 17):
+        if kb % S == 0 and cost(S) < best:
+            best, best_s = cost(S), S
+    return best_s if best <= 0.9 * cost(1) else 1
+
+
 class Lowerer:
     use_fused_attention = True  # bf16 sdpa as one fused tensor-core kernel (else GEMM + softmax + GEMM)
 
@@ -893,8 +930,32 @@ class Lowerer:
         kind = "3xtf32" if tf32 else a_dtype
         if tf32:
             flops = 2 * p.M * p.N * (p.K // 3) * p.batch  # the work of the fp32 product
-        self.emit(N.DP_K_GEMM, ops_, p, f"gemm {op.name} M{p.M} N{p.N} K{p.K} b{p.batch} {kind} epi{epi}",
-                  flops, nb)
+        label = f"gemm {op.name} M{p.M} N{p.N} K{p.K} b{p.batch} {kind} epi{epi}"
+        splits = 1
+        if p.batch == 1 and not shared_rows and not (epi & N.DP_EPI_SOFTMAX) and (tf32 or a_dtype == "bfloat16"):
+            splits = splitk_factor(p.M, p.N, p.K, tf32, p.b_layout)
+        if splits == 1:
+            self.emit(N.DP_K_GEMM, ops_, p, label, flops, nb)
+            return
+        # Split K: a batched GEMM over the K slices writes raw fp32 partial
+        # products to a workspace [S, M, N]; the reduce record sums them in
+        # slice order and applies the epilogue.
+        ws = self.new_buffer("arena", "float32", (splits, p.M, p.N), f"{cur.name}_splitk")
+        g = N.GemmParams.from_buffer_copy(bytes(p))
+        ks = p.K // splits
+        g.K, g.batch = ks, splits
+        g.stride_a = ks
+        g.stride_b = ks if p.b_layout == N.DP_B_NK else ks * p.ldb
+        g.c_dtype, g.ldc, g.stride_c = N.DP_F32, p.N, p.M * p.N
+        g.epilogue, g.alpha, g.bias_dtype, g.r_dtype, g.ldr, g.stride_r = 0, 0.0, 0, 0, 0, 0
+        self.emit(N.DP_K_GEMM, [a_buf.buf, b_buf.buf, ws, None, None], g, f"{label} splitk{splits}", flops,
+                  nb - out.buf.nbytes + ws.nbytes)
+        sp = N.SplitKParams()
+        sp.gemm = p
+        sp.splits, sp.slice_stride = splits, p.M * p.N
+        self.emit(N.DP_K_SPLITK, [ws, out.buf, bias.buf if bias is not None else None,
+                                  residual.buf if residual is not None else None], sp,
+                  f"splitk reduce {splits}x{p.M}x{p.N} epi{epi}", 0, ws.nbytes + out.buf.nbytes)
 
     # ------------------------------------------------------ row reductions
     def lower_rowreduce(self, op: Op) -> None:

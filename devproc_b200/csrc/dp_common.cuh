@@ -60,6 +60,8 @@ int launch_embedding(const dp_embedding_params &p, const void *ids, const void *
                      void *out, cudaStream_t s);
 int launch_rope(const dp_rope_params &p, const void *x, const void *cos, const void *sin, void *out,
                 cudaStream_t s);
+int launch_splitk_reduce(const dp_splitk_params &p, const void *ws, void *C, const void *bias, const void *res,
+                         cudaStream_t s);
 
 }  // namespace dp
 

@@ -94,6 +94,12 @@ int run_records(dp_program *prog, cudaStream_t s) {
         if (e != cudaSuccess) st = dp::cuda_status(e, "program copy record");
         break;
       }
+      case DP_K_SPLITK: {
+        dp_splitk_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_splitk_reduce(p, ops[0], const_cast<void *>(ops[1]), ops[2], ops[3], s);
+        break;
+      }
       default:
         st = dp::set_error(DP_ERR_PLAN, "program: unknown record kind " + std::to_string(rec.kernel));
     }

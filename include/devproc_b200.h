@@ -169,6 +169,24 @@ typedef struct dp_gemm_params {
 int dp_gemm(const dp_gemm_params *p, const void *A, const void *B, void *C,
             const void *bias, const void *residual, void *stream);
 
+/* ---- split-K reduction ------------------------------------------------------
+ * Second half of a GEMM whose K range was split into ``splits`` slices: the
+ * first half is dp_gemm batched over the slices (A and B advanced by the
+ * slice's K offset, fp32 C = the workspace, no epilogue), which leaves raw
+ * partial products in workspace[s][m][n] (slice s at s · slice_stride
+ * elements, rows of N).  This sums the slices in slice order (the same bits
+ * every run) and applies ``gemm``'s epilogue (alpha, bias, activation,
+ * residual or gate operand) and output dtype, writing C [M, N] (ldc).
+ * ``gemm.batch`` must be 1.  Same role as the reference's launch_matmul /
+ * launch_linear (src/devproc/backend/triton/templates/matmul.py:230-296),
+ * which had no split-K. */
+typedef struct dp_splitk_params {
+  dp_gemm_params gemm;
+  int64_t splits, slice_stride;
+} dp_splitk_params;
+int dp_gemm_splitk_reduce(const dp_splitk_params *p, const void *workspace, void *C, const void *bias,
+                          const void *residual, void *stream);
+
 /* ---- elementwise region (one kernel per fused IR dataflow region) --------
  * A small register program run per element of an iteration space of up to
  * DP_REGION_MAX_RANK dims.  Operands 0..n_in-1 are inputs, n_in.. are
@@ -278,7 +296,7 @@ int dp_rope(const dp_rope_params *p, const void *x, const void *cos, const void 
 enum { DP_SLOT_BOUND = 0, DP_SLOT_ARENA = 1 };
 enum {
   DP_K_PREPROC = 1, DP_K_ROWREDUCE = 2, DP_K_GEMM = 3, DP_K_REGION = 4,
-  DP_K_EMBEDDING = 5, DP_K_COPY = 6, DP_K_ATTENTION = 7, DP_K_ROPE = 8
+  DP_K_EMBEDDING = 5, DP_K_COPY = 6, DP_K_ATTENTION = 7, DP_K_ROPE = 8, DP_K_SPLITK = 9
 };
 typedef struct dp_plan_header {
   uint32_t magic, version, n_slots, n_records;
