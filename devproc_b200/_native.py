@@ -41,6 +41,7 @@ DP_B_NK, DP_B_KN = 0, 1
 DP_EPI_BIAS, DP_EPI_RELU, DP_EPI_GELU_ERF, DP_EPI_GELU_TANH, DP_EPI_RESIDUAL, DP_EPI_SILU = 1, 2, 4, 8, 16, 32
 DP_EPI_SOFTMAX = 64
 DP_EPI_MUL = 128
+DP_EPI_ARGMAX = 256
 
 DP_REGION_MAX_OPERANDS, DP_REGION_MAX_RANK, DP_REGION_MAX_INSTR = 8, 6, 64
 DP_REGION_MAX_CONST, DP_REGION_MAX_REGS = 32, 8
@@ -53,9 +54,9 @@ DP_NOALLOC_ARENA_BYTES = 64 << 20
 DP_RECORD_MAX_OPERANDS, DP_RECORD_PARAM_BYTES = 8, 1280
 DP_SLOT_BOUND, DP_SLOT_ARENA = 0, 1
 DP_K_PREPROC, DP_K_ROWREDUCE, DP_K_GEMM, DP_K_REGION, DP_K_EMBEDDING, DP_K_COPY, DP_K_ATTENTION, DP_K_ROPE, \
-    DP_K_SPLITK = range(1, 10)
+    DP_K_SPLITK, DP_K_ARGMAX_KEYS = range(1, 11)
 KERNEL_NAMES = {1: "preproc", 2: "rowreduce", 3: "gemm", 4: "region", 5: "embedding", 6: "copy", 7: "attention",
-                8: "rope", 9: "splitk"}
+                8: "rope", 9: "splitk", 10: "argmax_keys"}
 
 
 class PreprocParams(ctypes.Structure):
@@ -87,6 +88,10 @@ class GemmParams(ctypes.Structure):
 
 class SplitKParams(ctypes.Structure):
     _fields_ = [("gemm", GemmParams), ("splits", ctypes.c_int64), ("slice_stride", ctypes.c_int64)]
+
+
+class ArgmaxKeysParams(ctypes.Structure):
+    _fields_ = [("n", ctypes.c_int64), ("mode", ctypes.c_int32), ("out_dtype", ctypes.c_int32)]
 
 
 class RegionDesc(ctypes.Structure):
@@ -142,7 +147,7 @@ class PlanRecord(ctypes.Structure):
 
 PARAM_STRUCTS = {DP_K_PREPROC: PreprocParams, DP_K_ROWREDUCE: RowReduceParams, DP_K_GEMM: GemmParams,
                  DP_K_REGION: RegionDesc, DP_K_EMBEDDING: EmbeddingParams, DP_K_ATTENTION: AttentionParams,
-                 DP_K_ROPE: RopeParams, DP_K_SPLITK: SplitKParams}
+                 DP_K_ROPE: RopeParams, DP_K_SPLITK: SplitKParams, DP_K_ARGMAX_KEYS: ArgmaxKeysParams}
 
 # (symbol, argtypes) of every exported function, in header order.
 _VP = ctypes.c_void_p
@@ -158,6 +163,7 @@ EXPORTS = {
     "dp_rowreduce": [ctypes.POINTER(RowReduceParams), _VP, _VP, _VP, _VP, _VP],
     "dp_gemm": [ctypes.POINTER(GemmParams), _VP, _VP, _VP, _VP, _VP, _VP],
     "dp_gemm_splitk_reduce": [ctypes.POINTER(SplitKParams), _VP, _VP, _VP, _VP, _VP],
+    "dp_argmax_keys": [ctypes.POINTER(ArgmaxKeysParams), _VP, _VP, _VP],
     "dp_region": [ctypes.POINTER(RegionDesc), ctypes.POINTER(_VP), _VP],
     "dp_embedding": [ctypes.POINTER(EmbeddingParams), _VP, _VP, _VP, _VP],
     "dp_attention": [ctypes.POINTER(AttentionParams), _VP, _VP, _VP, _VP, _VP],
@@ -283,6 +289,10 @@ def gemm(p: GemmParams, a, b, c, bias=None, residual=None, stream=None) -> None:
 def gemm_splitk_reduce(p: SplitKParams, workspace, c, bias=None, residual=None, stream=None) -> None:
     check(lib().dp_gemm_splitk_reduce(ctypes.byref(p), _ptr(workspace), _ptr(c), _ptr(bias), _ptr(residual),
                                       _stream(stream)), "dp_gemm_splitk_reduce")
+
+
+def argmax_keys(p: ArgmaxKeysParams, keys, out=None, stream=None) -> None:
+    check(lib().dp_argmax_keys(ctypes.byref(p), _ptr(keys), _ptr(out), _stream(stream)), "dp_argmax_keys")
 
 
 def region(d: RegionDesc, operands, stream=None) -> None:

@@ -828,6 +828,7 @@ class Lowerer:
         # plain row-major layout of the GEMM's own output.
         sym = (out_shape, contiguous_strides(out_shape))
         pending: List[Op] = []
+        argmax_op = None
         while True:
             nxt = self.single_use(cur)
             if nxt is None or id(nxt) in self.done:
@@ -896,6 +897,12 @@ class Lowerer:
             elif nxt.name == "to" and nxt.attr("dtype") in ("float32", "bfloat16", "float16"):
                 c_dtype = nxt.attr("dtype")
                 last = True
+            elif (nxt.name == "argmax" and op.name == "linear" and p.batch == 1 and not shared_rows
+                  and (tf32 or a_dtype == "bfloat16") and len(shp) >= 1 and shp[-1] == p.N
+                  and nxt.attr("dim", -1) % len(shp) == len(shp) - 1 and not nxt.attr("keepdim", False)):
+                # the row argmax of the GEMM's result, reduced in the epilogue: the logits are never stored
+                argmax_op = nxt
+                last = True
             else:
                 break
             for v in pending:
@@ -903,6 +910,8 @@ class Lowerer:
             pending = []
             self.done.add(id(nxt))
             cur = nxt.outputs[0]
+            if argmax_op is not None:
+                break
             out_shape = tuple(cur.type.shape)
             sym = (out_shape, contiguous_strides(out_shape))
             if last:
@@ -922,6 +931,8 @@ class Lowerer:
             p.r_dtype = N.DTYPE_CODE[residual.buf.dtype]
             p.ldr = p.N
             p.stride_r = p.M * p.N if p.batch > 1 and not shared_rows else 0
+        if argmax_op is not None:
+            return self.emit_gemm_argmax(op, p, tf32, a_dtype, a_buf, b_buf, bias, residual, c_dtype, cur)
         out = self.new_value_view(cur, dtype=c_dtype)
         flops = 2 * p.M * p.N * p.K * p.batch
         ops_ = [a_buf.buf, b_buf.buf, out.buf, bias.buf if bias is not None else None,
@@ -956,6 +967,38 @@ class Lowerer:
         self.emit(N.DP_K_SPLITK, [ws, out.buf, bias.buf if bias is not None else None,
                                   residual.buf if residual is not None else None], sp,
                   f"splitk reduce {splits}x{p.M}x{p.N} epi{epi}", 0, ws.nbytes + out.buf.nbytes)
+
+    def emit_gemm_argmax(self, op, p, tf32, a_dtype, a_buf, b_buf, bias, residual, logits_dtype, idx_val) -> None:
+        """A linear whose only consumer is a row argmax: three records - clear
+        one uint64 key per row, the GEMM with the argmax epilogue (each tile
+        folds its rows' (value, first column) into the keys by atomicMax), and
+        the keys to indices (with a following int cast folded in)."""
+        idx_dtype = idx_val.type.dtype
+        nxt = self.single_use(idx_val)
+        if nxt is not None and nxt.name == "to" and nxt.attr("dtype") in ("int32", "int64"):
+            idx_dtype = nxt.attr("dtype")
+            self.done.add(id(nxt))
+            idx_val = nxt.outputs[0]
+        keys = self.new_buffer("arena", "int64", (p.M,), f"{idx_val.name}_keys")
+        self.emit(N.DP_K_ARGMAX_KEYS, [keys, None], N.ArgmaxKeysParams(p.M, 0, 0), f"argmax keys clear {p.M}", 0,
+                  keys.nbytes)
+        p.epilogue |= N.DP_EPI_ARGMAX
+        p.c_dtype = N.DTYPE_CODE[logits_dtype]
+        p.ldc, p.stride_c = p.N, 0
+        if bias is not None:
+            p.bias_dtype = N.DTYPE_CODE[bias.buf.dtype]
+        if residual is not None:
+            p.r_dtype = N.DTYPE_CODE[residual.buf.dtype]
+            p.ldr = p.N
+        ops_ = [a_buf.buf, b_buf.buf, keys, bias.buf if bias is not None else None,
+                residual.buf if residual is not None else None]
+        flops = 2 * p.M * p.N * (p.K // 3 if tf32 else p.K)
+        kind = "3xtf32" if tf32 else a_dtype
+        self.emit(N.DP_K_GEMM, ops_, p, f"gemm {op.name} M{p.M} N{p.N} K{p.K} b1 {kind} epi{p.epilogue} argmax",
+                  flops, sum(b.nbytes for b in ops_ if b is not None))
+        out = self.new_value_view(idx_val, dtype=idx_dtype)
+        self.emit(N.DP_K_ARGMAX_KEYS, [keys, out.buf], N.ArgmaxKeysParams(p.M, 1, N.DTYPE_CODE[idx_dtype]),
+                  f"argmax keys -> {idx_dtype} {p.M}", 0, keys.nbytes + out.buf.nbytes)
 
     # ------------------------------------------------------ row reductions
     def lower_rowreduce(self, op: Op) -> None:

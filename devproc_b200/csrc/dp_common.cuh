@@ -62,6 +62,7 @@ int launch_rope(const dp_rope_params &p, const void *x, const void *cos, const v
                 cudaStream_t s);
 int launch_splitk_reduce(const dp_splitk_params &p, const void *ws, void *C, const void *bias, const void *res,
                          cudaStream_t s);
+int launch_argmax_keys(const dp_argmax_keys_params &p, void *keys, void *out, cudaStream_t s);
 
 }  // namespace dp
 

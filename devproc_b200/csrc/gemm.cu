@@ -32,6 +32,10 @@ int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C, 
     DP_REQUIRE(p.epilogue == DP_EPI_SOFTMAX, DP_ERR_ARG, "gemm: the softmax epilogue takes no other epilogue flag");
     DP_REQUIRE(p.N <= 256, DP_ERR_UNSUPPORTED, "gemm: the softmax epilogue needs N <= 256");
   }
+  if (p.epilogue & DP_EPI_ARGMAX)
+    DP_REQUIRE(p.batch == 1 && !(p.epilogue & DP_EPI_SOFTMAX) &&
+                   (reinterpret_cast<uintptr_t>(C) & 7) == 0,
+               DP_ERR_ARG, "gemm: the argmax epilogue needs batch 1, no softmax and 8-byte aligned keys");
   const bool tf32 = p.a_dtype == DP_TF32 && p.b_dtype == DP_TF32;
   if ((p.a_dtype == DP_BF16 && p.b_dtype == DP_BF16) || (tf32 && p.b_layout == DP_B_NK)) {
     // operand rows and batch strides must be 16-byte multiples for TMA
@@ -41,8 +45,9 @@ int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C, 
                        p.stride_a2 % v == 0 && p.stride_b2 % v == 0 && al(A) && al(B);
     if (tc_ok) return launch_gemm_tc(p, A, B, C, bias, res, s);
   }
-  DP_REQUIRE(!(p.epilogue & DP_EPI_SOFTMAX), DP_ERR_UNSUPPORTED,
-             "gemm: the softmax epilogue runs only on the tensor-core path (bf16, 16-byte aligned operands)");
+  DP_REQUIRE(!(p.epilogue & (DP_EPI_SOFTMAX | DP_EPI_ARGMAX)), DP_ERR_UNSUPPORTED,
+             "gemm: the softmax and argmax epilogues run only on the tensor-core path (bf16 or TF32, 16-byte "
+             "aligned operands)");
   return launch_gemm_simt(p, A, B, C, bias, res, s);
 }
 

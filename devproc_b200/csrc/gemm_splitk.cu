@@ -1,5 +1,6 @@
-// Split-K reduction: the second half of a GEMM whose K range was split.
+// Helper kernels of the GEMM: the split-K reduction and the argmax keys.
 //
+// Split-K reduction: the second half of a GEMM whose K range was split.
 // A GEMM with few output tiles and a long K (the fp32 token pipeline's
 // M = 1024 linears: 8 or 32 CTA-pair tiles for 74 pairs) leaves most SMs idle
 // if each tile walks all of K.  The lowering then runs it as a batched GEMM
@@ -7,6 +8,10 @@
 // workspace [S, M, N], and this kernel sums the slices in slice order (the
 // same bits every run), applies the GEMM's epilogue (alpha, bias, activation,
 // residual or gate operand) and writes C in its dtype.
+//
+// Argmax keys: a GEMM with the DP_EPI_ARGMAX epilogue reduces each row of its
+// result to one 64-bit key by atomicMax; argmax_keys_kernel zeroes the keys
+// before it and turns them into column indices after it.
 #include "dp_gemm_epilogue.cuh"
 
 namespace dpk_splitk {
@@ -39,6 +44,20 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(dp_splitk_params sp,
   }
 }
 
+__global__ void argmax_keys_kernel(dp_argmax_keys_params p, unsigned long long *keys, void *out) {
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < p.n; i += (int64_t)gridDim.x * blockDim.x) {
+    if (p.mode == 0) {
+      keys[i] = 0ull;
+    } else {
+      const int64_t col = (int64_t)(0xFFFFFFFFu - (uint32_t)(keys[i] & 0xFFFFFFFFull));
+      if (p.out_dtype == DP_I32)
+        static_cast<int32_t *>(out)[i] = (int32_t)col;
+      else
+        static_cast<long long *>(out)[i] = col;
+    }
+  }
+}
+
 }  // namespace dpk_splitk
 
 namespace dp {
@@ -65,7 +84,26 @@ int launch_splitk_reduce(const dp_splitk_params &sp, const void *ws, void *C, co
   return DP_OK;
 }
 
+int launch_argmax_keys(const dp_argmax_keys_params &p, void *keys, void *out, cudaStream_t s) {
+  DP_REQUIRE(keys != nullptr && p.n > 0, DP_ERR_ARG, "argmax_keys: null keys or empty");
+  DP_REQUIRE(p.mode == 0 || p.mode == 1, DP_ERR_ARG, "argmax_keys: mode is 0 (clear) or 1 (indices)");
+  if (p.mode == 1) {
+    DP_REQUIRE(out != nullptr, DP_ERR_ARG, "argmax_keys: null output");
+    DP_REQUIRE(p.out_dtype == DP_I32 || p.out_dtype == DP_I64, DP_ERR_ARG, "argmax_keys: indices are i32 or i64");
+  }
+  int64_t blocks = (p.n + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  dpk_splitk::argmax_keys_kernel<<<(int)blocks, 256, 0, s>>>(p, static_cast<unsigned long long *>(keys), out);
+  DP_CHECK_CUDA(cudaGetLastError());
+  return DP_OK;
+}
+
 }  // namespace dp
+
+extern "C" int dp_argmax_keys(const dp_argmax_keys_params *p, void *keys, void *out, void *stream) {
+  if (!p) return dp::set_error(DP_ERR_ARG, "dp_argmax_keys: null params");
+  return dp::launch_argmax_keys(*p, keys, out, dp::as_stream(stream));
+}
 
 extern "C" int dp_gemm_splitk_reduce(const dp_splitk_params *p, const void *workspace, void *C, const void *bias,
                                      const void *residual, void *stream) {

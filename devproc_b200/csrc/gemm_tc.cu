@@ -363,6 +363,26 @@ __device__ __forceinline__ void epi16(float (&x)[16], int64_t n, int N, int epi,
   }
 }
 
+// Argmax key of value v in column col: order-preserving bits of v in the high
+// word (NaN above everything, -0 as +0) and 0xFFFFFFFF - col in the low word,
+// so the largest key belongs to the first column of the maximum (torch.argmax).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int64_t col) {
+  uint32_t k;
+  if (v != v) {
+    k = 0xFFFFFFFFu;
+  } else {
+    const uint32_t u = v == 0.0f ? 0u : __float_as_uint(v);
+    k = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  return ((unsigned long long)k << 32) | (unsigned long long)(0xFFFFFFFFu - (uint32_t)col);
+}
+
+__device__ __forceinline__ float round_to(float v, int dt) {
+  if (dt == DP_BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  if (dt == DP_F16) return __half2float(__float2half_rn(v));
+  return v;
+}
+
 __device__ __forceinline__ void tile_coords(const Shape &s, int t, int &b, int &tm, int &tn) {
   b = t / s.tiles_per_batch;
   const int r = t - b * s.tiles_per_batch;
@@ -647,7 +667,34 @@ __global__ void __launch_bounds__(kThreads, 1)
         sm_max = gm;
         sm_inv = 1.0f / tot;
       }
-      if (s.tma_store) {
+      if (p.epilogue & DP_EPI_ARGMAX) {
+        // The row's largest key over this warp's columns, then one atomicMax per row.
+        unsigned long long best = 0ull;
+        const int epi = p.epilogue & ~DP_EPI_ARGMAX;
+#pragma unroll 1
+        for (int c = col_lo / 16; c < col_hi / 16; ++c) {
+          const int64_t nb = (int64_t)tn * BN + c * 16;
+          if (nb >= s.N) break;
+          uint32_t r[16];
+          tmem_ld16(tbase + c * 16, r);
+          float x[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e) x[e] = __uint_as_float(r[e]) * (p.alpha != 0.0f ? p.alpha : 1.0f);
+          if (epi) epi16(x, nb, s.N, epi, bias, p.bias_dtype, p.c_dtype != DP_F32);
+#pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            if (nb + e >= s.N) break;
+            float v = x[e];
+            if ((epi & (DP_EPI_RESIDUAL | DP_EPI_MUL)) && m < s.M) {
+              const float rv = load_as_f32(res, ep.r_off + m * p.ldr + nb + e, p.r_dtype);
+              v = res_mul ? v * rv : v + rv;
+            }
+            const unsigned long long k = argmax_key(round_to(v, p.c_dtype), nb + e);
+            best = k > best ? k : best;
+          }
+        }
+        if (m < s.M && best) atomicMax(static_cast<unsigned long long *>(C) + ep.c_off + m, best);
+      } else if (s.tma_store) {
         bool stop = false;
 #pragma unroll 1
         for (int c = col_lo / chunk_cols; c < col_hi / chunk_cols; ++c) {
@@ -885,7 +932,8 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
   if (st != DP_OK) return st;
   const int cb = dtype_bytes(p.c_dtype);
   auto al16 = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
-  const bool tma_store = (p.ldc * cb) % 16 == 0 && (p.batch == 1 || (p.stride_c * cb) % 16 == 0) &&
+  const bool argmax = (p.epilogue & DP_EPI_ARGMAX) != 0;  // C holds one uint64 key per row
+  const bool tma_store = !argmax && (p.ldc * cb) % 16 == 0 && (p.batch == 1 || (p.stride_c * cb) % 16 == 0) &&
                          (b2 == 1 || (p.stride_c2 * cb) % 16 == 0) && al16(C) && (cb == 4 || cb == 2);
   bool tma_res = false;
   if (tma_store) {

@@ -100,6 +100,12 @@ int run_records(dp_program *prog, cudaStream_t s) {
         st = dp::launch_splitk_reduce(p, ops[0], const_cast<void *>(ops[1]), ops[2], ops[3], s);
         break;
       }
+      case DP_K_ARGMAX_KEYS: {
+        dp_argmax_keys_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_argmax_keys(p, const_cast<void *>(ops[0]), const_cast<void *>(ops[1]), s);
+        break;
+      }
       default:
         st = dp::set_error(DP_ERR_PLAN, "program: unknown record kind " + std::to_string(rec.kernel));
     }

@@ -152,7 +152,17 @@ enum {
   DP_EPI_SOFTMAX = 64,
   /* Multiply by the residual operand instead of adding it (excludes
    * DP_EPI_RESIDUAL). */
-  DP_EPI_MUL = 128
+  DP_EPI_MUL = 128,
+  /* Row argmax of the epilogue's result instead of storing it: each output
+   * value (after alpha, bias, activation and residual, rounded to c_dtype)
+   * becomes a key (order-preserving bits << 32 | 0xFFFFFFFF - column; NaN
+   * ranks highest, -0 ranks with +0) and C is a uint64 key per row, updated
+   * with atomicMax, so the largest key is the first column of the maximum.
+   * The keys must be zero before the launch and become indices with
+   * dp_argmax_keys.  batch 1, tensor-core operands, no softmax.  Fuses the
+   * reference's argmax template (templates/reduce.py:11-62) into the GEMM
+   * that produces its input: the logits are never written. */
+  DP_EPI_ARGMAX = 256
 };
 typedef struct dp_gemm_params {
   int64_t M, N, K;
@@ -186,6 +196,15 @@ typedef struct dp_splitk_params {
 } dp_splitk_params;
 int dp_gemm_splitk_reduce(const dp_splitk_params *p, const void *workspace, void *C, const void *bias,
                           const void *residual, void *stream);
+
+/* ---- argmax keys ---------------------------------------------------------
+ * mode 0: keys[0..n) = 0 (before a DP_EPI_ARGMAX GEMM); mode 1: out[i] =
+ * the column index in keys[i] as out_dtype (DP_I32 or DP_I64). */
+typedef struct dp_argmax_keys_params {
+  int64_t n;
+  int32_t mode, out_dtype;
+} dp_argmax_keys_params;
+int dp_argmax_keys(const dp_argmax_keys_params *p, void *keys, void *out, void *stream);
 
 /* ---- elementwise region (one kernel per fused IR dataflow region) --------
  * A small register program run per element of an iteration space of up to
@@ -296,7 +315,8 @@ int dp_rope(const dp_rope_params *p, const void *x, const void *cos, const void 
 enum { DP_SLOT_BOUND = 0, DP_SLOT_ARENA = 1 };
 enum {
   DP_K_PREPROC = 1, DP_K_ROWREDUCE = 2, DP_K_GEMM = 3, DP_K_REGION = 4,
-  DP_K_EMBEDDING = 5, DP_K_COPY = 6, DP_K_ATTENTION = 7, DP_K_ROPE = 8, DP_K_SPLITK = 9
+  DP_K_EMBEDDING = 5, DP_K_COPY = 6, DP_K_ATTENTION = 7, DP_K_ROPE = 8, DP_K_SPLITK = 9,
+  DP_K_ARGMAX_KEYS = 10
 };
 typedef struct dp_plan_header {
   uint32_t magic, version, n_slots, n_records;

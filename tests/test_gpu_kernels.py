@@ -751,3 +751,42 @@ def test_split_k_linear_matches_fp64(cuda, dtype, M, K, Nn):
     assert ((got - ref).abs() <= tol * mag).all(), ((got - ref).abs() / mag).max()
     again = prog.run(x, r)[0]
     assert torch.equal(again.double(), got)  # slices are summed in a fixed order
+
+
+# ------------------------------------------------------- argmax epilogue
+class _LinearArgmax(torch.nn.Module):
+    def __init__(self, k, n, dtype):
+        super().__init__()
+        self.lin = torch.nn.Linear(k, n).to(dtype)
+
+    def forward(self, x):
+        return self.lin(x).argmax(-1).to(torch.int32)
+
+
+@pytest.mark.parametrize("dtype,M,K,Nn", [(torch.float32, 512, 512, 3000), (torch.bfloat16, 300, 256, 1000)])
+def test_argmax_epilogue_matches_oracle_and_breaks_ties_first(cuda, dtype, M, K, Nn):
+    """linear -> argmax lowers to one GEMM whose epilogue folds each row into a
+    (value, first column) key; the logits are never stored.  Indices must equal
+    the oracle's (torch.argmax of the same-dtype logits) on every row whose
+    top-2 gap exceeds the float bar, and columns with identical logits (rows of
+    the weight duplicated, a large shared bias) must give the first column."""
+    torch.manual_seed(1)
+    m = _LinearArgmax(K, Nn, dtype).eval()
+    x = torch.randn(M, K).to(dtype)
+    prog = devproc.compile(m, x)
+    assert [r["kernel"] for r in prog.spec.records][-3:] == ["argmax_keys", "gemm", "argmax_keys"]
+    ir = devproc.from_torch(m, x, backend="ir")
+    name = [v.name for v in ir.inputs if v.name not in ir.constants][0]
+    got = prog.run(x)[0]
+    ref = interp.run_function(ir, {name: x})[0]
+    logits = (x.double() @ m.lin.weight.double().T + m.lin.bias.double())
+    top2 = logits.topk(2, -1).values
+    decided = (top2[:, 0] - top2[:, 1]) > (1e-4 if dtype == torch.float32 else 2e-2) * logits.abs().max()
+    assert decided.float().mean() > 0.5
+    assert got.dtype == torch.int32 and torch.equal(got[decided], ref[decided])
+    with torch.no_grad():  # columns 7, 11 and 700 identical and dominant: every row picks 7
+        m.lin.weight[11] = m.lin.weight[7]
+        m.lin.weight[700] = m.lin.weight[7]
+        m.lin.bias[7] = m.lin.bias[11] = m.lin.bias[700] = 1000.0
+    prog = devproc.compile(m, x)
+    assert (prog.run(x)[0] == 7).all()

@@ -120,10 +120,14 @@ def test_noalloc_binds_sub_range_slots():
         torch.testing.assert_close(out.cpu(), oracle, rtol=1e-4, atol=1e-6)
 
 
+class _ScaledSoftmax(torch.nn.Module):
+    def forward(self, x):
+        return torch.softmax(x * 2.0, dim=-1)
+
+
 def test_noalloc_rejects_plans_over_the_limit():
     _gpu()
-    m = workloads.TokenPipeline().eval()
-    prog = devproc.compile(m, workloads.token_ids())  # 8 x 128 tokens: logits alone are 131 MB
+    prog = devproc.compile(_ScaledSoftmax(), torch.zeros(8192, 4096))  # the scaled input is a 128 MiB intermediate
     assert prog.spec.arena_bytes > N.DP_NOALLOC_ARENA_BYTES
     plan = prog.spec.plan
     st = N.lib().dp_program_run_noalloc(plan, len(plan), None, None, 0, None)
