@@ -135,9 +135,38 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 __device__ __forceinline__ bool aborted(volatile int *f) { return *f != 0; }
+
+// One lane of a converged warp, as elect.sync picks it: the producer and MMA
+// roles run their loops on the whole warp and issue each TMA / tcgen05
+// instruction from the elected lane, so the instructions' operands are
+// warp-uniform (a single-lane loop measured slower in the GEMM).
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t.reg .b32 R;\n\t"
+      "elect.sync R|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+__device__ __forceinline__ bool mbar_done(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(su32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // 0.2 s slices re-reading the abort flag, 2 s in total; on giving up records
-// DP_DEVERR_TIMEOUT and raises the abort flag.
+// DP_DEVERR_TIMEOUT and raises the abort flag.  A phase already complete
+// returns without reading the flag.
 __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, int site, volatile int *flag) {
+  if (mbar_done(bar, parity)) return true;
   for (int slice = 0; slice < 10; ++slice) {
     if (aborted(flag)) return false;
     if (mbar_wait_for(bar, parity, 200000000ull)) return true;
@@ -215,15 +244,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nb = s.kv_blocks;
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------- TMA producer
+    {
+      // ---------------- TMA producer (whole warp; the elected lane issues)
       int it = 0, local = 0;
       for (int item = blockIdx.x; item < s.items && !aborted(flag); item += gridDim.x, ++local) {
         int b, hk, rt;
         item_coords(s, item, b, hk, rt);
         if (!wait_or_abort(&q_empty, (local & 1) ^ 1, 500, flag)) break;
-        mbar_arrive_expect_tx(&q_full, s.q_bytes);
-        for (int x = 0; x < s.nd; ++x) tma_load(sq + x * kQBox, &map_q, x * 64, rt * BM, hk, b, &q_full);
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&q_full, s.q_bytes);
+          for (int x = 0; x < s.nd; ++x) tma_load(sq + x * kQBox, &map_q, x * 64, rt * BM, hk, b, &q_full);
+        }
+        __syncwarp();
         bool ok = true;
         for (int j = 0; j < nb; ++j, ++it) {
           const int st = it % s.stages;
@@ -232,14 +264,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t *sk = sk_ring + (size_t)st * s.nd * kKVBox;
-          mbar_arrive_expect_tx(&k_full[st], (uint32_t)s.nd * kKVBox);
-          for (int x = 0; x < s.nd; ++x) tma_load(sk + x * kKVBox, &map_k, x * 64, j * BKV, hk, b, &k_full[st]);
+          if (elect_one()) {
+            mbar_arrive_expect_tx(&k_full[st], (uint32_t)s.nd * kKVBox);
+            for (int x = 0; x < s.nd; ++x) tma_load(sk + x * kKVBox, &map_k, x * 64, j * BKV, hk, b, &k_full[st]);
+          }
+          __syncwarp();
         }
         if (!ok) break;
       }
     }
   } else if (warp == 3) {
-    if (lane == 0) {
+    {
       // ---------------- TMA producer of V: its own ring, so a K slot frees as
       // soon as its Q·Kᵀ is done instead of waiting for the block's P·V
       int it = 0;
@@ -254,15 +289,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t *sv = sv_ring + (size_t)st * s.ndv * kKVBox;
-          mbar_arrive_expect_tx(&v_full[st], (uint32_t)s.ndv * kKVBox);
-          for (int x = 0; x < s.ndv; ++x) tma_load(sv + x * kKVBox, &map_v, x * 64, j * BKV, hk, b, &v_full[st]);
+          if (elect_one()) {
+            mbar_arrive_expect_tx(&v_full[st], (uint32_t)s.ndv * kKVBox);
+            for (int x = 0; x < s.ndv; ++x) tma_load(sv + x * kKVBox, &map_v, x * 64, j * BKV, hk, b, &v_full[st]);
+          }
+          __syncwarp();
         }
         if (!ok) break;
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------- MMA issuer
+    {
+      // ---------------- MMA issuer (whole warp; the elected lane issues)
       const uint32_t id_s = idesc(BM, BKV, 0), id_pv = idesc(BM, s.dvp, 1);
       int it = 0, jg = 0, local = 0;
       bool ok = true;
@@ -278,12 +316,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t ak = su32(sk_ring + (size_t)st * s.nd * kKVBox);
           for (int k = 0; k < s.ks; ++k) {
             const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;  // 64-wide box, 16-wide step
-            mma(tmem + sb * kSCols, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
-                k > 0 ? 1u : 0u);
+            if (elect_one())
+              mma(tmem + sb * kSCols, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
+                  k > 0 ? 1u : 0u);
           }
-          commit(&s_full[sb]);
-          commit(&k_empty[st]);               // K_j is read once S_j is complete
-          if (j == nb - 1) commit(&q_empty);  // the item's last read of Q: the next Q may load now
+          if (elect_one()) {
+            commit(&s_full[sb]);
+            commit(&k_empty[st]);               // K_j is read once S_j is complete
+            if (j == nb - 1) commit(&q_empty);  // the item's last read of Q: the next Q may load now
+          }
+          __syncwarp();
           return true;
         };
         if (!issue_s(0)) break;
@@ -309,15 +351,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_after();
           const uint32_t ap = su32(sp + pb * kPBytes), av = su32(sv_ring + (size_t)st * s.ndv * kKVBox);
           for (int k = 0; k < BKV / 16; ++k)  // 16 keys per step: P atom k / 4, V rows k·16
-            mma(t_o, desc_k(ap + (uint32_t)(k >> 2) * kPBox + (uint32_t)(k & 3) * 32), desc_mn(av + k * 2048, kKVBox),
-                id_pv, (j > 0 || k > 0) ? 1u : 0u);
-          commit(&v_empty[st]);   // V_j is read
-          commit(&p_free[pb]);    // P_j is read and O holds blocks ≤ j
+            if (elect_one())
+              mma(t_o, desc_k(ap + (uint32_t)(k >> 2) * kPBox + (uint32_t)(k & 3) * 32),
+                  desc_mn(av + k * 2048, kKVBox), id_pv, (j > 0 || k > 0) ? 1u : 0u);
+          if (elect_one()) {
+            commit(&v_empty[st]);   // V_j is read
+            commit(&p_free[pb]);    // P_j is read and O holds blocks ≤ j
+          }
+          __syncwarp();
         }
         it += nb;
         jg += nb;
         if (!ok) break;
-        commit(&o_full);
+        if (elect_one()) commit(&o_full);
+        __syncwarp();
       }
     }
   } else if (warp >= 4) {
