@@ -504,6 +504,34 @@ def reference_arm(args):
     print(json.dumps(line), flush=True)
 
 
+def measure_h2d_gbs(timer, host, dev):
+    """Pinned host -> device copy bandwidth of this rank with every rank copying
+    at once (best of 5 copies of ``host``), and the sum over ranks."""
+    dst = torch.empty_like(host, device=dev)
+    dst.copy_(host, non_blocking=True)
+    torch.cuda.synchronize()
+    best = None
+    for _ in range(5):
+        timer.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(timer.stream)
+        dst.copy_(host, non_blocking=True)
+        e1.record(timer.stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    per_rank = host.numel() * host.element_size() / (best / 1e3) / 1e9
+    total = per_rank
+    if timer.world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([per_rank], dtype=torch.float64, device=dev)
+        dist.all_reduce(t)
+        total = t.item()
+    del dst
+    return per_rank, total
+
+
 def measure_peer_copy_gbs(dev, world, rank):
     """Peer copy bandwidth rank 1 -> rank 0 over NVLink measured in this run
     (copy engine, 256 MiB, best of 5), broadcast to every rank; None on one GPU."""
@@ -592,6 +620,9 @@ def main():
     e2e_value = B * world / (e2e_ms / 1e3)
     h2d = images_host.numel() * images_host.element_size()
     d2h = sum(o.numel() * o.element_size() for o in outs[-1])
+    # the host link: H2D of every rank at once (the step's device->host copy runs the other way, overlapped)
+    h2d_rank, h2d_total = measure_h2d_gbs(timer, host_in[0], dev)
+    link_bound = h2d_total * 1e9 / (h2d / B)  # images/s if the input copies ran at that rate back to back
 
     # ---- with the final gather: every step's bf16 output goes to rank 0 (ShardedRuntime.run), overlapped
     gather = None
@@ -646,7 +677,11 @@ def main():
                                  "sleep outside the region (device time of queued steps)"},
             "regions": t["regions"], "ms_region_min": t["ms_region_min"], "ms_region_max": t["ms_region_max"],
             "e2e": {"value": e2e_value, "unit": "images/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "path": "Runtime.run(images=pinned host uint8) -> pinned host bf16"},
+                    "path": "Runtime.run(images=pinned host uint8) -> pinned host bf16",
+                    "host_link": {"h2d_gbs_rank0": h2d_rank, "h2d_gbs_all_ranks": h2d_total,
+                                  "bound_images_per_s": link_bound, "frac": e2e_value / link_bound,
+                                  "note": "pinned H2D copies of every rank at once, best of 5; the bound is the "
+                                          "input bytes at that aggregate rate"}},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": ncu_traffic(), "peak_kind": peak_kind,
                          "kernel": "preproc_u8c3_kernel<bf16> (NHWC u8 -> NCHW bf16)",
