@@ -314,13 +314,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!wait_or_abort(&s_free[sb], ((jgj >> 1) & 1) ^ 1, 540 + sb, flag)) return false;
           fence_after();
           const uint32_t ak = su32(sk_ring + (size_t)st * s.nd * kKVBox);
-          for (int k = 0; k < s.ks; ++k) {
-            const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;  // 64-wide box, 16-wide step
-            if (elect_one())
+          if (elect_one()) {
+            for (int k = 0; k < s.ks; ++k) {
+              const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;  // 64-wide box, 16-wide step
               mma(tmem + sb * kSCols, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
                   k > 0 ? 1u : 0u);
-          }
-          if (elect_one()) {
+            }
             commit(&s_full[sb]);
             commit(&k_empty[st]);               // K_j is read once S_j is complete
             if (j == nb - 1) commit(&q_empty);  // the item's last read of Q: the next Q may load now
@@ -350,11 +349,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           fence_after();
           const uint32_t ap = su32(sp + pb * kPBytes), av = su32(sv_ring + (size_t)st * s.ndv * kKVBox);
-          for (int k = 0; k < BKV / 16; ++k)  // 16 keys per step: P atom k / 4, V rows k·16
-            if (elect_one())
+          if (elect_one()) {
+            for (int k = 0; k < BKV / 16; ++k)  // 16 keys per step: P atom k / 4, V rows k·16
               mma(t_o, desc_k(ap + (uint32_t)(k >> 2) * kPBox + (uint32_t)(k & 3) * 32),
                   desc_mn(av + k * 2048, kKVBox), id_pv, (j > 0 || k > 0) ? 1u : 0u);
-          if (elect_one()) {
             commit(&v_empty[st]);   // V_j is read
             commit(&p_free[pb]);    // P_j is read and O holds blocks ≤ j
           }

@@ -579,17 +579,20 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t a_desc0 = smem_desc(sa);
           const uint64_t b_desc0 = b_mn ? smem_desc_mn(sb) : smem_desc(sb);
           const int kh_end = kb + 1 == s.k_blocks ? s.last_boxes : Cfg<CG>::kKBoxes;  // boxes past K hold zeros only
+          if (elect_one()) {
 #pragma unroll
-          for (int kh = 0; kh < Cfg<CG>::kKBoxes; ++kh) {
-            if (kh >= kh_end) break;
+            for (int kh = 0; kh < Cfg<CG>::kKBoxes; ++kh) {
+              if (kh >= kh_end) break;
 #pragma unroll
-            for (int k = 0; k < BK / 16; ++k) {
-              const uint64_t adesc = a_desc0 + (uint64_t)((kh * kTileABytes + k * 32) >> 4);
-              const uint64_t bdesc = b_desc0 + (uint64_t)((kh * b_box_bytes<CG>() + k * b_kstep) >> 4);
-              if (elect_one()) mma_issue<CG>(tmem_d, adesc, bdesc, idesc, (kb | kh | k) != 0, tf32);
+              for (int k = 0; k < BK / 16; ++k) {
+                const uint64_t adesc = a_desc0 + (uint64_t)((kh * kTileABytes + k * 32) >> 4);
+                const uint64_t bdesc = b_desc0 + (uint64_t)((kh * b_box_bytes<CG>() + k * b_kstep) >> 4);
+                mma_issue<CG>(tmem_d, adesc, bdesc, idesc, (kb | kh | k) != 0, tf32);
+              }
             }
+            mma_commit<CG>(&empty[st]);  // stage is free (in both CTAs) once these MMAs have read it
           }
-          if (elect_one()) mma_commit<CG>(&empty[st]);  // stage is free (in both CTAs) once these MMAs have read it
+          __syncwarp();
         }
         if (!ok) break;
         if (elect_one()) mma_commit<CG>(&acc_full[a]);  // accumulator complete
