@@ -242,6 +242,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t t_o = tmem + 2 * kSCols;  // output accumulator columns
   volatile int *flag = &abort_flag;
   const int nb = s.kv_blocks;
+  // With two ring stages a K / V slot and a score / P buffer share their index
+  // (both are the block count mod 2), so the producers wait on the score and
+  // P barriers instead of separate K / V "empty" barriers.
+  const bool merged = s.stages == 2;
 
   if (warp == 0) {
     {
@@ -259,7 +263,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int j = 0; j < nb; ++j, ++it) {
           const int st = it % s.stages;
-          if (!wait_or_abort(&k_empty[st], ((it / s.stages) & 1) ^ 1, 510 + st, flag)) {
+          // Two stages: slot st is free once S of block it − 2 (score buffer st) is complete,
+          // so the K ring waits on s_full and the MMA thread commits one barrier less per block.
+          const bool free_k = merged ? (it < 2 || wait_or_abort(&s_full[st], ((it - 2) >> 1) & 1, 510 + st, flag))
+                                     : wait_or_abort(&k_empty[st], ((it / s.stages) & 1) ^ 1, 510 + st, flag);
+          if (!free_k) {
             ok = false;
             break;
           }
@@ -284,7 +292,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         bool ok = true;
         for (int j = 0; j < nb; ++j, ++it) {
           const int st = it % s.stages;
-          if (!wait_or_abort(&v_empty[st], ((it / s.stages) & 1) ^ 1, 515 + st, flag)) {
+          // Two stages: slot st is free once P·V of block it − 2 (P buffer st) is complete.
+          const bool free_v = merged ? (it < 2 || wait_or_abort(&p_free[st], ((it - 2) >> 1) & 1, 515 + st, flag))
+                                     : wait_or_abort(&v_empty[st], ((it / s.stages) & 1) ^ 1, 515 + st, flag);
+          if (!free_v) {
             ok = false;
             break;
           }
@@ -321,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   k > 0 ? 1u : 0u);
             }
             commit(&s_full[sb]);
-            commit(&k_empty[st]);               // K_j is read once S_j is complete
+            if (!merged) commit(&k_empty[st]);  // K_j is read once S_j is complete
             if (j == nb - 1) commit(&q_empty);  // the item's last read of Q: the next Q may load now
           }
           __syncwarp();
@@ -353,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int k = 0; k < BKV / 16; ++k)  // 16 keys per step: P atom k / 4, V rows k·16
               mma(t_o, desc_k(ap + (uint32_t)(k >> 2) * kPBox + (uint32_t)(k & 3) * 32),
                   desc_mn(av + k * 2048, kKVBox), id_pv, (j > 0 || k > 0) ? 1u : 0u);
-            commit(&v_empty[st]);   // V_j is read
+            if (!merged) commit(&v_empty[st]);  // V_j is read
             commit(&p_free[pb]);    // P_j is read and O holds blocks ≤ j
           }
           __syncwarp();
