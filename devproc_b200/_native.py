@@ -54,9 +54,9 @@ DP_NOALLOC_ARENA_BYTES = 64 << 20
 DP_RECORD_MAX_OPERANDS, DP_RECORD_PARAM_BYTES = 8, 1280
 DP_SLOT_BOUND, DP_SLOT_ARENA = 0, 1
 DP_K_PREPROC, DP_K_ROWREDUCE, DP_K_GEMM, DP_K_REGION, DP_K_EMBEDDING, DP_K_COPY, DP_K_ATTENTION, DP_K_ROPE, \
-    DP_K_SPLITK, DP_K_ARGMAX_KEYS = range(1, 11)
+    DP_K_SPLITK, DP_K_ARGMAX_KEYS, DP_K_GEMM_SK = range(1, 12)
 KERNEL_NAMES = {1: "preproc", 2: "rowreduce", 3: "gemm", 4: "region", 5: "embedding", 6: "copy", 7: "attention",
-                8: "rope", 9: "splitk", 10: "argmax_keys"}
+                8: "rope", 9: "splitk", 10: "argmax_keys", 11: "gemm_sk"}
 
 
 class PreprocParams(ctypes.Structure):
@@ -88,6 +88,10 @@ class GemmParams(ctypes.Structure):
 
 class SplitKParams(ctypes.Structure):
     _fields_ = [("gemm", GemmParams), ("splits", ctypes.c_int64), ("slice_stride", ctypes.c_int64)]
+
+
+class StreamKParams(ctypes.Structure):
+    _fields_ = [("gemm", GemmParams), ("workspace_bytes", ctypes.c_int64)]
 
 
 class ArgmaxKeysParams(ctypes.Structure):
@@ -147,7 +151,8 @@ class PlanRecord(ctypes.Structure):
 
 PARAM_STRUCTS = {DP_K_PREPROC: PreprocParams, DP_K_ROWREDUCE: RowReduceParams, DP_K_GEMM: GemmParams,
                  DP_K_REGION: RegionDesc, DP_K_EMBEDDING: EmbeddingParams, DP_K_ATTENTION: AttentionParams,
-                 DP_K_ROPE: RopeParams, DP_K_SPLITK: SplitKParams, DP_K_ARGMAX_KEYS: ArgmaxKeysParams}
+                 DP_K_ROPE: RopeParams, DP_K_SPLITK: SplitKParams, DP_K_ARGMAX_KEYS: ArgmaxKeysParams,
+                 DP_K_GEMM_SK: StreamKParams}
 
 # (symbol, argtypes) of every exported function, in header order.
 _VP = ctypes.c_void_p
@@ -163,6 +168,8 @@ EXPORTS = {
     "dp_rowreduce": [ctypes.POINTER(RowReduceParams), _VP, _VP, _VP, _VP, _VP],
     "dp_gemm": [ctypes.POINTER(GemmParams), _VP, _VP, _VP, _VP, _VP, _VP],
     "dp_gemm_splitk_reduce": [ctypes.POINTER(SplitKParams), _VP, _VP, _VP, _VP, _VP],
+    "dp_gemm_streamk_workspace": [ctypes.POINTER(GemmParams), ctypes.POINTER(ctypes.c_int64)],
+    "dp_gemm_streamk": [ctypes.POINTER(StreamKParams), _VP, _VP, _VP, _VP, _VP, _VP, _VP],
     "dp_argmax_keys": [ctypes.POINTER(ArgmaxKeysParams), _VP, _VP, _VP],
     "dp_region": [ctypes.POINTER(RegionDesc), ctypes.POINTER(_VP), _VP],
     "dp_embedding": [ctypes.POINTER(EmbeddingParams), _VP, _VP, _VP, _VP],
@@ -289,6 +296,18 @@ def gemm(p: GemmParams, a, b, c, bias=None, residual=None, stream=None) -> None:
 def gemm_splitk_reduce(p: SplitKParams, workspace, c, bias=None, residual=None, stream=None) -> None:
     check(lib().dp_gemm_splitk_reduce(ctypes.byref(p), _ptr(workspace), _ptr(c), _ptr(bias), _ptr(residual),
                                       _stream(stream)), "dp_gemm_splitk_reduce")
+
+
+def gemm_streamk_workspace(p: GemmParams) -> int:
+    """Bytes of stream-K workspace that always suffice for ``p`` on the current device."""
+    n = ctypes.c_int64(0)
+    check(lib().dp_gemm_streamk_workspace(ctypes.byref(p), ctypes.byref(n)), "dp_gemm_streamk_workspace")
+    return n.value
+
+
+def gemm_streamk(p: StreamKParams, a, b, c, workspace, bias=None, residual=None, stream=None) -> None:
+    check(lib().dp_gemm_streamk(ctypes.byref(p), _ptr(a), _ptr(b), _ptr(c), _ptr(bias), _ptr(residual),
+                                _ptr(workspace), _stream(stream)), "dp_gemm_streamk")
 
 
 def argmax_keys(p: ArgmaxKeysParams, keys, out=None, stream=None) -> None:

@@ -223,8 +223,44 @@ def splitk_factor(M: int, N: int, K: int, tf32: bool, b_layout: int) -> int:
     return best_s if best <= 0.9 * cost(1) else 1
 
 
+def streamk_bytes(M: int, n: int, K: int, batch: int, tf32: bool, epilogue: int) -> int:
+    """Workspace bytes of a stream-K tensor-core GEMM, 0 = whole tiles.
+
+    Same plan as the kernel's launcher (for 148 SMs; the launcher re-plans
+    for the device it runs on and uses whole tiles if the plan changes):
+    the tiles past the last full wave (``rem``, with ``waves`` full waves of
+    CTA groups) are split by K stage when each group's even share of their
+    stages is at least half a tile (at most three runs per tile) and waves x
+    stages + the share + 2 + 1.5 per partial handed on is at most 0.9 of the
+    whole-tile time, (waves + 1) x stages.  The workspace is the per-tile counters
+    plus one 128 KB fp32 partial slot per SM (the C-ABI's bound).
+    """
+    if epilogue & (N.DP_EPI_SOFTMAX | N.DP_EPI_ARGMAX):
+        return 0
+    cg = 2 if (M > 128 and n > 128) else 1
+    groups = _SMS // cg
+    tiles = -(-M // (128 * cg)) * -(-n // 256) * batch
+    kb = -(-K // ((32 if tf32 else 64) * (2 if cg == 2 else 1)))
+    rem, waves = tiles % groups, tiles // groups
+    if rem == 0 or kb < 4:
+        return 0
+    ipp = -(-rem * kb // groups)
+    if 2 * ipp < kb:
+        return 0
+    runs = -(-kb // ipp) + 1
+    if waves * kb + ipp + 2.0 + 1.5 * (runs - 1) > 0.9 * (waves + 1) * kb:
+        return 0
+    counters = -(-4 * -(-M // 128) * -(-n // 256) * batch // 256) * 256
+    return counters + _SMS * 64 * 128 * 16
+
+
 class Lowerer:
     use_fused_attention = True  # bf16 sdpa as one fused tensor-core kernel (else GEMM + softmax + GEMM)
+    # GEMMs with a ragged last wave split it by K stage.  Off by default: on
+    # B200 the split runs' hand-off (partial write, wait, read back, a second
+    # epilogue) costs more than the idle CTA pairs it fills - 3,200 x 1,024,
+    # K 4,096 runs 41.0 us split against 36.4 us with whole tiles.
+    use_streamk = False
 
     def __init__(self, fn: Function, const_names=(), const_tensors=None):
         self.fn = fn
@@ -946,7 +982,15 @@ class Lowerer:
         if p.batch == 1 and not shared_rows and not (epi & N.DP_EPI_SOFTMAX) and (tf32 or a_dtype == "bfloat16"):
             splits = splitk_factor(p.M, p.N, p.K, tf32, p.b_layout)
         if splits == 1:
-            self.emit(N.DP_K_GEMM, ops_, p, label, flops, nb)
+            skb = streamk_bytes(p.M, p.N, p.K, p.batch, tf32, epi) if (tf32 or a_dtype == "bfloat16") else 0
+            if skb and self.use_streamk:
+                # Tiles past the last full wave split by K stage over every CTA group.
+                sp = N.StreamKParams()
+                sp.gemm, sp.workspace_bytes = p, skb
+                ws = self.new_buffer("arena", "uint8", (skb,), f"{cur.name}_streamk")
+                self.emit(N.DP_K_GEMM_SK, ops_ + [ws], sp, f"{label} streamk", flops, nb)
+            else:
+                self.emit(N.DP_K_GEMM, ops_, p, label, flops, nb)
             return
         # Split K: a batched GEMM over the K slices writes raw fp32 partial
         # products to a workspace [S, M, N]; the reduce record sums them in

@@ -51,8 +51,12 @@ inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s
 int launch_preproc(const dp_preproc_params &p, const void *in, void *out, cudaStream_t s);
 int launch_rowreduce(const dp_rowreduce_params &p, const void *in, const void *w,
                      const void *b, void *out, cudaStream_t s);
+// sk_workspace / sk_bytes: optional stream-K workspace (dp_gemm_streamk).
 int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C,
-                const void *bias, const void *res, cudaStream_t s);
+                const void *bias, const void *res, cudaStream_t s, void *sk_workspace = nullptr,
+                int64_t sk_bytes = 0);
+int launch_gemm_streamk(const dp_streamk_params &p, const void *A, const void *B, void *C, const void *bias,
+                        const void *res, void *workspace, cudaStream_t s);
 int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t s);
 int launch_attention(const dp_attention_params &p, const void *q, const void *k, const void *v, void *o,
                      cudaStream_t s);

@@ -59,7 +59,10 @@ struct Epilogue {
 
 int launch_gemm_simt(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias,
                      const void *res, cudaStream_t s);
+// sk_workspace (optional): stream-K workspace of sk_bytes; the tile-past-the-
+// last-wave split is used only when the cost model picks it and it fits.
 int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias,
-                   const void *res, cudaStream_t s);
+                   const void *res, cudaStream_t s, void *sk_workspace = nullptr, int64_t sk_bytes = 0);
+int64_t gemm_streamk_workspace_bound(const dp_gemm_params &p);
 
 }  // namespace dp

@@ -8,7 +8,7 @@
 namespace dp {
 
 int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C, const void *bias, const void *res,
-                cudaStream_t s) {
+                cudaStream_t s, void *sk_workspace, int64_t sk_bytes) {
   DP_REQUIRE(A && B && C, DP_ERR_ARG, "gemm: null A/B/C");
   DP_REQUIRE(p.M > 0 && p.N > 0 && p.K > 0 && p.batch > 0, DP_ERR_SHAPE, "gemm: sizes must be positive");
   DP_REQUIRE(p.lda >= p.K, DP_ERR_SHAPE, "gemm: lda < K");
@@ -43,12 +43,19 @@ int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C, 
     auto al = [](const void *q) { return reinterpret_cast<uintptr_t>(q) % 16 == 0; };
     const bool tc_ok = p.lda % v == 0 && p.ldb % v == 0 && p.stride_a % v == 0 && p.stride_b % v == 0 &&
                        p.stride_a2 % v == 0 && p.stride_b2 % v == 0 && al(A) && al(B);
-    if (tc_ok) return launch_gemm_tc(p, A, B, C, bias, res, s);
+    if (tc_ok) return launch_gemm_tc(p, A, B, C, bias, res, s, sk_workspace, sk_bytes);
   }
   DP_REQUIRE(!(p.epilogue & (DP_EPI_SOFTMAX | DP_EPI_ARGMAX)), DP_ERR_UNSUPPORTED,
              "gemm: the softmax and argmax epilogues run only on the tensor-core path (bf16 or TF32, 16-byte "
              "aligned operands)");
   return launch_gemm_simt(p, A, B, C, bias, res, s);
+}
+
+int launch_gemm_streamk(const dp_streamk_params &p, const void *A, const void *B, void *C, const void *bias,
+                        const void *res, void *workspace, cudaStream_t s) {
+  DP_REQUIRE(p.workspace_bytes >= 0 && (workspace != nullptr || p.workspace_bytes == 0), DP_ERR_ARG,
+             "gemm_streamk: workspace_bytes without a workspace");
+  return launch_gemm(p.gemm, A, B, C, bias, res, s, workspace, p.workspace_bytes);
 }
 
 }  // namespace dp
@@ -57,4 +64,17 @@ extern "C" int dp_gemm(const dp_gemm_params *p, const void *A, const void *B, vo
                        const void *residual, void *stream) {
   if (!p) return dp::set_error(DP_ERR_ARG, "dp_gemm: null params");
   return dp::launch_gemm(*p, A, B, C, bias, residual, dp::as_stream(stream));
+}
+
+extern "C" int dp_gemm_streamk_workspace(const dp_gemm_params *p, int64_t *bytes) {
+  if (!p || !bytes) return dp::set_error(DP_ERR_ARG, "dp_gemm_streamk_workspace: null argument");
+  DP_REQUIRE(p->M > 0 && p->N > 0 && p->batch > 0, DP_ERR_SHAPE, "dp_gemm_streamk_workspace: sizes must be positive");
+  *bytes = dp::gemm_streamk_workspace_bound(*p);
+  return DP_OK;
+}
+
+extern "C" int dp_gemm_streamk(const dp_streamk_params *p, const void *A, const void *B, void *C, const void *bias,
+                               const void *residual, void *workspace, void *stream) {
+  if (!p) return dp::set_error(DP_ERR_ARG, "dp_gemm_streamk: null params");
+  return dp::launch_gemm_streamk(*p, A, B, C, bias, residual, workspace, dp::as_stream(stream));
 }

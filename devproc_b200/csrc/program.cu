@@ -106,6 +106,13 @@ int run_records(dp_program *prog, cudaStream_t s) {
         st = dp::launch_argmax_keys(p, const_cast<void *>(ops[0]), const_cast<void *>(ops[1]), s);
         break;
       }
+      case DP_K_GEMM_SK: {
+        dp_streamk_params p;
+        memcpy(&p, rec.params, sizeof(p));
+        st = dp::launch_gemm_streamk(p, ops[0], ops[1], const_cast<void *>(ops[2]), ops[3], ops[4],
+                                     const_cast<void *>(ops[5]), s);
+        break;
+      }
       default:
         st = dp::set_error(DP_ERR_PLAN, "program: unknown record kind " + std::to_string(rec.kernel));
     }

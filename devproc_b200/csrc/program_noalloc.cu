@@ -129,6 +129,12 @@ int launch_record(const dp_plan_record &rec, const void *const *ops, cudaStream_
       memcpy(&p, rec.params, sizeof(p));
       return dp::launch_argmax_keys(p, const_cast<void *>(ops[0]), const_cast<void *>(ops[1]), s);
     }
+    case DP_K_GEMM_SK: {
+      dp_streamk_params p;
+      memcpy(&p, rec.params, sizeof(p));
+      return dp::launch_gemm_streamk(p, ops[0], ops[1], const_cast<void *>(ops[2]), ops[3], ops[4],
+                                     const_cast<void *>(ops[5]), s);
+    }
     default:
       return dp::set_error(DP_ERR_PLAN, "unknown record kind " + std::to_string(rec.kernel));
   }
@@ -182,7 +188,7 @@ extern "C" int dp_program_run_noalloc(const void *plan, size_t plan_bytes, void 
   for (uint32_t r = 0; r < h.n_records; ++r) {
     dp_plan_record rec;
     memcpy(&rec, records + (size_t)r * sizeof(dp_plan_record), sizeof(rec));
-    DP_REQUIRE(rec.kernel >= DP_K_PREPROC && rec.kernel <= DP_K_ARGMAX_KEYS, DP_ERR_PLAN,
+    DP_REQUIRE(rec.kernel >= DP_K_PREPROC && rec.kernel <= DP_K_GEMM_SK, DP_ERR_PLAN,
                "program record " + std::to_string(r) + ": unknown record kind " + std::to_string(rec.kernel));
     DP_REQUIRE(rec.n_operands <= DP_RECORD_MAX_OPERANDS, DP_ERR_PLAN,
                "program record " + std::to_string(r) + ": too many operands");

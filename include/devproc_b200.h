@@ -197,6 +197,28 @@ typedef struct dp_splitk_params {
 int dp_gemm_splitk_reduce(const dp_splitk_params *p, const void *workspace, void *C, const void *bias,
                           const void *residual, void *stream);
 
+/* ---- stream-K GEMM ------------------------------------------------------
+ * dp_gemm for GEMMs whose last wave of output tiles would leave CTA groups
+ * idle (e.g. 3,200 x 1,024 with K 4,096: 52 tiles of 256 x 256 for 74 CTA
+ * pairs): the K stages of the tiles past the last full wave are dealt out
+ * evenly over every group, and the group that computes a tile's last stages
+ * adds the earlier groups' fp32 partials (read back in group order, the same
+ * bits every run) before the epilogue.  The kernel uses the split only when
+ * its cost model picks it for this device and ``workspace_bytes`` holds it;
+ * otherwise this is dp_gemm.  The softmax and argmax epilogues never split.
+ * ``workspace`` (16-byte aligned, device memory) is scratch for the call:
+ * per-tile counters (cleared by the call on ``stream``) and one partial tile
+ * per group.  Same role as the reference's launch_matmul / launch_linear
+ * (src/devproc/backend/triton/templates/matmul.py:230-296). */
+typedef struct dp_streamk_params {
+  dp_gemm_params gemm;
+  int64_t workspace_bytes;
+} dp_streamk_params;
+/* Bytes of workspace that always suffice for *p on the current device. */
+int dp_gemm_streamk_workspace(const dp_gemm_params *p, int64_t *bytes);
+int dp_gemm_streamk(const dp_streamk_params *p, const void *A, const void *B, void *C, const void *bias,
+                    const void *residual, void *workspace, void *stream);
+
 /* ---- argmax keys ---------------------------------------------------------
  * mode 0: keys[0..n) = 0 (before a DP_EPI_ARGMAX GEMM); mode 1: out[i] =
  * the column index in keys[i] as out_dtype (DP_I32 or DP_I64). */
@@ -316,7 +338,7 @@ enum { DP_SLOT_BOUND = 0, DP_SLOT_ARENA = 1 };
 enum {
   DP_K_PREPROC = 1, DP_K_ROWREDUCE = 2, DP_K_GEMM = 3, DP_K_REGION = 4,
   DP_K_EMBEDDING = 5, DP_K_COPY = 6, DP_K_ATTENTION = 7, DP_K_ROPE = 8, DP_K_SPLITK = 9,
-  DP_K_ARGMAX_KEYS = 10
+  DP_K_ARGMAX_KEYS = 10, DP_K_GEMM_SK = 11
 };
 typedef struct dp_plan_header {
   uint32_t magic, version, n_slots, n_records;

@@ -753,6 +753,92 @@ def test_split_k_linear_matches_fp64(cuda, dtype, M, K, Nn):
     assert torch.equal(again.double(), got)  # slices are summed in a fixed order
 
 
+# ------------------------------------------------------- stream-K GEMM
+@pytest.mark.parametrize("M,Nn,K,batch,c_dtype,epi,ldc_pad", [
+    # the action expert's down projection: 52 pair tiles for 74 CTA pairs
+    (3200, 1024, 4096, 1, torch.bfloat16, N.DP_EPI_BIAS | N.DP_EPI_GELU_TANH | N.DP_EPI_RESIDUAL, 0),
+    (3200, 1024, 4096, 1, torch.float32, 0, 0),
+    # single-CTA tiles: 79 tiles for 148 CTAs
+    (100, 20000, 2048, 1, torch.bfloat16, N.DP_EPI_BIAS, 0),
+    # batched, ragged edges, output rows not 16-byte multiples (no TMA store)
+    (1000, 600, 3000, 3, torch.bfloat16, N.DP_EPI_RESIDUAL, 1),
+])
+def test_streamk_gemm_matches_fp64(cuda, M, Nn, K, batch, c_dtype, epi, ldc_pad):
+    """dp_gemm_streamk: the K stages of the tiles past the last full wave are
+    dealt out over every CTA group and the tile-ending group adds the earlier
+    partials.  Checked against the fp64 product (bf16 bar), bit-identical on
+    a second run (partials are added in a fixed order), and the per-tile
+    arrival counters show the split really ran."""
+    g = torch.Generator().manual_seed(M + K + batch)
+    a = torch.randn(batch, M, K, generator=g).bfloat16().to(cuda)
+    w = (torch.randn(batch, Nn, K, generator=g) * 0.05).bfloat16().to(cuda)
+    bias = torch.randn(Nn, generator=g).to(c_dtype).to(cuda)
+    ldc = Nn + ldc_pad
+    res = torch.randn(batch, M, ldc, generator=g).to(c_dtype).to(cuda)
+    c = torch.zeros(batch, M, ldc, dtype=c_dtype, device=cuda)
+    p = N.GemmParams()
+    p.M, p.N, p.K, p.lda, p.ldb, p.ldc, p.ldr, p.batch = M, Nn, K, K, K, ldc, ldc, batch
+    p.stride_a, p.stride_b, p.stride_c, p.stride_r = M * K, Nn * K, M * ldc, M * ldc
+    p.a_dtype = p.b_dtype = N.DP_BF16
+    p.c_dtype = p.r_dtype = p.bias_dtype = _dt(c)
+    p.b_layout = N.DP_B_NK
+    p.epilogue = epi
+    sp = N.StreamKParams()
+    sp.gemm, sp.workspace_bytes = p, N.gemm_streamk_workspace(p)
+    ws = torch.zeros(sp.workspace_bytes, dtype=torch.uint8, device=cuda)
+    N.gemm_streamk(sp, a, w, c, ws, bias=bias, residual=res)
+    _sync()
+    counters = ws[:4 * 64].view(torch.int32).cpu()
+    assert int(counters.max()) > 0, "the stream-K split did not run"
+    acc = a.double() @ w.double().transpose(-1, -2)
+    mag = a.double().abs() @ w.double().abs().transpose(-1, -2)
+    if epi & N.DP_EPI_BIAS:
+        acc = acc + bias.double()
+        mag = mag + bias.double().abs()
+    if epi & N.DP_EPI_GELU_TANH:
+        acc = torch.nn.functional.gelu(acc, approximate="tanh")
+    if epi & N.DP_EPI_RESIDUAL:
+        acc = acc + res[..., :Nn].double()
+        mag = mag + res[..., :Nn].double().abs()
+    got = c[..., :Nn].double()
+    tol = 2e-2 if c_dtype == torch.bfloat16 else 1e-3
+    assert ((got - acc).abs() <= tol * mag + 1e-3).all(), ((got - acc).abs() / (mag + 1e-3)).max()
+    if ldc_pad:
+        assert (c[..., Nn:] == 0).all()  # padding columns untouched
+    first = c.clone()
+    N.gemm_streamk(sp, a, w, c, ws, bias=bias, residual=res)
+    _sync()
+    assert torch.equal(c, first)
+    # the same call without a workspace runs whole tiles and agrees within rounding
+    whole = torch.zeros_like(c)
+    N.gemm(p, a, w, whole, bias=bias, residual=res)
+    _sync()
+    assert ((whole[..., :Nn].double() - got).abs() <= tol * mag + 1e-3).all()
+
+
+def test_streamk_linear_program_matches_fp64(cuda):
+    """With stream-K switched on, a compiled bf16 linear + GELU + residual with
+    a ragged last wave runs as one stream-K record; fp64 bar as for the other
+    bf16 linears."""
+    from devproc_b200.backend.b200.lowering import Lowerer
+    torch.manual_seed(1)
+    m = _LinearGelu(4096, 1024, torch.bfloat16).eval()
+    x = torch.randn(3200, 4096).to(torch.bfloat16)
+    r = torch.randn(3200, 1024).to(torch.bfloat16)
+    Lowerer.use_streamk = True
+    try:
+        prog = devproc.compile(m, x, r)
+    finally:
+        Lowerer.use_streamk = False
+    assert [rec["kernel"] for rec in prog.spec.records] == ["gemm_sk"], prog.describe()
+    got = prog.run(x, r)[0].double()
+    w, b = m.lin.weight.double(), m.lin.bias.double()
+    ref = torch.nn.functional.gelu(x.double() @ w.T + b) + r.double()
+    mag = (x.double().abs() @ w.abs().T) + b.abs() + r.double().abs()
+    assert ((got - ref).abs() <= 2e-2 * mag).all(), ((got - ref).abs() / mag).max()
+    assert torch.equal(prog.run(x, r)[0].double(), got)
+
+
 # ------------------------------------------------------- argmax epilogue
 class _LinearArgmax(torch.nn.Module):
     def __init__(self, k, n, dtype):

@@ -45,6 +45,29 @@ def test_token_pipeline_fuses_epilogues_and_argmax_cast():
     assert [i.name for i in prog.spec.inputs] == ["l_ids_"]
 
 
+def test_ragged_last_wave_gemm_splits_by_k_stage():
+    """With stream-K switched on, a bf16 linear with fewer 256 x 256 tiles than
+    CTA pairs (3,200 x 1,024, K 4,096: 52 tiles for 74 pairs) lowers to one
+    stream-K GEMM record with an arena workspace; GEMMs whose last wave is
+    full or nearly so, or whose K is short, keep whole tiles."""
+    from devproc_b200.backend.b200.lowering import Lowerer, streamk_bytes
+    m = torch.nn.Linear(4096, 1024).to(torch.bfloat16)
+    x = torch.randn(3200, 4096).to(torch.bfloat16)
+    assert kernels(devproc.compile(m, x)) == ["gemm"]  # opt-in: whole tiles by default
+    Lowerer.use_streamk = True
+    try:
+        prog = devproc.compile(m, x)
+    finally:
+        Lowerer.use_streamk = False
+    assert kernels(prog) == ["gemm_sk"]
+    assert "streamk" in prog.spec.records[0]["label"]
+    assert streamk_bytes(3200, 1024, 4096, 1, False, 0) > 74 * 256 * 1024
+    assert streamk_bytes(3200, 1024, 4096, 1, False, N.DP_EPI_SOFTMAX) == 0
+    assert streamk_bytes(8192, 8192, 8192, 1, False, 0) == 0        # 1,024 tiles: the ragged wave is a small share
+    assert streamk_bytes(3200, 4096, 1024, 1, False, 0) == 0        # 208 tiles, 8 K stages each
+    assert streamk_bytes(148 * 128, 256, 4096, 1, False, 0) == 0    # 74 pair tiles: one full wave
+
+
 def test_elementwise_chain_is_one_region():
     @devproc.kernel
     def f(x, y):

@@ -47,6 +47,7 @@ STRUCTS = {"dp_preproc_params": N.PreprocParams, "dp_rowreduce_params": N.RowRed
            "dp_gemm_params": N.GemmParams, "dp_region_desc": N.RegionDesc, "dp_embedding_params": N.EmbeddingParams,
            "dp_attention_params": N.AttentionParams, "dp_rope_params": N.RopeParams,
            "dp_splitk_params": N.SplitKParams, "dp_argmax_keys_params": N.ArgmaxKeysParams,
+           "dp_streamk_params": N.StreamKParams,
            "dp_plan_header": N.PlanHeader, "dp_plan_slot": N.PlanSlot, "dp_plan_record": N.PlanRecord}
 
 
