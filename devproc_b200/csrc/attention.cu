@@ -201,6 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t *sk_ring = sp + 2 * kPBytes;  // two P tiles: softmax writes P_{j+1} while P_j is still being read
   uint8_t *sv_ring = sk_ring + (size_t)s.stages * s.nd * kKVBox;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  dp::pdl_trigger();
 
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 1);
@@ -241,6 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = tmem_slot;
   const uint32_t t_o = tmem + 2 * kSCols;  // output accumulator columns
   volatile int *flag = &abort_flag;
+  dp::pdl_wait();  // set-up above touches no global memory; the previous kernel's results are visible from here
   const int nb = s.kv_blocks;
   // With two ring stages a K / V slot and a score / P buffer share their index
   // (both are the block count mod 2), so the producers wait on the score and
@@ -612,7 +614,7 @@ int launch_blocks(const dp_attention_params &p, Shape s, const void *q, const vo
   }
   int grid = dp::num_sms();
   if (grid > s.items) grid = s.items;
-  attn_kernel<BKV><<<grid, kThreads, smem, stream>>>(mq, mk, mv, s, static_cast<__nv_bfloat16 *>(o));
+  dp::launch_k(attn_kernel<BKV>, grid, kThreads, smem, stream, mq, mk, mv, s, static_cast<__nv_bfloat16 *>(o));
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }

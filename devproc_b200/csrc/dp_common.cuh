@@ -35,6 +35,45 @@ int kernel_blocks_per_sm(const void *func, int threads, size_t smem, bool max_ca
     if (!(cond)) return ::dp::set_error((code), (msg)); \
   } while (0)
 
+// Programmatic dependent launch.  Every kernel of this library is launched
+// with launch_k, which lets its grid start while the kernel before it on the
+// stream is still finishing, and every kernel calls pdl_wait() before its
+// first global-memory access (read or write): griddepcontrol.wait returns once
+// the previous grid has completed and its writes are visible, so stream order
+// holds.  pdl_trigger() at kernel entry lets the next grid launch as soon as
+// every CTA of this one has started; its CTAs then take SMs as this grid's
+// CTAs exit, instead of after the last one.  Both are no-ops for a grid
+// launched without the attribute.  Build switch: DP_PDL=0 launches plainly.
+#ifndef DP_PDL
+#define DP_PDL 1
+#endif
+__device__ __forceinline__ void pdl_wait() {
+#if DP_PDL
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+__device__ __forceinline__ void pdl_trigger() {
+#if DP_PDL
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args &&...args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = DP_PDL ? 1 : 0;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 inline int dtype_bytes(int dt) {
   switch (dt) {
     case DP_U8: case DP_I8: case DP_BOOL: return 1;

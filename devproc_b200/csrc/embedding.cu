@@ -13,6 +13,8 @@ template <typename V>
 __global__ void __launch_bounds__(256) gather_kernel(dp_embedding_params p, const void *__restrict__ ids,
                                                      const V *__restrict__ w, V *__restrict__ out,
                                                      int64_t row_vecs) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -48,13 +50,13 @@ int launch_embedding(const dp_embedding_params &p, const void *ids, const void *
   if (blocks > cap) blocks = cap;
   auto aligned = [](const void *q, int a) { return reinterpret_cast<uintptr_t>(q) % a == 0; };
   if (row_bytes % 16 == 0 && aligned(w, 16) && aligned(out, 16)) {
-    gather_kernel<uint4><<<(int)blocks, 256, 0, s>>>(p, ids, static_cast<const uint4 *>(w),
+    dp::launch_k(gather_kernel<uint4>, (int)blocks, 256, 0, s, p, ids, static_cast<const uint4 *>(w),
                                                     static_cast<uint4 *>(out), row_bytes / 16);
   } else if (row_bytes % 4 == 0 && aligned(w, 4) && aligned(out, 4)) {
-    gather_kernel<uint32_t><<<(int)blocks, 256, 0, s>>>(p, ids, static_cast<const uint32_t *>(w),
+    dp::launch_k(gather_kernel<uint32_t>, (int)blocks, 256, 0, s, p, ids, static_cast<const uint32_t *>(w),
                                                        static_cast<uint32_t *>(out), row_bytes / 4);
   } else {
-    gather_kernel<uint8_t><<<(int)blocks, 256, 0, s>>>(p, ids, static_cast<const uint8_t *>(w),
+    dp::launch_k(gather_kernel<uint8_t>, (int)blocks, 256, 0, s, p, ids, static_cast<const uint8_t *>(w),
                                                       static_cast<uint8_t *>(out), row_bytes);
   }
   DP_CHECK_CUDA(cudaGetLastError());

@@ -41,6 +41,8 @@ __global__ void __launch_bounds__(kThreads) sgemm_kernel(dp_gemm_params p, const
                                                          const TB *__restrict__ B, void *C,
                                                          const void *bias, const void *res, bool a_vec,
                                                          bool b_vec) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   __shared__ __align__(16) float As[2][BK][BM + 4];
   __shared__ __align__(16) float Bs[2][BK][BN + 4];
   const int64_t bz = blockIdx.z;
@@ -153,10 +155,10 @@ int launch_typed(const dp_gemm_params &p, const void *A, const void *B, void *C,
                      (p.stride_b2 * esz) % vbytes == 0;
   dim3 grid((unsigned)((p.N + BN - 1) / BN), (unsigned)((p.M + BM - 1) / BM), (unsigned)p.batch);
   if (p.b_layout == DP_B_NK)
-    sgemm_kernel<TA, TB, true><<<grid, kThreads, 0, s>>>(p, static_cast<const TA *>(A),
+    dp::launch_k(sgemm_kernel<TA, TB, true>, grid, kThreads, 0, s, p, static_cast<const TA *>(A),
                                                           static_cast<const TB *>(B), C, bias, res, a_vec, b_vec);
   else
-    sgemm_kernel<TA, TB, false><<<grid, kThreads, 0, s>>>(p, static_cast<const TA *>(A),
+    dp::launch_k(sgemm_kernel<TA, TB, false>, grid, kThreads, 0, s, p, static_cast<const TA *>(A),
                                                            static_cast<const TB *>(B), C, bias, res, a_vec, b_vec);
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;

@@ -18,6 +18,8 @@ namespace dpk_splitk {
 
 __global__ void __launch_bounds__(256) splitk_reduce_kernel(dp_splitk_params sp, const float *__restrict__ ws,
                                                              void *C, const void *bias, const void *res) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   const dp_gemm_params &p = sp.gemm;
   const dp::Epilogue ep(p, C, bias, res, 0);
   const int64_t nq = (p.N + 3) / 4;  // column quads per row
@@ -45,6 +47,8 @@ __global__ void __launch_bounds__(256) splitk_reduce_kernel(dp_splitk_params sp,
 }
 
 __global__ void argmax_keys_kernel(dp_argmax_keys_params p, unsigned long long *keys, void *out) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < p.n; i += (int64_t)gridDim.x * blockDim.x) {
     if (p.mode == 0) {
       keys[i] = 0ull;
@@ -79,7 +83,7 @@ int launch_splitk_reduce(const dp_splitk_params &sp, const void *ws, void *C, co
   int64_t blocks = (quads + 255) / 256;
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
-  dpk_splitk::splitk_reduce_kernel<<<(int)blocks, 256, 0, s>>>(sp, static_cast<const float *>(ws), C, bias, res);
+  dp::launch_k(dpk_splitk::splitk_reduce_kernel, (int)blocks, 256, 0, s, sp, static_cast<const float *>(ws), C, bias, res);
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }
@@ -93,7 +97,7 @@ int launch_argmax_keys(const dp_argmax_keys_params &p, void *keys, void *out, cu
   }
   int64_t blocks = (p.n + 255) / 256;
   if (blocks > 4096) blocks = 4096;
-  dpk_splitk::argmax_keys_kernel<<<(int)blocks, 256, 0, s>>>(p, static_cast<unsigned long long *>(keys), out);
+  dp::launch_k(dpk_splitk::argmax_keys_kernel, (int)blocks, 256, 0, s, p, static_cast<unsigned long long *>(keys), out);
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }

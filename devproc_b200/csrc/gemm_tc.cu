@@ -838,6 +838,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  dp::pdl_trigger();
   // The pair's leader (rank 0) issues the MMAs for both CTAs and owns the
   // barriers that gather both CTAs' operand bytes and epilogue releases.
   const uint32_t rank = CG == 2 ? cluster_rank() : 0;
@@ -882,6 +883,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_slot;
   volatile int *flag = &abort_flag;
+  dp::pdl_wait();  // set-up above touches no global memory; the previous kernel's results are visible from here
 
   if (warp == 0) {
     {
@@ -1564,22 +1566,24 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
     if (st != DP_OK) return st;
     if (!s.sk_ipp && grid > s.num_tiles) grid = s.num_tiles;
     if (cb == 4)
-      tc_gemm_kernel<4, 1><<<grid, kThreads, smem_bytes<1>(), stream>>>(ma, mb, mc, p, s, C, bias, res, ws, cnt);
+      dp::launch_k(tc_gemm_kernel<4, 1>, grid, kThreads, smem_bytes<1>(), stream, ma, mb, mc, p, s, C, bias, res, ws, cnt);
     else
-      tc_gemm_kernel<2, 1><<<grid, kThreads, smem_bytes<1>(), stream>>>(ma, mb, mc, p, s, C, bias, res, ws, cnt);
+      dp::launch_k(tc_gemm_kernel<2, 1>, grid, kThreads, smem_bytes<1>(), stream, ma, mb, mc, p, s, C, bias, res, ws, cnt);
   } else {
     auto kern = cb == 4 ? tc_gemm_kernel<4, 2> : tc_gemm_kernel<2, 2>;
     cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = 2;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;  // as dp::launch_k
+    attr[1].val.programmaticStreamSerializationAllowed = DP_PDL ? 1 : 0;
     cfg.blockDim = dim3(kThreads);
     cfg.dynamicSmemBytes = smem_bytes<2>();
     cfg.stream = stream;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = 1;  // the cluster shape (the occupancy query)
     // Co-resident pairs (clusters never straddle a GPC, so this can be below SMs / 2).
     static int pairs[kMaxDevices][2] = {};
     int &np = pairs[dev][cb == 4 ? 0 : 1];
@@ -1597,6 +1601,7 @@ int launch_gemm_tc(const dp_gemm_params &p, const void *A, const void *B, void *
     if (st != DP_OK) return st;
     const int grid_pairs = (s.sk_ipp || np < s.num_tiles) ? np : s.num_tiles;
     cfg.gridDim = dim3(2 * grid_pairs);
+    cfg.numAttrs = 2;  // cluster shape + programmatic dependent launch
     DP_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p, s, C, bias, res, ws, cnt));
   }
   DP_CHECK_CUDA(cudaGetLastError());

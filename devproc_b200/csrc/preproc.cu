@@ -118,6 +118,8 @@ __device__ __forceinline__ int staged_start(int oy, const Geo &g) {
 template <typename TIn, typename TOut, bool IN_NCHW, bool OUT_NCHW>
 __global__ void __launch_bounds__(kMaxThreads) preproc_bulk_kernel(Geo g, const TIn *__restrict__ in,
                                                                    TOut *__restrict__ out, int n_units) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[kStages];
   const int stage_elems = g.planes * g.plane_stride_s;
@@ -176,6 +178,8 @@ __global__ void __launch_bounds__(kMaxThreads) preproc_bulk_kernel(Geo g, const 
 template <typename TIn, typename TOut, bool IN_NCHW, bool OUT_NCHW>
 __global__ void __launch_bounds__(kMaxThreads) preproc_plain_kernel(Geo g, const TIn *__restrict__ in,
                                                                     TOut *__restrict__ out, int n_units) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   TIn *st = reinterpret_cast<TIn *>(smem_raw);
   const int plane_elems = g.rows_staged * g.row_elems;
@@ -371,6 +375,8 @@ constexpr int kFastRowsPerThread = 8;  // output rows a thread computes per unit
 template <typename TOut>
 __global__ void __launch_bounds__(kMaxThreads + 32) preproc_u8c3_kernel(FastGeo g, const uint8_t *__restrict__ in,
                                                                         TOut *__restrict__ out, int n_units) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full[kFastStages];
   __shared__ __align__(8) uint64_t empty[kFastStages];
@@ -514,7 +520,7 @@ int launch_fast(const dp_preproc_params &p, const void *in, void *out, cudaStrea
   if (st != DP_OK) return st;
   int grid = dp::num_sms() * per_sm;
   if (grid > n_units) grid = n_units;
-  kern<<<grid, threads, smem, s>>>(g, static_cast<const uint8_t *>(in), static_cast<TOut *>(out), n_units);
+  dp::launch_k(kern, grid, threads, smem, s, g, static_cast<const uint8_t *>(in), static_cast<TOut *>(out), n_units);
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }
@@ -540,7 +546,7 @@ int launch_typed(const Geo &g, const void *in, void *out, cudaStream_t s) {
     if (st != DP_OK) return st;
     int grid = sms * per_sm;
     if (grid > n_units) grid = n_units;
-    kern<<<grid, threads, smem, s>>>(g, static_cast<const TIn *>(in), static_cast<TOut *>(out), n_units);
+    dp::launch_k(kern, grid, threads, smem, s, g, static_cast<const TIn *>(in), static_cast<TOut *>(out), n_units);
   } else {
     auto kern = preproc_plain_kernel<TIn, TOut, IN_NCHW, OUT_NCHW>;
     const size_t smem = stage_bytes;
@@ -550,7 +556,7 @@ int launch_typed(const Geo &g, const void *in, void *out, cudaStream_t s) {
     if (st != DP_OK) return st;
     int grid = sms * per_sm;
     if (grid > n_units) grid = n_units;
-    kern<<<grid, threads, smem, s>>>(g, static_cast<const TIn *>(in), static_cast<TOut *>(out), n_units);
+    dp::launch_k(kern, grid, threads, smem, s, g, static_cast<const TIn *>(in), static_cast<TOut *>(out), n_units);
   }
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;

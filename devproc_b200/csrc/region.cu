@@ -156,6 +156,8 @@ __device__ __forceinline__ void store_run(void *ptr, int64_t off, int64_t st, in
 // item decomposition (more than 2^31 items).
 template <int E, bool WIDE>
 __global__ void __launch_bounds__(kThreads) region_kernel(const dp_region_desc d, Ops c, const Geom g) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < g.items; t += nthreads) {
     int64_t coord[kR];
@@ -215,6 +217,8 @@ __global__ void __launch_bounds__(kThreads) region_kernel(const dp_region_desc d
 // round trip, so 32/64-bit integers survive), E per work item.
 template <typename T, int E, bool WIDE>
 __global__ void __launch_bounds__(kThreads) copy_kernel(const T *__restrict__ in, T *__restrict__ out, const Geom g) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   const int64_t nthreads = (int64_t)gridDim.x * blockDim.x;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < g.items; t += nthreads) {
     int64_t coord[kR];
@@ -278,6 +282,8 @@ struct TDims {
 
 template <typename T>
 __global__ void __launch_bounds__(256) transpose_copy_kernel(TDims d, const T *__restrict__ in, T *__restrict__ out) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   __shared__ T tile[32][33];
   const int last = d.rank - 1;
   const int64_t j0 = (int64_t)blockIdx.y * 32, l0 = (int64_t)blockIdx.x * 32;
@@ -382,10 +388,10 @@ int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t 
       if (gx < (1ll << 31) && gy < 65536 && zcount < 65536) {
         dim3 grid((unsigned)gx, (unsigned)gy, (unsigned)zcount);
         switch (dtype_bytes(d.dtype[0])) {
-          case 1: transpose_copy_kernel<uint8_t><<<grid, 256, 0, s>>>(t, (const uint8_t *)ops[0], (uint8_t *)ops[1]); break;
-          case 2: transpose_copy_kernel<uint16_t><<<grid, 256, 0, s>>>(t, (const uint16_t *)ops[0], (uint16_t *)ops[1]); break;
-          case 4: transpose_copy_kernel<uint32_t><<<grid, 256, 0, s>>>(t, (const uint32_t *)ops[0], (uint32_t *)ops[1]); break;
-          default: transpose_copy_kernel<uint64_t><<<grid, 256, 0, s>>>(t, (const uint64_t *)ops[0], (uint64_t *)ops[1]); break;
+          case 1: dp::launch_k(transpose_copy_kernel<uint8_t>, grid, 256, 0, s, t, (const uint8_t *)ops[0], (uint8_t *)ops[1]); break;
+          case 2: dp::launch_k(transpose_copy_kernel<uint16_t>, grid, 256, 0, s, t, (const uint16_t *)ops[0], (uint16_t *)ops[1]); break;
+          case 4: dp::launch_k(transpose_copy_kernel<uint32_t>, grid, 256, 0, s, t, (const uint32_t *)ops[0], (uint32_t *)ops[1]); break;
+          default: dp::launch_k(transpose_copy_kernel<uint64_t>, grid, 256, 0, s, t, (const uint64_t *)ops[0], (uint64_t *)ops[1]); break;
         }
         DP_CHECK_CUDA(cudaGetLastError());
         return DP_OK;
@@ -421,26 +427,26 @@ int launch_region(const dp_region_desc &d, const void *const *ops, cudaStream_t 
     if (pure_copy) {                                                                                  \
       switch (dtype_bytes(d.dtype[0])) {                                                              \
         case 1:                                                                                       \
-          if (wide) copy_kernel<uint8_t, EE, true><<<grid, block, 0, s>>>((const uint8_t *)ops[0], (uint8_t *)ops[1], g); \
-          else copy_kernel<uint8_t, EE, false><<<grid, block, 0, s>>>((const uint8_t *)ops[0], (uint8_t *)ops[1], g);    \
+          if (wide) dp::launch_k(copy_kernel<uint8_t, EE, true>, grid, block, 0, s, (const uint8_t *)ops[0], (uint8_t *)ops[1], g); \
+          else dp::launch_k(copy_kernel<uint8_t, EE, false>, grid, block, 0, s, (const uint8_t *)ops[0], (uint8_t *)ops[1], g);    \
           break;                                                                                      \
         case 2:                                                                                       \
-          if (wide) copy_kernel<uint16_t, EE, true><<<grid, block, 0, s>>>((const uint16_t *)ops[0], (uint16_t *)ops[1], g); \
-          else copy_kernel<uint16_t, EE, false><<<grid, block, 0, s>>>((const uint16_t *)ops[0], (uint16_t *)ops[1], g);    \
+          if (wide) dp::launch_k(copy_kernel<uint16_t, EE, true>, grid, block, 0, s, (const uint16_t *)ops[0], (uint16_t *)ops[1], g); \
+          else dp::launch_k(copy_kernel<uint16_t, EE, false>, grid, block, 0, s, (const uint16_t *)ops[0], (uint16_t *)ops[1], g);    \
           break;                                                                                      \
         case 4:                                                                                       \
-          if (wide) copy_kernel<uint32_t, EE, true><<<grid, block, 0, s>>>((const uint32_t *)ops[0], (uint32_t *)ops[1], g); \
-          else copy_kernel<uint32_t, EE, false><<<grid, block, 0, s>>>((const uint32_t *)ops[0], (uint32_t *)ops[1], g);    \
+          if (wide) dp::launch_k(copy_kernel<uint32_t, EE, true>, grid, block, 0, s, (const uint32_t *)ops[0], (uint32_t *)ops[1], g); \
+          else dp::launch_k(copy_kernel<uint32_t, EE, false>, grid, block, 0, s, (const uint32_t *)ops[0], (uint32_t *)ops[1], g);    \
           break;                                                                                      \
         default:                                                                                      \
-          if (wide) copy_kernel<uint64_t, EE, true><<<grid, block, 0, s>>>((const uint64_t *)ops[0], (uint64_t *)ops[1], g); \
-          else copy_kernel<uint64_t, EE, false><<<grid, block, 0, s>>>((const uint64_t *)ops[0], (uint64_t *)ops[1], g);    \
+          if (wide) dp::launch_k(copy_kernel<uint64_t, EE, true>, grid, block, 0, s, (const uint64_t *)ops[0], (uint64_t *)ops[1], g); \
+          else dp::launch_k(copy_kernel<uint64_t, EE, false>, grid, block, 0, s, (const uint64_t *)ops[0], (uint64_t *)ops[1], g);    \
           break;                                                                                      \
       }                                                                                               \
     } else if (wide) {                                                                                \
-      region_kernel<EE, true><<<grid, block, 0, s>>>(d, c, g);                                        \
+      dp::launch_k(region_kernel<EE, true>, grid, block, 0, s, d, c, g);                                        \
     } else {                                                                                          \
-      region_kernel<EE, false><<<grid, block, 0, s>>>(d, c, g);                                       \
+      dp::launch_k(region_kernel<EE, false>, grid, block, 0, s, d, c, g);                                       \
     }                                                                                                 \
   } while (0)
   Ops c{};

@@ -72,6 +72,8 @@ template <typename TX, typename TT>
 __global__ void __launch_bounds__(kThreads) rope_kernel(RopeGeo g, const TX *__restrict__ x,
                                                         const TT *__restrict__ cosv, const TT *__restrict__ sinv,
                                                         TX *__restrict__ out) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   constexpr int VEC = 16 / (int)sizeof(TX);
   for (uint32_t u = blockIdx.x * (uint32_t)kThreads + threadIdx.x; u < g.items;
        u += gridDim.x * (uint32_t)kThreads) {
@@ -108,7 +110,7 @@ int launch_typed(const RopeGeo &g, const void *x, const void *c, const void *s, 
   int64_t blocks = ((int64_t)g.items + kThreads - 1) / kThreads;
   const int64_t cap = (int64_t)dp::num_sms() * (2048 / kThreads) * 4;
   if (blocks > cap) blocks = cap;
-  rope_kernel<TX, TT><<<(unsigned)blocks, kThreads, 0, st>>>(g, static_cast<const TX *>(x),
+  dp::launch_k(rope_kernel<TX, TT>, (unsigned)blocks, kThreads, 0, st, g, static_cast<const TX *>(x),
                                                               static_cast<const TT *>(c),
                                                               static_cast<const TT *>(s), static_cast<TX *>(o));
   DP_CHECK_CUDA(cudaGetLastError());

@@ -139,6 +139,8 @@ __device__ __forceinline__ void acc_step(float &acc, ArgVal &best, float v, long
 template <typename TIn, int VEC, int KIND>
 __global__ void __launch_bounds__(256) reduce_warp_kernel(dp_rowreduce_params p, const TIn *__restrict__ in,
                                                           void *out) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
@@ -247,6 +249,8 @@ template <typename TIn, typename TOut, int VEC, int NV>
 __global__ void __launch_bounds__(kMaxThreads) norm_kernel(dp_rowreduce_params p, const TIn *__restrict__ in,
                                                            const TIn *__restrict__ w, const TIn *__restrict__ bias,
                                                            TOut *__restrict__ out) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   __shared__ float red[32];
   const int64_t step = (int64_t)blockDim.x * VEC;
   const float n = (float)p.cols;
@@ -416,6 +420,8 @@ template <typename TIn, typename TOut, int VEC, int NV, int KIND>
 __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, const TIn *__restrict__ in,
                                                         const TIn *__restrict__ w, const TIn *__restrict__ bias,
                                                         TOut *__restrict__ out) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   // Rows need not hold a whole number of vectors: the one vector that
   // straddles the row end is read and written element by element.
   const int lane = threadIdx.x & 31;
@@ -582,6 +588,8 @@ template <typename T, int NV, int KIND>
 __global__ void __launch_bounds__(256) norm16_kernel(dp_rowreduce_params p, const T *__restrict__ in,
                                                      const T *__restrict__ w, const T *__restrict__ bias,
                                                      T *__restrict__ out) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   extern __shared__ uint4 wb_smem[];
   T *ws = reinterpret_cast<T *>(wb_smem);
   T *bs = ws + p.cols;
@@ -677,7 +685,7 @@ int launch_norm16_kind(const dp_rowreduce_params &p, const T *x, const T *w, con
   int64_t blocks = (p.rows * 32 + threads - 1) / threads;
   const int64_t cap = (int64_t)dp::num_sms() * per_sm;
   if (blocks > cap) blocks = cap;
-  norm16_kernel<T, NV, KIND><<<(int)blocks, threads, smem, s>>>(p, x, w, b, y);
+  dp::launch_k(norm16_kernel<T, NV, KIND>, (int)blocks, threads, smem, s, p, x, w, b, y);
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }
@@ -733,6 +741,8 @@ __global__ void __launch_bounds__(32 * kStagedWarps) norm_staged_kernel(dp_rowre
                                                                         const float *__restrict__ w,
                                                                         const float *__restrict__ bias,
                                                                         float *__restrict__ out, int row_floats) {
+  dp::pdl_trigger();
+  dp::pdl_wait();
   extern __shared__ __align__(16) float srow[];
   __shared__ __align__(8) uint64_t bars[kStagedWarps][2];
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
@@ -861,13 +871,13 @@ int launch_norm_warp(const dp_rowreduce_params &p, const void *in, const void *w
   auto *y = static_cast<TOut *>(out);
   switch (p.kind) {
     case DP_RED_SOFTMAX:
-      norm_warp_kernel<TIn, TOut, VEC, NV, DP_RED_SOFTMAX><<<(int)blocks, threads, 0, s>>>(p, x, wp, bp, y);
+      dp::launch_k(norm_warp_kernel<TIn, TOut, VEC, NV, DP_RED_SOFTMAX>, (int)blocks, threads, 0, s, p, x, wp, bp, y);
       break;
     case DP_RED_RMSNORM:
-      norm_warp_kernel<TIn, TOut, VEC, NV, DP_RED_RMSNORM><<<(int)blocks, threads, 0, s>>>(p, x, wp, bp, y);
+      dp::launch_k(norm_warp_kernel<TIn, TOut, VEC, NV, DP_RED_RMSNORM>, (int)blocks, threads, 0, s, p, x, wp, bp, y);
       break;
     default:
-      norm_warp_kernel<TIn, TOut, VEC, NV, DP_RED_LAYERNORM><<<(int)blocks, threads, 0, s>>>(p, x, wp, bp, y);
+      dp::launch_k(norm_warp_kernel<TIn, TOut, VEC, NV, DP_RED_LAYERNORM>, (int)blocks, threads, 0, s, p, x, wp, bp, y);
       break;
   }
   DP_CHECK_CUDA(cudaGetLastError());
@@ -888,11 +898,11 @@ int launch_stream(const dp_rowreduce_params &p, const void *in, void *out, cudaS
   if (blocks > cap) blocks = cap;
   const TIn *x = static_cast<const TIn *>(in);
   switch (p.kind) {
-    case DP_RED_SUM: reduce_warp_kernel<TIn, VEC, DP_RED_SUM><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
-    case DP_RED_MAX: reduce_warp_kernel<TIn, VEC, DP_RED_MAX><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
-    case DP_RED_MIN: reduce_warp_kernel<TIn, VEC, DP_RED_MIN><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
-    case DP_RED_MEAN: reduce_warp_kernel<TIn, VEC, DP_RED_MEAN><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
-    default: reduce_warp_kernel<TIn, VEC, DP_RED_ARGMAX><<<(int)blocks, threads, 0, s>>>(p, x, out); break;
+    case DP_RED_SUM: dp::launch_k(reduce_warp_kernel<TIn, VEC, DP_RED_SUM>, (int)blocks, threads, 0, s, p, x, out); break;
+    case DP_RED_MAX: dp::launch_k(reduce_warp_kernel<TIn, VEC, DP_RED_MAX>, (int)blocks, threads, 0, s, p, x, out); break;
+    case DP_RED_MIN: dp::launch_k(reduce_warp_kernel<TIn, VEC, DP_RED_MIN>, (int)blocks, threads, 0, s, p, x, out); break;
+    case DP_RED_MEAN: dp::launch_k(reduce_warp_kernel<TIn, VEC, DP_RED_MEAN>, (int)blocks, threads, 0, s, p, x, out); break;
+    default: dp::launch_k(reduce_warp_kernel<TIn, VEC, DP_RED_ARGMAX>, (int)blocks, threads, 0, s, p, x, out); break;
   }
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
@@ -911,15 +921,15 @@ int launch_norm(const dp_rowreduce_params &p, const void *in, const void *w, con
   auto *bp = static_cast<const TIn *>(b);
   auto *y = static_cast<TOut *>(out);
   if (nv <= 1)
-    norm_kernel<TIn, TOut, VEC, 1><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+    dp::launch_k(norm_kernel<TIn, TOut, VEC, 1>, grid, threads, 0, s, p, x, wp, bp, y);
   else if (nv <= 2)
-    norm_kernel<TIn, TOut, VEC, 2><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+    dp::launch_k(norm_kernel<TIn, TOut, VEC, 2>, grid, threads, 0, s, p, x, wp, bp, y);
   else if (nv <= 4)
-    norm_kernel<TIn, TOut, VEC, 4><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+    dp::launch_k(norm_kernel<TIn, TOut, VEC, 4>, grid, threads, 0, s, p, x, wp, bp, y);
   else if (nv <= 8)
-    norm_kernel<TIn, TOut, VEC, 8><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+    dp::launch_k(norm_kernel<TIn, TOut, VEC, 8>, grid, threads, 0, s, p, x, wp, bp, y);
   else
-    norm_kernel<TIn, TOut, VEC, 0><<<grid, threads, 0, s>>>(p, x, wp, bp, y);
+    dp::launch_k(norm_kernel<TIn, TOut, VEC, 0>, grid, threads, 0, s, p, x, wp, bp, y);
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }
@@ -940,7 +950,7 @@ int launch_norm_staged(const dp_rowreduce_params &p, const void *in, const void 
     }
     int64_t blocks = (p.rows + kStagedWarps - 1) / kStagedWarps;
     if (blocks > dp::num_sms()) blocks = dp::num_sms();
-    kern<<<(int)blocks, 32 * kStagedWarps, smem, s>>>(p, static_cast<const float *>(in),
+    dp::launch_k(kern, (int)blocks, 32 * kStagedWarps, smem, s, p, static_cast<const float *>(in),
                                                       static_cast<const float *>(w), static_cast<const float *>(b),
                                                       static_cast<float *>(out), row_floats);
     DP_CHECK_CUDA(cudaGetLastError());
