@@ -42,6 +42,7 @@ DP_EPI_BIAS, DP_EPI_RELU, DP_EPI_GELU_ERF, DP_EPI_GELU_TANH, DP_EPI_RESIDUAL, DP
 DP_EPI_SOFTMAX = 64
 DP_EPI_MUL = 128
 DP_EPI_ARGMAX = 256
+DP_EPI_TF32SPLIT = 512
 
 DP_REGION_MAX_OPERANDS, DP_REGION_MAX_RANK, DP_REGION_MAX_INSTR = 8, 6, 64
 DP_REGION_MAX_CONST, DP_REGION_MAX_REGS = 32, 8
@@ -69,7 +70,7 @@ class PreprocParams(ctypes.Structure):
 
 class RowReduceParams(ctypes.Structure):
     _fields_ = [("kind", ctypes.c_int32), ("in_dtype", ctypes.c_int32), ("out_dtype", ctypes.c_int32),
-                ("has_weight", ctypes.c_int32), ("has_bias", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("has_weight", ctypes.c_int32), ("has_bias", ctypes.c_int32), ("out_split", ctypes.c_int32),
                 ("rows", ctypes.c_int64), ("cols", ctypes.c_int64), ("in_row_stride", ctypes.c_int64),
                 ("out_row_stride", ctypes.c_int64), ("eps", ctypes.c_float), ("weight_offset", ctypes.c_float)]
 

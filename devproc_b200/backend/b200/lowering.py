@@ -268,6 +268,8 @@ class Lowerer:
         self.const_tensors = dict(const_tensors or {})
         self.new_consts: List[Tuple[str, Buffer]] = []
         self.views: Dict[str, View] = {}
+        # values whose producer wrote them directly as a 3xTF32 operand [hi | hi | lo]
+        self.tf32_split_views: Dict[str, View] = {}
         self.buffers: List[Buffer] = []
         self.records: List[Record] = []
         self.done = set()   # ids of ops already lowered (fused)
@@ -769,8 +771,44 @@ class Lowerer:
         buf = self.derived_const(name, "float32", (value.type.shape[0], 3 * K))
         return View(buf, (value.type.shape[0], 3 * K), (3 * K, 1))
 
+    def tf32_fold_width(self, value: Value) -> int:
+        """K when ``value``'s only consumer is a linear that runs as 3xTF32 with
+        ``value`` as its activation (possibly through single-use reshapes that
+        keep the last dim), so that the producer can write the [hi | hi | lo]
+        operand itself instead of ``value`` (0 otherwise)."""
+        K = value.type.shape[-1]
+        v, nxt = value, self.single_use(value)
+        while (nxt is not None and nxt.name == "reshape" and id(nxt) not in self.done
+               and nxt.outputs[0].type.shape[-1] == K):
+            v = nxt.outputs[0]
+            nxt = self.single_use(v)
+        if (nxt is None or nxt.name != "linear" or nxt.inputs[0].name != v.name
+                or value.type.dtype != "float32" or len(self.sibling_linears(nxt)) > 1
+                or not self.tf32_split_ok(nxt)):
+            return 0
+        return K
+
+    def new_tf32_split_view(self, value: Value, K: int) -> View:
+        """The [rows, 3K] operand buffer that ``value``'s producer writes; the
+        reshapes between ``value`` and its linear are consumed here."""
+        rows = _prod(value.type.shape[:-1])
+        out = self.new_buffer("arena", "float32", (rows, 3 * K), value.name + "_3xtf32")
+        view = View(out, (rows, 3 * K), (3 * K, 1))
+        v = value
+        self.tf32_split_views[v.name] = view
+        nxt = self.single_use(v)
+        while nxt is not None and nxt.name == "reshape":
+            self.done.add(id(nxt))
+            v = nxt.outputs[0]
+            self.tf32_split_views[v.name] = view
+            nxt = self.single_use(v)
+        return view
+
     def tf32_split_rows(self, value: Value, K: int) -> View:
-        """[rows, 3K] = [x_hi | x_hi | x_lo] in one region."""
+        """[rows, 3K] = [x_hi | x_hi | x_lo]: written by the producer when it
+        could (embedding, split-K reduce, row norm), else one region."""
+        if value.name in self.tf32_split_views:
+            return self.tf32_split_views[value.name]
         rows = _prod(value.type.shape[:-1])
         src = self.views[value.name]
         flat = view_reshape(src.shape, src.strides, (rows, K))
@@ -1008,9 +1046,19 @@ class Lowerer:
         sp = N.SplitKParams()
         sp.gemm = p
         sp.splits, sp.slice_stride = splits, p.M * p.N
+        split_note = ""
+        K = self.tf32_fold_width(cur) if c_dtype == "float32" and not (epi & N.DP_EPI_ARGMAX) else 0
+        if K == p.N and cur.name in self.views and self.views[cur.name] is out and out.buf.first < 0:
+            # Feeding a 3xTF32 linear: the reduce stores [hi | hi | lo] rows.
+            del self.views[cur.name]
+            self.buffers.remove(out.buf)
+            out = self.new_tf32_split_view(cur, K)
+            sp.gemm.epilogue |= N.DP_EPI_TF32SPLIT
+            sp.gemm.ldc = 3 * p.N
+            split_note = " -> 3xtf32 operand"
         self.emit(N.DP_K_SPLITK, [ws, out.buf, bias.buf if bias is not None else None,
                                   residual.buf if residual is not None else None], sp,
-                  f"splitk reduce {splits}x{p.M}x{p.N} epi{epi}", 0, ws.nbytes + out.buf.nbytes)
+                  f"splitk reduce {splits}x{p.M}x{p.N} epi{epi}{split_note}", 0, ws.nbytes + out.buf.nbytes)
 
     def emit_gemm_argmax(self, op, p, tf32, a_dtype, a_buf, b_buf, bias, residual, logits_dtype, idx_val) -> None:
         """A linear whose only consumer is a row argmax: three records - clear
@@ -1111,10 +1159,17 @@ class Lowerer:
             p.has_weight = 1 if w is not None else 0
             p.has_bias = 1 if b is not None else 0
         p.out_dtype = N.DTYPE_CODE[out_dtype]
-        out = self.new_value_view(out_val, dtype=out_dtype)
+        K = self.tf32_fold_width(out_val) if op.name in ("softmax", "layer_norm", "rms_norm") else 0
+        if K and t.dtype == "float32" and out_dtype == "float32" and d == rank - 1 and cols <= 4096:
+            # Feeding a 3xTF32 linear: rows stored as [hi | hi | lo].
+            out = self.new_tf32_split_view(out_val, K)
+            p.out_split, p.out_row_stride = 1, 3 * cols
+        else:
+            out = self.new_value_view(out_val, dtype=out_dtype)
         nbytes = xv.buf.nbytes + out.buf.nbytes
         self.emit(N.DP_K_ROWREDUCE, [xv.buf, w.buf if w else None, b.buf if b else None, out.buf], p,
-                  f"rowreduce {op.name} {rows}x{cols} {t.dtype}->{out_dtype}", 0, nbytes)
+                  f"rowreduce {op.name} {rows}x{cols} {t.dtype}->{out_dtype}{' 3xtf32 operand' if p.out_split else ''}",
+                  0, nbytes)
 
     def _param_like(self, value: Value, dtype: str) -> View:
         v = self.contiguous(value)
@@ -1391,7 +1446,21 @@ class Lowerer:
     def lower_embedding(self, op: Op) -> None:
         ids = self.contiguous(op.inputs[0])
         w = self.contiguous(op.inputs[1])
-        out = self.new_value_view(op.outputs[0])
+        K = self.tf32_fold_width(op.outputs[0])
+        src = self.views[op.inputs[1].name]
+        if (K and src.buf.kind == "const" and src.buf.base is None and src.buf.name in self.const_tensors
+                and w.buf is src.buf and w.buf.dtype == "float32" and len(w.shape) == 2):
+            # Feeding a 3xTF32 linear: gather rows of the table split once at compile time.
+            import torch
+            name = src.buf.name + "|3xtf32rows"
+            if name not in self.const_tensors:
+                t = self.const_tensors[src.buf.name].float().reshape(w.shape)
+                hi = (t.contiguous().view(torch.int32) & -8192).view(torch.float32)
+                self.const_tensors[name] = torch.cat([hi, hi, t - hi], dim=1).contiguous()
+            w = View(self.derived_const(name, "float32", (w.shape[0], 3 * K)), (w.shape[0], 3 * K), (3 * K, 1))
+            out = self.new_tf32_split_view(op.outputs[0], K)
+        else:
+            out = self.new_value_view(op.outputs[0])
         p = N.EmbeddingParams()
         p.n_ids = _prod(ids.shape)
         p.vocab, p.dim = w.shape

@@ -44,6 +44,31 @@ struct Epilogue {
   __device__ __forceinline__ void store4(int64_t m, int64_t n, float v0, float v1, float v2, float v3) const {
     float v[4] = {v0, v1, v2, v3};
     const int64_t base = c_off + m * p.ldc + n;
+    if (p.epilogue & DP_EPI_TF32SPLIT) {  // [hi | hi | lo] blocks N columns apart (fp32 C)
+      float *c = static_cast<float *>(C) + base;
+      float hi[4], lo[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float x = n + j < p.N ? apply(m, n + j, v[j]) : 0.0f;
+        hi[j] = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+        lo[j] = x - hi[j];
+      }
+      if (n + 3 < p.N && (base & 3) == 0 && (p.N & 3) == 0 && (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
+        const float4 h4 = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *reinterpret_cast<float4 *>(c) = h4;
+        *reinterpret_cast<float4 *>(c + p.N) = h4;
+        *reinterpret_cast<float4 *>(c + 2 * p.N) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+        return;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (n + j >= p.N) break;
+        c[j] = hi[j];
+        c[p.N + j] = hi[j];
+        c[2 * p.N + j] = lo[j];
+      }
+      return;
+    }
     if (n + 3 < p.N && p.c_dtype == DP_F32 && (base & 3) == 0 &&
         (reinterpret_cast<uintptr_t>(C) & 15) == 0) {
 #pragma unroll

@@ -32,6 +32,8 @@ int launch_gemm(const dp_gemm_params &p, const void *A, const void *B, void *C, 
     DP_REQUIRE(p.epilogue == DP_EPI_SOFTMAX, DP_ERR_ARG, "gemm: the softmax epilogue takes no other epilogue flag");
     DP_REQUIRE(p.N <= 256, DP_ERR_UNSUPPORTED, "gemm: the softmax epilogue needs N <= 256");
   }
+  DP_REQUIRE(!(p.epilogue & DP_EPI_TF32SPLIT), DP_ERR_UNSUPPORTED,
+             "gemm: the 3xTF32 operand store is an epilogue of dp_gemm_splitk_reduce only");
   if (p.epilogue & DP_EPI_ARGMAX)
     DP_REQUIRE(p.batch == 1 && !(p.epilogue & DP_EPI_SOFTMAX) &&
                    (reinterpret_cast<uintptr_t>(C) & 7) == 0,

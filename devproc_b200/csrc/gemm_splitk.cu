@@ -76,7 +76,11 @@ int launch_splitk_reduce(const dp_splitk_params &sp, const void *ws, void *C, co
   DP_REQUIRE(p.ldc >= p.N, DP_ERR_SHAPE, "splitk: ldc < N");
   DP_REQUIRE(p.c_dtype == DP_F32 || p.c_dtype == DP_BF16 || p.c_dtype == DP_F16, DP_ERR_ARG,
              "splitk: C must be f32/bf16/f16");
-  DP_REQUIRE(!(p.epilogue & DP_EPI_SOFTMAX), DP_ERR_UNSUPPORTED, "splitk: no softmax epilogue");
+  DP_REQUIRE(!(p.epilogue & (DP_EPI_SOFTMAX | DP_EPI_ARGMAX)), DP_ERR_UNSUPPORTED,
+             "splitk: no softmax or argmax epilogue");
+  if (p.epilogue & DP_EPI_TF32SPLIT)
+    DP_REQUIRE(p.c_dtype == DP_F32 && p.ldc >= 3 * p.N, DP_ERR_ARG,
+               "splitk: the 3xTF32 operand store needs fp32 C with ldc >= 3 N");
   if (p.epilogue & DP_EPI_BIAS) DP_REQUIRE(bias != nullptr, DP_ERR_ARG, "splitk: bias");
   if (p.epilogue & (DP_EPI_RESIDUAL | DP_EPI_MUL)) DP_REQUIRE(res != nullptr, DP_ERR_ARG, "splitk: residual");
   const int64_t quads = p.M * ((p.N + 3) / 4);

@@ -542,6 +542,30 @@ __global__ void __launch_bounds__(256) norm_warp_kernel(dp_rowreduce_params p, c
           o[j] = t;
         }
       }
+      if constexpr (std::is_same<TOut, float>::value) {
+        if (p.out_split) {  // [hi | hi | lo], the operand of a 3xTF32 product
+          float hi[VEC], lo[VEC];
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            hi[j] = __uint_as_float(__float_as_uint(o[j]) & 0xffffe000u);
+            lo[j] = o[j] - hi[j];
+          }
+          if (full) {
+            store_vec<TOut, VEC>(y + c, hi);
+            store_vec<TOut, VEC>(y + p.cols + c, hi);
+            store_vec<TOut, VEC>(y + 2 * p.cols + c, lo);
+          } else {
+#pragma unroll
+            for (int j = 0; j < VEC; ++j)
+              if (c + j < p.cols) {
+                y[c + j] = hi[j];
+                y[p.cols + c + j] = hi[j];
+                y[2 * p.cols + c + j] = lo[j];
+              }
+          }
+          continue;
+        }
+      }
       if (full) {
         store_vec<TOut, VEC>(y + c, o);
       } else {
@@ -984,10 +1008,12 @@ int launch_norm_vec(const dp_rowreduce_params &p, const void *in, const void *w,
   if constexpr (std::is_same<TIn, float>::value && std::is_same<TOut, float>::value) {
     // Staged rows: whole float4 vectors, 16-byte aligned rows, two rows of a
     // warp within the shared-memory budget.
-    if (ok && p.cols % 4 == 0 && p.cols >= 1024 && p.cols * 4 * 2 * kStagedWarps <= 224 * 1024 &&
+    if (!p.out_split && ok && p.cols % 4 == 0 && p.cols >= 1024 && p.cols * 4 * 2 * kStagedWarps <= 224 * 1024 &&
         p.in_row_stride % 4 == 0 && p.out_row_stride % 4 == 0 && p.rows >= 4 * dp::num_sms())
       return launch_norm_staged(p, in, w, b, out, s);
   }
+  DP_REQUIRE(!p.out_split || aligned, DP_ERR_UNSUPPORTED,
+             "rowreduce: the 3xTF32 operand store needs 16-byte aligned rows and pointers");
   if (aligned) {
     const int64_t per_lane = (p.cols + 32 * V - 1) / (32 * V);  // vectors per lane for a warp-per-row pass
     if (per_lane <= 4) return launch_norm_warp<TIn, TOut, V, 4>(p, in, w, b, out, s);
@@ -1030,6 +1056,13 @@ int launch_rowreduce(const dp_rowreduce_params &p, const void *in, const void *w
   DP_REQUIRE(p.in_row_stride >= p.cols, DP_ERR_SHAPE, "rowreduce: in_row_stride < cols");
   DP_REQUIRE(p.kind >= DP_RED_SUM && p.kind <= DP_RED_LAYERNORM, DP_ERR_ARG, "rowreduce: bad kind");
   const bool value_kind = p.kind <= DP_RED_ARGMAX;
+  DP_REQUIRE(p.out_split == 0 || p.out_split == 1, DP_ERR_ARG, "rowreduce: out_split is 0 or 1");
+  if (p.out_split)
+    DP_REQUIRE(!value_kind && p.in_dtype == DP_F32 && p.out_dtype == DP_F32 && p.out_row_stride >= 3 * p.cols &&
+                   p.cols <= 4096,
+               DP_ERR_UNSUPPORTED,
+               "rowreduce: the 3xTF32 operand store needs fp32 softmax / norm rows of at most 4,096 columns and "
+               "out_row_stride >= 3 cols");
   if (value_kind) {
     if (p.kind == DP_RED_ARGMAX)
       DP_REQUIRE(p.out_dtype == DP_I32 || p.out_dtype == DP_I64, DP_ERR_SHAPE, "rowreduce: argmax writes i32/i64");

@@ -125,7 +125,12 @@ enum {
 };
 typedef struct dp_rowreduce_params {
   int32_t kind, in_dtype, out_dtype, has_weight;
-  int32_t has_bias, reserved;
+  int32_t has_bias;
+  /* softmax / RMSNorm / LayerNorm, fp32 in and out: 1 stores each output row
+   * as [hi | hi | lo] (hi = the value with the low 13 mantissa bits cleared,
+   * lo = value - hi) at out + row * out_row_stride, blocks cols apart, the
+   * operand of a following 3xTF32 product (out_row_stride >= 3 * cols). */
+  int32_t out_split;
   int64_t rows, cols;
   int64_t in_row_stride, out_row_stride;
   float eps, weight_offset;
@@ -162,7 +167,12 @@ enum {
    * dp_argmax_keys.  batch 1, tensor-core operands, no softmax.  Fuses the
    * reference's argmax template (templates/reduce.py:11-62) into the GEMM
    * that produces its input: the logits are never written. */
-  DP_EPI_ARGMAX = 256
+  DP_EPI_ARGMAX = 256,
+  /* Store each fp32 result v as the operand of a following 3xTF32 product:
+   * C is [M, 3N] (ldc >= 3N) and receives hi = v with the low 13 mantissa
+   * bits cleared at columns n and N + n, and lo = v - hi at 2N + n.  fp32 C;
+   * dp_gemm_splitk_reduce only (the reduce that finishes a split-K GEMM). */
+  DP_EPI_TF32SPLIT = 512
 };
 typedef struct dp_gemm_params {
   int64_t M, N, K;

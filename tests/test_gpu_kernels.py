@@ -839,6 +839,51 @@ def test_streamk_linear_program_matches_fp64(cuda):
     assert torch.equal(prog.run(x, r)[0].double(), got)
 
 
+# --------------------------------------------- 3xTF32 operands written by their producer
+def _tf32_split(x):
+    hi = (x.contiguous().view(torch.int32) & -8192).view(torch.float32)
+    return torch.cat([hi, hi, x - hi], dim=-1)
+
+
+def test_splitk_reduce_and_layernorm_store_3xtf32_operands(cuda):
+    """DP_EPI_TF32SPLIT on the split-K reduce and out_split on the fp32
+    LayerNorm store [hi | hi | lo] rows: bit-identical to the plain result
+    split afterwards (hi = the value with the low 13 mantissa bits cleared)."""
+    g = torch.Generator().manual_seed(5)
+    M, Nn, S = 300, 520, 3
+    ws = torch.randn(S, M, Nn, generator=g).to(cuda)
+    bias = torch.randn(Nn, generator=g).to(cuda)
+    sp = N.SplitKParams()
+    sp.gemm.M, sp.gemm.N, sp.gemm.K, sp.gemm.batch = M, Nn, 64, 1
+    sp.gemm.c_dtype = sp.gemm.bias_dtype = N.DP_F32
+    sp.gemm.epilogue = N.DP_EPI_BIAS | N.DP_EPI_GELU_ERF
+    sp.gemm.ldc = Nn
+    sp.splits, sp.slice_stride = S, M * Nn
+    plain = torch.empty(M, Nn, device=cuda)
+    N.gemm_splitk_reduce(sp, ws, plain, bias=bias)
+    sp.gemm.epilogue |= N.DP_EPI_TF32SPLIT
+    sp.gemm.ldc = 3 * Nn
+    split = torch.empty(M, 3 * Nn, device=cuda)
+    N.gemm_splitk_reduce(sp, ws, split, bias=bias)
+    _sync()
+    assert torch.equal(split.cpu(), _tf32_split(plain.cpu()))
+
+    x = torch.randn(M, Nn, generator=g).to(cuda)
+    w = torch.randn(Nn, generator=g).to(cuda)
+    b = torch.randn(Nn, generator=g).to(cuda)
+    p = N.RowReduceParams()
+    p.kind, p.in_dtype, p.out_dtype = N.DP_RED_LAYERNORM, N.DP_F32, N.DP_F32
+    p.has_weight, p.has_bias, p.rows, p.cols, p.in_row_stride, p.out_row_stride = 1, 1, M, Nn, Nn, Nn
+    p.eps = 1e-5
+    ln = torch.empty(M, Nn, device=cuda)
+    N.rowreduce(p, x, ln, weight=w, bias=b)
+    p.out_split, p.out_row_stride = 1, 3 * Nn
+    ln3 = torch.empty(M, 3 * Nn, device=cuda)
+    N.rowreduce(p, x, ln3, weight=w, bias=b)
+    _sync()
+    assert torch.equal(ln3.cpu(), _tf32_split(ln.cpu()))
+
+
 # ------------------------------------------------------- argmax epilogue
 class _LinearArgmax(torch.nn.Module):
     def __init__(self, k, n, dtype):

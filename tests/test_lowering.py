@@ -26,17 +26,21 @@ def test_token_pipeline_fuses_epilogues_and_argmax_cast():
     m = workloads.TokenPipeline()
     prog = devproc.compile(m, workloads.token_ids())
     labels = [r["label"] for r in prog.spec.records]
-    # each fp32 linear is one 3xTF32 tensor-core GEMM fed by a [hi | hi | lo] split region; the two
-    # M = 1024 linears with few output tiles split K (a batched GEMM plus a reduce that applies the epilogue);
-    # the head's argmax (and the int32 cast) is reduced in the head GEMM's epilogue between a clear and a
-    # conversion of one key per row, so the 1024 x 32000 logits are never stored
-    assert kernels(prog) == ["embedding", "region", "gemm", "splitk", "region", "gemm", "splitk", "rowreduce",
-                             "region", "argmax_keys", "gemm", "argmax_keys"]
+    # each fp32 linear is one 3xTF32 tensor-core GEMM over a [hi | hi | lo] operand that its producer
+    # writes directly (the embedding gathers rows of a table split at compile time, the fc1 split-K
+    # reduce and the LayerNorm store the three blocks); the two M = 1024 linears with few output tiles
+    # split K (a batched GEMM plus a reduce that applies the epilogue); the head's argmax (and the int32
+    # cast) is reduced in the head GEMM's epilogue between a clear and a conversion of one key per row,
+    # so the 1024 x 32000 logits are never stored
+    assert kernels(prog) == ["embedding", "gemm", "splitk", "gemm", "splitk", "rowreduce",
+                             "argmax_keys", "gemm", "argmax_keys"]
     assert all("3xtf32" in lb for lb in labels if lb.startswith("gemm"))
-    assert "splitk2" in labels[2] and "splitk8" in labels[5] and "splitk" not in labels[10]
-    assert f"epi{N.DP_EPI_BIAS | N.DP_EPI_GELU_ERF}" in labels[3]
-    assert "argmax" in labels[10] and f"epi{N.DP_EPI_BIAS | N.DP_EPI_ARGMAX}" in labels[10]
-    assert "int32" in labels[11]
+    assert "splitk2" in labels[1] and "splitk8" in labels[3] and "splitk" not in labels[7]
+    assert f"epi{N.DP_EPI_BIAS | N.DP_EPI_GELU_ERF}" in labels[2] and "3xtf32 operand" in labels[2]
+    assert "3xtf32 operand" not in labels[4] and "3xtf32 operand" in labels[5]
+    assert labels[0] == "embedding 1024x1536"
+    assert "argmax" in labels[7] and f"epi{N.DP_EPI_BIAS | N.DP_EPI_ARGMAX}" in labels[7]
+    assert "int32" in labels[8]
     assert prog.spec.arena_bytes < 64 << 20
     w3 = [c for c in prog.spec.consts if c.name.endswith("|3xtf32")]
     assert len(w3) == 3 and w3[0].shape[1] == 3 * 512
