@@ -270,6 +270,8 @@ class Lowerer:
         self.views: Dict[str, View] = {}
         # values whose producer wrote them directly as a 3xTF32 operand [hi | hi | lo]
         self.tf32_split_views: Dict[str, View] = {}
+        # cat buffers by (dim, shape, dtype, first input): the last cat's view, output and inputs
+        self.cat_reuse: Dict[tuple, tuple] = {}
         self.buffers: List[Buffer] = []
         self.records: List[Record] = []
         self.done = set()   # ids of ops already lowered (fused)
@@ -1302,14 +1304,35 @@ class Lowerer:
 
     # ---------------------------------------------------------- cat / rope
     def lower_cat(self, op: Op) -> None:
-        """One copy region per input into its slice of the output buffer."""
-        out = self.new_value_view(op.outputs[0])
+        """One copy region per input into its slice of the output buffer.
+
+        A cat whose first input is the same value as an earlier cat's (a
+        layer's prefix keys, concatenated with new keys at every denoise step)
+        reuses that cat's buffer once nothing reads the earlier result any
+        more, and copies only the inputs that differ: the shared prefix is
+        written once."""
         d = op.attr("dim")
+        out_val = op.outputs[0]
+        key = (d, tuple(out_val.type.shape), out_val.type.dtype, op.inputs[0].name)
+        prev = self.cat_reuse.get(key)
+        same = [False] * len(op.inputs)
+        out = None
+        if prev is not None:
+            prev_view, prev_name, prev_inputs = prev
+            if (prev_name not in self.out_names and len(prev_inputs) == len(op.inputs)
+                    and all(id(u) in self.done for u in self.uses.get(prev_name, []))):
+                out = prev_view
+                self.views[out_val.name] = out
+                same = [a == v.name for a, v in zip(prev_inputs, op.inputs)]
+        if out is None:
+            out = self.new_value_view(out_val)
+        if out.contiguous and out_val.name not in self.out_names:
+            self.cat_reuse[key] = (out, out_val.name, [v.name for v in op.inputs])
         pos = 0
-        for v in op.inputs:
+        for v, kept in zip(op.inputs, same):
             src = self.views[v.name]
             n = v.type.shape[d]
-            if n:
+            if n and not kept:
                 dst = View(out.buf, src.shape, out.strides, out.offset + pos * out.strides[d])
                 rb = RegionBuilder(src.shape)
                 rb.store(dst, rb.load(src))
