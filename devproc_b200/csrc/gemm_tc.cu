@@ -492,6 +492,14 @@ __device__ __forceinline__ void tile_coords(const Shape &s, int t, int &b, int &
 
 __device__ __forceinline__ bool aborted(volatile int *flag) { return *flag != 0; }
 
+// A CTA pair's last column tile with at most 128 valid columns (N = 1,152 =
+// 4.5 tiles of 256) runs N = 128 MMAs: each CTA then supplies 64 columns of
+// B instead of 128, and the MMAs do no work on the missing half.
+template <int CG>
+__device__ __forceinline__ bool half_width(const Shape &s, int tn) {
+  return CG == 2 && !s.b_mn && s.N - tn * BN <= BN / 2;
+}
+
 // Waits in 0.2 s slices, re-reading the CTA's abort flag between slices, for
 // at most 2 s in total; on giving up records DP_DEVERR_TIMEOUT and raises the
 // abort flag so that the other roles stop too.
@@ -895,7 +903,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int b, tm, tn;
         tile_coords(s, u.t, b, tm, tn);
         const int row0 = tm * BM * CG + (int)rank * BM;               // this CTA's A rows
-        const int col0 = tn * BN + (int)rank * Cfg<CG>::kBRows;       // this CTA's B rows (N)
+        // this CTA's B rows (N): half of the pair's columns, 64 instead of 128 on a half-width tile
+        const int col0 = tn * BN + (int)rank * (half_width<CG>(s, tn) ? Cfg<CG>::kBRows / 2 : Cfg<CG>::kBRows);
         const int ba = (s.bcast & 1) ? 0 : b, bb = (s.bcast & 2) ? 0 : b;
         for (int kb = u.kb0; kb < u.kb1; ++kb, ++it) {
           const int st = it % kStages;
@@ -940,7 +949,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     if (rank == 0) {
       // ---------------- MMA issuer (the leader CTA's, for a pair; whole warp, the elected lane issues)
-      const uint32_t idesc = instr_desc(BM * CG, BN, s.b_mn, s.tf32 ? 2u : 1u);
+      const uint32_t idesc_full = instr_desc(BM * CG, BN, s.b_mn, s.tf32 ? 2u : 1u);
+      const uint32_t idesc_half = instr_desc(BM * CG, BN / 2, s.b_mn, s.tf32 ? 2u : 1u);
       const bool tf32 = s.tf32 != 0;
       const bool b_mn = s.b_mn != 0;
       const uint32_t b_kstep = b_mn ? 2048u : 32u;  // bytes per 16-deep K step of B (MN-major: 16 rows of 128 B)
@@ -949,6 +959,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int j = 0; j < sc.count() && !aborted(flag); ++j, ++local) {
         const Unit u = sched_unit(sc, s, cid, nclusters, j);
         const int a = local & 1;
+        int tb, tm, tn;
+        tile_coords(s, u.t, tb, tm, tn);
+        const uint32_t idesc = half_width<CG>(s, tn) ? idesc_half : idesc_full;
         if (!wait_or_abort<CG == 2>(&acc_empty[a], ((local >> 1) & 1) ^ 1, 310 + a, flag)) break;
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + (uint32_t)(a * BN);

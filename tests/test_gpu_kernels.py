@@ -477,7 +477,9 @@ def _bf16_gemm(cuda, M, Nn, K, epi=0, c_dtype=torch.float32, batch=1, bias=None,
     return a, w, c.cpu()
 
 
-@pytest.mark.parametrize("M,Nn,K", [(128, 256, 64), (256, 512, 1024), (37, 300, 72), (1, 10, 256), (300, 1000, 1152)])
+@pytest.mark.parametrize("M,Nn,K", [(128, 256, 64), (256, 512, 1024), (37, 300, 72), (1, 10, 256), (300, 1000, 1152),
+                                    # last column tile of at most 128 columns: N = 128 MMAs on CTA pairs
+                                    (512, 1152, 1152), (300, 640, 512), (1000, 136, 256)])
 def test_gemm_bf16_tensor_core_shapes(cuda, M, Nn, K):
     a, w, c = _bf16_gemm(cuda, M, Nn, K, seed=M + Nn)
     ref = a.float() @ w.float().transpose(-1, -2)
