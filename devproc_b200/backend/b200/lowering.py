@@ -272,6 +272,7 @@ class Lowerer:
         self.tf32_split_views: Dict[str, View] = {}
         # cat buffers by (dim, shape, dtype, first input): the last cat's view, output and inputs
         self.cat_reuse: Dict[tuple, tuple] = {}
+        self.op_index = {id(o): i for i, o in enumerate(fn.block.ops)}
         self.buffers: List[Buffer] = []
         self.records: List[Record] = []
         self.done = set()   # ids of ops already lowered (fused)
@@ -1320,7 +1321,7 @@ class Lowerer:
         if prev is not None:
             prev_view, prev_name, prev_inputs = prev
             if (prev_name not in self.out_names and len(prev_inputs) == len(op.inputs)
-                    and all(id(u) in self.done for u in self.uses.get(prev_name, []))):
+                    and not self.buffer_read_later(prev_view.buf, op)):
                 out = prev_view
                 self.views[out_val.name] = out
                 same = [a == v.name for a, v in zip(prev_inputs, op.inputs)]
@@ -1338,6 +1339,22 @@ class Lowerer:
                 rb.store(dst, rb.load(src))
                 self.emit_region(rb, f"cat {v.name} -> {op.outputs[0].name}[{pos}:{pos + n}]")
             pos += n
+
+    def buffer_read_later(self, buf: Buffer, current: Op) -> bool:
+        """Whether an op not lowered yet (other than ``current``) reads a value
+        whose view lies in ``buf`` (any view of it: reshapes, transposes and
+        slices alias it), or a function output does."""
+        def aliases(name: str) -> bool:
+            v = self.views.get(name)
+            return v is not None and (v.buf is buf or v.buf.root is buf)
+        ops = self.fn.block.ops
+        start = self.op_index.get(id(current), -1) + 1  # every op before the current one is lowered
+        for o in ops[start:]:
+            if id(o) in self.done:
+                continue
+            if any(aliases(v.name) for v in o.inputs):
+                return True
+        return any(aliases(n) for n in self.out_names)
 
     def lower_rope(self, op: Op) -> None:
         """out1 = x1·c1 − x2·s1, out2 = x2·c2 + x1·s2 over the two halves of the

@@ -286,6 +286,30 @@ def test_small_policy_lowering():
     assert prog.spec.outputs[0].shape == [2, 10, 8] and prog.spec.outputs[0].dtype == "float32"
 
 
+def test_cat_reuses_a_dead_buffer_with_the_same_prefix_only():
+    """cat(x, y2) may reuse the buffer of an earlier cat(x, y1) and copy only y2,
+    but not while the earlier result (or a view of it) is still to be read."""
+    from devproc_b200.dsl import ops as dsl_ops
+
+    @devproc.kernel
+    def dead(x, y1, y2):
+        a = dsl_ops.cat([x, y1], dim=0)
+        s = devproc.sigmoid(a)
+        b = dsl_ops.cat([x, y2], dim=0)
+        return devproc.add(s, b)
+
+    @devproc.kernel
+    def live(x, y1, y2):
+        a = dsl_ops.cat([x, y1], dim=0)
+        b = dsl_ops.cat([x, y2], dim=0)
+        return devproc.add(devproc.transpose(a, (1, 0)), devproc.transpose(b, (1, 0)))
+
+    x, y = torch.randn(6, 16), torch.randn(2, 16)
+    cats = lambda prog: [r["label"] for r in prog.spec.records if r["label"].startswith("cat")]
+    assert len(cats(devproc.compile(dead, x, y, y))) == 3    # x copied once
+    assert len(cats(devproc.compile(live, x, y, y))) == 4    # a is read after b: no reuse
+
+
 def test_fx_slicing_and_joining():
     """Indexing with slices / ints / None / ..., chunk, split, narrow and cat
     through the FX frontend agree with eager on the oracle."""
