@@ -35,7 +35,6 @@
 namespace dpk_attn {
 
 constexpr int BM = 128;        // query rows per item
-constexpr int kThreads = 256;
 constexpr int kMaxStages = 4;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kQBox = BM * 128;    // 16 KB: 128 rows × 64 bf16
@@ -48,6 +47,12 @@ struct Blk {
   static constexpr int kSCols = BKV;                    // one score buffer: BKV fp32 columns
   static constexpr uint32_t kKVBox = BKV * 128;         // one 64-column box of K or V: BKV rows × 128 B
   static constexpr uint32_t kPBytes = (BKV / 64) * kPBox;  // one P tile: BKV / 64 swizzle atoms along the keys
+  // 64-key blocks (head dims above 128) add four output-epilogue warps (8-11),
+  // so the softmax warps start the next item while an item's O is written;
+  // the 128-key kernel keeps the epilogue on the softmax warps (its softmax
+  // needs ~200 registers, which 384 threads could not have).
+  static constexpr bool kSepEpi = BKV == 64;
+  static constexpr int kThreads = kSepEpi ? 384 : 256;
 };
 
 struct Shape {
@@ -184,7 +189,7 @@ __device__ __forceinline__ void item_coords(const Shape &s, int item, int &b, in
 }
 
 template <int BKV>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                 const __grid_constant__ CUtensorMap map_v, const Shape s, __nv_bfloat16 *__restrict__ out) {
   constexpr int kSCols = Blk<BKV>::kSCols;
@@ -192,7 +197,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr uint32_t kPBytes = Blk<BKV>::kPBytes;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, q_empty, k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages],
-      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2], p_free[2], o_full, o_free;
+      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2], p_free[2], o_full, o_free, l_full[2];
+  __shared__ float l_rows[2][BM];  // separate epilogue: each row's softmax sum, by item parity
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -222,6 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     mbar_init(&o_full, 1);
     mbar_init(&o_free, 4);
+    for (int i = 0; i < 2; ++i) mbar_init(&l_full[i], 4);
     abort_flag = 0;
     fence_barrier_init();
   }
@@ -248,6 +255,49 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (both are the block count mod 2), so the producers wait on the score and
   // P barriers instead of separate K / V "empty" barriers.
   const bool merged = s.stages == 2;
+  // Separate output-epilogue warps (64-key blocks) when an item has at least
+  // three key blocks: the third block's wait on P buffer (jg - 2) then implies
+  // the P·V that waited for the previous item's epilogue, so a row-sum slot
+  // (l_rows, by item parity) is never rewritten before it is read.
+  const bool sep_epi = Blk<BKV>::kSepEpi && nb >= 3;
+  // O / l → bf16 → global for the rows of one item (thread = row); waits for
+  // O, releases it.  False when a wait gave up.
+  auto attn_epilogue_rows = [&](int b, int hk, int rt, int row, uint32_t lane_off, int lane, float l,
+                                int local) -> bool {
+    const bool of = wait_or_abort(&o_full, local & 1, 580, flag);
+    if (!__all_sync(0xffffffffu, of)) return false;
+    fence_after();
+    const int r = rt * BM + row;
+    const float inv = 1.0f / l;
+    __nv_bfloat16 *orow = nullptr;
+    if (r < s.R) {
+      const int hq = hk * s.group + r / s.L, pos = r % s.L;
+      orow = out + (int64_t)b * s.o_sb + (int64_t)hq * s.o_sh + (int64_t)pos * s.o_sl;
+    }
+    for (int c = 0; c < s.dvp / 16; ++c) {
+      uint32_t rr[16];
+      tld16(t_o + lane_off + c * 16, rr);
+      if (orow) {
+        __nv_bfloat162 h[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          h[e] = __floats2bfloat162_rn(__uint_as_float(rr[2 * e]) * inv, __uint_as_float(rr[2 * e + 1]) * inv);
+        const int c0 = c * 16;
+        if (c0 + 16 <= s.Dv) {
+          uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+          dst[0] = *reinterpret_cast<const uint4 *>(&h[0]);
+          dst[1] = *reinterpret_cast<const uint4 *>(&h[4]);
+        } else {
+          const __nv_bfloat16 *hv = reinterpret_cast<const __nv_bfloat16 *>(h);
+          for (int e = 0; c0 + e < s.Dv; ++e) orow[c0 + e] = hv[e];
+        }
+      }
+    }
+    fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&o_free);
+    return true;
+  };
 
   if (warp == 0) {
     {
@@ -378,13 +428,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         __syncwarp();
       }
     }
-  } else if (warp >= 4) {
-    // ---------------- softmax + epilogue: thread = query row (warp - 4)·32 + lane
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------- softmax (+ epilogue unless sep_epi): thread = query row (warp - 4)·32 + lane
     const int q4 = warp - 4;
     const int row = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     int jg = 0, local = 0;
     bool ok = true;
+    const bool sc_neg = s.scale_log2 < 0.0f;
+    const float sc = fabsf(s.scale_log2);
     for (int item = blockIdx.x; item < s.items && ok; item += gridDim.x, ++local) {
       int b, hk, rt;
       item_coords(s, item, b, hk, rt);
@@ -413,8 +465,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&s_free[sb]);  // this score buffer may take S_{j+2}
         const int k0 = j * BKV;
         float t8[8];
+        // The max runs on raw scores and the scale folds into the exponent's FMA;
+        // a negative scale negates the scores first (one warp-uniform branch).
+        if (sc_neg) {
 #pragma unroll
-        for (int e = 0; e < BKV; ++e) v[e] = (k0 + e < s.S) ? v[e] * s.scale_log2 : -INFINITY;
+          for (int e = 0; e < BKV; ++e) v[e] = -v[e];
+        }
+        if (k0 + BKV > s.S) {  // the last, partial key block only
+#pragma unroll
+          for (int e = 0; e < BKV; ++e) v[e] = (k0 + e < s.S) ? v[e] : -INFINITY;
+        }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {  // tree max: short dependency chains
           const float a = fmaxf(fmaxf(v[e], v[e + 8]), fmaxf(v[e + 16], v[e + 24]));
@@ -426,8 +486,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             t8[e] = fmaxf(t8[e], fmaxf(c, d));
           }
         }
-        const float mx = fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
-                               fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
+        const float mx = sc * fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
+                                    fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
         // This block's P tile is free once the P·V of block jg − 2 is complete.
         const int pb = jg & 1;
         if (jg >= 2) {
@@ -469,6 +529,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // P_j row as bf16 into the 128-byte-swizzled K-major tile
         // (BKV / 64 swizzle atoms of 64 keys, each 128 rows × 128 B)
         uint8_t *prow = sp + pb * kPBytes + row * 128;
+        const float nm = -m;  // p = 2^(score · scale − m), one FFMA and one ex2
         float part[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
         for (int ch = 0; ch < BKV / 8; ++ch) {
@@ -476,7 +537,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float acc = 0.0f;
 #pragma unroll
           for (int h = 0; h < 4; ++h) {
-            const float p0 = ex2(v[ch * 8 + 2 * h] - m), p1 = ex2(v[ch * 8 + 2 * h + 1] - m);
+            const float p0 = ex2(fmaf(v[ch * 8 + 2 * h], sc, nm)), p1 = ex2(fmaf(v[ch * 8 + 2 * h + 1], sc, nm));
             acc += p0 + p1;
             __nv_bfloat162 bb = __floats2bfloat162_rn(p0, p1);
             w[h] = *reinterpret_cast<uint32_t *>(&bb);
@@ -492,39 +553,30 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) mbar_arrive(&p_full[pb]);
       }
       if (!ok) break;
-      // ---------------- epilogue: O / l → bf16 → global
-      const bool of = wait_or_abort(&o_full, local & 1, 580, flag);
-      if (!__all_sync(0xffffffffu, of)) break;
-      fence_after();
-      const int r = rt * BM + row;
-      const float inv = 1.0f / l;
-      __nv_bfloat16 *orow = nullptr;
-      if (r < s.R) {
-        const int hq = hk * s.group + r / s.L, pos = r % s.L;
-        orow = out + (int64_t)b * s.o_sb + (int64_t)hq * s.o_sh + (int64_t)pos * s.o_sl;
+      if (sep_epi) {
+        // hand the row sums to the epilogue warps (they read O once o_full completes)
+        l_rows[local & 1][row] = l;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&l_full[local & 1]);
+        continue;
       }
-      for (int c = 0; c < s.dvp / 16; ++c) {
-        uint32_t rr[16];
-        tld16(t_o + lane_off + c * 16, rr);
-        if (orow) {
-          __nv_bfloat162 h[8];
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            h[e] = __floats2bfloat162_rn(__uint_as_float(rr[2 * e]) * inv, __uint_as_float(rr[2 * e + 1]) * inv);
-          const int c0 = c * 16;
-          if (c0 + 16 <= s.Dv) {
-            uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
-            dst[0] = *reinterpret_cast<const uint4 *>(&h[0]);
-            dst[1] = *reinterpret_cast<const uint4 *>(&h[4]);
-          } else {
-            const __nv_bfloat16 *hv = reinterpret_cast<const __nv_bfloat16 *>(h);
-            for (int e = 0; c0 + e < s.Dv; ++e) orow[c0 + e] = hv[e];
-          }
-        }
+      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l, local)) {
+        ok = false;
+        break;
       }
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&o_free);
+    }
+  } else if (Blk<BKV>::kSepEpi && warp >= 8) {
+    // ---------------- output epilogue warps: thread = query row (warp - 8)·32 + lane
+    const int q4 = warp - 8;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    int local = 0;
+    for (int item = blockIdx.x; item < s.items && sep_epi && !aborted(flag); item += gridDim.x, ++local) {
+      int b, hk, rt;
+      item_coords(s, item, b, hk, rt);
+      const bool lf = wait_or_abort(&l_full[local & 1], (local >> 1) & 1, 585 + (local & 1), flag);
+      if (!__all_sync(0xffffffffu, lf)) break;
+      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l_rows[local & 1][row], local)) break;
     }
   }
 
@@ -614,7 +666,7 @@ int launch_blocks(const dp_attention_params &p, Shape s, const void *q, const vo
   }
   int grid = dp::num_sms();
   if (grid > s.items) grid = s.items;
-  dp::launch_k(attn_kernel<BKV>, grid, kThreads, smem, stream, mq, mk, mv, s, static_cast<__nv_bfloat16 *>(o));
+  dp::launch_k(attn_kernel<BKV>, grid, Blk<BKV>::kThreads, smem, stream, mq, mk, mv, s, static_cast<__nv_bfloat16 *>(o));
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }
@@ -659,6 +711,10 @@ int launch_attention(const dp_attention_params &p, const void *q, const void *k,
   DP_REQUIRE(items < (1ll << 31), DP_ERR_UNSUPPORTED, "attention: too many work items");
   s.items = (int)items;
   s.scale_log2 = p.scale * 1.4426950408889634f;
+  // The kernel forms score · scale − max by one FMA, where a masked key's
+  // −∞ score times a zero scale would give NaN: a zero scale runs as 1e-30
+  // (every valid key's exponent is then 0 to within rounding, as for 0).
+  if (s.scale_log2 == 0.0f) s.scale_log2 = 1e-30f;
   s.o_sb = p.o_sb;
   s.o_sh = p.o_sh;
   s.o_sl = p.o_sl;

@@ -695,6 +695,33 @@ def test_fused_attention_rising_scores(cuda, D):
     assert torch.allclose(o.cpu().float(), ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item())
 
 
+@pytest.mark.parametrize("D,scale", [(256, -0.0625), (72, -0.125), (256, 0.0), (72, 0.0)])
+def test_fused_attention_negative_and_zero_scale(cuda, D, scale):
+    """The kernel takes the row max on raw scores and folds the scale into the
+    exponent: a negative scale (max of the negated scores) and a zero scale
+    (uniform weights over the valid keys, the partial last block masked) still
+    match softmax(scale · Q·Kᵀ)·V."""
+    torch.manual_seed(7 + D)
+    B, H, L, S = 1, 2, 130, 201
+    q = torch.randn(B, H, L, D).bfloat16()
+    k = torch.randn(B, H, S, D).bfloat16()
+    v = torch.randn(B, H, S, D).bfloat16()
+    o = torch.empty(B, H, L, D, dtype=torch.bfloat16, device=cuda)
+    p = N.AttentionParams()
+    p.batch, p.heads_kv, p.group, p.L, p.S, p.D, p.Dv = B, H, 1, L, S, D, D
+    p.q_sb, p.q_sh, p.q_sl = H * L * D, L * D, D
+    p.k_sb, p.k_sh, p.k_ss = H * S * D, S * D, D
+    p.v_sb, p.v_sh, p.v_ss = H * S * D, S * D, D
+    p.o_sb, p.o_sh, p.o_sl = H * L * D, L * D, D
+    p.scale, p.dtype = scale, N.DP_BF16
+    N.attention(p, q.to(cuda), k.to(cuda), v.to(cuda), o)
+    _sync()
+    ref = _attn_ref(q, k, v, scale)
+    got = o.cpu().float()
+    assert torch.isfinite(got).all()
+    assert torch.allclose(got, ref, rtol=2e-2, atol=2e-2 * ref.abs().max().item()), (got - ref).abs().max()
+
+
 def test_fused_attention_token_major_output(cuda):
     """One query head per key head with the output stored token-major [B, L, H, Dv]
     (the layout the following reshape reads for free) and strided q / k / v column
