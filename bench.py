@@ -55,7 +55,7 @@ import torch  # noqa: E402
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
 FALLBACK_BF16_TFLOPS_SUSTAINED = 1400.0
-CONFIG_NAMES = ("gemm", "reduce", "token", "vit", "vla")
+CONFIG_NAMES = ("gemm", "reduce", "attention", "token", "vit", "vla")
 
 
 def parse():
@@ -70,9 +70,9 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--min-region-s", type=float, default=1.0, help="repeat timed regions for about this long")
     ap.add_argument("--configs", default=None,
-                    help="comma list of extra configurations in the headline line (gemm,reduce,token,vit,vla); "
+                    help="comma list of extra configurations in the headline line (gemm,reduce,attention,token,vit,vla); "
                          "default: all on one GPU, none on several")
-    ap.add_argument("--workload", choices=["preprocess", "gemm", "reduce", "token", "vit", "vla"],
+    ap.add_argument("--workload", choices=["preprocess", "gemm", "reduce", "attention", "token", "vit", "vla"],
                     default="preprocess",
                     help="preprocess = the headline line; the others print one configuration's line alone")
     return ap.parse_args()
@@ -260,6 +260,56 @@ def cfg_gemm(args, dev, timer, cpu):
             "gpu_launches": K_steps * 2, "clocks": shapes["4096x4096x4096"]["clocks"],
             "config": {"workload": "GEMM 4096^3 and 8192x2048x16384, bf16 inputs N(0,1), fp32 accumulate",
                        "l2": "operands 64-320 MB; repeated launches over the same operands"}}
+
+
+def cfg_attention(args, dev, timer, cpu):
+    """The fused tcgen05 attention kernel alone at the three shapes the ViT and policy steps run:
+    SigLIP-shaped self-attention (128 images x 16 heads, 256 x 256, head dim 72), the Gemma-2B-shaped
+    prefill (64 samples, 8 query heads on 1 key/value head, 816 x 816, head dim 256) and the action
+    expert over the prefix cache (64 samples, 8 / 1 heads, 50 queries x 866 keys, head dim 256)."""
+    from devproc_b200 import _native as N
+    peak, kind = tensor_peak()
+    shapes = {}
+    K_steps = min(args.steps, 20)
+    for name, (B, Hk, g, L, S, D) in {"vit_128x16x256x256_d72": (128, 16, 1, 256, 256, 72),
+                                      "prefill_64x8q1kv_816x816_d256": (64, 1, 8, 816, 816, 256),
+                                      "expert_64x8q1kv_50x866_d256": (64, 1, 8, 50, 866, 256)}.items():
+        gen = torch.Generator(device=dev).manual_seed(0)
+        Hq = Hk * g
+        q = torch.randn(B, Hq, L, D, device=dev, generator=gen).bfloat16()
+        k = torch.randn(B, Hk, S, D, device=dev, generator=gen).bfloat16()
+        v = torch.randn(B, Hk, S, D, device=dev, generator=gen).bfloat16()
+        o = torch.empty(B, Hq, L, D, dtype=torch.bfloat16, device=dev)
+        p = N.AttentionParams()
+        p.batch, p.heads_kv, p.group, p.L, p.S, p.D, p.Dv = B, Hk, g, L, S, D, D
+        p.q_sb, p.q_sh, p.q_sl = Hq * L * D, L * D, D
+        p.k_sb, p.k_sh, p.k_ss = Hk * S * D, S * D, D
+        p.v_sb, p.v_sh, p.v_ss = Hk * S * D, S * D, D
+        p.o_sb, p.o_sh, p.o_sl = Hq * L * D, L * D, D
+        p.scale, p.dtype = D ** -0.5, N.DP_BF16
+        sp = timer.stream.cuda_stream
+        t = timer.run(lambda i: N.attention(p, q, k, v, o, stream=sp), K_steps, args.warmup)
+        N.raise_device_error(dev.index, "attention")
+        flops = 4.0 * B * Hq * L * S * D
+        tf = flops / (t["ms_per_step"] / 1e3) / 1e12
+        shapes[name] = {"us": t["ms_per_step"] * 1e3, "tflops": tf, "frac": tf / peak, "launches": K_steps,
+                        "regions": t["regions"], "clocks": t["clocks"],
+                        "operand_mb": (q.numel() + k.numel() + v.numel() + o.numel()) * 2 / 1e6}
+        del q, k, v, o
+    worst = min(shapes.values(), key=lambda v: v["tflops"])
+    return {"metric": "fused attention TFLOP/s (bf16, 4*rows*keys*head_dim per launch)",
+            "value": shapes["prefill_64x8q1kv_816x816_d256"]["tflops"], "unit": "TFLOP/s",
+            "higher_is_better": True, "dtype": "bf16", "shapes": shapes,
+            "roofline": {"bound": "tensor", "achieved": worst["tflops"], "peak": peak, "unit": "TFLOP/s",
+                         "frac": worst["tflops"] / peak, "peak_kind": kind, "kernel": "attn_kernel",
+                         "note": "the slowest shape; per shape in shapes"},
+            "gpu_launches": K_steps * len(shapes), "clocks": shapes["vit_128x16x256x256_d72"]["clocks"],
+            "cpu_baseline": None,
+            "config": {"workload": "fused attention at the ViT, prefill and action-expert shapes, q / k / v N(0,1)",
+                       "l2": "q, k, v and o take 302 / 481 / 83 MB (operand_mb per shape): the ViT and prefill "
+                             "operands exceed L2, the expert's fit in it",
+                       "cpu_baseline": "none: a sub-operation of the ViT and policy configurations, whose CPU "
+                                       "baselines cover it"}}
 
 
 def cfg_reduce(args, dev, timer, cpu):
@@ -452,7 +502,8 @@ def cfg_vla(args, dev, timer, cpu):
                                    "steps on 50x32 noise; bf16, random-init weights N(0, 0.02)"}}
 
 
-CONFIG_FNS = {"gemm": cfg_gemm, "reduce": cfg_reduce, "token": cfg_token, "vit": cfg_vit, "vla": cfg_vla}
+CONFIG_FNS = {"gemm": cfg_gemm, "reduce": cfg_reduce, "attention": cfg_attention, "token": cfg_token, "vit": cfg_vit,
+              "vla": cfg_vla}
 
 
 # ----------------------------------------------------------- headline (C2)

@@ -20,6 +20,12 @@
 //            write P_j = 2^(s − m) as bf16 into one of two 128-byte-swizzled
 //            shared tiles (so P_{j+1} is written while P_j·V_j runs), and at
 //            the end O / l → bf16 → global.
+// With 128-key blocks (head dims ≤ 128) the output accumulator is double
+// buffered in TMEM and an item's epilogue runs after the next item's first P
+// block, so the wait for its last P·V overlaps that softmax; the MMA issuer
+// starts the next item's first Q·Kᵀ before this item's last P·V.  Where every
+// warp's 32 rows lie in one head, O goes out through a free P tile and one
+// TMA tensor store per warp instead of row-per-thread global stores.
 // The running max is raised lazily (only when a block's max exceeds it by
 // more than 2^8): P then stays ≤ 256, exact in bf16's exponent range, and O
 // and l are rescaled by 2^(m_old − m_new) only on those rare blocks.
@@ -53,6 +59,10 @@ struct Blk {
   // needs ~200 registers, which 384 threads could not have).
   static constexpr bool kSepEpi = BKV == 64;
   static constexpr int kThreads = kSepEpi ? 384 : 256;
+  // 128-key blocks: two output accumulators (2·128 score + 2·128 output
+  // columns = 512), an item's epilogue deferred past the next item's first
+  // P block (the softmax warps run it).
+  static constexpr bool kDblO = BKV == 128;
 };
 
 struct Shape {
@@ -62,6 +72,7 @@ struct Shape {
   int ks;       // K = 16 MMA steps covering D
   int dvp;      // PV MMA N: Dv rounded up to 16
   int stages;
+  int o_tma;    // 1: O leaves through shared memory and TMA tensor stores (map_o)
   int tiles_r, items, kv_blocks, heads_kv, group;
   uint32_t stage_bytes, q_bytes;
   float scale_log2;
@@ -78,6 +89,16 @@ __device__ __forceinline__ void tma_load(void *dst, const CUtensorMap *map, int 
       "l"(map), "r"(x), "r"(y), "r"(z), "r"(w), "r"(su32(bar))
       : "memory");
 }
+
+// TMA tensor store of a 64-column × 32-row box from 128-byte-swizzled shared memory
+__device__ __forceinline__ void tma_store(const CUtensorMap *map, const void *src, int x, int y, int z, int w) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(map),
+               "r"(x), "r"(y), "r"(z), "r"(w), "r"(su32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 __device__ __forceinline__ uint64_t desc_k(uint32_t addr) {  // K-major, 128-byte swizzle, 8-row groups 1024 B
   return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
@@ -191,13 +212,15 @@ __device__ __forceinline__ void item_coords(const Shape &s, int item, int &b, in
 template <int BKV>
 __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                const __grid_constant__ CUtensorMap map_v, const Shape s, __nv_bfloat16 *__restrict__ out) {
+                const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o, const Shape s,
+                __nv_bfloat16 *__restrict__ out) {
   constexpr int kSCols = Blk<BKV>::kSCols;
   constexpr uint32_t kKVBox = Blk<BKV>::kKVBox;
   constexpr uint32_t kPBytes = Blk<BKV>::kPBytes;
+  constexpr bool kDblO = Blk<BKV>::kDblO;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, q_empty, k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages],
-      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2], p_free[2], o_full, o_free, l_full[2];
+      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2], p_free[2], o_full[2], o_free[2], l_full[2];
   __shared__ float l_rows[2][BM];  // separate epilogue: each row's softmax sum, by item parity
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
@@ -226,8 +249,10 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
       mbar_init(&p_full[i], 4);
       mbar_init(&p_free[i], 1);
     }
-    mbar_init(&o_full, 1);
-    mbar_init(&o_free, 4);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&o_full[i], 1);
+      mbar_init(&o_free[i], 4);
+    }
     for (int i = 0; i < 2; ++i) mbar_init(&l_full[i], 4);
     abort_flag = 0;
     fence_barrier_init();
@@ -247,7 +272,11 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = tmem_slot;
-  const uint32_t t_o = tmem + 2 * kSCols;  // output accumulator columns
+  // Output accumulator of an item (by its per-CTA index): one buffer, or two
+  // 128-column buffers by item parity; each buffer's barrier phase counts its uses.
+  auto o_buf = [&](int local) { return kDblO ? (local & 1) : 0; };
+  auto o_phase = [&](int local) { return (uint32_t)(kDblO ? ((local >> 1) & 1) : (local & 1)); };
+  auto t_o = [&](int local) { return tmem + 2 * kSCols + (kDblO ? (uint32_t)(local & 1) * 128u : 0u); };
   volatile int *flag = &abort_flag;
   dp::pdl_wait();  // set-up above touches no global memory; the previous kernel's results are visible from here
   const int nb = s.kv_blocks;
@@ -261,14 +290,52 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
   // (l_rows, by item parity) is never rewritten before it is read.
   const bool sep_epi = Blk<BKV>::kSepEpi && nb >= 3;
   // O / l → bf16 → global for the rows of one item (thread = row); waits for
-  // O, releases it.  False when a wait gave up.
-  auto attn_epilogue_rows = [&](int b, int hk, int rt, int row, uint32_t lane_off, int lane, float l,
-                                int local) -> bool {
-    const bool of = wait_or_abort(&o_full, local & 1, 580, flag);
+  // O, releases it.  With ``stage`` (a free P tile, 128-byte swizzled like P)
+  // each warp writes its 32 rows there and one lane stores them with TMA;
+  // otherwise every thread stores its own row.  False when a wait gave up.
+  auto attn_epilogue_rows = [&](int b, int hk, int rt, int row, uint32_t lane_off, int lane, float l, int local,
+                                uint8_t *stage) -> bool {
+    const int ob = o_buf(local);
+    const bool of = wait_or_abort(&o_full[ob], o_phase(local), 580, flag);
     if (!__all_sync(0xffffffffu, of)) return false;
     fence_after();
-    const int r = rt * BM + row;
+    const uint32_t to = t_o(local) + lane_off;
     const float inv = 1.0f / l;
+    if (stage) {
+      uint8_t *srow = stage + row * 128;
+      const uint32_t sw = (uint32_t)(row & 7);
+      for (int c = 0; c < s.dvp / 16; ++c) {
+        uint32_t rr[16];
+        tld16(to + c * 16, rr);
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          __nv_bfloat162 h =
+              __floats2bfloat162_rn(__uint_as_float(rr[2 * e]) * inv, __uint_as_float(rr[2 * e + 1]) * inv);
+          w[e] = *reinterpret_cast<uint32_t *>(&h);
+        }
+        const int cc = 2 * c;  // 16-byte chunks of 8 columns; 64-column atoms of 128 rows
+        *reinterpret_cast<uint4 *>(srow + (cc >> 3) * kPBox + (((uint32_t)(cc & 7) ^ sw) << 4)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4 *>(srow + ((cc + 1) >> 3) * kPBox + (((uint32_t)((cc + 1) & 7) ^ sw) << 4)) =
+            make_uint4(w[4], w[5], w[6], w[7]);
+      }
+      fence_before();
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&o_free[ob]);  // O is read: the P·V two items on may overwrite it
+        const int q4 = row >> 5, r0 = rt * BM + q4 * 32;
+        if (r0 < s.R) {  // a warp's 32 rows lie in one head (checked on the host)
+          const int hq = hk * s.group + r0 / s.L, pos = r0 % s.L;
+          for (int x = 0; x < s.ndv; ++x) tma_store(&map_o, stage + x * kPBox + q4 * 32 * 128, x * 64, pos, hq, b);
+        }
+        bulk_commit();
+      }
+      __syncwarp();
+      return true;
+    }
+    const int r = rt * BM + row;
     __nv_bfloat16 *orow = nullptr;
     if (r < s.R) {
       const int hq = hk * s.group + r / s.L, pos = r % s.L;
@@ -276,7 +343,7 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     }
     for (int c = 0; c < s.dvp / 16; ++c) {
       uint32_t rr[16];
-      tld16(t_o + lane_off + c * 16, rr);
+      tld16(to + c * 16, rr);
       if (orow) {
         __nv_bfloat162 h[8];
 #pragma unroll
@@ -295,7 +362,7 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     }
     fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&o_free);
+    if (lane == 0) mbar_arrive(&o_free[ob]);
     return true;
   };
 
@@ -365,40 +432,62 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     {
       // ---------------- MMA issuer (whole warp; the elected lane issues)
       const uint32_t id_s = idesc(BM, BKV, 0), id_pv = idesc(BM, s.dvp, 1);
+      const uint32_t aq = su32(sq);
+      // S of global block ``itj`` (score buffer jgj % 2); ``last``: the item's last read of Q
+      auto issue_s = [&](int itj, int jgj, bool last) -> bool {
+        const int st = itj % s.stages, sb = jgj & 1;
+        if (!wait_or_abort(&k_full[st], (itj / s.stages) & 1, 530 + st, flag)) return false;
+        if (!wait_or_abort(&s_free[sb], ((jgj >> 1) & 1) ^ 1, 540 + sb, flag)) return false;
+        fence_after();
+        const uint32_t ak = su32(sk_ring + (size_t)st * s.nd * kKVBox);
+        if (elect_one()) {
+          for (int k = 0; k < s.ks; ++k) {
+            const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;  // 64-wide box, 16-wide step
+            mma(tmem + sb * kSCols, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
+                k > 0 ? 1u : 0u);
+          }
+          commit(&s_full[sb]);
+          if (!merged) commit(&k_empty[st]);  // K_j is read once S_j is complete
+          if (last) commit(&q_empty);         // the next item's Q may load now
+        }
+        __syncwarp();
+        return true;
+      };
+      // 128-key blocks, two or more per item: the next item's first S is issued
+      // before this item's last P·V (its Q and K arrive while this item's last
+      // softmax block runs), so the softmax warps find it complete.  (With
+      // 64-key blocks and long key ranges, waiting there for the next Q delayed
+      // the last P·V more than it gained: prefill shape 146 -> 158 us.)
+      const bool ahead = kDblO && nb >= 2;
       int it = 0, jg = 0, local = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < s.items && ok && !aborted(flag); item += gridDim.x, ++local) {
-        if (!wait_or_abort(&q_full, local & 1, 520, flag)) break;
-        fence_after();
-        const uint32_t aq = su32(sq);
-        auto issue_s = [&](int j) -> bool {  // S_j into score buffer (jg + j) % 2
-          const int itj = it + j, jgj = jg + j, st = itj % s.stages, sb = jgj & 1;
-          if (!wait_or_abort(&k_full[st], (itj / s.stages) & 1, 530 + st, flag)) return false;
-          if (!wait_or_abort(&s_free[sb], ((jgj >> 1) & 1) ^ 1, 540 + sb, flag)) return false;
+        if (!(ahead && local > 0)) {
+          if (!wait_or_abort(&q_full, local & 1, 520, flag)) break;
           fence_after();
-          const uint32_t ak = su32(sk_ring + (size_t)st * s.nd * kKVBox);
-          if (elect_one()) {
-            for (int k = 0; k < s.ks; ++k) {
-              const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;  // 64-wide box, 16-wide step
-              mma(tmem + sb * kSCols, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
-                  k > 0 ? 1u : 0u);
-            }
-            commit(&s_full[sb]);
-            if (!merged) commit(&k_empty[st]);  // K_j is read once S_j is complete
-            if (j == nb - 1) commit(&q_empty);  // the item's last read of Q: the next Q may load now
-          }
-          __syncwarp();
-          return true;
-        };
-        if (!issue_s(0)) break;
+          if (!issue_s(it, jg, nb == 1)) break;
+        }
+        const int ob = o_buf(local);
         for (int j = 0; j < nb; ++j) {
-          if (j + 1 < nb && !issue_s(j + 1)) {
-            ok = false;
-            break;
+          if (j + 1 < nb) {
+            if (!issue_s(it + j + 1, jg + j + 1, j + 1 == nb - 1)) {
+              ok = false;
+              break;
+            }
+          } else if (ahead && item + (int)gridDim.x < s.items) {
+            if (!wait_or_abort(&q_full, (local + 1) & 1, 520, flag)) {
+              ok = false;
+              break;
+            }
+            fence_after();
+            if (!issue_s(it + nb, jg + nb, false)) {
+              ok = false;
+              break;
+            }
           }
           const int itj = it + j, jgj = jg + j, st = itj % s.stages, pb = jgj & 1;
-          // the previous item's epilogue has read O before this item's first P·V overwrites it
-          if (j == 0 && !wait_or_abort(&o_free, (local & 1) ^ 1, 521, flag)) {
+          // the epilogue of the item that last used this output buffer has read it
+          if (j == 0 && !wait_or_abort(&o_free[ob], o_phase(local) ^ 1, 521, flag)) {
             ok = false;
             break;
           }
@@ -412,9 +501,10 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
           }
           fence_after();
           const uint32_t ap = su32(sp + pb * kPBytes), av = su32(sv_ring + (size_t)st * s.ndv * kKVBox);
+          const uint32_t to = t_o(local);
           if (elect_one()) {
             for (int k = 0; k < BKV / 16; ++k)  // 16 keys per step: P atom k / 4, V rows k·16
-              mma(t_o, desc_k(ap + (uint32_t)(k >> 2) * kPBox + (uint32_t)(k & 3) * 32),
+              mma(to, desc_k(ap + (uint32_t)(k >> 2) * kPBox + (uint32_t)(k & 3) * 32),
                   desc_mn(av + k * 2048, kKVBox), id_pv, (j > 0 || k > 0) ? 1u : 0u);
             if (!merged) commit(&v_empty[st]);  // V_j is read
             commit(&p_free[pb]);    // P_j is read and O holds blocks ≤ j
@@ -424,7 +514,7 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
         it += nb;
         jg += nb;
         if (!ok) break;
-        if (elect_one()) commit(&o_full);
+        if (elect_one()) commit(&o_full[ob]);
         __syncwarp();
       }
     }
@@ -437,6 +527,12 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     bool ok = true;
     const bool sc_neg = s.scale_log2 < 0.0f;
     const float sc = fabsf(s.scale_log2);
+    // Deferred epilogue (two output buffers): the previous item, run after this
+    // item's first P block; ``staged``: the P tile this warp's TMA store of it
+    // still reads (−1: none), waited for before P is written there again.
+    bool pend = false;
+    int pend_b = 0, pend_hk = 0, pend_rt = 0, pend_local = 0, staged = -1;
+    float pend_l = 0.0f;
     for (int item = blockIdx.x; item < s.items && ok; item += gridDim.x, ++local) {
       int b, hk, rt;
       item_coords(s, item, b, hk, rt);
@@ -517,17 +613,23 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
             l *= alpha;
             m = mx;
           }
+          const uint32_t to = t_o(local) + lane_off;
           for (int c = 0; c < s.dvp / 16; ++c) {
             uint32_t r[16];
-            tld16(t_o + lane_off + c * 16, r);
+            tld16(to + c * 16, r);
 #pragma unroll
             for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tst16(t_o + lane_off + c * 16, r);
+            tst16(to + c * 16, r);
           }
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
         // P_j row as bf16 into the 128-byte-swizzled K-major tile
         // (BKV / 64 swizzle atoms of 64 keys, each 128 rows × 128 B)
+        if (staged == pb) {  // a TMA store still reading this tile finishes first
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+          staged = -1;
+        }
         uint8_t *prow = sp + pb * kPBytes + row * 128;
         const float nm = -m;  // p = 2^(score · scale − m), one FFMA and one ex2
         float part[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
@@ -551,8 +653,29 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
         fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[pb]);
+        if (kDblO && j == 0 && pend) {
+          // the previous item's output: its last P·V has had this block's softmax to finish;
+          // the other P tile is free (its last reader was that P·V)
+          uint8_t *stage = s.o_tma ? sp + (pb ^ 1) * kPBytes : nullptr;
+          if (staged >= 0) {
+            if (lane == 0) bulk_wait_read0();
+            __syncwarp();
+            staged = -1;
+          }
+          if (!attn_epilogue_rows(pend_b, pend_hk, pend_rt, row, lane_off, lane, pend_l, pend_local, stage)) {
+            ok = false;
+            break;
+          }
+          if (stage) staged = pb ^ 1;
+          pend = false;
+        }
       }
       if (!ok) break;
+      if (kDblO) {
+        pend = true;
+        pend_b = b, pend_hk = hk, pend_rt = rt, pend_local = local, pend_l = l;
+        continue;
+      }
       if (sep_epi) {
         // hand the row sums to the epilogue warps (they read O once o_full completes)
         l_rows[local & 1][row] = l;
@@ -560,11 +683,22 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
         if (lane == 0) mbar_arrive(&l_full[local & 1]);
         continue;
       }
-      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l, local)) {
+      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l, local, nullptr)) {
         ok = false;
         break;
       }
     }
+    if (kDblO && ok && pend) {
+      // the last item: every P·V is complete once its O is, so either P tile is free
+      if (staged >= 0) {
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+      }
+      uint8_t *stage = s.o_tma ? sp + (jg & 1) * kPBytes : nullptr;
+      attn_epilogue_rows(pend_b, pend_hk, pend_rt, row, lane_off, lane, pend_l, pend_local, stage);
+    }
+    if (lane == 0) bulk_wait_all();  // this warp's output stores are complete before the CTA exits
+    __syncwarp();
   } else if (Blk<BKV>::kSepEpi && warp >= 8) {
     // ---------------- output epilogue warps: thread = query row (warp - 8)·32 + lane
     const int q4 = warp - 8;
@@ -576,7 +710,7 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
       item_coords(s, item, b, hk, rt);
       const bool lf = wait_or_abort(&l_full[local & 1], (local >> 1) & 1, 585 + (local & 1), flag);
       if (!__all_sync(0xffffffffu, lf)) break;
-      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l_rows[local & 1][row], local)) break;
+      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l_rows[local & 1][row], local, nullptr)) break;
     }
   }
 
@@ -609,20 +743,27 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// bf16 tensor (cols, rows, d2, d3) with element strides (row, s2, s3), boxes of 64 × box_rows.
-int make_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t d2, int64_t d3, int64_t rs,
-             int64_t s2, int64_t s3, int box_rows) {
+// bf16 tensor (cols, rows, d2, d3) with element strides (row, s2, s3), boxes of 64 × box_rows,
+// 128-byte swizzle; the driver's result code, no error recorded.
+CUresult encode_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t d2, int64_t d3,
+                    int64_t rs, int64_t s2, int64_t s3, int box_rows) {
   EncodeTiledFn fn = encode_fn();
-  DP_REQUIRE(fn != nullptr, DP_ERR_CUDA, "attention: cuTensorMapEncodeTiled unavailable");
+  if (fn == nullptr) return CUDA_ERROR_NOT_FOUND;
   if (d2 <= 1) s2 = rows * rs;
   if (d3 <= 1) s3 = d2 * s2;
   cuuint64_t dims[4] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)d2, (cuuint64_t)d3};
   cuuint64_t strides[3] = {(cuuint64_t)(rs * 2), (cuuint64_t)(s2 * 2), (cuuint64_t)(s3 * 2)};
   cuuint32_t box[4] = {64, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+int make_map(CUtensorMap *map, const void *base, int64_t cols, int64_t rows, int64_t d2, int64_t d3, int64_t rs,
+             int64_t s2, int64_t s3, int box_rows) {
+  DP_REQUIRE(encode_fn() != nullptr, DP_ERR_CUDA, "attention: cuTensorMapEncodeTiled unavailable");
+  const CUresult r = encode_map(map, base, cols, rows, d2, d3, rs, s2, s3, box_rows);
   DP_REQUIRE(r == CUDA_SUCCESS, DP_ERR_CUDA,
              "attention: cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
   return DP_OK;
@@ -655,6 +796,14 @@ int launch_blocks(const dp_attention_params &p, Shape s, const void *q, const vo
   if (st != DP_OK) return st;
   st = make_map(&mv, v, p.Dv, p.S, p.heads_kv, p.batch, p.v_ss, p.v_sh, p.v_sb, BKV);
   if (st != DP_OK) return st;
+  // O as (Dv, L, query heads, batch) in boxes of 64 columns × 32 rows, for 128-key blocks
+  // where every warp's 32 rows lie in one head (one query head per item, or L a multiple of 32).
+  CUtensorMap mo;
+  std::memset(&mo, 0, sizeof(mo));
+  s.o_tma = 0;
+  if (Blk<BKV>::kDblO && (p.group == 1 || p.L % 32 == 0) &&
+      encode_map(&mo, o, p.Dv, p.L, p.heads_kv * p.group, p.batch, p.o_sl, p.o_sh, p.o_sb, 32) == CUDA_SUCCESS)
+    s.o_tma = 1;
   const size_t smem = (size_t)s.q_bytes + 2 * Blk<BKV>::kPBytes + (size_t)stages * s.stage_bytes + 1024;
   int dev = 0;
   DP_CHECK_CUDA(cudaGetDevice(&dev));
@@ -666,7 +815,8 @@ int launch_blocks(const dp_attention_params &p, Shape s, const void *q, const vo
   }
   int grid = dp::num_sms();
   if (grid > s.items) grid = s.items;
-  dp::launch_k(attn_kernel<BKV>, grid, Blk<BKV>::kThreads, smem, stream, mq, mk, mv, s, static_cast<__nv_bfloat16 *>(o));
+  dp::launch_k(attn_kernel<BKV>, grid, Blk<BKV>::kThreads, smem, stream, mq, mk, mv, mo, s,
+               static_cast<__nv_bfloat16 *>(o));
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }
