@@ -20,12 +20,8 @@
 //            write P_j = 2^(s − m) as bf16 into one of two 128-byte-swizzled
 //            shared tiles (so P_{j+1} is written while P_j·V_j runs), and at
 //            the end O / l → bf16 → global.
-// With 128-key blocks (head dims ≤ 128) the output accumulator is double
-// buffered in TMEM and an item's epilogue runs after the next item's first P
-// block, so the wait for its last P·V overlaps that softmax; the MMA issuer
-// starts the next item's first Q·Kᵀ before this item's last P·V.  Where every
-// warp's 32 rows lie in one head, O goes out through a free P tile and one
-// TMA tensor store per warp instead of row-per-thread global stores.
+// Head dims ≤ 128 use 128-key blocks in attn_split_kernel (below), whose
+// eight softmax warps split every block's keys in two halves.
 // The running max is raised lazily (only when a block's max exceeds it by
 // more than 2^8): P then stays ≤ 256, exact in bf16's exponent range, and O
 // and l are rescaled by 2^(m_old − m_new) only on those rare blocks.
@@ -45,24 +41,19 @@ constexpr int kMaxStages = 4;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kQBox = BM * 128;    // 16 KB: 128 rows × 64 bf16
 constexpr uint32_t kPBox = BM * 128;    // 16 KB: 128 rows × 64 bf16 keys of P
-// Keys per block: 64, or 128 for head dims ≤ 128 (half the per-block
-// hand-offs; two 128-column score buffers and a ≤ 128-column output still fit
-// the 512 TMEM columns, and two stages still fit shared memory).
+// Keys per block: 64 (attn_kernel), or 128 for head dims ≤ 128
+// (attn_split_kernel: half the per-block hand-offs; two 128-column score
+// buffers and two ≤ 128-column half outputs fit the 512 TMEM columns, and two
+// stages still fit shared memory).
 template <int BKV>
 struct Blk {
   static constexpr int kSCols = BKV;                    // one score buffer: BKV fp32 columns
   static constexpr uint32_t kKVBox = BKV * 128;         // one 64-column box of K or V: BKV rows × 128 B
   static constexpr uint32_t kPBytes = (BKV / 64) * kPBox;  // one P tile: BKV / 64 swizzle atoms along the keys
   // 64-key blocks (head dims above 128) add four output-epilogue warps (8-11),
-  // so the softmax warps start the next item while an item's O is written;
-  // the 128-key kernel keeps the epilogue on the softmax warps (its softmax
-  // needs ~200 registers, which 384 threads could not have).
+  // so the softmax warps start the next item while an item's O is written.
   static constexpr bool kSepEpi = BKV == 64;
   static constexpr int kThreads = kSepEpi ? 384 : 256;
-  // 128-key blocks: two output accumulators (2·128 score + 2·128 output
-  // columns = 512), an item's epilogue deferred past the next item's first
-  // P block (the softmax warps run it).
-  static constexpr bool kDblO = BKV == 128;
 };
 
 struct Shape {
@@ -212,15 +203,13 @@ __device__ __forceinline__ void item_coords(const Shape &s, int item, int &b, in
 template <int BKV>
 __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     attn_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o, const Shape s,
-                __nv_bfloat16 *__restrict__ out) {
+                const __grid_constant__ CUtensorMap map_v, const Shape s, __nv_bfloat16 *__restrict__ out) {
   constexpr int kSCols = Blk<BKV>::kSCols;
   constexpr uint32_t kKVBox = Blk<BKV>::kKVBox;
   constexpr uint32_t kPBytes = Blk<BKV>::kPBytes;
-  constexpr bool kDblO = Blk<BKV>::kDblO;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, q_empty, k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages],
-      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2], p_free[2], o_full[2], o_free[2], l_full[2];
+      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2], p_free[2], o_full, o_free, l_full[2];
   __shared__ float l_rows[2][BM];  // separate epilogue: each row's softmax sum, by item parity
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
@@ -249,10 +238,8 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
       mbar_init(&p_full[i], 4);
       mbar_init(&p_free[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_free[i], 4);
-    }
+    mbar_init(&o_full, 1);
+    mbar_init(&o_free, 4);
     for (int i = 0; i < 2; ++i) mbar_init(&l_full[i], 4);
     abort_flag = 0;
     fence_barrier_init();
@@ -272,11 +259,7 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
   __syncthreads();
   fence_after();
   const uint32_t tmem = tmem_slot;
-  // Output accumulator of an item (by its per-CTA index): one buffer, or two
-  // 128-column buffers by item parity; each buffer's barrier phase counts its uses.
-  auto o_buf = [&](int local) { return kDblO ? (local & 1) : 0; };
-  auto o_phase = [&](int local) { return (uint32_t)(kDblO ? ((local >> 1) & 1) : (local & 1)); };
-  auto t_o = [&](int local) { return tmem + 2 * kSCols + (kDblO ? (uint32_t)(local & 1) * 128u : 0u); };
+  const uint32_t t_o = tmem + 2 * kSCols;  // output accumulator columns
   volatile int *flag = &abort_flag;
   dp::pdl_wait();  // set-up above touches no global memory; the previous kernel's results are visible from here
   const int nb = s.kv_blocks;
@@ -290,52 +273,14 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
   // (l_rows, by item parity) is never rewritten before it is read.
   const bool sep_epi = Blk<BKV>::kSepEpi && nb >= 3;
   // O / l → bf16 → global for the rows of one item (thread = row); waits for
-  // O, releases it.  With ``stage`` (a free P tile, 128-byte swizzled like P)
-  // each warp writes its 32 rows there and one lane stores them with TMA;
-  // otherwise every thread stores its own row.  False when a wait gave up.
-  auto attn_epilogue_rows = [&](int b, int hk, int rt, int row, uint32_t lane_off, int lane, float l, int local,
-                                uint8_t *stage) -> bool {
-    const int ob = o_buf(local);
-    const bool of = wait_or_abort(&o_full[ob], o_phase(local), 580, flag);
+  // O, releases it.  False when a wait gave up.
+  auto attn_epilogue_rows = [&](int b, int hk, int rt, int row, uint32_t lane_off, int lane, float l,
+                                int local) -> bool {
+    const bool of = wait_or_abort(&o_full, local & 1, 580, flag);
     if (!__all_sync(0xffffffffu, of)) return false;
     fence_after();
-    const uint32_t to = t_o(local) + lane_off;
-    const float inv = 1.0f / l;
-    if (stage) {
-      uint8_t *srow = stage + row * 128;
-      const uint32_t sw = (uint32_t)(row & 7);
-      for (int c = 0; c < s.dvp / 16; ++c) {
-        uint32_t rr[16];
-        tld16(to + c * 16, rr);
-        uint32_t w[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          __nv_bfloat162 h =
-              __floats2bfloat162_rn(__uint_as_float(rr[2 * e]) * inv, __uint_as_float(rr[2 * e + 1]) * inv);
-          w[e] = *reinterpret_cast<uint32_t *>(&h);
-        }
-        const int cc = 2 * c;  // 16-byte chunks of 8 columns; 64-column atoms of 128 rows
-        *reinterpret_cast<uint4 *>(srow + (cc >> 3) * kPBox + (((uint32_t)(cc & 7) ^ sw) << 4)) =
-            make_uint4(w[0], w[1], w[2], w[3]);
-        *reinterpret_cast<uint4 *>(srow + ((cc + 1) >> 3) * kPBox + (((uint32_t)((cc + 1) & 7) ^ sw) << 4)) =
-            make_uint4(w[4], w[5], w[6], w[7]);
-      }
-      fence_before();
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&o_free[ob]);  // O is read: the P·V two items on may overwrite it
-        const int q4 = row >> 5, r0 = rt * BM + q4 * 32;
-        if (r0 < s.R) {  // a warp's 32 rows lie in one head (checked on the host)
-          const int hq = hk * s.group + r0 / s.L, pos = r0 % s.L;
-          for (int x = 0; x < s.ndv; ++x) tma_store(&map_o, stage + x * kPBox + q4 * 32 * 128, x * 64, pos, hq, b);
-        }
-        bulk_commit();
-      }
-      __syncwarp();
-      return true;
-    }
     const int r = rt * BM + row;
+    const float inv = 1.0f / l;
     __nv_bfloat16 *orow = nullptr;
     if (r < s.R) {
       const int hq = hk * s.group + r / s.L, pos = r % s.L;
@@ -343,7 +288,7 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     }
     for (int c = 0; c < s.dvp / 16; ++c) {
       uint32_t rr[16];
-      tld16(to + c * 16, rr);
+      tld16(t_o + lane_off + c * 16, rr);
       if (orow) {
         __nv_bfloat162 h[8];
 #pragma unroll
@@ -362,7 +307,7 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     }
     fence_before();
     __syncwarp();
-    if (lane == 0) mbar_arrive(&o_free[ob]);
+    if (lane == 0) mbar_arrive(&o_free);
     return true;
   };
 
@@ -432,62 +377,40 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     {
       // ---------------- MMA issuer (whole warp; the elected lane issues)
       const uint32_t id_s = idesc(BM, BKV, 0), id_pv = idesc(BM, s.dvp, 1);
-      const uint32_t aq = su32(sq);
-      // S of global block ``itj`` (score buffer jgj % 2); ``last``: the item's last read of Q
-      auto issue_s = [&](int itj, int jgj, bool last) -> bool {
-        const int st = itj % s.stages, sb = jgj & 1;
-        if (!wait_or_abort(&k_full[st], (itj / s.stages) & 1, 530 + st, flag)) return false;
-        if (!wait_or_abort(&s_free[sb], ((jgj >> 1) & 1) ^ 1, 540 + sb, flag)) return false;
-        fence_after();
-        const uint32_t ak = su32(sk_ring + (size_t)st * s.nd * kKVBox);
-        if (elect_one()) {
-          for (int k = 0; k < s.ks; ++k) {
-            const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;  // 64-wide box, 16-wide step
-            mma(tmem + sb * kSCols, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
-                k > 0 ? 1u : 0u);
-          }
-          commit(&s_full[sb]);
-          if (!merged) commit(&k_empty[st]);  // K_j is read once S_j is complete
-          if (last) commit(&q_empty);         // the next item's Q may load now
-        }
-        __syncwarp();
-        return true;
-      };
-      // 128-key blocks, two or more per item: the next item's first S is issued
-      // before this item's last P·V (its Q and K arrive while this item's last
-      // softmax block runs), so the softmax warps find it complete.  (With
-      // 64-key blocks and long key ranges, waiting there for the next Q delayed
-      // the last P·V more than it gained: prefill shape 146 -> 158 us.)
-      const bool ahead = kDblO && nb >= 2;
       int it = 0, jg = 0, local = 0;
       bool ok = true;
       for (int item = blockIdx.x; item < s.items && ok && !aborted(flag); item += gridDim.x, ++local) {
-        if (!(ahead && local > 0)) {
-          if (!wait_or_abort(&q_full, local & 1, 520, flag)) break;
+        if (!wait_or_abort(&q_full, local & 1, 520, flag)) break;
+        fence_after();
+        const uint32_t aq = su32(sq);
+        auto issue_s = [&](int j) -> bool {  // S_j into score buffer (jg + j) % 2
+          const int itj = it + j, jgj = jg + j, st = itj % s.stages, sb = jgj & 1;
+          if (!wait_or_abort(&k_full[st], (itj / s.stages) & 1, 530 + st, flag)) return false;
+          if (!wait_or_abort(&s_free[sb], ((jgj >> 1) & 1) ^ 1, 540 + sb, flag)) return false;
           fence_after();
-          if (!issue_s(it, jg, nb == 1)) break;
-        }
-        const int ob = o_buf(local);
+          const uint32_t ak = su32(sk_ring + (size_t)st * s.nd * kKVBox);
+          if (elect_one()) {
+            for (int k = 0; k < s.ks; ++k) {
+              const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;  // 64-wide box, 16-wide step
+              mma(tmem + sb * kSCols, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
+                  k > 0 ? 1u : 0u);
+            }
+            commit(&s_full[sb]);
+            if (!merged) commit(&k_empty[st]);  // K_j is read once S_j is complete
+            if (j == nb - 1) commit(&q_empty);  // the item's last read of Q: the next Q may load now
+          }
+          __syncwarp();
+          return true;
+        };
+        if (!issue_s(0)) break;
         for (int j = 0; j < nb; ++j) {
-          if (j + 1 < nb) {
-            if (!issue_s(it + j + 1, jg + j + 1, j + 1 == nb - 1)) {
-              ok = false;
-              break;
-            }
-          } else if (ahead && item + (int)gridDim.x < s.items) {
-            if (!wait_or_abort(&q_full, (local + 1) & 1, 520, flag)) {
-              ok = false;
-              break;
-            }
-            fence_after();
-            if (!issue_s(it + nb, jg + nb, false)) {
-              ok = false;
-              break;
-            }
+          if (j + 1 < nb && !issue_s(j + 1)) {
+            ok = false;
+            break;
           }
           const int itj = it + j, jgj = jg + j, st = itj % s.stages, pb = jgj & 1;
-          // the epilogue of the item that last used this output buffer has read it
-          if (j == 0 && !wait_or_abort(&o_free[ob], o_phase(local) ^ 1, 521, flag)) {
+          // the previous item's epilogue has read O before this item's first P·V overwrites it
+          if (j == 0 && !wait_or_abort(&o_free, (local & 1) ^ 1, 521, flag)) {
             ok = false;
             break;
           }
@@ -501,10 +424,9 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
           }
           fence_after();
           const uint32_t ap = su32(sp + pb * kPBytes), av = su32(sv_ring + (size_t)st * s.ndv * kKVBox);
-          const uint32_t to = t_o(local);
           if (elect_one()) {
             for (int k = 0; k < BKV / 16; ++k)  // 16 keys per step: P atom k / 4, V rows k·16
-              mma(to, desc_k(ap + (uint32_t)(k >> 2) * kPBox + (uint32_t)(k & 3) * 32),
+              mma(t_o, desc_k(ap + (uint32_t)(k >> 2) * kPBox + (uint32_t)(k & 3) * 32),
                   desc_mn(av + k * 2048, kKVBox), id_pv, (j > 0 || k > 0) ? 1u : 0u);
             if (!merged) commit(&v_empty[st]);  // V_j is read
             commit(&p_free[pb]);    // P_j is read and O holds blocks ≤ j
@@ -514,7 +436,7 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
         it += nb;
         jg += nb;
         if (!ok) break;
-        if (elect_one()) commit(&o_full[ob]);
+        if (elect_one()) commit(&o_full);
         __syncwarp();
       }
     }
@@ -527,12 +449,6 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
     bool ok = true;
     const bool sc_neg = s.scale_log2 < 0.0f;
     const float sc = fabsf(s.scale_log2);
-    // Deferred epilogue (two output buffers): the previous item, run after this
-    // item's first P block; ``staged``: the P tile this warp's TMA store of it
-    // still reads (−1: none), waited for before P is written there again.
-    bool pend = false;
-    int pend_b = 0, pend_hk = 0, pend_rt = 0, pend_local = 0, staged = -1;
-    float pend_l = 0.0f;
     for (int item = blockIdx.x; item < s.items && ok; item += gridDim.x, ++local) {
       int b, hk, rt;
       item_coords(s, item, b, hk, rt);
@@ -613,23 +529,17 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
             l *= alpha;
             m = mx;
           }
-          const uint32_t to = t_o(local) + lane_off;
           for (int c = 0; c < s.dvp / 16; ++c) {
             uint32_t r[16];
-            tld16(to + c * 16, r);
+            tld16(t_o + lane_off + c * 16, r);
 #pragma unroll
             for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-            tst16(to + c * 16, r);
+            tst16(t_o + lane_off + c * 16, r);
           }
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
         // P_j row as bf16 into the 128-byte-swizzled K-major tile
         // (BKV / 64 swizzle atoms of 64 keys, each 128 rows × 128 B)
-        if (staged == pb) {  // a TMA store still reading this tile finishes first
-          if (lane == 0) bulk_wait_read0();
-          __syncwarp();
-          staged = -1;
-        }
         uint8_t *prow = sp + pb * kPBytes + row * 128;
         const float nm = -m;  // p = 2^(score · scale − m), one FFMA and one ex2
         float part[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
@@ -653,29 +563,8 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
         fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&p_full[pb]);
-        if (kDblO && j == 0 && pend) {
-          // the previous item's output: its last P·V has had this block's softmax to finish;
-          // the other P tile is free (its last reader was that P·V)
-          uint8_t *stage = s.o_tma ? sp + (pb ^ 1) * kPBytes : nullptr;
-          if (staged >= 0) {
-            if (lane == 0) bulk_wait_read0();
-            __syncwarp();
-            staged = -1;
-          }
-          if (!attn_epilogue_rows(pend_b, pend_hk, pend_rt, row, lane_off, lane, pend_l, pend_local, stage)) {
-            ok = false;
-            break;
-          }
-          if (stage) staged = pb ^ 1;
-          pend = false;
-        }
       }
       if (!ok) break;
-      if (kDblO) {
-        pend = true;
-        pend_b = b, pend_hk = hk, pend_rt = rt, pend_local = local, pend_l = l;
-        continue;
-      }
       if (sep_epi) {
         // hand the row sums to the epilogue warps (they read O once o_full completes)
         l_rows[local & 1][row] = l;
@@ -683,22 +572,11 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
         if (lane == 0) mbar_arrive(&l_full[local & 1]);
         continue;
       }
-      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l, local, nullptr)) {
+      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l, local)) {
         ok = false;
         break;
       }
     }
-    if (kDblO && ok && pend) {
-      // the last item: every P·V is complete once its O is, so either P tile is free
-      if (staged >= 0) {
-        if (lane == 0) bulk_wait_read0();
-        __syncwarp();
-      }
-      uint8_t *stage = s.o_tma ? sp + (jg & 1) * kPBytes : nullptr;
-      attn_epilogue_rows(pend_b, pend_hk, pend_rt, row, lane_off, lane, pend_l, pend_local, stage);
-    }
-    if (lane == 0) bulk_wait_all();  // this warp's output stores are complete before the CTA exits
-    __syncwarp();
   } else if (Blk<BKV>::kSepEpi && warp >= 8) {
     // ---------------- output epilogue warps: thread = query row (warp - 8)·32 + lane
     const int q4 = warp - 8;
@@ -710,8 +588,444 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
       item_coords(s, item, b, hk, rt);
       const bool lf = wait_or_abort(&l_full[local & 1], (local >> 1) & 1, 585 + (local & 1), flag);
       if (!__all_sync(0xffffffffu, lf)) break;
-      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l_rows[local & 1][row], local, nullptr)) break;
+      if (!attn_epilogue_rows(b, hk, rt, row, lane_off, lane, l_rows[local & 1][row], local)) break;
     }
+  }
+
+  __syncthreads();
+  if (aborted(flag) && threadIdx.x == 0) {
+    const uint64_t t0 = globaltimer_ns();  // let copies and MMAs in flight drain (bounded)
+    while (globaltimer_ns() - t0 < 2000000ull) {
+    }
+  }
+  __syncthreads();
+  if (warp == 2) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// 128-key blocks (head dims ≤ 128) with each block's keys split between two
+// softmax warps per TMEM lane quadrant: warps 4-7 take keys 0-63 of every
+// block, warps 8-11 keys 64-127.  One softmax warp per SM sub-partition was
+// latency-bound (about 1,700 cycles of dependent issue plus 1,000 of MUFU per
+// 128-key block); two warps per sub-partition overlap each other.  Each half
+// keeps its own running max m_h, sum l_h and output accumulator O_h in TMEM
+// (O_h += P_h · V_h over its 64 keys), so the halves never exchange anything
+// per block; at the end of an item they exchange (m_h, l_h) once and every
+// warp writes its share of the columns of
+//   O = (2^(m_0 − M)·O_0 + 2^(m_1 − M)·O_1) / (2^(m_0 − M)·l_0 + 2^(m_1 − M)·l_1),
+// M = max(m_0, m_1).  A half that has seen no valid key yet (short key
+// ranges) has m_h = −∞, l_h = 0, O_h = 0 and weight 0.
+//   TMEM: two 128-column score buffers (S_j = Q·K_jᵀ, N = 128, both halves at
+//   once) and O_0, O_1 at columns 256 and 384.
+//   Shared memory: the layout of attn_kernel<128>; P tile pb holds P_0 in its
+//   first 64-key atom and P_1 in its second.  After an item's last block the
+//   tile the next item writes first carries the (m, l) exchange and the other
+//   tile stages the output for the per-warp TMA tensor stores.
+// ---------------------------------------------------------------------------
+constexpr int kSplitThreads = 384;
+
+__global__ void __launch_bounds__(kSplitThreads, 1)
+    attn_split_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                      const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
+                      const Shape s, __nv_bfloat16 *__restrict__ out) {
+  constexpr int BKV = 128;
+  constexpr uint32_t kKVBox = Blk<BKV>::kKVBox;
+  constexpr uint32_t kPBytes = Blk<BKV>::kPBytes;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t q_full, q_empty, k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages],
+      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2][2], p_free[2][2], o_full, o_free, xch[4], xdone;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sq = smem;
+  uint8_t *sp = sq + s.q_bytes;
+  uint8_t *sk_ring = sp + 2 * kPBytes;
+  uint8_t *sv_ring = sk_ring + (size_t)s.stages * s.nd * kKVBox;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  dp::pdl_trigger();
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 1);
+    mbar_init(&q_empty, 1);
+    for (int i = 0; i < kMaxStages; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 8);
+      for (int h = 0; h < 2; ++h) {
+        mbar_init(&p_full[i][h], 4);
+        mbar_init(&p_free[i][h], 1);
+      }
+    }
+    mbar_init(&o_full, 1);
+    mbar_init(&o_free, 8);
+    for (int i = 0; i < 4; ++i) mbar_init(&xch[i], 2);
+    mbar_init(&xdone, 8);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_q) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_k) : "memory");
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&map_v) : "memory");
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(&tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int *flag = &abort_flag;
+  dp::pdl_wait();
+  const int nb = s.kv_blocks;
+  const bool merged = s.stages == 2;  // K / V slot index = score / P buffer index (block count mod 2)
+
+  if (warp == 0) {
+    // ---------------- TMA producer of Q and K (whole warp; the elected lane issues)
+    int it = 0, local = 0;
+    for (int item = blockIdx.x; item < s.items && !aborted(flag); item += gridDim.x, ++local) {
+      int b, hk, rt;
+      item_coords(s, item, b, hk, rt);
+      if (!wait_or_abort(&q_empty, (local & 1) ^ 1, 600, flag)) break;
+      if (elect_one()) {
+        mbar_arrive_expect_tx(&q_full, s.q_bytes);
+        for (int x = 0; x < s.nd; ++x) tma_load(sq + x * kQBox, &map_q, x * 64, rt * BM, hk, b, &q_full);
+      }
+      __syncwarp();
+      bool ok = true;
+      for (int j = 0; j < nb; ++j, ++it) {
+        const int st = it % s.stages;
+        const bool free_k = merged ? (it < 2 || wait_or_abort(&s_full[st], ((it - 2) >> 1) & 1, 610 + st, flag))
+                                   : wait_or_abort(&k_empty[st], ((it / s.stages) & 1) ^ 1, 610 + st, flag);
+        if (!free_k) {
+          ok = false;
+          break;
+        }
+        uint8_t *sk = sk_ring + (size_t)st * s.nd * kKVBox;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&k_full[st], (uint32_t)s.nd * kKVBox);
+          for (int x = 0; x < s.nd; ++x) tma_load(sk + x * kKVBox, &map_k, x * 64, j * BKV, hk, b, &k_full[st]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 3) {
+    // ---------------- TMA producer of V
+    int it = 0;
+    for (int item = blockIdx.x; item < s.items && !aborted(flag); item += gridDim.x) {
+      int b, hk, rt;
+      item_coords(s, item, b, hk, rt);
+      bool ok = true;
+      for (int j = 0; j < nb; ++j, ++it) {
+        const int st = it % s.stages;
+        // two stages: slot st is free once both halves' P·V of block it − 2 are complete
+        const uint32_t ph = ((it - 2) >> 1) & 1;
+        const bool free_v = merged ? (it < 2 || (wait_or_abort(&p_free[st][0], ph, 615 + st, flag) &&
+                                                 wait_or_abort(&p_free[st][1], ph, 615 + st, flag)))
+                                   : wait_or_abort(&v_empty[st], ((it / s.stages) & 1) ^ 1, 615 + st, flag);
+        if (!free_v) {
+          ok = false;
+          break;
+        }
+        uint8_t *sv = sv_ring + (size_t)st * s.ndv * kKVBox;
+        if (elect_one()) {
+          mbar_arrive_expect_tx(&v_full[st], (uint32_t)s.ndv * kKVBox);
+          for (int x = 0; x < s.ndv; ++x) tma_load(sv + x * kKVBox, &map_v, x * 64, j * BKV, hk, b, &v_full[st]);
+        }
+        __syncwarp();
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer (whole warp; the elected lane issues)
+    const uint32_t id_s = idesc(BM, BKV, 0), id_pv = idesc(BM, s.dvp, 1);
+    const uint32_t aq = su32(sq);
+    auto issue_s = [&](int itj, int jgj, bool last) -> bool {
+      const int st = itj % s.stages, sb = jgj & 1;
+      if (!wait_or_abort(&k_full[st], (itj / s.stages) & 1, 630 + st, flag)) return false;
+      if (!wait_or_abort(&s_free[sb], ((jgj >> 1) & 1) ^ 1, 640 + sb, flag)) return false;
+      fence_after();
+      const uint32_t ak = su32(sk_ring + (size_t)st * s.nd * kKVBox);
+      if (elect_one()) {
+        for (int k = 0; k < s.ks; ++k) {
+          const uint32_t box = (uint32_t)(k >> 2), sub = (uint32_t)(k & 3) * 32;
+          mma(tmem + sb * BKV, desc_k(aq + box * kQBox + sub), desc_k(ak + box * kKVBox + sub), id_s,
+              k > 0 ? 1u : 0u);
+        }
+        commit(&s_full[sb]);
+        if (!merged) commit(&k_empty[st]);
+        if (last) commit(&q_empty);
+      }
+      __syncwarp();
+      return true;
+    };
+    // An item's first S is issued after the previous item's last P·V: issuing
+    // it before made that P·V wait for this item's Q load (about 6,000 cycles
+    // from issue to arrival at the ViT shape; 8% slower).
+    int it = 0, jg = 0, local = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < s.items && ok && !aborted(flag); item += gridDim.x, ++local) {
+      if (!wait_or_abort(&q_full, local & 1, 620, flag)) break;
+      fence_after();
+      if (!issue_s(it, jg, nb == 1)) break;
+      for (int j = 0; j < nb && ok; ++j) {
+        if (j + 1 < nb && !(ok = issue_s(it + j + 1, jg + j + 1, j + 1 == nb - 1))) break;
+        const int itj = it + j, jgj = jg + j, st = itj % s.stages, pb = jgj & 1;
+        // every warp has read the previous item's O_0 and O_1
+        if (j == 0 && !(ok = wait_or_abort(&o_free, (local & 1) ^ 1, 621, flag))) break;
+        if (!(ok = wait_or_abort(&v_full[st], (itj / s.stages) & 1, 635 + st, flag))) break;
+        const uint32_t av = su32(sv_ring + (size_t)st * s.ndv * kKVBox);
+        for (int h = 0; h < 2 && ok; ++h) {
+          if (!(ok = wait_or_abort(&p_full[pb][h], (jgj >> 1) & 1, 650 + 2 * pb + h, flag))) break;
+          fence_after();
+          const uint32_t ap = su32(sp + pb * kPBytes + h * kPBox);
+          if (elect_one()) {
+            for (int k = 0; k < 4; ++k)  // 16 keys per step: V rows (4h + k)·16
+              mma(tmem + 256 + h * 128, desc_k(ap + (uint32_t)k * 32), desc_mn(av + (4 * h + k) * 2048, kKVBox),
+                  id_pv, (j > 0 || k > 0) ? 1u : 0u);
+            commit(&p_free[pb][h]);  // P_h of block j is read, O_h holds blocks ≤ j
+            if (h == 1 && !merged) commit(&v_empty[st]);
+          }
+          __syncwarp();
+        }
+      }
+      it += nb;
+      jg += nb;
+      if (!ok) break;
+      if (elect_one()) commit(&o_full);
+      __syncwarp();
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax halves and the epilogue: thread = query row q4·32 + lane
+    const int h = (warp - 4) >> 2, q4 = warp & 3;
+    const int row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const uint32_t t_oh = tmem + 256 + (uint32_t)h * 128 + lane_off;  // this half's output accumulator
+    const bool sc_neg = s.scale_log2 < 0.0f;
+    const float sc = fabsf(s.scale_log2);
+    const int nchunk = s.dvp / 16, c_lo = 4 * h, c_hi = min(4 * h + 4, nchunk);  // this warp's output columns
+    int jg = 0, local = 0, staged = -1;  // staged: the P tile this warp's TMA store still reads
+    bool ok = true;
+    auto wait_staged = [&](int tile) {
+      if (staged == tile) {
+        if (lane == 0) bulk_wait_read0();
+        __syncwarp();
+        staged = -1;
+      }
+    };
+    for (int item = blockIdx.x; item < s.items && ok; item += gridDim.x, ++local) {
+      int b, hk, rt;
+      item_coords(s, item, b, hk, rt);
+      float m = -INFINITY, l = 0.0f;
+      for (int j = 0; j < nb; ++j, ++jg) {
+        const int sb = jg & 1;
+        if (!__all_sync(0xffffffffu, wait_or_abort(&s_full[sb], (jg >> 1) & 1, 660 + sb, flag))) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        float v[64];
+        {
+          uint32_t r[4][16];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) tld16_async(tmem + lane_off + sb * BKV + h * 64 + c * 16, r[c]);
+          tld_wait();
+#pragma unroll
+          for (int c = 0; c < 4; ++c)
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[c * 16 + e] = __uint_as_float(r[c][e]);
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&s_free[sb]);
+        const int k0 = j * BKV + h * 64;
+        if (sc_neg) {
+#pragma unroll
+          for (int e = 0; e < 64; ++e) v[e] = -v[e];
+        }
+        if (k0 + 64 > s.S) {  // the partial tail of the key range (possibly all of this half)
+#pragma unroll
+          for (int e = 0; e < 64; ++e) v[e] = (k0 + e < s.S) ? v[e] : -INFINITY;
+        }
+        float t8[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float a = fmaxf(fmaxf(v[e], v[e + 8]), fmaxf(v[e + 16], v[e + 24]));
+          const float b2 = fmaxf(fmaxf(v[e + 32], v[e + 40]), fmaxf(v[e + 48], v[e + 56]));
+          t8[e] = fmaxf(a, b2);
+        }
+        const float mx = sc * fmaxf(fmaxf(fmaxf(t8[0], t8[1]), fmaxf(t8[2], t8[3])),
+                                    fmaxf(fmaxf(t8[4], t8[5]), fmaxf(t8[6], t8[7])));
+        const int pb = jg & 1;
+        if (jg >= 2) {  // P_h of block jg − 2 (same tile) has been read
+          if (!__all_sync(0xffffffffu, wait_or_abort(&p_free[pb][h], ((jg >> 1) & 1) ^ 1, 670 + pb, flag))) {
+            ok = false;
+            break;
+          }
+          fence_after();
+        }
+        if (j == 0) {
+          m = mx;
+        } else if (__any_sync(0xffffffffu, mx > m + 8.0f)) {
+          // O_h holds every issued block of this half before it is rescaled
+          const int prev = jg - 1;
+          if (!__all_sync(0xffffffffu, wait_or_abort(&p_free[prev & 1][h], (prev >> 1) & 1, 675, flag))) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          float alpha = 1.0f;
+          if (mx > m + 8.0f) {
+            alpha = ex2(m - mx);  // 0 while this half had no valid key (m = −∞)
+            l *= alpha;
+            m = mx;
+          }
+          for (int c = 0; c < nchunk; ++c) {
+            uint32_t r[16];
+            tld16(t_oh + c * 16, r);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+            tst16(t_oh + c * 16, r);
+          }
+          asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        }
+        if (j == 0 && local > 0) {
+          // the previous item's (m, l) exchange in this tile has been read by every warp
+          if (!__all_sync(0xffffffffu, wait_or_abort(&xdone, (local - 1) & 1, 680, flag))) {
+            ok = false;
+            break;
+          }
+        }
+        wait_staged(pb);
+        uint8_t *prow = sp + pb * kPBytes + h * kPBox + row * 128;
+        const float nm = m == -INFINITY ? 0.0f : -m;  // p = 2^(score · scale − m); 0 for masked keys
+        float part[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int ch = 0; ch < 8; ++ch) {
+          uint32_t w[4];
+          float acc = 0.0f;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float p0 = ex2(fmaf(v[ch * 8 + 2 * q], sc, nm)), p1 = ex2(fmaf(v[ch * 8 + 2 * q + 1], sc, nm));
+            acc += p0 + p1;
+            __nv_bfloat162 bb = __floats2bfloat162_rn(p0, p1);
+            w[q] = *reinterpret_cast<uint32_t *>(&bb);
+          }
+          part[ch] = acc;
+          *reinterpret_cast<uint4 *>(prow + ((ch ^ (row & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+        l += ((part[0] + part[1]) + (part[2] + part[3])) + ((part[4] + part[5]) + (part[6] + part[7]));
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&p_full[pb][h]);
+      }
+      if (!ok) break;
+
+      // ---- end of the item: exchange (m, l) through the tile the next item writes first
+      const int xt = jg & 1, yt = xt ^ 1;  // exchange tile, staging tile
+      if (jg >= 2) {  // this half's P in the exchange tile (block jg − 2) has been read
+        if (!__all_sync(0xffffffffu, wait_or_abort(&p_free[xt][h], ((jg - 2) >> 1) & 1, 685, flag))) {
+          ok = false;
+          break;
+        }
+        fence_after();
+      }
+      wait_staged(xt);
+      *reinterpret_cast<float2 *>(sp + xt * kPBytes + h * kPBox + row * 128) = make_float2(m, l);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xch[q4]);
+      if (!__all_sync(0xffffffffu, wait_or_abort(&xch[q4], local & 1, 686 + q4, flag))) {
+        ok = false;
+        break;
+      }
+      const float2 other = *reinterpret_cast<const float2 *>(sp + xt * kPBytes + (h ^ 1) * kPBox + row * 128);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xdone);
+      const float m0 = h == 0 ? m : other.x, l0 = h == 0 ? l : other.y;
+      const float m1 = h == 0 ? other.x : m, l1 = h == 0 ? other.y : l;
+      const float M = fmaxf(m0, m1);  // finite: key 0 is valid, so half 0 of block 0 has a score
+      const float a0 = ex2(m0 - M), a1 = ex2(m1 - M);
+      const float inv = 1.0f / (a0 * l0 + a1 * l1);
+      const float f0 = a0 * inv, f1 = a1 * inv;
+
+      if (!__all_sync(0xffffffffu, wait_or_abort(&o_full, local & 1, 690, flag))) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      const bool tma = s.o_tma != 0;
+      uint8_t *srow = sp + yt * kPBytes + row * 128;
+      if (tma) wait_staged(yt);
+      const int r = rt * BM + row;
+      __nv_bfloat16 *orow = nullptr;
+      if (!tma && r < s.R) {
+        const int hq = hk * s.group + r / s.L, pos = r % s.L;
+        orow = out + (int64_t)b * s.o_sb + (int64_t)hq * s.o_sh + (int64_t)pos * s.o_sl;
+      }
+      for (int c = c_lo; c < c_hi; ++c) {
+        uint32_t r0[16], r1[16];
+        tld16_async(tmem + 256 + lane_off + c * 16, r0);
+        tld16_async(tmem + 384 + lane_off + c * 16, r1);
+        tld_wait();
+        uint32_t w[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float x0 = fmaf(__uint_as_float(r0[2 * e]), f0, __uint_as_float(r1[2 * e]) * f1);
+          const float x1 = fmaf(__uint_as_float(r0[2 * e + 1]), f0, __uint_as_float(r1[2 * e + 1]) * f1);
+          __nv_bfloat162 hh = __floats2bfloat162_rn(x0, x1);
+          w[e] = *reinterpret_cast<uint32_t *>(&hh);
+        }
+        if (tma) {
+          const int cc = 2 * c;  // 16-byte chunks of 8 columns in the 64-column atom c / 4 (= h)
+          *reinterpret_cast<uint4 *>(srow + (cc >> 3) * kPBox + (((uint32_t)(cc & 7) ^ (uint32_t)(row & 7)) << 4)) =
+              make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4 *>(srow + ((cc + 1) >> 3) * kPBox +
+                                     (((uint32_t)((cc + 1) & 7) ^ (uint32_t)(row & 7)) << 4)) =
+              make_uint4(w[4], w[5], w[6], w[7]);
+        } else if (orow) {
+          const int c0 = c * 16;
+          if (c0 + 16 <= s.Dv) {
+            uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+            dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+            dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+          } else {
+            const __nv_bfloat16 *hv = reinterpret_cast<const __nv_bfloat16 *>(w);
+            for (int e = 0; c0 + e < s.Dv; ++e) orow[c0 + e] = hv[e];
+          }
+        }
+      }
+      fence_before();
+      if (tma) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&o_free);  // O_0 and O_1 are read for this warp's rows and columns
+        if (tma && c_lo < c_hi) {
+          const int r0 = rt * BM + q4 * 32;
+          if (r0 < s.R) {  // a warp's 32 rows lie in one head (checked on the host)
+            const int hq = hk * s.group + r0 / s.L, pos = r0 % s.L;
+            tma_store(&map_o, sp + yt * kPBytes + h * kPBox + q4 * 32 * 128, h * 64, pos, hq, b);
+          }
+          bulk_commit();
+        }
+      }
+      __syncwarp();
+      if (tma && c_lo < c_hi) staged = yt;
+    }
+    if (lane == 0) bulk_wait_all();  // this warp's output stores are complete before the CTA exits
+    __syncwarp();
   }
 
   __syncthreads();
@@ -801,7 +1115,7 @@ int launch_blocks(const dp_attention_params &p, Shape s, const void *q, const vo
   CUtensorMap mo;
   std::memset(&mo, 0, sizeof(mo));
   s.o_tma = 0;
-  if (Blk<BKV>::kDblO && (p.group == 1 || p.L % 32 == 0) &&
+  if (BKV == 128 && (p.group == 1 || p.L % 32 == 0) &&
       encode_map(&mo, o, p.Dv, p.L, p.heads_kv * p.group, p.batch, p.o_sl, p.o_sh, p.o_sb, 32) == CUDA_SUCCESS)
     s.o_tma = 1;
   const size_t smem = (size_t)s.q_bytes + 2 * Blk<BKV>::kPBytes + (size_t)stages * s.stage_bytes + 1024;
@@ -809,14 +1123,25 @@ int launch_blocks(const dp_attention_params &p, Shape s, const void *q, const vo
   DP_CHECK_CUDA(cudaGetDevice(&dev));
   static size_t attr_bytes[64] = {};  // one per kernel instantiation (BKV) and device
   DP_REQUIRE(dev >= 0 && dev < 64, DP_ERR_UNSUPPORTED, "attention: device ordinal out of range");
-  if (smem > attr_bytes[dev]) {
-    DP_CHECK_CUDA(cudaFuncSetAttribute(attn_kernel<BKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_bytes[dev] = smem;
-  }
+  // 128-key blocks run the split-softmax kernel, 64-key blocks attn_kernel
   int grid = dp::num_sms();
   if (grid > s.items) grid = s.items;
-  dp::launch_k(attn_kernel<BKV>, grid, Blk<BKV>::kThreads, smem, stream, mq, mk, mv, mo, s,
-               static_cast<__nv_bfloat16 *>(o));
+  if constexpr (BKV == 128) {
+    if (smem > attr_bytes[dev]) {
+      DP_CHECK_CUDA(
+          cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      attr_bytes[dev] = smem;
+    }
+    dp::launch_k(attn_split_kernel, grid, kSplitThreads, smem, stream, mq, mk, mv, mo, s,
+                 static_cast<__nv_bfloat16 *>(o));
+  } else {
+    if (smem > attr_bytes[dev]) {
+      DP_CHECK_CUDA(cudaFuncSetAttribute(attn_kernel<BKV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      attr_bytes[dev] = smem;
+    }
+    dp::launch_k(attn_kernel<BKV>, grid, Blk<BKV>::kThreads, smem, stream, mq, mk, mv, s,
+                 static_cast<__nv_bfloat16 *>(o));
+  }
   DP_CHECK_CUDA(cudaGetLastError());
   return DP_OK;
 }
