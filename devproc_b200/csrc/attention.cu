@@ -610,7 +610,8 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
 // softmax warps per TMEM lane quadrant: warps 4-7 take keys 0-63 of every
 // block, warps 8-11 keys 64-127.  One softmax warp per SM sub-partition was
 // latency-bound (about 1,700 cycles of dependent issue plus 1,000 of MUFU per
-// 128-key block); two warps per sub-partition overlap each other.  Each half
+// 128-key block); two warps per sub-partition can overlap each other's
+// latencies (measured: a few per cent at the ViT shape).  Each half
 // keeps its own running max m_h, sum l_h and output accumulator O_h in TMEM
 // (O_h += P_h · V_h over its 64 keys), so the halves never exchange anything
 // per block; at the end of an item they exchange (m_h, l_h) once and every
@@ -620,8 +621,9 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
 // ranges) has m_h = −∞, l_h = 0, O_h = 0 and weight 0.
 //   TMEM: two 128-column score buffers (S_j = Q·K_jᵀ, N = 128, both halves at
 //   once) and O_0, O_1 at columns 256 and 384.
-//   Shared memory: the layout of attn_kernel<128>; P tile pb holds P_0 in its
-//   first 64-key atom and P_1 in its second.  After an item's last block the
+//   Shared memory: the Q tile, two P tiles of 128 keys and the K / V rings, as
+//   in attn_kernel; P tile pb holds P_0 in its first 64-key atom and P_1 in its
+//   second.  After an item's last block the
 //   tile the next item writes first carries the (m, l) exchange and the other
 //   tile stages the output for the per-warp TMA tensor stores.
 // ---------------------------------------------------------------------------
