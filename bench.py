@@ -25,8 +25,9 @@ Prints ONE JSON line (rank 0):
   configs        (one GPU) the other benchmark configurations, each with its
                  own CUDA-event timing, roofline, clocks and CPU baseline: the
                  bf16 GEMM template at 4096³ and 8192×2048×16384, the row
-                 reductions over fp32 [65536, 4096], the fp32 token pipeline,
-                 the ViT classifier and the pi0.5-shaped policy.
+                 reductions over fp32 [65536, 4096], the fused attention kernel
+                 alone at the ViT / prefill / expert shapes, the fp32 token
+                 pipeline, the ViT classifier and the pi0.5-shaped policy.
 ``--impl reference`` times only the preprocessing CPU path (rank 0).
 
 Timed regions: before each region a ~2 ms device sleep (outside the region)
