@@ -137,6 +137,19 @@ __device__ __forceinline__ void tld16_async(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// two columns of a warp's 32 TMEM lanes (one value pair per row)
+__device__ __forceinline__ void tst2(uint32_t taddr, float a, float b) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x2.b32 [%0], {%1, %2};" ::"r"(taddr), "r"(__float_as_uint(a)),
+               "r"(__float_as_uint(b))
+               : "memory");
+}
+__device__ __forceinline__ void tld2(uint32_t taddr, float &a, float &b) {
+  uint32_t x, y;
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];" : "=r"(x), "=r"(y) : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  a = __uint_as_float(x);
+  b = __uint_as_float(y);
+}
 __device__ __forceinline__ void tst16(uint32_t taddr, const uint32_t (&r)[16]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
@@ -628,8 +641,16 @@ __global__ void __launch_bounds__(Blk<BKV>::kThreads, 1)
 //   tile stages the output for the per-warp TMA tensor stores.
 // ---------------------------------------------------------------------------
 constexpr int kSplitThreads = 384;
+// Outputs of at most 112 columns (kSep): four more warps (12-15) combine and
+// store each item's output, so the softmax warps go on to the next item as
+// soon as their last P block is written.  A softmax warp leaves its (m, l) in
+// columns 126-127 of its half's O_h in TMEM (the P·V MMAs and rescales touch
+// only the first dvp columns); the epilogue warps read both halves' values and
+// O_0, O_1, release the accumulators and then store the rows.
+constexpr int kSepThreads = 512, kSepMaxDv = 112, kMLCol = 126, kSepChunks = kSepMaxDv / 16;
 
-__global__ void __launch_bounds__(kSplitThreads, 1)
+template <bool kSep>
+__global__ void __launch_bounds__(kSep ? kSepThreads : kSplitThreads, 1)
     attn_split_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                       const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_o,
                       const Shape s, __nv_bfloat16 *__restrict__ out) {
@@ -638,7 +659,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
   constexpr uint32_t kPBytes = Blk<BKV>::kPBytes;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t q_full, q_empty, k_full[kMaxStages], k_empty[kMaxStages], v_full[kMaxStages],
-      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2][2], p_free[2][2], o_full, o_free, xch[4], xdone;
+      v_empty[kMaxStages], s_full[2], s_free[2], p_full[2][2], p_free[2][2], o_full, o_free, xch[4], xdone,
+      lrdy;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -667,7 +689,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       }
     }
     mbar_init(&o_full, 1);
-    mbar_init(&o_free, 8);
+    mbar_init(&o_free, kSep ? 4 : 8);  // the epilogue warps, or all eight softmax warps
+    mbar_init(&lrdy, 8);
     for (int i = 0; i < 4; ++i) mbar_init(&xch[i], 2);
     mbar_init(&xdone, 8);
     abort_flag = 0;
@@ -809,8 +832,8 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
       if (elect_one()) commit(&o_full);
       __syncwarp();
     }
-  } else if (warp >= 4) {
-    // ---------------- softmax halves and the epilogue: thread = query row q4·32 + lane
+  } else if (warp >= 4 && warp < 12) {
+    // ---------------- softmax halves (and the epilogue without kSep): thread = query row q4·32 + lane
     const int h = (warp - 4) >> 2, q4 = warp & 3;
     const int row = q4 * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
@@ -903,7 +926,7 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
           }
           asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         }
-        if (j == 0 && local > 0) {
+        if (!kSep && j == 0 && local > 0) {
           // the previous item's (m, l) exchange in this tile has been read by every warp
           if (!__all_sync(0xffffffffu, wait_or_abort(&xdone, (local - 1) & 1, 680, flag))) {
             ok = false;
@@ -935,6 +958,20 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
         if (lane == 0) mbar_arrive(&p_full[pb][h]);
       }
       if (!ok) break;
+      if constexpr (kSep) {
+        // (m, l) to the epilogue warps, once they have read the previous item's
+        if (local > 0 && !__all_sync(0xffffffffu, wait_or_abort(&o_free, (local - 1) & 1, 694, flag))) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        tst2(tmem + lane_off + 256 + (uint32_t)h * 128 + kMLCol, m, l);
+        asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&lrdy);
+        continue;
+      }
 
       // ---- end of the item: exchange (m, l) through the tile the next item writes first
       const int xt = jg & 1, yt = xt ^ 1;  // exchange tile, staging tile
@@ -1028,6 +1065,61 @@ __global__ void __launch_bounds__(kSplitThreads, 1)
     }
     if (lane == 0) bulk_wait_all();  // this warp's output stores are complete before the CTA exits
     __syncwarp();
+  } else if (kSep && warp >= 12) {
+    // ---------------- output epilogue (kSep): thread = query row q4·32 + lane, every column
+    const int q4 = warp & 3, row = q4 * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const int nchunk = s.dvp / 16;
+    int local = 0;
+    for (int item = blockIdx.x; item < s.items && !aborted(flag); item += gridDim.x, ++local) {
+      int b, hk, rt;
+      item_coords(s, item, b, hk, rt);
+      if (!__all_sync(0xffffffffu, wait_or_abort(&lrdy, local & 1, 695, flag))) break;
+      if (!__all_sync(0xffffffffu, wait_or_abort(&o_full, local & 1, 696, flag))) break;
+      fence_after();
+      float m0, l0, m1, l1;
+      tld2(tmem + lane_off + 256 + kMLCol, m0, l0);
+      tld2(tmem + lane_off + 384 + kMLCol, m1, l1);
+      const float M = fmaxf(m0, m1);  // finite: key 0 is valid, so half 0 of block 0 has a score
+      const float a0 = ex2(m0 - M), a1 = ex2(m1 - M);
+      const float inv = 1.0f / (a0 * l0 + a1 * l1);
+      const float f0 = a0 * inv, f1 = a1 * inv;
+      uint32_t pk[kSepChunks][8];  // the row as bf16 pairs, so the accumulators are released before the stores
+#pragma unroll
+      for (int c = 0; c < kSepChunks; ++c) {
+        if (c < nchunk) {
+          uint32_t r0[16], r1[16];
+          tld16_async(tmem + lane_off + 256 + c * 16, r0);
+          tld16_async(tmem + lane_off + 384 + c * 16, r1);
+          tld_wait();
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float x0 = fmaf(__uint_as_float(r0[2 * e]), f0, __uint_as_float(r1[2 * e]) * f1);
+            const float x1 = fmaf(__uint_as_float(r0[2 * e + 1]), f0, __uint_as_float(r1[2 * e + 1]) * f1);
+            __nv_bfloat162 hh = __floats2bfloat162_rn(x0, x1);
+            pk[c][e] = *reinterpret_cast<uint32_t *>(&hh);
+          }
+        }
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&o_free);  // O_0, O_1 and (m, l) are read for this warp's rows
+      const int r = rt * BM + row;
+      if (r < s.R) {
+        const int hq = hk * s.group + r / s.L, pos = r % s.L;
+        __nv_bfloat16 *orow = out + (int64_t)b * s.o_sb + (int64_t)hq * s.o_sh + (int64_t)pos * s.o_sl;
+#pragma unroll
+        for (int c = 0; c < kSepChunks; ++c) {
+          const int c0 = c * 16;
+          if (c < nchunk) {
+            uint4 *dst = reinterpret_cast<uint4 *>(orow + c0);
+            dst[0] = make_uint4(pk[c][0], pk[c][1], pk[c][2], pk[c][3]);
+            // Dv is a multiple of 8: a last chunk holds 8 or 16 columns
+            if (c0 + 16 <= s.Dv) dst[1] = make_uint4(pk[c][4], pk[c][5], pk[c][6], pk[c][7]);
+          }
+        }
+      }
+    }
   }
 
   __syncthreads();
@@ -1129,12 +1221,16 @@ int launch_blocks(const dp_attention_params &p, Shape s, const void *q, const vo
   int grid = dp::num_sms();
   if (grid > s.items) grid = s.items;
   if constexpr (BKV == 128) {
-    if (smem > attr_bytes[dev]) {
-      DP_CHECK_CUDA(
-          cudaFuncSetAttribute(attn_split_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      attr_bytes[dev] = smem;
+    // outputs of at most 112 columns: separate epilogue warps
+    const bool sep = s.dvp <= kSepMaxDv;
+    static size_t attr_sep[64] = {};
+    size_t &attr = sep ? attr_sep[dev] : attr_bytes[dev];
+    auto kern = sep ? attn_split_kernel<true> : attn_split_kernel<false>;
+    if (smem > attr) {
+      DP_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      attr = smem;
     }
-    dp::launch_k(attn_split_kernel, grid, kSplitThreads, smem, stream, mq, mk, mv, mo, s,
+    dp::launch_k(kern, grid, sep ? kSepThreads : kSplitThreads, smem, stream, mq, mk, mv, mo, s,
                  static_cast<__nv_bfloat16 *>(o));
   } else {
     if (smem > attr_bytes[dev]) {
